@@ -1,0 +1,186 @@
+/*
+ * synapse_cuda.h -- C ABI of the B200 (sm_100a) backend for Synapse's
+ * quantized-matmul hot path.
+ *
+ * Conventions follow synapse.h (reference: synapse/synapse.h:25-35 and
+ * zig/src/ffi/exports.zig:1-3,55-63): every function returns a syn_status_t,
+ * no exception crosses the boundary, null pointers are checked first, and a
+ * zero-sized call returns SYN_OK without touching memory. Unlike the CPU
+ * library, compute entry points take DEVICE pointers and a cudaStream_t
+ * (passed as void*, NULL = legacy default stream); they are stream-ordered
+ * and never synchronise. Handles (context, weights) are library-owned.
+ *
+ * Paths cited below are relative to the reference's `synapse/` root.
+ */
+#ifndef SYNAPSE_CUDA_H
+#define SYNAPSE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* Status codes: 0-8 are synapse.h:27-35; 9-12 are new for the GPU.    */
+/* ------------------------------------------------------------------ */
+typedef int32_t syn_status_t;
+
+#define SYN_OK                     0
+#define SYN_ERR_NULL_PTR           1
+#define SYN_ERR_INVALID_ARG        2
+#define SYN_ERR_OUT_OF_MEMORY      3
+#define SYN_ERR_SHAPE_MISMATCH     4
+#define SYN_ERR_NOT_CONTIGUOUS     5
+#define SYN_ERR_INVALID_AXIS       6
+#define SYN_ERR_INVALID_DIMENSIONS 7
+#define SYN_ERR_INTERNAL           8
+#define SYN_ERR_CUDA               9
+#define SYN_ERR_NCCL               10
+#define SYN_ERR_TIMEOUT            11
+#define SYN_ERR_UNSUPPORTED        12
+
+/* Capability report: same struct as synapse.h (syn_capability_summary_t,
+ * zig/src/ffi/exports.zig:98-106) with a new backend id. */
+#ifndef SYN_CAPABILITY_SUMMARY_DEFINED
+#define SYN_CAPABILITY_SUMMARY_DEFINED
+typedef struct syn_capability_summary_t {
+    uint32_t abi_version;
+    uint32_t target_arch;
+    uint32_t target_os;
+    uint32_t simd_backend;
+    uint32_t runtime_profile;
+    uint32_t support_level;
+    uint64_t feature_bits;
+} syn_capability_summary_t;
+#endif
+
+#define SYN_BACKEND_CUDA_SM100 3
+#define SYN_CUDA_FEATURE_INT8_QUANT (1ULL << 4)  /* = SYN_FEATURE_INT8_QUANT */
+#define SYN_CUDA_FEATURE_Q4_0_GEMV  (1ULL << 5)  /* = SYN_FEATURE_Q4_0_GEMV */
+#define SYN_CUDA_FEATURE_QMATMUL    (1ULL << 16) /* format-generic weight handles */
+
+/* Weight formats accepted by syn_cuda_weight_upload. */
+typedef enum syn_qformat_t {
+    SYN_QFMT_INT8_KN = 0, /* reference GEMM layout: int8 [K,N] + f32 scales [N]
+                             (quantization/primitives/int8_linear.rs:10-18) */
+    SYN_QFMT_Q4_0 = 1,    /* GGUF blocks, 18 B / 32 (weight_loading/gguf.rs:294-330) */
+    SYN_QFMT_Q8_0 = 2,    /* GGUF blocks, 34 B / 32 (gguf.rs:255-288) */
+    SYN_QFMT_Q4_K = 3,    /* GGUF super-blocks, 144 B / 256 (gguf.rs:375-431) */
+    SYN_QFMT_Q6_K = 4     /* GGUF super-blocks, 210 B / 256 (gguf.rs:440-487) */
+} syn_qformat_t;
+
+typedef struct syn_cuda_ctx_s syn_cuda_ctx_t;
+typedef struct syn_cuda_weight_s syn_cuda_weight_t;
+
+/* ------------------------------------------------------------------ */
+/* Context and capability                                              */
+/* ------------------------------------------------------------------ */
+
+/* Binds a device and creates the library state for it. New (the CPU
+ * library has no context); replaces the implicit global state of
+ * zig/src/ffi/exports.zig:47-49. */
+syn_status_t syn_cuda_context_create(int device, syn_cuda_ctx_t **out);
+syn_status_t syn_cuda_context_destroy(syn_cuda_ctx_t *ctx);
+
+/* Replaces syn_capability_summary (zig/src/ffi/exports.zig:230-290). */
+syn_status_t syn_cuda_capability_summary(syn_capability_summary_t *out);
+
+/* Text of a status code, and of the last CUDA error seen on this thread. */
+const char *syn_cuda_status_string(syn_status_t status);
+const char *syn_cuda_last_error(void);
+
+/* ------------------------------------------------------------------ */
+/* Reference-mirroring entry points (device pointers, stream-ordered)  */
+/* ------------------------------------------------------------------ */
+
+/* Replaces syn_quantize_per_channel_int8 (synapse.h:341-350,
+ * zig/src/ffi/exports.zig:1275-1289, zig/src/ops/quantize.zig:12-47).
+ * Bit-exact with the reference. channels==0 or channel_size==0 ->
+ * SYN_ERR_INVALID_ARG, as in the reference. */
+syn_status_t syn_cuda_quantize_per_channel_int8(const float *data,
+                                                size_t channels,
+                                                size_t channel_size,
+                                                int8_t *out, float *scales,
+                                                void *stream);
+
+/* Load-time weight quantisation on the device: replaces
+ * MinMaxCalibration::compute_scales (quantization/primitives/calibration.rs:11-24)
+ * + QuantizedLinear::from_f32_with_scales + transpose_i8
+ * (quantization/primitives/int8_linear.rs:21-70). w: f32 [n,k] row-major;
+ * out_kn: int8 [k,n] (the reference's GEMM layout); scales: f32 [n].
+ * Bit-exact with the reference. */
+syn_status_t syn_cuda_quantize_weights_int8(const float *w, size_t n, size_t k,
+                                            int8_t *out_kn, float *scales,
+                                            void *stream);
+
+/* Replaces syn_qgemm_int8 (synapse.h:359-368,
+ * zig/src/ffi/exports.zig:1313-1350, zig/src/ops/qmatmul.zig:37-99).
+ * C = diag(scales_a) (A_i8 B_i8) diag(scales_b), B in the reference's
+ * [K,N] layout with row stride ldb. C is fully overwritten. Bit-exact with
+ * the reference, including the M>16 per-512-K-chunk float epilogue. */
+syn_status_t syn_cuda_qgemm_int8(size_t m, size_t n, size_t k,
+                                 const int8_t *a, size_t lda,
+                                 const int8_t *b, size_t ldb,
+                                 float *c, size_t ldc,
+                                 const float *scales_a,
+                                 const float *scales_b, void *stream);
+
+/* Replaces syn_q4_0_gemv (zig/src/ffi/exports.zig:1614-1628, bound at
+ * crates/synapse-sys/src/lib.rs:413-420; qmatmul.zig:276-343). b_q4 holds
+ * the raw 18-byte Q4_0 blocks of an [N,K] matrix. k % 32 != 0 ->
+ * SYN_ERR_SHAPE_MISMATCH. Matches within 1e-3 relative error. */
+syn_status_t syn_cuda_q4_0_gemv(size_t n, size_t k, const float *a,
+                                const uint8_t *b_q4, float *c, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* Weight handles: one-time repack into the coalesced HBM layout       */
+/* ------------------------------------------------------------------ */
+
+/* Uploads one linear layer's weights (host memory) and repacks them on the
+ * device. Replaces the load-time step of QuantizedLinear::from_f32
+ * (int8_linear.rs:35-70, INT8_KN: host = int8 [K,N], scales = f32 [N]) and
+ * of the GGUF loader (weight_loading/gguf.rs:156-248, block formats:
+ * host = raw blocks of an [N,K] row-major matrix, scales = NULL).
+ * Block formats need k % 32 (Q4_0, Q8_0) or k % 256 (Q4_K, Q6_K) == 0,
+ * else SYN_ERR_SHAPE_MISMATCH. Synchronous. */
+syn_status_t syn_cuda_weight_upload(syn_cuda_ctx_t *ctx, syn_qformat_t fmt,
+                                    const void *host, size_t n, size_t k,
+                                    const float *scales_or_null,
+                                    syn_cuda_weight_t **out);
+syn_status_t syn_cuda_weight_destroy(syn_cuda_weight_t *w);
+
+/* Device bytes held by the repacked weight (HBM footprint). */
+syn_status_t syn_cuda_weight_bytes(const syn_cuda_weight_t *w, size_t *bytes);
+
+/* Debug hook: writes the dequantised [N,K] f32 matrix to host memory with
+ * the reference's own formulas (gguf.rs:255-487 for block formats,
+ * dequantizePerChannelInt8 quantize.zig:90-106 for INT8), bit-exact. */
+syn_status_t syn_cuda_weight_dequant(const syn_cuda_weight_t *w,
+                                     float *host_out);
+
+/* Format-generic fused dequant matmul: y[m,N] = x[m,K] * W^T on device
+ * pointers. INT8: quantises each x row (quantize.zig:12-47) and applies the
+ * W8A8 product bit-exactly like QuantizedLinear::forward
+ * (int8_linear.rs:87-117). Block formats follow the reference's route
+ * "dequantise to f32, then matmul_t" (gguf.rs + ops/matmul.rs:55-79)
+ * within 1e-3 relative error. */
+syn_status_t syn_cuda_qmatmul(syn_cuda_ctx_t *ctx, const syn_cuda_weight_t *w,
+                              const float *x, size_t m, float *y,
+                              void *stream);
+
+/* INT8 weight handle with activations already quantised (x_i8 [m,K],
+ * scales_x [m]); mirrors QuantizedLinear::forward_pre_quantized
+ * (int8_linear.rs:124-165). Bit-exact. */
+syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t *ctx,
+                                            const syn_cuda_weight_t *w,
+                                            const int8_t *x_i8,
+                                            const float *scales_x, size_t m,
+                                            float *y, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SYNAPSE_CUDA_H */

@@ -1,0 +1,56 @@
+"""ctypes binding of libsynapse_cuda.so (include/synapse_cuda.h).
+
+The library is loaded from this package directory only; there is no fallback.
+If it is missing, importing synapse_b200 raises ImportError with the build
+command to run.
+"""
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsynapse_cuda.so")
+
+c_size = ctypes.c_size_t
+c_vp = ctypes.c_void_p
+c_st = ctypes.c_int32
+
+# name -> (restype, argtypes). Every symbol declared in include/synapse_cuda.h.
+SIGNATURES = {
+    "syn_cuda_context_create": (c_st, [ctypes.c_int, ctypes.POINTER(c_vp)]),
+    "syn_cuda_context_destroy": (c_st, [c_vp]),
+    "syn_cuda_capability_summary": (c_st, [c_vp]),
+    "syn_cuda_status_string": (ctypes.c_char_p, [c_st]),
+    "syn_cuda_last_error": (ctypes.c_char_p, []),
+    "syn_cuda_quantize_per_channel_int8": (c_st, [c_vp, c_size, c_size, c_vp, c_vp, c_vp]),
+    "syn_cuda_quantize_weights_int8": (c_st, [c_vp, c_size, c_size, c_vp, c_vp, c_vp]),
+    "syn_cuda_qgemm_int8": (c_st, [c_size, c_size, c_size, c_vp, c_size, c_vp, c_size, c_vp,
+                                   c_size, c_vp, c_vp, c_vp]),
+    "syn_cuda_q4_0_gemv": (c_st, [c_size, c_size, c_vp, c_vp, c_vp, c_vp]),
+    "syn_cuda_weight_upload": (c_st, [c_vp, ctypes.c_int, c_vp, c_size, c_size, c_vp,
+                                      ctypes.POINTER(c_vp)]),
+    "syn_cuda_weight_destroy": (c_st, [c_vp]),
+    "syn_cuda_weight_bytes": (c_st, [c_vp, ctypes.POINTER(c_size)]),
+    "syn_cuda_weight_dequant": (c_st, [c_vp, c_vp]),
+    "syn_cuda_qmatmul": (c_st, [c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
+    "syn_cuda_qmatmul_int8_prequant": (c_st, [c_vp, c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
+}
+
+
+class CapabilitySummary(ctypes.Structure):
+    _fields_ = [("abi_version", ctypes.c_uint32), ("target_arch", ctypes.c_uint32),
+                ("target_os", ctypes.c_uint32), ("simd_backend", ctypes.c_uint32),
+                ("runtime_profile", ctypes.c_uint32), ("support_level", ctypes.c_uint32),
+                ("feature_bits", ctypes.c_uint64)]
+
+
+def load(path=LIB_PATH):
+    if not os.path.exists(path):
+        raise ImportError(
+            f"{path} is missing: build it with `python -m synapse_b200.build` "
+            "(the CUDA backend has no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib

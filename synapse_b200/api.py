@@ -1,0 +1,286 @@
+"""Python mirror of the reference's interface for the quantized-matmul path.
+
+Function names, argument meaning and error behaviour follow the reference's
+safe wrappers (crates/synapse-core/src/lib.rs:602-775) and the INT8 layer
+(crates/synapse-inference/src/quantization/primitives/int8_linear.rs), but
+operate on CUDA tensors through the C ABI in include/synapse_cuda.h. torch
+is used only for device memory and the current stream.
+"""
+import ctypes
+import enum
+
+import torch
+
+from . import _lib
+
+
+class SynapseError(RuntimeError):
+    """Mirrors synapse_core::SynapseError (status code -> variant)."""
+
+    NAMES = {1: "NullPointer", 2: "InvalidArg", 3: "OutOfMemory", 4: "ShapeMismatch",
+             5: "NotContiguous", 6: "InvalidAxis", 7: "InvalidDimensions", 8: "Internal",
+             9: "Cuda", 10: "Nccl", 11: "Timeout", 12: "Unsupported"}
+
+    def __init__(self, status, where=""):
+        self.status = int(status)
+        self.variant = self.NAMES.get(self.status, "Unknown")
+        detail = ""
+        if self.status == 9:
+            detail = " " + lib().syn_cuda_last_error().decode(errors="replace")
+        super().__init__(f"{where}: {self.variant} ({self.status}){detail}")
+
+
+_LIB = None
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        from . import lib as loaded
+        _LIB = loaded
+    return _LIB
+
+
+def _check(status, where):
+    if status != 0:
+        raise SynapseError(status, where)
+
+
+class QFormat(enum.IntEnum):
+    INT8_KN = 0
+    Q4_0 = 1
+    Q8_0 = 2
+    Q4_K = 3
+    Q6_K = 4
+
+
+_BLOCK = {QFormat.Q4_0: (32, 18), QFormat.Q8_0: (32, 34), QFormat.Q4_K: (256, 144),
+          QFormat.Q6_K: (256, 210)}
+
+
+def row_bytes(fmt, k):
+    """Bytes of one K-element row in the reference's storage format."""
+    fmt = QFormat(fmt)
+    if fmt == QFormat.INT8_KN:
+        return k
+    elems, nbytes = _BLOCK[fmt]
+    if k % elems:
+        raise SynapseError(4, "row_bytes")
+    return k // elems * nbytes
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            raise SynapseError(2, "expected CUDA tensors")
+        if not t.is_contiguous():
+            raise SynapseError(5, "expected contiguous tensors")
+
+
+def capability_summary():
+    s = _lib.CapabilitySummary()
+    _check(lib().syn_cuda_capability_summary(ctypes.byref(s)), "capability_summary")
+    return {f: getattr(s, f) for f, _ in s._fields_}
+
+
+def quantize_per_channel_int8(data, channels, channel_size):
+    """synapse_core::quantize_per_channel_int8 (synapse-core/src/lib.rs:602-625):
+    returns (int8 [channels*channel_size], f32 [channels])."""
+    if channels == 0 or channel_size == 0:
+        raise SynapseError(2, "quantize_per_channel_int8")
+    if data.numel() != channels * channel_size:
+        raise SynapseError(4, "quantize_per_channel_int8")
+    _need_cuda(data)
+    out = torch.empty(channels * channel_size, dtype=torch.int8, device=data.device)
+    scales = torch.empty(channels, dtype=torch.float32, device=data.device)
+    _check(lib().syn_cuda_quantize_per_channel_int8(_ptr(data), channels, channel_size,
+                                                    _ptr(out), _ptr(scales), _stream(data)),
+           "quantize_per_channel_int8")
+    return out, scales
+
+
+def quantize_weights_int8(w, out_features, in_features):
+    """MinMaxCalibration + QuantizedLinear::from_f32_with_scales + transpose_i8
+    (int8_linear.rs:35-70): returns (int8 [in, out] GEMM layout, f32 [out])."""
+    _need_cuda(w)
+    if w.numel() != out_features * in_features:
+        raise SynapseError(4, "quantize_weights_int8")
+    q = torch.empty(in_features * out_features, dtype=torch.int8, device=w.device)
+    s = torch.empty(out_features, dtype=torch.float32, device=w.device)
+    _check(lib().syn_cuda_quantize_weights_int8(_ptr(w), out_features, in_features, _ptr(q),
+                                                _ptr(s), _stream(w)), "quantize_weights_int8")
+    return q, s
+
+
+def qgemm_int8(m, n, k, a, b, scales_a, scales_b):
+    """synapse_core::qgemm_int8 (synapse-core/src/lib.rs:654-689): lda=k,
+    ldb=n, ldc=n; returns f32 [m*n]."""
+    if m == 0 or n == 0 or k == 0:
+        return torch.zeros(m * n, dtype=torch.float32,
+                           device=a.device if isinstance(a, torch.Tensor) else "cuda")
+    if a.numel() < m * k or b.numel() < k * n:
+        raise SynapseError(4, "qgemm_int8")
+    if scales_a.numel() < m or scales_b.numel() < n:
+        raise SynapseError(4, "qgemm_int8")
+    _need_cuda(a, b, scales_a, scales_b)
+    c = torch.empty(m * n, dtype=torch.float32, device=a.device)
+    _check(lib().syn_cuda_qgemm_int8(m, n, k, _ptr(a), k, _ptr(b), n, _ptr(c), n,
+                                     _ptr(scales_a), _ptr(scales_b), _stream(a)), "qgemm_int8")
+    return c
+
+
+def q4_0_gemv(n, k, a, b_q4):
+    """synapse_core::q4_0_gemv (synapse-core/src/lib.rs:754-775): returns f32 [n]."""
+    if n == 0 or k == 0:
+        return torch.zeros(n, dtype=torch.float32, device="cuda")
+    if k % 32 != 0:
+        raise SynapseError(4, "q4_0_gemv")
+    if a.numel() < k:
+        raise SynapseError(4, "q4_0_gemv")
+    _need_cuda(a, b_q4)
+    if b_q4.numel() < n * (k // 32) * 18:
+        raise SynapseError(4, "q4_0_gemv")
+    c = torch.empty(n, dtype=torch.float32, device=a.device)
+    _check(lib().syn_cuda_q4_0_gemv(n, k, _ptr(a), _ptr(b_q4), _ptr(c), _stream(a)),
+           "q4_0_gemv")
+    return c
+
+
+class Context:
+    """One library context per device (syn_cuda_context_create)."""
+
+    def __init__(self, device=0):
+        self.device = int(device)
+        h = ctypes.c_void_p()
+        _check(lib().syn_cuda_context_create(self.device, ctypes.byref(h)), "context_create")
+        self.handle = h
+
+    def close(self):
+        if self.handle:
+            lib().syn_cuda_context_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class QuantizedWeight:
+    """A repacked weight matrix [n, k] held in HBM (syn_cuda_weight_upload).
+
+    `data` is host bytes in the reference's storage format: for INT8_KN the
+    int8 [k, n] GEMM layout with `scales` f32 [n]; for block formats the raw
+    GGUF blocks of the row-major [n, k] matrix.
+    """
+
+    def __init__(self, ctx, fmt, data, n, k, scales=None):
+        import numpy as np
+        self.ctx, self.fmt, self.n, self.k = ctx, QFormat(fmt), int(n), int(k)
+        buf = np.ascontiguousarray(np.asarray(data).view(np.uint8).reshape(-1))
+        if buf.size < self.n * row_bytes(self.fmt, self.k):
+            raise SynapseError(4, "QuantizedWeight")
+        sc = None
+        if scales is not None:
+            sc = np.ascontiguousarray(np.asarray(scales, dtype=np.float32))
+        h = ctypes.c_void_p()
+        _check(lib().syn_cuda_weight_upload(
+            ctx.handle, int(self.fmt), buf.ctypes.data_as(ctypes.c_void_p), self.n, self.k,
+            sc.ctypes.data_as(ctypes.c_void_p) if sc is not None else None, ctypes.byref(h)),
+            "weight_upload")
+        self.handle = h
+
+    @property
+    def device_bytes(self):
+        v = ctypes.c_size_t()
+        _check(lib().syn_cuda_weight_bytes(self.handle, ctypes.byref(v)), "weight_bytes")
+        return v.value
+
+    @property
+    def format_bytes(self):
+        """Bytes of the weight in the reference's own format (roofline basis)."""
+        extra = 4 * self.n if self.fmt == QFormat.INT8_KN else 0
+        return self.n * row_bytes(self.fmt, self.k) + extra
+
+    def dequant(self):
+        import numpy as np
+        out = np.empty((self.n, self.k), dtype=np.float32)
+        _check(lib().syn_cuda_weight_dequant(self.handle, out.ctypes.data_as(ctypes.c_void_p)),
+               "weight_dequant")
+        return out
+
+    def matmul(self, x, out=None):
+        """y [m, n] = x [m, k] @ W^T (syn_cuda_qmatmul)."""
+        _need_cuda(x)
+        if x.dtype != torch.float32 or x.shape[-1] != self.k:
+            raise SynapseError(4, "matmul")
+        m = x.numel() // self.k
+        if out is None:
+            out = torch.empty(m, self.n, dtype=torch.float32, device=x.device)
+        _check(lib().syn_cuda_qmatmul(self.ctx.handle, self.handle, _ptr(x), m, _ptr(out),
+                                      _stream(x)), "qmatmul")
+        return out
+
+    def matmul_pre_quantized(self, x_int8, scales_x, m, out=None):
+        _need_cuda(x_int8, scales_x)
+        if out is None:
+            out = torch.empty(m, self.n, dtype=torch.float32, device=x_int8.device)
+        _check(lib().syn_cuda_qmatmul_int8_prequant(self.ctx.handle, self.handle, _ptr(x_int8),
+                                                    _ptr(scales_x), m, _ptr(out),
+                                                    _stream(x_int8)), "qmatmul_int8_prequant")
+        return out
+
+    def close(self):
+        if self.handle:
+            lib().syn_cuda_weight_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class QuantizedLinear:
+    """Mirror of QuantizedLinear (int8_linear.rs:10-171) on the GPU.
+
+    from_f32 quantises on the device with the reference's calibration and
+    rounding, keeps the reference's [in, out] int8 layout plus [out] scales
+    (for inspection / memory_bytes) and holds a repacked weight handle.
+    """
+
+    def __init__(self, ctx, weights_int8, scales, out_features, in_features):
+        self.weights_int8 = weights_int8  # host numpy int8 [in*out]
+        self.scales = scales              # host numpy f32 [out]
+        self.out_features, self.in_features = out_features, in_features
+        self.weight = QuantizedWeight(ctx, QFormat.INT8_KN, weights_int8, out_features,
+                                      in_features, scales)
+
+    @classmethod
+    def from_f32(cls, ctx, weights, out_features, in_features):
+        w = torch.as_tensor(weights, dtype=torch.float32).reshape(-1).to(f"cuda:{ctx.device}")
+        q, s = quantize_weights_int8(w.contiguous(), out_features, in_features)
+        return cls(ctx, q.cpu().numpy(), s.cpu().numpy(), out_features, in_features)
+
+    def forward(self, x, m):
+        if m == 0 or self.in_features == 0 or self.out_features == 0:
+            return torch.zeros(m * self.out_features, dtype=torch.float32, device="cuda")
+        return self.weight.matmul(x.reshape(m, self.in_features)).reshape(-1)
+
+    def forward_pre_quantized(self, x_int8, scales_x, m):
+        if m == 0:
+            return torch.zeros(0, dtype=torch.float32, device="cuda")
+        return self.weight.matmul_pre_quantized(x_int8, scales_x, m).reshape(-1)
+
+    def memory_bytes(self):
+        return self.weights_int8.size + 4 * self.scales.size

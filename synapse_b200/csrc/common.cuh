@@ -1,0 +1,127 @@
+// common.cuh -- shared helpers for the sm_100a quantized-matmul backend.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/synapse_cuda.h"
+
+namespace syn {
+
+// ----------------------------------------------------------------------------
+// Error plumbing: every entry point returns a syn_status_t; CUDA errors map to
+// SYN_ERR_CUDA and the last CUDA error string is kept per thread.
+// ----------------------------------------------------------------------------
+void set_last_cuda_error(cudaError_t e, const char* where);
+
+#define SYN_CUDA_TRY(expr)                          \
+  do {                                              \
+    cudaError_t _e = (expr);                        \
+    if (_e != cudaSuccess) {                        \
+      ::syn::set_last_cuda_error(_e, #expr);        \
+      return SYN_ERR_CUDA;                          \
+    }                                               \
+  } while (0)
+
+#define SYN_LAUNCH_CHECK(where)                     \
+  do {                                              \
+    cudaError_t _e = cudaGetLastError();            \
+    if (_e != cudaSuccess) {                        \
+      ::syn::set_last_cuda_error(_e, where);        \
+      return SYN_ERR_CUDA;                          \
+    }                                               \
+  } while (0)
+
+int num_sms();
+
+// ----------------------------------------------------------------------------
+// f16 -> f32. Two conversions exist in the reference and they disagree on
+// subnormals:
+//  * zig/src/ops/qmatmul.zig:346-371 (used by syn_q4_0_gemv) is exact IEEE;
+//  * weight_loading/converter.rs:12-40 (used by every GGUF dequantiser) starts
+//    its normalisation counter at 1, which halves each subnormal.
+// Both are reproduced bit-exactly: the exact value is built from the bits,
+// and for the loader flavour a subnormal is halved (exact in f32).
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float f16_exact(uint16_t h) {
+  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t e = (h >> 10) & 0x1Fu;
+  uint32_t m = h & 0x3FFu;
+  if (e == 0) {
+    // subnormal or zero: m * 2^-24, exact in f32
+    float v = __uint2float_rn(m) * 5.9604644775390625e-8f;
+    return __uint_as_float(__float_as_uint(v) | sign);
+  }
+  if (e == 31) return __uint_as_float(sign | 0x7F800000u | (m << 13));
+  return __uint_as_float(sign | ((e + 112u) << 23) | (m << 13));
+}
+
+__device__ __forceinline__ float f16_loader(uint16_t h) {
+  float v = f16_exact(h);
+  if (((h >> 10) & 0x1Fu) == 0) v *= 0.5f;  // converter.rs subnormal quirk
+  return v;
+}
+
+// ----------------------------------------------------------------------------
+// 4-way byte dot products (dp4a) with explicit operand signedness.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a_signed, uint32_t b_unsigned, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_signed), "r"(b_unsigned), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a_unsigned, uint32_t b_signed, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a_unsigned), "r"(b_signed), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Streaming 16-byte load that bypasses L1 allocation (weights are read once).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint16_t ld_nc_u16(const void* p) {
+  uint16_t r;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace syn
