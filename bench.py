@@ -40,9 +40,17 @@ def peaks():
     return FALLBACK_HBM, "fallback"
 
 
+CASE_FILTER = None  # "FMT:N:K" restricts the sweep to one GEMV (profiling runs)
+
+
 def sweep_cases():
     from synapse_b200 import synth
-    return [(fmt, n, k) for fmt in synth.FORMATS for n in synth.SWEEP_N for k in synth.SWEEP_K]
+    from synapse_b200.api import QFormat
+    cases = [(fmt, n, k) for fmt in synth.FORMATS for n in synth.SWEEP_N for k in synth.SWEEP_K]
+    if CASE_FILTER:
+        f, n, k = CASE_FILTER.split(":")
+        cases = [(QFormat[f], int(n), int(k))]
+    return cases
 
 
 def case_bytes(fmt, n, k, m=1):
@@ -138,14 +146,28 @@ def run_synapse(args, rank, world, local_rank):
         del data
     step_bytes = sum(c["bytes"] for c in cases)
     stream = torch.cuda.current_stream(dev)
+    from synapse_b200.graph import CapturedSequence
+    fmt_names = sorted({sb.QFormat(c["fmt"]).name for c in cases},
+                       key=lambda nm: int(sb.QFormat[nm]))
+    by_fmt = {nm: [c for c in cases if sb.QFormat(c["fmt"]).name == nm] for nm in fmt_names}
 
-    def step(events=None):
-        for i, c in enumerate(cases):
-            if events is not None:
-                events[i][0].record(stream)
-            c["w"].matmul(c["x"], out=c["y"])
-            if events is not None:
-                events[i][1].record(stream)
+    def gemvs(cs):
+        def run():
+            for c in cs:
+                c["w"].matmul(c["x"], out=c["y"])
+        return run
+
+    def gemvs_e2e(cs):
+        def run():
+            for c in cs:
+                c["x"].copy_(c["x_pin"], non_blocking=True)
+                c["w"].matmul(c["x"], out=c["y"])
+                c["y_pin"].copy_(c["y"], non_blocking=True)
+        return run
+
+    # One CUDA graph per format (15 GEMVs each); a step replays the five.
+    graphs = {nm: CapturedSequence(gemvs(by_fmt[nm]), dev) for nm in fmt_names}
+    graphs_e2e = {nm: CapturedSequence(gemvs_e2e(by_fmt[nm]), dev) for nm in fmt_names}
 
     def barrier():
         torch.cuda.synchronize(dev)
@@ -153,25 +175,34 @@ def run_synapse(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        step()
-    barrier()
+    def timed(gs):
+        """K timed steps of replays; returns (total ms, per-format ms)."""
+        for _ in range(args.warmup):
+            for nm in fmt_names:
+                gs[nm].replay()
+        barrier()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(fmt_names) + 1)]
+              for _ in range(args.steps)]
+        barrier()
+        # Keep the device busy while the host enqueues every replay, so the
+        # timed region measures device time, not host submission latency.
+        torch.cuda._sleep(20_000_000)
+        for s in range(args.steps):
+            ev[s][0].record(stream)
+            for i, nm in enumerate(fmt_names):
+                gs[nm].replay()
+                ev[s][i + 1].record(stream)
+        barrier()
+        total = ev[0][0].elapsed_time(ev[-1][-1])
+        per = {nm: sum(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(args.steps))
+               for i, nm in enumerate(fmt_names)}
+        return total, per
 
-    # Timed region: K steps; per-launch events give the per-kernel times.
-    per = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            for _ in cases] for _ in range(args.steps)]
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local_rank)
     clocks.start()
     time.sleep(0.3)
-    barrier()
-    t0.record(stream)
-    for s in range(args.steps):
-        step(per[s])
-    t1.record(stream)
-    barrier()
+    ms, fmt_ms = timed(graphs)
     clk = clocks.stop()
-    ms = t0.elapsed_time(t1)
     if dist is not None:
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -179,18 +210,11 @@ def run_synapse(args, rank, world, local_rank):
     ms_per_step = ms / args.steps
     value = world * step_bytes * args.steps / (ms / 1e3) / 1e9
 
-    # per-format kernel times
-    fmt_ms = {}
-    fmt_bytes = {}
-    for s in range(args.steps):
-        for i, c in enumerate(cases):
-            nm = sb.QFormat(c["fmt"]).name
-            fmt_ms[nm] = fmt_ms.get(nm, 0.0) + per[s][i][0].elapsed_time(per[s][i][1])
-            fmt_bytes[nm] = fmt_bytes.get(nm, 0) + c["bytes"]
+    fmt_bytes = {nm: args.steps * sum(c["bytes"] for c in by_fmt[nm]) for nm in fmt_names}
     per_format = {nm: {"GB/s": round(fmt_bytes[nm] / (fmt_ms[nm] / 1e3) / 1e9, 1),
-                       "ms_per_step": round(fmt_ms[nm] / args.steps, 4)} for nm in fmt_ms}
+                       "ms_per_step": round(fmt_ms[nm] / args.steps, 4)} for nm in fmt_names}
     dom = max(fmt_ms, key=fmt_ms.get)
-    launches_dom = 15
+    launches_dom = len(by_fmt[dom])
     achieved = fmt_bytes[dom] / (fmt_ms[dom] / 1e3) / 1e9
     peak, peak_src = peaks()
     ratio = traffic_from_profile(dom)
@@ -198,23 +222,9 @@ def run_synapse(args, rank, world, local_rank):
     if ratio is not None:
         traffic = ratio * (fmt_bytes[dom] / args.steps / launches_dom)
 
-    # e2e: the public API with host buffers; H2D of x and D2H of y per GEMV.
-    for _ in range(max(1, args.warmup)):
-        for c in cases:
-            c["x"].copy_(c["x_pin"], non_blocking=True)
-            c["w"].matmul(c["x"], out=c["y"])
-            c["y_pin"].copy_(c["y"], non_blocking=True)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        for c in cases:
-            c["x"].copy_(c["x_pin"], non_blocking=True)
-            c["w"].matmul(c["x"], out=c["y"])
-            c["y_pin"].copy_(c["y"], non_blocking=True)
-    e1.record(stream)
-    barrier()
-    ems = e0.elapsed_time(e1)
+    # e2e: the public API with host buffers (pinned): every step copies each
+    # GEMV's x host->device and reads its y back device->host.
+    ems, _ = timed(graphs_e2e)
     if dist is not None:
         tt = torch.tensor([ems], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -241,13 +251,14 @@ def run_synapse(args, rank, world, local_rank):
                        "parallelism": f"replicas x{world}"},
             "hbm_frac": round(value / world / peak, 4),
             "per_format": per_format,
-            "roofline": {"bound": "hbm", "kernel": f"k_qgemv<{dom}>",
+            "roofline": {"bound": "hbm", "kernel": f"k_qgemv<{dom}> ({launches_dom} launches/step)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "traffic": traffic},
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": len(cases) * args.steps,
+            "launch": "one CUDA graph per format (15 GEMVs), 5 replays per step",
             "clocks": clk,
             "cpu_baseline": cpu,
         }
@@ -386,7 +397,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="synapse", choices=["synapse", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, help="FMT:N:K -- time one GEMV only (profiling)")
     args = ap.parse_args()
+    global CASE_FILTER
+    CASE_FILTER = args.case
+    if args.case:
+        args.no_cpu_baseline = True
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -84,6 +84,11 @@ typedef struct syn_cuda_weight_s syn_cuda_weight_t;
 syn_status_t syn_cuda_context_create(int device, syn_cuda_ctx_t **out);
 syn_status_t syn_cuda_context_destroy(syn_cuda_ctx_t *ctx);
 
+/* Reads and clears the context's device-side error word, where kernels
+ * record asynchronous failures such as SYN_ERR_TIMEOUT. New (the CPU
+ * library has no asynchronous errors). Synchronous. */
+syn_status_t syn_cuda_context_get_error(syn_cuda_ctx_t *ctx, int32_t *status);
+
 /* Replaces syn_capability_summary (zig/src/ffi/exports.zig:230-290). */
 syn_status_t syn_cuda_capability_summary(syn_capability_summary_t *out);
 

@@ -18,6 +18,7 @@ c_st = ctypes.c_int32
 SIGNATURES = {
     "syn_cuda_context_create": (c_st, [ctypes.c_int, ctypes.POINTER(c_vp)]),
     "syn_cuda_context_destroy": (c_st, [c_vp]),
+    "syn_cuda_context_get_error": (c_st, [c_vp, ctypes.POINTER(ctypes.c_int32)]),
     "syn_cuda_capability_summary": (c_st, [c_vp]),
     "syn_cuda_status_string": (ctypes.c_char_p, [c_st]),
     "syn_cuda_last_error": (ctypes.c_char_p, []),
@@ -46,7 +47,7 @@ class CapabilitySummary(ctypes.Structure):
 def load(path=LIB_PATH):
     if not os.path.exists(path):
         raise ImportError(
-            f"{path} is missing: build it with `python -m synapse_b200.build` "
+            f"{path} is missing: build it with `python synapse_b200/build.py` "
             "(the CUDA backend has no CPU fallback)")
     lib = ctypes.CDLL(path)
     for name, (res, args) in SIGNATURES.items():

@@ -1,6 +1,6 @@
 """Builds the sm_100a shared library libsynapse_cuda.so in-tree with nvcc.
 
-`python -m synapse_b200.build` (or synapse_b200.build.build()) compiles every
+`python synapse_b200/build.py` (or __graft_entry__.build()) compiles every
 .cu file under csrc/ into synapse_b200/libsynapse_cuda.so. The library is a
 plain C ABI (include/synapse_cuda.h); it links the CUDA runtime statically so
 it loads on any box with the driver.

@@ -76,8 +76,10 @@ size_t src_row_bytes(int fmt, size_t k) {
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
 // Lays out the repacked arrays of `w` inside one allocation; returns bytes.
+// Rows are stored in groups of 32 (row-interleaved tiles), zero padded.
 size_t layout(syn_cuda_weight_s* w, uint8_t* base) {
-  size_t off = 0, n = w->n, k = w->k;
+  size_t off = 0;
+  const size_t n = (w->n + 31) / 32 * 32, k = w->k;
   auto take = [&](size_t bytes) {
     uint8_t* p = base ? base + off : nullptr;
     off = align256(off + bytes);
@@ -103,12 +105,71 @@ size_t layout(syn_cuda_weight_s* w, uint8_t* base) {
     case SYN_QFMT_Q6_K:
       w->q = take(n * k / 2);
       w->qh = take(n * (k / 32) * 8);
-      w->sc = reinterpret_cast<int8_t*>(take(n * (k / 16)));
+      w->sc = reinterpret_cast<int8_t*>(take(n * (k / 32) * 2));
       w->d = reinterpret_cast<uint16_t*>(take(n * (k / 256) * 2));
       break;
   }
   return off;
 }
+
+// Grows one of the context's scratch buffers (zero-filled). Growth frees the
+// old buffer, so it waits for the device first; it is refused while `st` is
+// being captured into a graph.
+syn_status_t grow(void** buf, size_t* cap, size_t bytes, cudaStream_t st) {
+  if (bytes <= *cap) return SYN_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  SYN_CUDA_TRY(cudaStreamIsCapturing(st, &cs));
+  if (cs != cudaStreamCaptureStatusNone) return SYN_ERR_UNSUPPORTED;
+  SYN_CUDA_TRY(cudaDeviceSynchronize());
+  cudaFree(*buf);
+  *buf = nullptr;
+  *cap = 0;
+  const size_t want = align256(bytes) * 2;
+  cudaError_t e = cudaMalloc(buf, want);
+  if (e == cudaSuccess) e = cudaMemset(*buf, 0, want);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "cudaMalloc(scratch)");
+    return SYN_ERR_OUT_OF_MEMORY;
+  }
+  *cap = want;
+  return SYN_OK;
+}
+
+syn_status_t ensure_scratch(syn_cuda_ctx_s* ctx, const syn_cuda_weight_s* w, size_t m,
+                            cudaStream_t st) {
+  syn_status_t s = grow(reinterpret_cast<void**>(&ctx->part), &ctx->part_bytes,
+                        gemv_partial_bytes(w->fmt, m, w->n, w->kp), st);
+  if (s != SYN_OK) return s;
+  return grow(reinterpret_cast<void**>(&ctx->cnt), &ctx->cnt_bytes, gemv_counter_bytes(m, w->n),
+              st);
+}
+
+// Stream-ordered scratch for the context-free entry points: `extra` leading
+// bytes for the caller, then partials and zeroed counters; freed after the
+// launch (stream-ordered).
+struct CallScratch {
+  void* mem = nullptr;
+  float* part = nullptr;
+  int* cnt = nullptr;
+  syn_status_t init(int fmt, size_t m, size_t n, size_t kp, size_t extra, cudaStream_t st) {
+    const size_t pb = align256(gemv_partial_bytes(fmt, m, n, kp));
+    const size_t cb = align256(gemv_counter_bytes(m, n));
+    SYN_CUDA_TRY(cudaMallocAsync(&mem, extra + pb + cb + 256, st));
+    part = reinterpret_cast<float*>(static_cast<uint8_t*>(mem) + extra);
+    cnt = reinterpret_cast<int*>(static_cast<uint8_t*>(mem) + extra + pb);
+    SYN_CUDA_TRY(cudaMemsetAsync(cnt, 0, cb, st));
+    return SYN_OK;
+  }
+  syn_status_t release(syn_status_t s, cudaStream_t st) {
+    if (!mem) return s;
+    cudaError_t e = cudaFreeAsync(mem, st);
+    if (s == SYN_OK && e != cudaSuccess) {
+      set_last_cuda_error(e, "cudaFreeAsync");
+      return SYN_ERR_CUDA;
+    }
+    return s;
+  }
+};
 
 }  // namespace
 }  // namespace syn
@@ -164,12 +225,26 @@ syn_status_t syn_cuda_context_create(int device, syn_cuda_ctx_t** out) {
   c->device = device;
   c->sms = num_sms();
   cudaError_t e = cudaStreamCreateWithFlags(&c->upload_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&c->err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->err, 0, sizeof(int));
   if (e != cudaSuccess) {
-    set_last_cuda_error(e, "cudaStreamCreate");
+    set_last_cuda_error(e, "syn_cuda_context_create");
+    if (c->err) cudaFree(c->err);
+    if (c->upload_stream) cudaStreamDestroy(c->upload_stream);
     delete c;
-    return SYN_ERR_CUDA;
+    return e == cudaErrorMemoryAllocation ? SYN_ERR_OUT_OF_MEMORY : SYN_ERR_CUDA;
   }
   *out = c;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_context_get_error(syn_cuda_ctx_t* ctx, int32_t* status) {
+  if (!ctx || !status) return SYN_ERR_NULL_PTR;
+  DeviceGuard g(ctx->device);
+  int v = 0;
+  SYN_CUDA_TRY(cudaMemcpy(&v, ctx->err, sizeof(int), cudaMemcpyDeviceToHost));
+  SYN_CUDA_TRY(cudaMemset(ctx->err, 0, sizeof(int)));
+  *status = v;
   return SYN_OK;
 }
 
@@ -177,19 +252,22 @@ syn_status_t syn_cuda_context_destroy(syn_cuda_ctx_t* ctx) {
   if (!ctx) return SYN_ERR_NULL_PTR;
   {
     DeviceGuard g(ctx->device);
+    cudaDeviceSynchronize();
     cudaStreamDestroy(ctx->upload_stream);
+    cudaFree(ctx->part);
+    cudaFree(ctx->cnt);
+    cudaFree(ctx->err);
   }
   delete ctx;
   return SYN_OK;
 }
 
 syn_status_t syn_cuda_quantize_per_channel_int8(const float* data, size_t channels,
-                                                size_t channel_size, int8_t* out,
-                                                float* scales, void* stream) {
+                                                size_t channel_size, int8_t* out, float* scales,
+                                                void* stream) {
   if (!data || !out || !scales) return SYN_ERR_NULL_PTR;
   if (channels == 0 || channel_size == 0) return SYN_ERR_INVALID_ARG;
-  return launch_quantize_rows(data, channels, channel_size, out, scales,
-                              (cudaStream_t)stream);
+  return launch_quantize_rows(data, channels, channel_size, out, scales, (cudaStream_t)stream);
 }
 
 syn_status_t syn_cuda_quantize_weights_int8(const float* w, size_t n, size_t k, int8_t* out_kn,
@@ -206,34 +284,38 @@ syn_status_t syn_cuda_qgemm_int8(size_t m, size_t n, size_t k, const int8_t* a, 
   if (m == 0 || n == 0 || k == 0) return SYN_OK;
   if (lda < k || ldb < n || ldc < n) return SYN_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  // The reference's [K,N] operand is transposed into the coalesced [N,kp]
-  // layout in stream-ordered scratch memory, then the repacked kernels run.
+  // The reference's [K,N] operand is transposed into the coalesced
+  // row-interleaved layout in stream-ordered scratch, then the GEMV runs.
   syn_cuda_weight_s w{};
   w.fmt = SYN_QFMT_INT8_KN;
   w.n = n;
   w.k = k;
   w.kp = (k + 31) / 32 * 32;
-  void* scratch = nullptr;
-  SYN_CUDA_TRY(cudaMallocAsync(&scratch, w.n * w.kp, st));
-  w.q = static_cast<uint8_t*>(scratch);
-  w.sb = const_cast<float*>(scales_b);
-  syn_status_t s = repack_weight(&w, reinterpret_cast<const uint8_t*>(b), ldb, nullptr, st);
+  const size_t wbytes = align256((n + 31) / 32 * 32 * w.kp);
+  CallScratch cs;
+  syn_status_t s = cs.init(w.fmt, m, n, w.kp, wbytes, st);
+  if (s != SYN_OK) return cs.release(s, st);
+  w.buf = cs.mem;
+  w.bytes = wbytes;
+  w.q = static_cast<uint8_t*>(cs.mem);
+  w.sb = const_cast<float*>(scales_b);  // read only for rows < n
+  s = repack_weight(&w, reinterpret_cast<const uint8_t*>(b), ldb, nullptr, st);
   if (s == SYN_OK)
-    s = launch_qgemv(&w, nullptr, lda, a, scales_a, m, c, ldc, m > 16 ? 1 : 0, st);
-  cudaError_t e = cudaFreeAsync(scratch, st);
-  if (s == SYN_OK && e != cudaSuccess) {
-    set_last_cuda_error(e, "cudaFreeAsync");
-    s = SYN_ERR_CUDA;
-  }
-  return s;
+    s = launch_qgemv(&w, nullptr, lda, a, scales_a, m, c, ldc, m > 16 ? 1 : 0, cs.part, cs.cnt,
+                     nullptr, st);
+  return cs.release(s, st);
 }
 
-syn_status_t syn_cuda_q4_0_gemv(size_t n, size_t k, const float* a, const uint8_t* b_q4,
-                                float* c, void* stream) {
+syn_status_t syn_cuda_q4_0_gemv(size_t n, size_t k, const float* a, const uint8_t* b_q4, float* c,
+                                void* stream) {
   if (!a || !b_q4 || !c) return SYN_ERR_NULL_PTR;
   if (n == 0 || k == 0) return SYN_OK;
   if (k % 32 != 0) return SYN_ERR_SHAPE_MISMATCH;
-  return launch_q4_0_raw(n, k, a, b_q4, c, (cudaStream_t)stream);
+  cudaStream_t st = (cudaStream_t)stream;
+  CallScratch cs;
+  syn_status_t s = cs.init(SYN_QFMT_Q4_0, 1, n, k, 0, st);
+  if (s == SYN_OK) s = launch_q4_0_raw(n, k, a, b_q4, c, cs.part, cs.cnt, nullptr, st);
+  return cs.release(s, st);
 }
 
 syn_status_t syn_cuda_weight_upload(syn_cuda_ctx_t* ctx, syn_qformat_t fmt, const void* host,
@@ -266,19 +348,23 @@ syn_status_t syn_cuda_weight_upload(syn_cuda_ctx_t* ctx, syn_qformat_t fmt, cons
   }
   layout(w, static_cast<uint8_t*>(w->buf));
 
+  // raw bytes (and INT8 scales) staged in a temporary device buffer
   void* tmp = nullptr;
   syn_status_t s = SYN_OK;
   cudaStream_t st = ctx->upload_stream;
+  const size_t sc_off = align256(src_bytes);
   do {
-    e = cudaMalloc(&tmp, src_bytes + 16);
+    e = cudaMalloc(&tmp, sc_off + n * sizeof(float) + 16);
     if (e != cudaSuccess) { s = SYN_ERR_OUT_OF_MEMORY; break; }
     e = cudaMemcpyAsync(tmp, host, src_bytes, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) { s = SYN_ERR_CUDA; break; }
+    float* d_sc = nullptr;
     if (fmt == SYN_QFMT_INT8_KN) {
-      e = cudaMemcpyAsync(w->sb, scales_or_null, n * sizeof(float), cudaMemcpyHostToDevice, st);
+      d_sc = reinterpret_cast<float*>(static_cast<uint8_t*>(tmp) + sc_off);
+      e = cudaMemcpyAsync(d_sc, scales_or_null, n * sizeof(float), cudaMemcpyHostToDevice, st);
       if (e != cudaSuccess) { s = SYN_ERR_CUDA; break; }
     }
-    s = repack_weight(w, static_cast<const uint8_t*>(tmp), 0, nullptr, st);
+    s = repack_weight(w, static_cast<const uint8_t*>(tmp), 0, d_sc, st);
     if (s != SYN_OK) break;
     e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) { s = SYN_ERR_CUDA; break; }
@@ -335,9 +421,11 @@ syn_status_t syn_cuda_qmatmul(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w, c
   DeviceGuard g(w->device);
   if (!g.ok) return SYN_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
-  if (w->fmt == SYN_QFMT_INT8_KN)
-    return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, m > 16 ? 1 : 0, st);
-  return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, 0, st);
+  syn_status_t s = ensure_scratch(ctx, w, m, st);
+  if (s != SYN_OK) return s;
+  const int chunked = (w->fmt == SYN_QFMT_INT8_KN && m > 16) ? 1 : 0;
+  return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, chunked, ctx->part, ctx->cnt,
+                      ctx->err, st);
 }
 
 syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w,
@@ -348,8 +436,11 @@ syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t* ctx, const syn_cuda_
   if (m == 0) return SYN_OK;
   DeviceGuard g(w->device);
   if (!g.ok) return SYN_ERR_CUDA;
-  return launch_qgemv(w, nullptr, w->k, x_i8, scales_x, m, y, w->n, m > 16 ? 1 : 0,
-                      (cudaStream_t)stream);
+  cudaStream_t st = (cudaStream_t)stream;
+  syn_status_t s = ensure_scratch(ctx, w, m, st);
+  if (s != SYN_OK) return s;
+  return launch_qgemv(w, nullptr, w->k, x_i8, scales_x, m, y, w->n, m > 16 ? 1 : 0, ctx->part,
+                      ctx->cnt, ctx->err, st);
 }
 
 }  // extern "C"

@@ -1,9 +1,10 @@
 // common.cuh -- shared helpers for the sm_100a quantized-matmul backend.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
-#include <stdint.h>
 #include <stddef.h>
+#include <stdint.h>
 
 #include "../../include/synapse_cuda.h"
 
@@ -15,22 +16,22 @@ namespace syn {
 // ----------------------------------------------------------------------------
 void set_last_cuda_error(cudaError_t e, const char* where);
 
-#define SYN_CUDA_TRY(expr)                          \
-  do {                                              \
-    cudaError_t _e = (expr);                        \
-    if (_e != cudaSuccess) {                        \
-      ::syn::set_last_cuda_error(_e, #expr);        \
-      return SYN_ERR_CUDA;                          \
-    }                                               \
+#define SYN_CUDA_TRY(expr)                   \
+  do {                                       \
+    cudaError_t _e = (expr);                 \
+    if (_e != cudaSuccess) {                 \
+      ::syn::set_last_cuda_error(_e, #expr); \
+      return SYN_ERR_CUDA;                   \
+    }                                        \
   } while (0)
 
-#define SYN_LAUNCH_CHECK(where)                     \
-  do {                                              \
-    cudaError_t _e = cudaGetLastError();            \
-    if (_e != cudaSuccess) {                        \
-      ::syn::set_last_cuda_error(_e, where);        \
-      return SYN_ERR_CUDA;                          \
-    }                                               \
+#define SYN_LAUNCH_CHECK(where)              \
+  do {                                       \
+    cudaError_t _e = cudaGetLastError();     \
+    if (_e != cudaSuccess) {                 \
+      ::syn::set_last_cuda_error(_e, where); \
+      return SYN_ERR_CUDA;                   \
+    }                                        \
   } while (0)
 
 int num_sms();
@@ -41,26 +42,23 @@ int num_sms();
 //  * zig/src/ops/qmatmul.zig:346-371 (used by syn_q4_0_gemv) is exact IEEE;
 //  * weight_loading/converter.rs:12-40 (used by every GGUF dequantiser) starts
 //    its normalisation counter at 1, which halves each subnormal.
-// Both are reproduced bit-exactly: the exact value is built from the bits,
-// and for the loader flavour a subnormal is halved (exact in f32).
+// Both are reproduced bit-exactly.
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ float f16_exact(uint16_t h) {
-  uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
-  uint32_t e = (h >> 10) & 0x1Fu;
-  uint32_t m = h & 0x3FFu;
-  if (e == 0) {
-    // subnormal or zero: m * 2^-24, exact in f32
-    float v = __uint2float_rn(m) * 5.9604644775390625e-8f;
-    return __uint_as_float(__float_as_uint(v) | sign);
-  }
-  if (e == 31) return __uint_as_float(sign | 0x7F800000u | (m << 13));
-  return __uint_as_float(sign | ((e + 112u) << 23) | (m << 13));
+  // hardware half -> single conversion: exact for every finite input
+  return __half2float(__ushort_as_half(h));
 }
 
 __device__ __forceinline__ float f16_loader(uint16_t h) {
-  float v = f16_exact(h);
-  if (((h >> 10) & 0x1Fu) == 0) v *= 0.5f;  // converter.rs subnormal quirk
-  return v;
+  // converter.rs subnormal quirk: exponent field 0 -> half the IEEE value
+  // (zero stays zero); halving is exact in f32.
+  return f16_exact(h) * ((h & 0x7C00u) ? 1.0f : 0.5f);
+}
+
+// Exact int -> float for |v| < 2^22 with two ALU/FMA ops (no conversion
+// unit): the integer is placed in the mantissa of 1.5 * 2^23, bias removed.
+__device__ __forceinline__ float i2f_small(int v) {
+  return __int_as_float(v + 0x4B400000) - 12582912.0f;
 }
 
 // ----------------------------------------------------------------------------
@@ -87,7 +85,7 @@ __device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
   return d;
 }
 
-// Streaming 16-byte load that bypasses L1 allocation (weights are read once).
+// Streaming loads that bypass L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -122,6 +120,17 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// ----------------------------------------------------------------------------
+// Programmatic dependent launch (griddepcontrol). A kernel launched with
+// programmatic stream serialisation may start before its predecessor ends;
+// griddep_wait() blocks until the predecessor has completed and its memory
+// is visible. Launched without the attribute both are no-ops.
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 }  // namespace syn

@@ -1,23 +1,38 @@
 // gemv.cu -- decode-path fused dequant GEMV for all five weight formats.
 //
-// One kernel per (format, activation rows MT, weight rows per warp R):
-//  1. Prologue (per CTA, into shared memory): the MT activation rows are
-//     converted once. INT8 weights: per-row INT8 quantisation exactly as
-//     quantize.zig:12-47 (W8A8 like QuantizedLinear::forward,
-//     int8_linear.rs:87-117). Block formats: each 32-element block of x is
-//     scaled to 16-bit integers (|xq| <= 32767, per-block f32 scale) and
-//     split into a signed high byte and an unsigned low byte, so that every
-//     product runs as exact 4-way integer dot products (dp4a); the per-block
-//     integer sums are exact and the only rounding is the 2^-16 relative
-//     activation quantisation plus the f32 sum over blocks.
-//  2. Main loop: each warp owns R output rows; lane l streams 32-element
-//     block b = l + 32 i of each row with 16-byte non-allocating loads
-//     (512 contiguous bytes per warp per plane), dequantises with one or two
-//     logic ops per 8 weights, and accumulates; a warp-shuffle reduction
-//     finishes each row.
-// The grid is persistent (bounded by occupancy) and strides over rows.
+// Layout. Weights are repacked row-interleaved by 32 (repack.cu): for a
+// group of 32 rows and one 32-element block, the 32 rows' bytes are stored
+// back to back. Lane l of a warp owns row 32g + l, so one warp-wide 16-byte
+// load reads a 512-byte contiguous tile (4-bit formats; two loads for 8-bit
+// ones) and every lane accumulates its own row: no cross-lane reduction.
+//
+// Work decomposition. Grid = (row groups, K splits, activation-row slices).
+// A CTA covers 32 rows x a contiguous range of kr blocks; its 8 warps split
+// that range evenly. Each warp converts the activations of its own blocks
+// (see below) into shared memory, then streams its weight tiles four at a
+// time (the first four are requested before griddepcontrol.wait, since
+// weights never depend on the preceding kernel). Warp partials are summed in
+// warp order through shared memory; when K is split across CTAs, the CTA
+// partials go to scratch and the last CTA to arrive for a row group (atomic
+// counter, reset by that CTA) sums them in K order. The result is
+// deterministic.
+//
+// Activations.
+//   INT8 weights: per-row INT8 quantisation exactly as quantize.zig:12-47
+//     (row max over all of K, one CTA-wide reduction); W8A8 like
+//     QuantizedLinear::forward (int8_linear.rs:87-117). Products are exact
+//     int32 per 512-element K chunk (shared-memory integer atomics), and the
+//     epilogue reproduces qmatmul.zig: float(acc) * sa * sb for M <= 16
+//     (one accumulator over K) and, for M > 16, C = 0; C += float(chunk) *
+//     sa * sb in chunk order (qmatmul.zig:68-98), every op rounded.
+//   Block formats: each 32-element block is scaled to 16-bit integers
+//     (|xq| <= 32767, one f32 scale per block) and split into a signed high
+//     byte and an unsigned low byte ("planes"), so every product runs as
+//     exact 4-way integer dot products (dp4a) with exact block sums; the only
+//     roundings are the 2^-16 relative activation quantisation and the f32
+//     sums over blocks.
+#include <algorithm>
 #include <mutex>
-#include <unordered_map>
 
 #include "internal.cuh"
 
@@ -27,199 +42,98 @@ namespace {
 enum : int { F_INT8 = SYN_QFMT_INT8_KN, F_Q4_0 = SYN_QFMT_Q4_0, F_Q8_0 = SYN_QFMT_Q8_0,
              F_Q4_K = SYN_QFMT_Q4_K, F_Q6_K = SYN_QFMT_Q6_K, F_Q4_0RAW = 100 };
 
+constexpr int WARPS = 8;
+constexpr int THREADS = WARPS * 32;
+constexpr int U = 4;  // weight tiles in flight per warp
+
+__host__ __device__ constexpr bool interleaved(int f) {
+  return f == F_Q4_0 || f == F_Q4_K || f == F_Q6_K || f == F_Q4_0RAW;
+}
+
+// Shared-memory bytes of one activation block (one 32-element block of one
+// activation row):
+//   INT8  : 32 int8 codes.
+//   blocks: 4 planes of 16 bytes -- interleaved formats: p0/p1 = high bytes
+//           of even/odd elements, p2/p3 = low bytes (element 2i of a block
+//           pairs with the low nibble of byte i); natural order (Q8_0):
+//           p0/p1 = high bytes of elements 0-15 / 16-31, p2/p3 = low bytes --
+//           then float2 sums (sum of xq over elements 0-15 / 16-31, exact),
+//           f32 block scale, pad.
+__host__ __device__ constexpr int act_block_bytes(int fmt) { return fmt == F_INT8 ? 32 : 80; }
+
 struct GemvParams {
   const uint8_t* q;
   const uint16_t* d;
   const float* sb;
   const uint8_t* hdr;
   const uint8_t* qh;
-  const int8_t* sc;
-  long long n, k, kp, nblk;
+  const uint16_t* sc;
   const float* x;
-  long long ldx;
   const int8_t* xq;
-  long long ldxq;
   const float* sx;
-  long long m;
+  long long ldx;
+  int n, k, kp, nblk, nsb, groups;
+  int kr, nks, nchunks;
+  int m;
   float* y;
   long long ldy;
   int chunked;
+  float* part;  // [m][nks or nchunks][groups*32]
+  int* cnt;     // [m slices][groups]
+  int* err;
 };
 
-constexpr int WARPS = 8;
-constexpr int THREADS = WARPS * 32;
-
-__host__ __device__ constexpr bool interleaved(int f) {
-  return f == F_Q4_0 || f == F_Q4_K || f == F_Q6_K || f == F_Q4_0RAW;
-}
-
-// Shared-memory bytes per activation row.
-__host__ __device__ inline long long act_stride(int fmt, long long kp, long long nblk) {
-  if (fmt == F_INT8) return kp + 16;
-  return ((76 * nblk) + 15) / 16 * 16;
-}
-
 // ---------------------------------------------------------------------------
-// Prologues
+// Weight tiles
 // ---------------------------------------------------------------------------
-template <int MT>
-__device__ void prologue_int8(const GemvParams& p, long long m0, uint8_t* smem) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float red[WARPS];
-  const long long stride = act_stride(F_INT8, p.kp, p.nblk);
-  for (int mm = 0; mm < MT; mm++) {
-    long long m = m0 + mm;
-    int8_t* xs = reinterpret_cast<int8_t*>(smem + mm * stride);
-    float* sa = reinterpret_cast<float*>(smem + mm * stride + p.kp);
-    if (m >= p.m) {
-      for (long long i = threadIdx.x; i < p.kp; i += THREADS) xs[i] = 0;
-      if (threadIdx.x == 0) *sa = 0.0f;
-      continue;
-    }
-    if (p.xq) {  // pre-quantised activations (forward_pre_quantized)
-      const int8_t* src = p.xq + m * p.ldxq;
-      for (long long i = threadIdx.x; i < p.kp; i += THREADS) xs[i] = i < p.k ? src[i] : 0;
-      if (threadIdx.x == 0) *sa = p.sx[m];
-      continue;
-    }
-    const float* xr = p.x + m * p.ldx;
-    float amax = 0.0f;
-    for (long long i = threadIdx.x; i < p.k; i += THREADS) amax = fmaxf(amax, fabsf(xr[i]));
-    amax = warp_max(amax);
-    if (lane == 0) red[warp] = amax;
-    __syncthreads();
-    amax = red[0];
-#pragma unroll
-    for (int w = 1; w < WARPS; w++) amax = fmaxf(amax, red[w]);
-    __syncthreads();
-    // quantize.zig:28-45: zero row -> scale 1, q 0; else scale = max/127,
-    // q = clamp(round(x * (127/max)), -127, 127), round half away from zero.
-    if (amax == 0.0f) {
-      for (long long i = threadIdx.x; i < p.kp; i += THREADS) xs[i] = 0;
-      if (threadIdx.x == 0) *sa = 1.0f;
-    } else {
-      float inv = __fdiv_rn(127.0f, amax);
-      for (long long i = threadIdx.x; i < p.kp; i += THREADS) {
-        int8_t v = 0;
-        if (i < p.k) {
-          float r = roundf(__fmul_rn(xr[i], inv));
-          r = fminf(127.0f, fmaxf(-127.0f, r));
-          v = (int8_t)(int)r;
-        }
-        xs[i] = v;
-      }
-      if (threadIdx.x == 0) *sa = __fdiv_rn(amax, 127.0f);
-    }
-  }
-}
+template <int FMT> struct WB;
+template <> struct WB<F_INT8> { uint4 a, b; };
+template <> struct WB<F_Q8_0> { uint4 a, b; uint32_t d; };
+template <> struct WB<F_Q4_0> { uint4 a; uint32_t d; };
+template <> struct WB<F_Q4_0RAW> { uint4 a; uint32_t d; };
+template <> struct WB<F_Q4_K> { uint4 a; uint4 h; };
+template <> struct WB<F_Q6_K> { uint4 a; uint2 qh; uint32_t sd; };
 
-template <int FMT, int MT>
-__device__ void prologue_blocks(const GemvParams& p, long long m0, uint8_t* smem) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long nblk = p.nblk;
-  const long long stride = act_stride(FMT, p.kp, nblk);
-  for (long long t = warp; t < MT * nblk; t += WARPS) {
-    int mm = (int)(t / nblk);
-    long long b = t - (long long)mm * nblk;
-    long long m = m0 + mm;
-    uint8_t* base = smem + mm * stride;
-    float x = (m < p.m) ? p.x[m * p.ldx + b * 32 + lane] : 0.0f;
-    float amax = warp_max(fabsf(x));
-    int xq = 0;
-    float s = 0.0f;
-    if (amax > 0.0f) {
-      float inv = 32767.0f / amax;
-      xq = __float2int_rn(x * inv);
-      xq = max(-32767, min(32767, xq));
-      s = amax / 32767.0f;
-    }
-    uint8_t hb = (uint8_t)((xq >> 8) & 0xFF);  // signed high byte
-    uint8_t lb = (uint8_t)(xq & 0xFF);         // unsigned low byte
-    int plane, slot;
-    if (interleaved(FMT)) {
-      plane = lane & 1;  // element 2i -> even plane, 2i+1 -> odd plane
-      slot = lane >> 1;
-    } else {
-      plane = lane >> 4;  // natural order: bytes 0-15, 16-31
-      slot = lane & 15;
-    }
-    base[(plane)*nblk * 16 + b * 16 + slot] = hb;
-    base[(plane + 2) * nblk * 16 + b * 16 + slot] = lb;
-    int s0 = warp_sum_i(lane < 16 ? xq : 0);
-    int s1 = warp_sum_i(lane >= 16 ? xq : 0);
-    if (lane == 0) {
-      reinterpret_cast<int2*>(base + 64 * nblk)[b] = make_int2(s0, s1);
-      reinterpret_cast<float*>(base + 72 * nblk)[b] = s;
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Per-format block dot products. Each returns this lane's contribution of
-// one 32-element block of one weight row against one activation row.
-// ---------------------------------------------------------------------------
-struct WBlk {
-  uint4 a, b;      // weight bytes (b used by INT8/Q8_0)
-  uint32_t meta0;  // f16 scale bits / packed int8 scales
-  uint2 meta1;     // Q6_K high bits or Q4_K 16-byte header (first half)
-  uint2 meta2;     // Q4_K header second half
-};
-
-struct ABlk {
-  uint4 p0, p1, p2, p3;
-  int2 sums;
-  float s;
-};
-
+// Loads block b of this lane's row (group g, lane l).
 template <int FMT>
-__device__ __forceinline__ void load_w(const GemvParams& p, long long n, long long b, WBlk& w) {
+__device__ __forceinline__ void load_w(const GemvParams& p, int g, int b, int l, WB<FMT>& w) {
+  const size_t t = ((size_t)g * p.nblk + b) * 32 + l;  // row-interleaved tile index
   if constexpr (FMT == F_INT8) {
-    const uint8_t* src = p.q + n * p.kp + b * 32;
+    const uint8_t* src = p.q + t * 32;
     w.a = ld_stream16(src);
     w.b = ld_stream16(src + 16);
   } else if constexpr (FMT == F_Q8_0) {
-    const uint8_t* src = p.q + n * p.k + b * 32;
+    const uint8_t* src = p.q + t * 32;
     w.a = ld_stream16(src);
     w.b = ld_stream16(src + 16);
-    w.meta0 = ld_nc_u16(p.d + n * p.nblk + b);
+    w.d = ld_nc_u16(p.d + t);
   } else if constexpr (FMT == F_Q4_0) {
-    w.a = ld_stream16(p.q + n * (p.k / 2) + b * 16);
-    w.meta0 = ld_nc_u16(p.d + n * p.nblk + b);
+    w.a = ld_stream16(p.q + t * 16);
+    w.d = ld_nc_u16(p.d + t);
   } else if constexpr (FMT == F_Q4_K) {
-    w.a = ld_stream16(p.q + n * (p.k / 2) + b * 16);
-    const uint4 h = __ldg(reinterpret_cast<const uint4*>(p.hdr + (n * (p.k / 256) + (b >> 3)) * 16));
-    w.meta1 = make_uint2(h.x, h.y);
-    w.meta2 = make_uint2(h.z, h.w);
+    w.a = ld_stream16(p.q + t * 16);
+    const size_t th = ((size_t)g * p.nsb + (b >> 3)) * 32 + l;
+    w.h = __ldg(reinterpret_cast<const uint4*>(p.hdr + th * 16));
   } else if constexpr (FMT == F_Q6_K) {
-    w.a = ld_stream16(p.q + n * (p.k / 2) + b * 16);
-    w.meta1 = ld_stream8(p.qh + (n * p.nblk + b) * 8);
-    uint32_t scp = ld_nc_u16(reinterpret_cast<const uint16_t*>(p.sc) + n * p.nblk + b);
-    uint32_t dd = ld_nc_u16(p.d + n * (p.k / 256) + (b >> 3));
-    w.meta0 = scp | (dd << 16);
-  } else {  // F_Q4_0RAW: reference 18-byte blocks, 2-byte aligned
-    const uint16_t* src = reinterpret_cast<const uint16_t*>(p.q + (n * p.nblk + b) * 18);
+    w.a = ld_stream16(p.q + t * 16);
+    w.qh = ld_stream8(p.qh + t * 8);
+    const size_t th = ((size_t)g * p.nsb + (b >> 3)) * 32 + l;
+    w.sd = (uint32_t)ld_nc_u16(p.sc + t) | ((uint32_t)__ldg(p.d + th) << 16);
+  } else {  // F_Q4_0RAW: reference 18-byte blocks of row 32g + l, 2-byte aligned
+    const int row = g * 32 + l;
+    if (row >= p.n) {
+      w.a = make_uint4(0, 0, 0, 0);
+      w.d = 0;
+      return;
+    }
+    const uint16_t* src =
+        reinterpret_cast<const uint16_t*>(p.q + ((size_t)row * p.nblk + b) * 18);
     uint32_t h[9];
 #pragma unroll
-    for (int i = 0; i < 9; i++) h[i] = ld_nc_u16(src + i);
-    w.meta0 = h[0];
+    for (int i = 0; i < 9; i++) h[i] = __ldg(src + i);
+    w.d = h[0];
     w.a = make_uint4(h[1] | (h[2] << 16), h[3] | (h[4] << 16), h[5] | (h[6] << 16),
                      h[7] | (h[8] << 16));
-  }
-}
-
-template <int FMT>
-__device__ __forceinline__ void load_a(const uint8_t* base, long long nblk, long long b, ABlk& a) {
-  if constexpr (FMT == F_INT8) {
-    const uint4* src = reinterpret_cast<const uint4*>(base + b * 32);
-    a.p0 = src[0];
-    a.p1 = src[1];
-  } else {
-    a.p0 = reinterpret_cast<const uint4*>(base)[b];
-    a.p1 = reinterpret_cast<const uint4*>(base + nblk * 16)[b];
-    a.p2 = reinterpret_cast<const uint4*>(base + nblk * 32)[b];
-    a.p3 = reinterpret_cast<const uint4*>(base + nblk * 48)[b];
-    a.sums = reinterpret_cast<const int2*>(base + 64 * nblk)[b];
-    a.s = reinterpret_cast<const float*>(base + 72 * nblk)[b];
   }
 }
 
@@ -227,8 +141,27 @@ __device__ __forceinline__ uint32_t w4(const uint4& v, int j) {
   return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
 }
 
-// INT8: exact int32 partial sum of the block.
-__device__ __forceinline__ int dot_int8(const WBlk& w, const ABlk& a) {
+struct AB {
+  uint4 p0, p1, p2, p3;
+  float2 sums;
+  float s;
+};
+
+template <int FMT>
+__device__ __forceinline__ void load_act(const uint8_t* blk, AB& a) {
+  const uint4* v = reinterpret_cast<const uint4*>(blk);
+  a.p0 = v[0];
+  a.p1 = v[1];
+  if constexpr (FMT != F_INT8) {
+    a.p2 = v[2];
+    a.p3 = v[3];
+    const float4 t = reinterpret_cast<const float4*>(blk)[4];
+    a.sums = make_float2(t.x, t.y);
+    a.s = t.z;
+  }
+}
+
+__device__ __forceinline__ int dot_int8(const WB<F_INT8>& w, const AB& a) {
   int acc = 0;
   acc = dp4a_ss(a.p0.x, w.a.x, acc);
   acc = dp4a_ss(a.p0.y, w.a.y, acc);
@@ -241,29 +174,32 @@ __device__ __forceinline__ int dot_int8(const WBlk& w, const ABlk& a) {
   return acc;
 }
 
-// sum_i q_i * xq_i for unsigned nibble codes q (interleaved planes).
-__device__ __forceinline__ int dot_nib(const uint4& q, const ABlk& a) {
+// sum_i q_i * xq_i (exact, as float) for unsigned nibble codes q against
+// interleaved planes: the high-plane and low-plane sums are each below 2^17.
+__device__ __forceinline__ float dot_nib(const uint4& q, const AB& a) {
   int hl = 0, hh = 0, ll = 0, lh = 0;
 #pragma unroll
   for (int j = 0; j < 4; j++) {
-    uint32_t wq = w4(q, j);
-    uint32_t lo = wq & 0x0F0F0F0Fu;
-    uint32_t hi16 = wq & 0xF0F0F0F0u;  // 16 * high nibble, exact after >> 4
+    const uint32_t wq = w4(q, j);
+    const uint32_t lo = wq & 0x0F0F0F0Fu;
+    const uint32_t hi16 = wq & 0xF0F0F0F0u;  // 16 * high nibble; exact after >> 4
     hl = dp4a_su(w4(a.p0, j), lo, hl);
     hh = dp4a_su(w4(a.p1, j), hi16, hh);
     ll = dp4a_uu(w4(a.p2, j), lo, ll);
     lh = dp4a_uu(w4(a.p3, j), hi16, lh);
   }
-  return (hl + (hh >> 4)) * 256 + ll + (lh >> 4);
+  return fmaf(256.0f, i2f_small(hl + (hh >> 4)), i2f_small(ll + (lh >> 4)));
 }
 
 template <int FMT>
-__device__ __forceinline__ float dot_f(const WBlk& w, const ABlk& a) {
+__device__ __forceinline__ float dot_block(const WB<FMT>& w, const AB& a, int b) {
   if constexpr (FMT == F_Q4_0 || FMT == F_Q4_0RAW) {
-    int iq = dot_nib(w.a, a) - 8 * (a.sums.x + a.sums.y);
-    float d = (FMT == F_Q4_0) ? f16_loader((uint16_t)w.meta0) : f16_exact((uint16_t)w.meta0);
-    return (float)iq * (a.s * d);
+    // gguf.rs:318-324 / qmatmul.zig:306-311: value = (nib - 8) * d
+    const float iq = dot_nib(w.a, a) - 8.0f * (a.sums.x + a.sums.y);
+    const float d = (FMT == F_Q4_0) ? f16_loader((uint16_t)w.d) : f16_exact((uint16_t)w.d);
+    return iq * (a.s * d);
   } else if constexpr (FMT == F_Q8_0) {
+    // gguf.rs:276-285: value = d * q
     int ih = 0, il = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -272,292 +208,525 @@ __device__ __forceinline__ float dot_f(const WBlk& w, const ABlk& a) {
       il = dp4a_us(w4(a.p2, j), w4(w.a, j), il);
       il = dp4a_us(w4(a.p3, j), w4(w.b, j), il);
     }
-    float d = f16_loader((uint16_t)w.meta0);
-    return (float)(ih * 256 + il) * (a.s * d);
-  } else {
-    return 0.0f;
-  }
-}
-
-// Q4_K (gguf.rs:400-427): 6-bit scale / min unpack for sub-block s, then
-// sum_i x_i (q_i sc - m) = sc * sum(q xq) - m * sum(xq), times the block scale.
-__device__ __forceinline__ float dot_q4k(const WBlk& w, const ABlk& a, int s) {
-  uint32_t h0 = w.meta1.x, y = w.meta1.y, z = w.meta2.x, wv = w.meta2.y;
-  float dd = f16_loader((uint16_t)(h0 & 0xFFFF));
-  float dmin = f16_loader((uint16_t)(h0 >> 16));
-  uint32_t scv, mnv;
-  if (s < 4) {
-    int sh = 8 * s;
-    scv = (y >> sh) & 0x3F;
-    mnv = ((z >> sh) & 0xFF) >> 4 | (((wv >> sh) & 0x0F) << 4);
-  } else {
-    int sh = 8 * (s - 4);
-    uint32_t ys = (y >> sh) & 0xFF;
-    scv = ((z >> sh) & 0x0F) | ((ys >> 6) << 4);
-    mnv = (((wv >> sh) & 0xFF) >> 4) | (((ys >> 4) & 0x0C) << 4);
-  }
-  float scl = dd * (float)scv;
-  float mval = dmin * (float)mnv;
-  int iq = dot_nib(w.a, a);
-  return a.s * (scl * (float)iq - mval * (float)(a.sums.x + a.sums.y));
-}
-
-__device__ __forceinline__ float dot_q6k(const WBlk& w, const ABlk& a) {
-  int h0 = 0, l0 = 0, h1 = 0, l1 = 0;
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    uint32_t wq = w4(w.a, j);
-    uint32_t H = (j < 2) ? w.meta1.x : w.meta1.y;
-    uint32_t he = (j & 1) ? (H & 0x30303030u) : ((H << 4) & 0x30303030u);
-    uint32_t ho = (j & 1) ? ((H >> 2) & 0x30303030u) : ((H << 2) & 0x30303030u);
-    uint32_t qe = (wq & 0x0F0F0F0Fu) | he;
-    uint32_t qo = ((wq >> 4) & 0x0F0F0F0Fu) | ho;
-    if (j < 2) {
-      h0 = dp4a_su(w4(a.p0, j), qe, h0);
-      h0 = dp4a_su(w4(a.p1, j), qo, h0);
-      l0 = dp4a_uu(w4(a.p2, j), qe, l0);
-      l0 = dp4a_uu(w4(a.p3, j), qo, l0);
+    const float iq = fmaf(256.0f, i2f_small(ih), i2f_small(il));
+    return iq * (a.s * f16_loader((uint16_t)w.d));
+  } else if constexpr (FMT == F_Q4_K) {
+    // gguf.rs:400-427: 6-bit scale/min unpack for sub-block s; value =
+    // q * (d * scale_s) - dmin * min_s, so the block contributes
+    // sc * sum(q xq) - m * sum(xq), times the activation block scale.
+    const int s = b & 7;
+    const uint32_t y = w.h.y, z = w.h.z, wv = w.h.w;
+    const float dd = f16_loader((uint16_t)(w.h.x & 0xFFFF));
+    const float dmin = f16_loader((uint16_t)(w.h.x >> 16));
+    uint32_t scv, mnv;
+    if (s < 4) {
+      const int sh = 8 * s;
+      scv = (y >> sh) & 0x3F;
+      mnv = (((z >> sh) & 0xFF) >> 4) | (((wv >> sh) & 0x0F) << 4);
     } else {
-      h1 = dp4a_su(w4(a.p0, j), qe, h1);
-      h1 = dp4a_su(w4(a.p1, j), qo, h1);
-      l1 = dp4a_uu(w4(a.p2, j), qe, l1);
-      l1 = dp4a_uu(w4(a.p3, j), qo, l1);
+      const int sh = 8 * (s - 4);
+      const uint32_t ys = (y >> sh) & 0xFF;
+      scv = ((z >> sh) & 0x0F) | ((ys >> 6) << 4);
+      mnv = (((wv >> sh) & 0xFF) >> 4) | (((ys >> 4) & 0x0C) << 4);
     }
+    const float iq = dot_nib(w.a, a);
+    return a.s * ((dd * (float)scv) * iq - (dmin * (float)mnv) * (a.sums.x + a.sums.y));
+  } else {  // F_Q6_K, gguf.rs:462-483: value = (q6 - 32) * (sc * d)
+    int h0 = 0, l0 = 0, h1 = 0, l1 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint32_t wq = w4(w.a, j);
+      const uint32_t H = (j < 2) ? w.qh.x : w.qh.y;
+      const uint32_t he = (j & 1) ? (H & 0x30303030u) : ((H << 4) & 0x30303030u);
+      const uint32_t ho = (j & 1) ? ((H >> 2) & 0x30303030u) : ((H << 2) & 0x30303030u);
+      const uint32_t qe = (wq & 0x0F0F0F0Fu) | he;
+      const uint32_t qo = ((wq >> 4) & 0x0F0F0F0Fu) | ho;
+      if (j < 2) {
+        h0 = dp4a_su(w4(a.p0, j), qe, h0);
+        h0 = dp4a_su(w4(a.p1, j), qo, h0);
+        l0 = dp4a_uu(w4(a.p2, j), qe, l0);
+        l0 = dp4a_uu(w4(a.p3, j), qo, l0);
+      } else {
+        h1 = dp4a_su(w4(a.p0, j), qe, h1);
+        h1 = dp4a_su(w4(a.p1, j), qo, h1);
+        l1 = dp4a_uu(w4(a.p2, j), qe, l1);
+        l1 = dp4a_uu(w4(a.p3, j), qo, l1);
+      }
+    }
+    const float i0 = fmaf(256.0f, i2f_small(h0), i2f_small(l0)) - 32.0f * a.sums.x;
+    const float i1 = fmaf(256.0f, i2f_small(h1), i2f_small(l1)) - 32.0f * a.sums.y;
+    const float dd = f16_loader((uint16_t)(w.sd >> 16));
+    const float sc0 = (float)(int8_t)(w.sd & 0xFF) * dd;
+    const float sc1 = (float)(int8_t)((w.sd >> 8) & 0xFF) * dd;
+    return a.s * (i0 * sc0 + i1 * sc1);
   }
-  int i0 = h0 * 256 + l0 - 32 * a.sums.x;
-  int i1 = h1 * 256 + l1 - 32 * a.sums.y;
-  float dd = f16_loader((uint16_t)(w.meta0 >> 16));
-  float sc0 = (float)(int8_t)(w.meta0 & 0xFF) * dd;
-  float sc1 = (float)(int8_t)((w.meta0 >> 8) & 0xFF) * dd;
-  return a.s * ((float)i0 * sc0 + (float)i1 * sc1);
+}
+
+// ---------------------------------------------------------------------------
+// Activation prologues (per warp, over the warp's own blocks [wb0, wb1)).
+// ---------------------------------------------------------------------------
+template <int FMT>
+__device__ void prep_blocks(const float* xr, bool live, int wb0, int wb1, uint8_t* act, int cb0) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane & 7;  // elements 4j..4j+3 of the block
+  for (int b0 = wb0; b0 < wb1; b0 += 4) {
+    const int b = b0 + (lane >> 3);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live && b < wb1) v = *reinterpret_cast<const float4*>(xr + (size_t)b * 32 + 4 * j);
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
+    float scale = 0.0f;
+    if (amax > 0.0f) {
+      const float inv = 32767.0f / amax;
+      q0 = max(-32767, min(32767, __float2int_rn(v.x * inv)));
+      q1 = max(-32767, min(32767, __float2int_rn(v.y * inv)));
+      q2 = max(-32767, min(32767, __float2int_rn(v.z * inv)));
+      q3 = max(-32767, min(32767, __float2int_rn(v.w * inv)));
+      scale = amax / 32767.0f;
+    }
+    int ssum = q0 + q1 + q2 + q3;
+    ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
+    ssum += __shfl_xor_sync(0xffffffffu, ssum, 2);
+    if (b >= wb1) continue;
+    uint8_t* blk = act + (size_t)(b - cb0) * act_block_bytes(FMT);
+    // signed high bytes / unsigned low bytes
+    const uint32_t h0 = (q0 >> 8) & 0xFF, h1 = (q1 >> 8) & 0xFF, h2 = (q2 >> 8) & 0xFF,
+                   h3 = (q3 >> 8) & 0xFF;
+    const uint32_t l0 = q0 & 0xFF, l1 = q1 & 0xFF, l2 = q2 & 0xFF, l3 = q3 & 0xFF;
+    if constexpr (interleaved(FMT)) {
+      // elements 4j, 4j+2 are even -> even-plane slots 2j, 2j+1
+      uint16_t* P = reinterpret_cast<uint16_t*>(blk);
+      P[0 * 8 + j] = (uint16_t)(h0 | (h2 << 8));
+      P[1 * 8 + j] = (uint16_t)(h1 | (h3 << 8));
+      P[2 * 8 + j] = (uint16_t)(l0 | (l2 << 8));
+      P[3 * 8 + j] = (uint16_t)(l1 | (l3 << 8));
+    } else {
+      uint32_t* P = reinterpret_cast<uint32_t*>(blk);
+      const int half = j >> 2, o = j & 3;
+      P[half * 4 + o] = h0 | (h1 << 8) | (h2 << 16) | (h3 << 24);
+      P[(half + 2) * 4 + o] = l0 | (l1 << 8) | (l2 << 16) | (l3 << 24);
+    }
+    float* tail = reinterpret_cast<float*>(blk + 64);
+    if (j == 0) {
+      tail[0] = (float)ssum;
+      tail[2] = scale;
+    }
+    if (j == 4) tail[1] = (float)ssum;
+  }
+}
+
+// INT8: codes of the warp's blocks, given the row's 127/max factor.
+__device__ void prep_int8(const GemvParams& p, int m, bool live, float inv, bool zero_row, int wb0,
+                          int wb1, uint8_t* act, int cb0) {
+  const int lane = threadIdx.x & 31;
+  for (int b0 = wb0; b0 < wb1; b0 += 4) {
+    const int b = b0 + (lane >> 3), j = lane & 7;
+    if (b >= wb1) continue;
+    uint32_t word = 0;
+    if (live && !zero_row) {
+      if (p.xq) {
+        const int8_t* src = p.xq + (long long)m * p.ldx + (size_t)b * 32 + 4 * j;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int kk = b * 32 + 4 * j + e;
+          const uint32_t v = kk < p.k ? (uint8_t)src[e] : 0u;
+          word |= v << (8 * e);
+        }
+      } else {
+        const float* src = p.x + (long long)m * p.ldx + (size_t)b * 32 + 4 * j;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int kk = b * 32 + 4 * j + e;
+          int8_t v = 0;
+          if (kk < p.k) {
+            float r = roundf(__fmul_rn(src[e], inv));
+            r = fminf(127.0f, fmaxf(-127.0f, r));
+            v = (int8_t)(int)r;
+          }
+          word |= (uint32_t)(uint8_t)v << (8 * e);
+        }
+      }
+    }
+    reinterpret_cast<uint32_t*>(act + (size_t)(b - cb0) * 32)[j] = word;
+  }
 }
 
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int FMT, int MT, int R>
-__global__ void __launch_bounds__(THREADS) k_qgemv(GemvParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const long long m0 = (long long)blockIdx.y * MT;
-  if constexpr (FMT == F_INT8)
-    prologue_int8<MT>(p, m0, smem);
-  else
-    prologue_blocks<FMT, MT>(p, m0, smem);
+template <int FMT, int MT>
+__global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  __shared__ float red[WARPS][MT][32];
+  __shared__ float srow[MT];  // INT8: per-row activation scale sa
+  __shared__ float sinv[MT];  // INT8: 127 / max (0 for an all-zero row)
+  __shared__ int slast;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x, ks = blockIdx.y, m0 = blockIdx.z * MT;
+  const int cb0 = ks * p.kr, cb1 = min(p.nblk, cb0 + p.kr);
+  const int per = (cb1 - cb0 + WARPS - 1) / WARPS;
+  const int wb0 = min(cb1, cb0 + warp * per), wb1 = min(cb1, wb0 + per);
+  const int row = g * 32 + lane;
+  const int act_stride = p.kr * act_block_bytes(FMT);  // per activation row
+  // INT8 chunk sums live after the activations: [MT][chunks of this CTA][32]
+  const int cc0 = cb0 >> 4, ncc = ((cb1 + 15) >> 4) - cc0;
+  int* csum = reinterpret_cast<int*>(sm + MT * act_stride);
+
+  // First tiles: independent of the preceding kernel.
+  WB<FMT> w[U];
+#pragma unroll
+  for (int u = 0; u < U; u++)
+    if (wb0 + u < wb1) load_w<FMT>(p, g, wb0 + u, lane, w[u]);
+
+  griddep_wait();  // x may be written by the preceding kernel
+  griddep_launch();
+
+  // ---- activation prologue ----
+  if constexpr (FMT == F_INT8) {
+    for (int i = threadIdx.x; i < MT * ncc * 32; i += THREADS) csum[i] = 0;
+    for (int mm = 0; mm < MT; mm++) {
+      const int m = m0 + mm;
+      if (m >= p.m) continue;  // uniform across the CTA
+      if (p.xq) {
+        if (threadIdx.x == 0) srow[mm] = p.sx[m];
+        continue;
+      }
+      // quantize.zig:12-47: the row max spans all of K
+      const float* xr = p.x + (long long)m * p.ldx;
+      float amax = 0.0f;
+      for (int i = threadIdx.x; i < p.k; i += THREADS) amax = fmaxf(amax, fabsf(xr[i]));
+      amax = warp_max(amax);
+      if (lane == 0) red[warp][mm][0] = amax;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float a = red[0][mm][0];
+        for (int i = 1; i < WARPS; i++) a = fmaxf(a, red[i][mm][0]);
+        srow[mm] = (a == 0.0f) ? 1.0f : __fdiv_rn(a, 127.0f);
+        sinv[mm] = (a == 0.0f) ? 0.0f : __fdiv_rn(127.0f, a);
+      }
+      __syncthreads();
+    }
+    __syncthreads();
+    for (int mm = 0; mm < MT; mm++) {
+      const int m = m0 + mm;
+      const bool live = m < p.m;
+      const float inv = (live && !p.xq) ? sinv[mm] : 0.0f;
+      prep_int8(p, m, live, inv, live && !p.xq && inv == 0.0f, wb0, wb1, sm + mm * act_stride,
+                cb0);
+    }
+  } else {
+    for (int mm = 0; mm < MT; mm++) {
+      const int m = m0 + mm;
+      prep_blocks<FMT>(p.x + (long long)(m < p.m ? m : 0) * p.ldx, m < p.m, wb0, wb1,
+                       sm + mm * act_stride, cb0);
+    }
+  }
+  __syncthreads();  // INT8 chunk sums zeroed, every warp's activations ready
+
+  // ---- main loop: U tiles per iteration ----
+  float facc[MT];
+  int ich[MT];
+#pragma unroll
+  for (int mm = 0; mm < MT; mm++) {
+    facc[mm] = 0.0f;
+    ich[mm] = 0;
+  }
+  int cur_chunk = wb0 >> 4;
+
+  for (int b0 = wb0; b0 < wb1; b0 += U) {
+    if (b0 != wb0) {
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (b0 + u < wb1) load_w<FMT>(p, g, b0 + u, lane, w[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int b = b0 + u;
+      if (b >= wb1) break;
+      if constexpr (FMT == F_INT8) {
+        if ((b >> 4) != cur_chunk) {  // flush the finished 512-element chunk
+#pragma unroll
+          for (int mm = 0; mm < MT; mm++) {
+            atomicAdd(&csum[(mm * ncc + cur_chunk - cc0) * 32 + lane], ich[mm]);
+            ich[mm] = 0;
+          }
+          cur_chunk = b >> 4;
+        }
+      }
+#pragma unroll
+      for (int mm = 0; mm < MT; mm++) {
+        AB a;
+        load_act<FMT>(sm + mm * act_stride + (b - cb0) * act_block_bytes(FMT), a);
+        if constexpr (FMT == F_INT8)
+          ich[mm] += dot_int8(w[u], a);
+        else
+          facc[mm] += dot_block<FMT>(w[u], a, b);
+      }
+    }
+  }
+  if constexpr (FMT == F_INT8) {
+    if (wb0 < wb1) {
+#pragma unroll
+      for (int mm = 0; mm < MT; mm++)
+        atomicAdd(&csum[(mm * ncc + cur_chunk - cc0) * 32 + lane], ich[mm]);
+    }
+  } else {
+#pragma unroll
+    for (int mm = 0; mm < MT; mm++) red[warp][mm][lane] = facc[mm];
+  }
   __syncthreads();
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long stride = act_stride(FMT, p.kp, p.nblk);
-  const long long total_warps = (long long)gridDim.x * WARPS;
-  const long long iters = (p.nblk + 31) / 32;
-
-  for (long long row0 = ((long long)blockIdx.x * WARPS + warp) * R; row0 < p.n;
-       row0 += total_warps * R) {
-    float facc[R][MT];
-    int iacc[R][MT];
-#pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-      for (int mm = 0; mm < MT; mm++) {
-        facc[r][mm] = 0.0f;
-        iacc[r][mm] = 0;
-      }
-
-    for (long long it = 0; it < iters; it++) {
-      const long long b = it * 32 + lane;
-      const bool valid = b < p.nblk;
-      WBlk w[R];
-#pragma unroll
-      for (int r = 0; r < R; r++) {
-        if (valid && row0 + r < p.n) {
-          load_w<FMT>(p, row0 + r, b, w[r]);
-        } else {
-          w[r].a = make_uint4(0, 0, 0, 0);
-          w[r].b = make_uint4(0, 0, 0, 0);
-          w[r].meta0 = 0;
-          w[r].meta1 = make_uint2(0, 0);
-          w[r].meta2 = make_uint2(0, 0);
-        }
-      }
-#pragma unroll
-      for (int mm = 0; mm < MT; mm++) {
-        ABlk a;
-        if (valid) {
-          load_a<FMT>(smem + mm * stride, p.nblk, b, a);
-        } else {
-          a.p0 = a.p1 = a.p2 = a.p3 = make_uint4(0, 0, 0, 0);
-          a.sums = make_int2(0, 0);
-          a.s = 0.0f;
-        }
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-          if constexpr (FMT == F_INT8) {
-            int part = dot_int8(w[r], a);
+  // ---- CTA result per (activation row, weight row) ----
+  const bool split = p.nks > 1;
+  const long long G32 = (long long)p.groups * 32;
+  if (warp < MT) {
+    const int mm = warp, m = m0 + mm;
+    if (m < p.m) {
+      if constexpr (FMT == F_INT8) {
+        if (!split) {
+          if (row < p.n) {
+            const float sa = srow[mm], sbv = p.sb[row];
+            float out = 0.0f;
             if (p.chunked) {
-              // qmatmul.zig:68-98 (M>16): float sum over 512-wide K chunks in
-              // increasing order. Lanes 0-15 hold chunk 2*it, 16-31 chunk 2*it+1.
-#pragma unroll
-              for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-              int part_hi = __shfl_sync(0xffffffffu, part, 16);
-              if (lane == 0 && row0 + r < p.n) {
-                const float sa = reinterpret_cast<const float*>(smem + mm * stride + p.kp)[0];
-                const float sbv = p.sb[row0 + r];
-                facc[r][mm] = facc[r][mm] + ((float)part * sa) * sbv;
-                if (it * 32 + 16 < p.nblk)
-                  facc[r][mm] = facc[r][mm] + ((float)part_hi * sa) * sbv;
-              }
+              for (int c = 0; c < ncc; c++)
+                out = __fadd_rn(
+                    out, __fmul_rn(__fmul_rn((float)csum[(mm * ncc + c) * 32 + lane], sa), sbv));
             } else {
-              iacc[r][mm] += part;
+              int tot = 0;
+              for (int c = 0; c < ncc; c++) tot += csum[(mm * ncc + c) * 32 + lane];
+              out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
             }
-          } else if constexpr (FMT == F_Q4_K) {
-            facc[r][mm] += dot_q4k(w[r], a, (int)(b & 7));
-          } else if constexpr (FMT == F_Q6_K) {
-            facc[r][mm] += dot_q6k(w[r], a);
-          } else {
-            facc[r][mm] += dot_f<FMT>(w[r], a);
-          }
-        }
-      }
-    }
-
-    // Finish each (row, activation row) pair.
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-#pragma unroll
-      for (int mm = 0; mm < MT; mm++) {
-        const long long n = row0 + r, m = m0 + mm;
-        if constexpr (FMT == F_INT8) {
-          if (p.chunked) {
-            if (lane == 0 && n < p.n && m < p.m) p.y[m * p.ldy + n] = facc[r][mm];
-          } else {
-            int tot = warp_sum_i(iacc[r][mm]);
-            if (lane == 0 && n < p.n && m < p.m) {
-              const float sa = reinterpret_cast<const float*>(smem + mm * stride + p.kp)[0];
-              // qmatmul.zig:218-223: f_acc * sa * sb, left to right.
-              p.y[m * p.ldy + n] = __fmul_rn(__fmul_rn((float)tot, sa), p.sb[n]);
-            }
+            p.y[(long long)m * p.ldy + row] = out;
           }
         } else {
-          float v = warp_sum(facc[r][mm]);
-          if (lane == 0 && n < p.n && m < p.m) p.y[m * p.ldy + n] = v;
+          float* dst = p.part + (long long)m * p.nchunks * G32;
+          for (int c = 0; c < ncc; c++)
+            dst[(long long)(cc0 + c) * G32 + row] = __int_as_float(csum[(mm * ncc + c) * 32 + lane]);
+        }
+      } else {
+        float v = 0.0f;
+#pragma unroll
+        for (int i = 0; i < WARPS; i++) v += red[i][mm][lane];
+        if (!split) {
+          if (row < p.n) p.y[(long long)m * p.ldy + row] = v;
+        } else {
+          p.part[((long long)m * p.nks + ks) * G32 + row] = v;
         }
       }
+    }
+  }
+  if (!split) return;
+
+  // ---- split K: the last CTA of this row group sums the partials in order ----
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* c = p.cnt + (long long)blockIdx.z * p.groups + g;
+    const int arrived = atomicAdd(c, 1);
+    slast = (arrived == p.nks - 1);
+    if (slast) *c = 0;  // self-reset for the next launch
+  }
+  __syncthreads();
+  if (!slast) return;
+  __threadfence();
+  if (warp < MT) {
+    const int mm = warp, m = m0 + mm;
+    if (m < p.m && row < p.n) {
+      float out = 0.0f;
+      if constexpr (FMT == F_INT8) {
+        const float* src = p.part + (long long)m * p.nchunks * G32;
+        const float sa = srow[mm], sbv = p.sb[row];
+        if (p.chunked) {
+          for (int c = 0; c < p.nchunks; c++) {
+            const int cv = __float_as_int(__ldcg(src + c * G32 + row));
+            out = __fadd_rn(out, __fmul_rn(__fmul_rn((float)cv, sa), sbv));
+          }
+        } else {
+          int tot = 0;
+          for (int c = 0; c < p.nchunks; c++) tot += __float_as_int(__ldcg(src + c * G32 + row));
+          out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
+        }
+      } else {
+        const float* src = p.part + (long long)m * p.nks * G32;
+        for (int s = 0; s < p.nks; s++) out += __ldcg(src + s * G32 + row);
+      }
+      p.y[(long long)m * p.ldy + row] = out;
     }
   }
 }
 
 // ---------------------------------------------------------------------------
-// Host-side launch
+// Host-side planning and launch
 // ---------------------------------------------------------------------------
-struct OccKey {
-  const void* f;
-  long long smem;
-  bool operator==(const OccKey& o) const { return f == o.f && smem == o.smem; }
-};
-struct OccHash {
-  size_t operator()(const OccKey& k) const {
-    return std::hash<const void*>()(k.f) ^ (std::hash<long long>()(k.smem) << 1);
-  }
+struct Plan {
+  int groups, nblk, kr, nks, nchunks, mt;
+  size_t smem;
 };
 
-int occupancy(const void* f, long long smem) {
-  static std::mutex mu;
-  static std::unordered_map<OccKey, int, OccHash> cache;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  OccKey key{f, smem * 64 + dev};
-  std::lock_guard<std::mutex> g(mu);
-  auto it = cache.find(key);
-  if (it != cache.end()) return it->second;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  int nb = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, f, THREADS, (size_t)smem);
-  if (nb < 1) nb = 0;
-  cache[key] = nb;
-  return nb;
+int mt_for(size_t m) { return m == 1 ? 1 : (m == 2 ? 2 : 4); }
+
+Plan make_plan(int fmt, size_t m, size_t n, size_t kp) {
+  Plan pl{};
+  pl.groups = (int)((n + 31) / 32);
+  pl.nblk = (int)(kp / 32);
+  pl.nchunks = (pl.nblk + 15) / 16;
+  pl.mt = mt_for(m);
+  const int sms = num_sms();
+  // Aim at ~4 CTAs per SM: split K until the grid fills the GPU, keeping at
+  // least one block per warp (INT8: whole 512-element chunks per CTA).
+  const int target = sms * 4;
+  const int mslices = (int)((m + pl.mt - 1) / pl.mt);
+  int nks = target / std::max(1, pl.groups * mslices);
+  const int maxks = fmt == F_INT8 ? std::max(1, pl.nblk / 16) : std::max(1, pl.nblk / WARPS);
+  nks = std::max(1, std::min(nks, maxks));
+  int kr = (pl.nblk + nks - 1) / nks;
+  if (fmt == F_INT8) kr = (kr + 15) / 16 * 16;
+  // shared memory bound (activations of MT rows)
+  const int abb = fmt == F_INT8 ? 32 : 80;
+  while ((size_t)pl.mt * kr * abb > 96 * 1024 && kr > 16) kr = (kr + 1) / 2;
+  if (fmt == F_INT8) kr = (kr + 15) / 16 * 16;
+  pl.kr = kr;
+  pl.nks = (pl.nblk + kr - 1) / kr;
+  const int ncc = (kr + 15) / 16 + 1;
+  pl.smem = (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
+  return pl;
 }
 
-template <int FMT, int MT, int R>
-syn_status_t launch_t(const GemvParams& p, cudaStream_t st) {
-  const void* f = reinterpret_cast<const void*>(&k_qgemv<FMT, MT, R>);
-  long long smem = MT * act_stride(FMT, p.kp, p.nblk);
-  if (smem > 227 * 1024) return SYN_ERR_UNSUPPORTED;
-  int occ = occupancy(f, smem);
-  if (occ < 1) return SYN_ERR_UNSUPPORTED;
-  long long need = (p.n + (long long)WARPS * R - 1) / ((long long)WARPS * R);
-  long long cap = (long long)num_sms() * occ;
-  dim3 grid((unsigned)(need < cap ? need : cap), (unsigned)((p.m + MT - 1) / MT));
-  k_qgemv<FMT, MT, R><<<grid, THREADS, (size_t)smem, st>>>(p);
-  SYN_LAUNCH_CHECK("k_qgemv");
-  return SYN_OK;
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 template <int FMT, int MT>
-syn_status_t launch_r(const GemvParams& p, cudaStream_t st) {
-  const long long sms = num_sms();
-  if (p.n >= WARPS * 4 * 2 * sms) return launch_t<FMT, MT, 4>(p, st);
-  if (p.n >= WARPS * 2 * 2 * sms) return launch_t<FMT, MT, 2>(p, st);
-  return launch_t<FMT, MT, 1>(p, st);
+syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
+  static std::mutex mu;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> guard(mu);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      cudaFuncSetAttribute(k_qgemv<FMT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           200 * 1024);
+      attr_set[dev] = true;
+    }
+  }
+  dim3 grid((unsigned)pl.groups, (unsigned)pl.nks, (unsigned)((p.m + MT - 1) / MT));
+  cudaError_t e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.smem, st, p);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "k_qgemv");
+    return SYN_ERR_CUDA;
+  }
+  return SYN_OK;
 }
 
 template <int FMT>
-syn_status_t launch_m(const GemvParams& p, cudaStream_t st) {
-  if (p.m == 1) return launch_r<FMT, 1>(p, st);
-  if (p.m == 2) return launch_r<FMT, 2>(p, st);
-  syn_status_t s = launch_r<FMT, 4>(p, st);
-  if (s == SYN_ERR_UNSUPPORTED) s = launch_r<FMT, 1>(p, st);  // shared memory bound
-  return s;
+syn_status_t launch_m(const GemvParams& p, const Plan& pl, cudaStream_t st) {
+  if (pl.mt == 1) return launch_t<FMT, 1>(p, pl, st);
+  if (pl.mt == 2) return launch_t<FMT, 2>(p, pl, st);
+  return launch_t<FMT, 4>(p, pl, st);
+}
+
+syn_status_t run_gemv(int fmt, const GemvParams& p, const Plan& pl, cudaStream_t st) {
+  switch (fmt) {
+    case F_INT8: return launch_m<F_INT8>(p, pl, st);
+    case F_Q4_0: return launch_m<F_Q4_0>(p, pl, st);
+    case F_Q8_0: return launch_m<F_Q8_0>(p, pl, st);
+    case F_Q4_K: return launch_m<F_Q4_K>(p, pl, st);
+    case F_Q6_K: return launch_m<F_Q6_K>(p, pl, st);
+    case F_Q4_0RAW: return launch_t<F_Q4_0RAW, 1>(p, pl, st);
+  }
+  return SYN_ERR_INVALID_ARG;
+}
+
+void fill_common(GemvParams& p, const Plan& pl, float* part, int* cnt, int* err) {
+  p.groups = pl.groups;
+  p.nblk = pl.nblk;
+  p.kr = pl.kr;
+  p.nks = pl.nks;
+  p.nchunks = pl.nchunks;
+  p.part = part;
+  p.cnt = cnt;
+  p.err = err;
 }
 
 }  // namespace
 
+size_t gemv_partial_bytes(int fmt, size_t m, size_t n, size_t kp) {
+  const Plan pl = make_plan(fmt == SYN_QFMT_INT8_KN ? F_INT8 : F_Q4_0, m, n, kp);
+  if (pl.nks <= 1) return 0;
+  const size_t per = fmt == SYN_QFMT_INT8_KN ? (size_t)pl.nchunks : (size_t)pl.nks;
+  return m * per * (size_t)pl.groups * 32 * sizeof(float);
+}
+
+size_t gemv_counter_bytes(size_t m, size_t n) {
+  return ((m + 3) / 4 * 4) * ((n + 31) / 32) * sizeof(int);
+}
+
 syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx,
-                          const int8_t* xq, const float* sx, size_t m, float* y,
-                          size_t ldy, int chunked, cudaStream_t st) {
+                          const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
+                          int chunked, float* part, int* cnt, int* err, cudaStream_t st) {
+  if (w->n > 0x7FFFFFFFull || w->kp > 0x3FFFFFFFull || m > 0xFFFFull) return SYN_ERR_UNSUPPORTED;
+  // the float4 activation loads of the block formats need 16-byte aligned rows
+  if (w->fmt != SYN_QFMT_INT8_KN && ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 3)))
+    return SYN_ERR_NOT_CONTIGUOUS;
+  const int fk = w->fmt == SYN_QFMT_INT8_KN ? F_INT8 : w->fmt;
+  const Plan pl = make_plan(fk, m, w->n, w->kp);
   GemvParams p{};
   p.q = w->q;
   p.d = w->d;
   p.sb = w->sb;
   p.hdr = w->hdr;
   p.qh = w->qh;
-  p.sc = w->sc;
-  p.n = (long long)w->n;
-  p.k = (long long)w->k;
-  p.kp = (long long)w->kp;
-  p.nblk = (long long)(w->kp / 32);
+  p.sc = reinterpret_cast<const uint16_t*>(w->sc);
   p.x = x;
-  p.ldx = (long long)ldx;
   p.xq = xq;
-  p.ldxq = (long long)ldx;
   p.sx = sx;
-  p.m = (long long)m;
+  p.ldx = (long long)ldx;
+  p.n = (int)w->n;
+  p.k = (int)w->k;
+  p.kp = (int)w->kp;
+  p.nsb = (int)(w->k / 256);
+  p.m = (int)m;
   p.y = y;
   p.ldy = (long long)ldy;
   p.chunked = chunked;
-  switch (w->fmt) {
-    case SYN_QFMT_INT8_KN: return launch_m<F_INT8>(p, st);
-    case SYN_QFMT_Q4_0: return launch_m<F_Q4_0>(p, st);
-    case SYN_QFMT_Q8_0: return launch_m<F_Q8_0>(p, st);
-    case SYN_QFMT_Q4_K: return launch_m<F_Q4_K>(p, st);
-    case SYN_QFMT_Q6_K: return launch_m<F_Q6_K>(p, st);
-  }
-  return SYN_ERR_INVALID_ARG;
+  fill_common(p, pl, part, cnt, err);
+  if (pl.nks > 1 && (!part || !cnt)) return SYN_ERR_INTERNAL;
+  return run_gemv(fk, p, pl, st);
 }
 
 syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* b, float* c,
-                             cudaStream_t st) {
+                             float* part, int* cnt, int* err, cudaStream_t st) {
+  if (n > 0x7FFFFFFFull || k > 0x3FFFFFFFull) return SYN_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(a) & 15) return SYN_ERR_NOT_CONTIGUOUS;
+  const Plan pl = make_plan(F_Q4_0, 1, n, k);
   GemvParams p{};
   p.q = b;
-  p.n = (long long)n;
-  p.k = (long long)k;
-  p.kp = (long long)k;
-  p.nblk = (long long)(k / 32);
   p.x = a;
   p.ldx = (long long)k;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.kp = (int)k;
   p.m = 1;
   p.y = c;
   p.ldy = (long long)n;
-  return launch_r<F_Q4_0RAW, 1>(p, st);
+  fill_common(p, pl, part, cnt, err);
+  if (pl.nks > 1 && (!part || !cnt)) return SYN_ERR_INTERNAL;
+  return run_gemv(F_Q4_0RAW, p, pl, st);
 }
 
 }  // namespace syn

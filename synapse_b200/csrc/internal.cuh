@@ -3,20 +3,27 @@
 
 #include "common.cuh"
 
+// One context per device and per issuing stream: the scratch buffers are
+// reused by every call made through the context, in stream order.
 struct syn_cuda_ctx_s {
   int device;
   int sms;
   cudaStream_t upload_stream;
+  float* part;       // per-(row, K-split) partial sums of split GEMVs
+  size_t part_bytes;
+  int* cnt;          // per-row-group arrival counters; zero between launches
+  size_t cnt_bytes;
+  int* err;          // device-side error word (e.g. SYN_ERR_TIMEOUT)
 };
 
 // Repacked weight in HBM. One allocation; the views below point into it.
-// Per output row n the arrays hold, in K order (see repack.cu):
-//   INT8  : q[N][kp] int8 (kp = K rounded up to 32, zero padded), sb[N] f32
-//   Q4_0  : q[N][K/2] nibbles (as in the GGUF block), d[N][K/32] f16 bits
-//   Q8_0  : q[N][K] int8, d[N][K/32] f16 bits
-//   Q4_K  : q[N][K/2] nibbles, hdr[N][K/256][16] (d, dmin, 12 scale bytes)
-//   Q6_K  : q[N][K/2] low nibbles, qh[N][K/32][8] high bits (re-arranged),
-//           sc[N][K/16] int8 scales, d[N][K/256] f16 bits
+// Rows are row-interleaved by 32 (see repack.cu for the exact layout):
+//   INT8  : q tiles of 32 rows x 32 int8 (kp = K rounded up to 32), sb f32
+//   Q4_0  : q tiles of 32 rows x 16 nibble bytes, d f16 bits per row-block
+//   Q8_0  : q tiles of 32 rows x 32 int8, d f16 bits per row-block
+//   Q4_K  : q tiles of 32 rows x 16 nibble bytes, hdr 16 B per row-superblock
+//   Q6_K  : q low-nibble tiles, qh 8 B per row-block (re-arranged high bits),
+//           sc 2 int8 scales per row-block, d f16 bits per row-superblock
 struct syn_cuda_weight_s {
   int fmt;
   int device;
@@ -34,31 +41,38 @@ struct syn_cuda_weight_s {
 
 namespace syn {
 
-// Launches the fused activation-prologue GEMV for rows [0, m) of x.
-// x: f32 [m, k] (row stride ldx) or, when xq != nullptr (INT8 only), int8
-// [m, k] (row stride ldx) with per-row scales sx. y: f32 [m, n] (row stride ldy).
-// chunked=1 selects the reference's M>16 INT8 epilogue (per-512-K chunks).
+// Scratch of a GEMV over m activation rows: partial sums (0 when K is not
+// split across CTAs) and per-row-group arrival counters (zero before the
+// first launch; the kernel leaves them zero).
+size_t gemv_partial_bytes(int fmt, size_t m, size_t n, size_t kp);
+size_t gemv_counter_bytes(size_t m, size_t n);
+
+// Launches the fused GEMV for rows [0, m) of x (programmatic dependent
+// launch). x: f32 [m, k] (row stride ldx; 16-byte aligned rows) or, when
+// xq != nullptr (INT8 only), int8 [m, k] (row stride ldx) with per-row
+// scales sx. y: f32 [m, n] (row stride ldy). chunked=1 selects the
+// reference's M>16 INT8 epilogue (per-512-K chunks). err: device error word
+// or nullptr.
 syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx,
-                          const int8_t* xq, const float* sx, size_t m, float* y,
-                          size_t ldy, int chunked, cudaStream_t st);
+                          const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
+                          int chunked, float* part, int* cnt, int* err, cudaStream_t st);
 
 // Raw-layout Q4_0 GEMV over the reference's 18-byte blocks (M = 1).
-syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a,
-                             const uint8_t* b, float* c, cudaStream_t st);
+syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* b, float* c,
+                             float* part, int* cnt, int* err, cudaStream_t st);
 
 // Per-row INT8 quantisation (quantize.zig:12-47).
-syn_status_t launch_quantize_rows(const float* x, size_t rows, size_t cols,
-                                  int8_t* out, float* scales, cudaStream_t st);
+syn_status_t launch_quantize_rows(const float* x, size_t rows, size_t cols, int8_t* out,
+                                  float* scales, cudaStream_t st);
 
 // Load-time per-output-row INT8 weight quantisation into the [K,N] layout.
 syn_status_t launch_quantize_weights(const float* w, size_t n, size_t k, int8_t* out_kn,
                                      float* scales, cudaStream_t st);
 
-// Repack kernels (repack.cu).
-// ld_src: row stride of an INT8_KN source (0 = n); ignored by block formats.
+// Repack kernels (repack.cu). ld_src: row stride of an INT8_KN source
+// (0 = n); ignored by block formats. w->buf / w->bytes are zero-filled first.
 syn_status_t repack_weight(syn_cuda_weight_s* w, const uint8_t* d_src, size_t ld_src,
                            const float* d_scales, cudaStream_t st);
-syn_status_t dequant_weight(const syn_cuda_weight_s* w, float* d_out,
-                            cudaStream_t st);
+syn_status_t dequant_weight(const syn_cuda_weight_s* w, float* d_out, cudaStream_t st);
 
 }  // namespace syn

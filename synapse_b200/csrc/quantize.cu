@@ -1,10 +1,18 @@
-// quantize.cu -- per-row (per-channel) INT8 activation quantisation.
+// quantize.cu -- per-row INT8 quantisation kernels.
 //
-// Bit-exact restatement of quantizePerChannelInt8 (zig/src/ops/quantize.zig:12-47):
-// max_abs over the row; a zero row gets scale 1.0 and all-zero codes; else
-// scale = max_abs / 127, q = clamp(round(x * (127 / max_abs)), -127, 127)
-// with round-half-away-from-zero. Division and multiply are IEEE
-// round-to-nearest (__fdiv_rn / __fmul_rn), as in the Zig f32 code.
+// k_quantize_rows: bit-exact restatement of quantizePerChannelInt8
+// (zig/src/ops/quantize.zig:12-47): max_abs over the row; a zero row gets
+// scale 1.0 and all-zero codes; else scale = max_abs / 127,
+// q = clamp(round(x * (127 / max_abs)), -127, 127), round half away from zero.
+// Division and multiply are IEEE round-to-nearest (__fdiv_rn / __fmul_rn),
+// as in the Zig f32 code.
+//
+// k_quantize_weights: load-time weight quantisation (reference:
+// MinMaxCalibration::compute_scales, quantization/primitives/calibration.rs:11-24,
+// and QuantizedLinear::from_f32_with_scales + transpose_i8,
+// quantization/primitives/int8_linear.rs:21-70): per output row
+// s = max|w| / 127 (1.0 for a zero row), q = clamp(round(w * (1/s)), -128, 127),
+// written in the reference's GEMM layout [K, N].
 #include "internal.cuh"
 
 namespace syn {
@@ -12,31 +20,26 @@ namespace {
 
 constexpr int QT = 256;
 
-__global__ void __launch_bounds__(QT) k_quantize_rows(const float* __restrict__ x, long long cols,
-                                                      int8_t* __restrict__ out,
-                                                      float* __restrict__ scales) {
-  const long long row = blockIdx.x;
-  const float* xr = x + row * cols;
-  int8_t* orow = out + row * cols;
+__device__ __forceinline__ float block_max_abs(const float* row, long long cols) {
   __shared__ float red[QT / 32];
   float amax = 0.0f;
-  // 16-byte vector path when the row is aligned, scalar otherwise.
-  const bool vec = ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) && (cols % 4 == 0);
-  if (vec) {
-    const float4* x4 = reinterpret_cast<const float4*>(xr);
-    for (long long i = threadIdx.x; i < cols / 4; i += QT) {
-      float4 v = x4[i];
-      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-  } else {
-    for (long long i = threadIdx.x; i < cols; i += QT) amax = fmaxf(amax, fabsf(xr[i]));
-  }
+  for (long long i = threadIdx.x; i < cols; i += QT) amax = fmaxf(amax, fabsf(row[i]));
   amax = warp_max(amax);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   amax = red[0];
 #pragma unroll
   for (int w = 1; w < QT / 32; w++) amax = fmaxf(amax, red[w]);
+  return amax;
+}
+
+__global__ void __launch_bounds__(QT) k_quantize_rows(const float* __restrict__ x, long long cols,
+                                                      int8_t* __restrict__ out,
+                                                      float* __restrict__ scales) {
+  const long long row = blockIdx.x;
+  const float* xr = x + row * cols;
+  int8_t* orow = out + row * cols;
+  const float amax = block_max_abs(xr, cols);
   if (amax == 0.0f) {
     for (long long i = threadIdx.x; i < cols; i += QT) orow[i] = 0;
     if (threadIdx.x == 0) scales[row] = 1.0f;
@@ -51,6 +54,22 @@ __global__ void __launch_bounds__(QT) k_quantize_rows(const float* __restrict__ 
   if (threadIdx.x == 0) scales[row] = __fdiv_rn(amax, 127.0f);
 }
 
+__global__ void __launch_bounds__(QT) k_quantize_weights(const float* __restrict__ w, long long n,
+                                                         long long k, int8_t* __restrict__ out_kn,
+                                                         float* __restrict__ scales) {
+  const long long ch = blockIdx.x;
+  const float* row = w + ch * k;
+  const float amax = block_max_abs(row, k);
+  const float s = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+  const float inv_s = __fdiv_rn(1.0f, s);
+  for (long long j = threadIdx.x; j < k; j += QT) {
+    float r = roundf(__fmul_rn(row[j], inv_s));
+    r = fminf(127.0f, fmaxf(-128.0f, r));
+    out_kn[j * n + ch] = (int8_t)(int)r;
+  }
+  if (threadIdx.x == 0) scales[ch] = s;
+}
+
 }  // namespace
 
 syn_status_t launch_quantize_rows(const float* x, size_t rows, size_t cols, int8_t* out,
@@ -61,43 +80,6 @@ syn_status_t launch_quantize_rows(const float* x, size_t rows, size_t cols, int8
   return SYN_OK;
 }
 
-}  // namespace syn
-
-// ---------------------------------------------------------------------------
-// Load-time weight quantisation (reference: MinMaxCalibration::compute_scales,
-// quantization/primitives/calibration.rs:11-24, and
-// QuantizedLinear::from_f32_with_scales + transpose_i8,
-// quantization/primitives/int8_linear.rs:21-70): per output row
-// s = max|w| / 127 (1.0 for a zero row), q = clamp(round(w * (1/s)), -128, 127),
-// written in the reference's GEMM layout [K, N].
-// ---------------------------------------------------------------------------
-namespace syn {
-namespace {
-__global__ void __launch_bounds__(QT) k_quantize_weights(const float* __restrict__ w, long long n,
-                                                         long long k, int8_t* __restrict__ out_kn,
-                                                         float* __restrict__ scales) {
-  const long long ch = blockIdx.x;
-  const float* row = w + ch * k;
-  __shared__ float red[QT / 32];
-  float amax = 0.0f;
-  for (long long i = threadIdx.x; i < k; i += QT) amax = fmaxf(amax, fabsf(row[i]));
-  amax = warp_max(amax);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-  __syncthreads();
-  amax = red[0];
-#pragma unroll
-  for (int i = 1; i < QT / 32; i++) amax = fmaxf(amax, red[i]);
-  const float s = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
-  const float inv_s = __fdiv_rn(1.0f, s);
-  for (long long j = threadIdx.x; j < k; j += QT) {
-    float r = roundf(__fmul_rn(row[j], inv_s));
-    r = fminf(127.0f, fmaxf(-128.0f, r));
-    out_kn[j * n + ch] = (int8_t)(int)r;
-  }
-  if (threadIdx.x == 0) scales[ch] = s;
-}
-}  // namespace
-
 syn_status_t launch_quantize_weights(const float* w, size_t n, size_t k, int8_t* out_kn,
                                      float* scales, cudaStream_t st) {
   if (n > 0x7FFFFFFFull) return SYN_ERR_INVALID_ARG;
@@ -105,4 +87,5 @@ syn_status_t launch_quantize_weights(const float* w, size_t n, size_t k, int8_t*
   SYN_LAUNCH_CHECK("k_quantize_weights");
   return SYN_OK;
 }
+
 }  // namespace syn
