@@ -184,6 +184,25 @@ syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t *ctx,
                                             const float *scales_x, size_t m,
                                             float *y, void *stream);
 
+/* Allocation-free variant of syn_cuda_qmatmul. It has no counterpart in the
+ * reference: it is for callers that must not allocate device memory while
+ * they run (latency-critical decode loops, processes whose device memory is
+ * owned by an external pool or budget, hosts that forbid the CUDA
+ * allocator). Same inputs, outputs and results as syn_cuda_qmatmul; no
+ * context is needed, and the weight's device must be current.
+ * Its scratch (split-K partial sums and arrival counters) is a fixed device
+ * array of SYN_CUDA_NOALLOC_SCRATCH_BYTES that every GPU loading the library
+ * keeps until exit. A call needing more returns SYN_ERR_OUT_OF_MEMORY without
+ * launching anything. The first call on a device looks the array up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array and each resets its counters first: calls
+ * whose execution overlaps on the GPU (other streams, other threads) race
+ * and must be serialised by the caller. */
+#define SYN_CUDA_NOALLOC_SCRATCH_BYTES (4u << 20)
+syn_status_t syn_cuda_qmatmul_noalloc(const syn_cuda_weight_t *w,
+                                      const float *x, size_t m, float *y,
+                                      void *stream);
+
 #ifdef __cplusplus
 }
 #endif

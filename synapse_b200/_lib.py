@@ -34,6 +34,7 @@ SIGNATURES = {
     "syn_cuda_weight_dequant": (c_st, [c_vp, c_vp]),
     "syn_cuda_qmatmul": (c_st, [c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
     "syn_cuda_qmatmul_int8_prequant": (c_st, [c_vp, c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
+    "syn_cuda_qmatmul_noalloc": (c_st, [c_vp, c_vp, c_size, c_vp, c_vp]),
 }
 
 
