@@ -2,29 +2,34 @@
 //
 // Layout. Weights are repacked row-interleaved by 32 (repack.cu): for a
 // group of 32 rows and one 32-element block, the 32 rows' bytes are stored
-// back to back. Lane l of a warp owns row 32g + l, so one warp-wide 16-byte
-// load reads a 512-byte contiguous tile (4-bit formats; two loads for 8-bit
-// ones) and every lane accumulates its own row: no cross-lane reduction.
+// back to back, and all tiles of one row group follow each other in K order.
+// Lane l of a warp owns row 32g + l, so every lane accumulates its own row:
+// no cross-lane reduction.
 //
 // Work decomposition. Grid = (row groups, K splits, activation-row slices).
-// A CTA covers 32 rows x a contiguous range of kr blocks; its 8 warps split
-// that range evenly. Each warp converts the activations of its own blocks
-// (see below) into shared memory, then streams its weight tiles four at a
-// time (the first four are requested before griddepcontrol.wait, since
-// weights never depend on the preceding kernel). Warp partials are summed in
-// warp order through shared memory; when K is split across CTAs, the CTA
-// partials go to scratch and the last CTA to arrive for a row group (atomic
-// counter, reset by that CTA) sums them in K order. The result is
-// deterministic.
+// A CTA covers 32 rows x a contiguous range of kr blocks (a multiple of 16,
+// i.e. of 512 K elements). The CTA's weights are therefore one contiguous run
+// of bytes per array, which k_qgemv_tma streams into a ring of shared-memory
+// stages (16 blocks each) with 1-D bulk TMA copies issued by a producer warp;
+// the copies are issued before griddepcontrol.wait (weights never depend on
+// the preceding kernel), so under programmatic dependent launch they overlap
+// the tail of the kernel before. Eight consumer warps each take two blocks of
+// a stage. Warp partials are summed in warp order through shared memory;
+// when K is split across CTAs, the CTA partials go to scratch and the last
+// CTA to arrive for a row group (atomic counter, reset by that CTA) sums them
+// in K order. Results are deterministic.
 //
-// Activations.
+// The raw-layout Q4_0 GEMV (syn_q4_0_gemv, 18-byte blocks, 2-byte aligned)
+// cannot be bulk-copied; k_qgemv streams it with direct loads instead.
+//
+// Activations (converted per CTA, only for its K range, in shared memory).
 //   INT8 weights: per-row INT8 quantisation exactly as quantize.zig:12-47
-//     (row max over all of K, one CTA-wide reduction); W8A8 like
-//     QuantizedLinear::forward (int8_linear.rs:87-117). Products are exact
-//     int32 per 512-element K chunk (shared-memory integer atomics), and the
-//     epilogue reproduces qmatmul.zig: float(acc) * sa * sb for M <= 16
-//     (one accumulator over K) and, for M > 16, C = 0; C += float(chunk) *
-//     sa * sb in chunk order (qmatmul.zig:68-98), every op rounded.
+//     (row max over all of K); W8A8 like QuantizedLinear::forward
+//     (int8_linear.rs:87-117). Products are exact int32 per 512-element K
+//     chunk, and the epilogue reproduces qmatmul.zig: float(acc) * sa * sb
+//     for M <= 16 (one accumulator over K) and, for M > 16, C = 0; C +=
+//     float(chunk) * sa * sb in chunk order (qmatmul.zig:68-98), every op
+//     rounded.
 //   Block formats: each 32-element block is scaled to 16-bit integers
 //     (|xq| <= 32767, one f32 scale per block) and split into a signed high
 //     byte and an unsigned low byte ("planes"), so every product runs as
@@ -33,6 +38,9 @@
 //     sums over blocks.
 #include <algorithm>
 #include <mutex>
+#include <set>
+#include <string>
+#include <vector>
 
 #include "internal.cuh"
 
@@ -42,13 +50,15 @@ namespace {
 enum : int { F_INT8 = SYN_QFMT_INT8_KN, F_Q4_0 = SYN_QFMT_Q4_0, F_Q8_0 = SYN_QFMT_Q8_0,
              F_Q4_K = SYN_QFMT_Q4_K, F_Q6_K = SYN_QFMT_Q6_K, F_Q4_0RAW = 100 };
 
-constexpr int WARPS = 8;
-constexpr int THREADS = WARPS * 32;
-constexpr int U = 4;  // weight tiles in flight per warp
+constexpr int WARPS = 8;              // consumer warps
+constexpr int THREADS = WARPS * 32;   // consumer threads (named barrier 1)
+constexpr int U = 4;                  // direct kernel: tiles in flight per warp
+constexpr int SB = 16;                // blocks per stage (one 512-element chunk)
 
 __host__ __device__ constexpr bool interleaved(int f) {
   return f == F_Q4_0 || f == F_Q4_K || f == F_Q6_K || f == F_Q4_0RAW;
 }
+__host__ __device__ constexpr bool eight_bit(int f) { return f == F_INT8 || f == F_Q8_0; }
 
 // Shared-memory bytes of one activation block (one 32-element block of one
 // activation row):
@@ -60,6 +70,25 @@ __host__ __device__ constexpr bool interleaved(int f) {
 //           then float2 sums (sum of xq over elements 0-15 / 16-31, exact),
 //           f32 block scale, pad.
 __host__ __device__ constexpr int act_block_bytes(int fmt) { return fmt == F_INT8 ? 32 : 80; }
+
+// Stage layout (TMA kernel): per block of the stage, the 32-row tile of each
+// array, in the same order as in HBM.
+template <int FMT>
+struct Stage {
+  static constexpr int QT = eight_bit(FMT) ? 1024 : 512;                    // q tile
+  static constexpr int DT = (FMT == F_Q4_0 || FMT == F_Q8_0) ? 64 : 0;      // d tile
+  static constexpr int HT = (FMT == F_Q4_K) ? 512 : 0;   // header tile, per 8 blocks
+  static constexpr int QHT = (FMT == F_Q6_K) ? 256 : 0;  // high-bit tile
+  static constexpr int SCT = (FMT == F_Q6_K) ? 64 : 0;   // scale tile
+  static constexpr int D6T = (FMT == F_Q6_K) ? 64 : 0;   // super-block scale tile, per 8
+  static constexpr int OFF_D = SB * QT;
+  static constexpr int OFF_H = OFF_D + SB * DT;
+  static constexpr int OFF_QH = OFF_H + (SB / 8) * HT;
+  static constexpr int OFF_SC = OFF_QH + SB * QHT;
+  static constexpr int OFF_D6 = OFF_SC + SB * SCT;
+  static constexpr int BYTES = (OFF_D6 + (SB / 8) * D6T + 127) / 128 * 128;
+  static constexpr int NS = eight_bit(FMT) ? 3 : 4;  // ring depth
+};
 
 struct GemvParams {
   const uint8_t* q;
@@ -83,6 +112,14 @@ struct GemvParams {
   int* err;
 };
 
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+}
+
+__device__ __forceinline__ void report(const GemvParams& p, int code) {
+  if (p.err) atomicExch(p.err, code);
+}
+
 // ---------------------------------------------------------------------------
 // Weight tiles
 // ---------------------------------------------------------------------------
@@ -94,18 +131,18 @@ template <> struct WB<F_Q4_0RAW> { uint4 a; uint32_t d; };
 template <> struct WB<F_Q4_K> { uint4 a; uint4 h; };
 template <> struct WB<F_Q6_K> { uint4 a; uint2 qh; uint32_t sd; };
 
-// Loads block b of this lane's row (group g, lane l).
+// Direct global load of block b of this lane's row (group g, lane l).
 template <int FMT>
 __device__ __forceinline__ void load_w(const GemvParams& p, int g, int b, int l, WB<FMT>& w) {
   const size_t t = ((size_t)g * p.nblk + b) * 32 + l;  // row-interleaved tile index
   if constexpr (FMT == F_INT8) {
-    const uint8_t* src = p.q + t * 32;
+    const uint8_t* src = p.q + (t >> 5) * 1024 + (t & 31) * 16;  // two half-planes
     w.a = ld_stream16(src);
-    w.b = ld_stream16(src + 16);
+    w.b = ld_stream16(src + 512);
   } else if constexpr (FMT == F_Q8_0) {
-    const uint8_t* src = p.q + t * 32;
+    const uint8_t* src = p.q + (t >> 5) * 1024 + (t & 31) * 16;
     w.a = ld_stream16(src);
-    w.b = ld_stream16(src + 16);
+    w.b = ld_stream16(src + 512);
     w.d = ld_nc_u16(p.d + t);
   } else if constexpr (FMT == F_Q4_0) {
     w.a = ld_stream16(p.q + t * 16);
@@ -134,6 +171,30 @@ __device__ __forceinline__ void load_w(const GemvParams& p, int g, int b, int l,
     w.d = h[0];
     w.a = make_uint4(h[1] | (h[2] << 16), h[3] | (h[4] << 16), h[5] | (h[6] << 16),
                      h[7] | (h[8] << 16));
+  }
+}
+
+// Block bl (0..15) of a stage in shared memory, this lane's row.
+template <int FMT>
+__device__ __forceinline__ void load_w_smem(const uint8_t* st, int bl, int l, WB<FMT>& w) {
+  using S = Stage<FMT>;
+  const int t = bl * 32 + l;
+  if constexpr (eight_bit(FMT)) {
+    const uint8_t* src = st + bl * 1024 + l * 16;
+    w.a = *reinterpret_cast<const uint4*>(src);
+    w.b = *reinterpret_cast<const uint4*>(src + 512);
+    if constexpr (FMT == F_Q8_0) w.d = reinterpret_cast<const uint16_t*>(st + S::OFF_D)[t];
+  } else {
+    w.a = *reinterpret_cast<const uint4*>(st + t * 16);
+    if constexpr (FMT == F_Q4_0) w.d = reinterpret_cast<const uint16_t*>(st + S::OFF_D)[t];
+    if constexpr (FMT == F_Q4_K)
+      w.h = reinterpret_cast<const uint4*>(st + S::OFF_H)[(bl >> 3) * 32 + l];
+    if constexpr (FMT == F_Q6_K) {
+      w.qh = reinterpret_cast<const uint2*>(st + S::OFF_QH)[t];
+      w.sd = (uint32_t)reinterpret_cast<const uint16_t*>(st + S::OFF_SC)[t] |
+             ((uint32_t)reinterpret_cast<const uint16_t*>(st + S::OFF_D6)[(bl >> 3) * 32 + l]
+              << 16);
+    }
   }
 }
 
@@ -263,7 +324,8 @@ __device__ __forceinline__ float dot_block(const WB<FMT>& w, const AB& a, int b)
 }
 
 // ---------------------------------------------------------------------------
-// Activation prologues (per warp, over the warp's own blocks [wb0, wb1)).
+// Activation conversion (per warp, over the warp's share [wb0, wb1) of the
+// CTA's blocks).
 // ---------------------------------------------------------------------------
 template <int FMT>
 __device__ void prep_blocks(const float* xr, bool live, int wb0, int wb1, uint8_t* act, int cb0) {
@@ -353,24 +415,279 @@ __device__ void prep_int8(const GemvParams& p, int m, bool live, float inv, bool
   }
 }
 
+template <int MT>
+struct CtaShared {
+  float red[WARPS][MT][32];
+  float srow[MT];  // INT8: per-row activation scale sa
+  float sinv[MT];  // INT8: 127 / max (0 for an all-zero row)
+  int slast;
+};
+
+// Converts the CTA's activation blocks [cb0, cb1) of MT rows into `act`
+// (consumer threads only; ends with a consumer barrier). INT8 also zeroes
+// the chunk sums `csum` ([MT][ncc][32]).
+template <int FMT, int MT>
+__device__ void cta_prologue(const GemvParams& p, int m0, int cb0, int cb1, uint8_t* act,
+                             int* csum, int ncc, CtaShared<MT>& sh) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per = (cb1 - cb0 + WARPS - 1) / WARPS;
+  const int wb0 = min(cb1, cb0 + warp * per), wb1 = min(cb1, wb0 + per);
+  const int act_stride = p.kr * act_block_bytes(FMT);
+  if constexpr (FMT == F_INT8) {
+    for (int i = threadIdx.x; i < MT * ncc * 32; i += THREADS) csum[i] = 0;
+    for (int mm = 0; mm < MT; mm++) {
+      const int m = m0 + mm;
+      if (m >= p.m) continue;  // uniform across the CTA
+      if (p.xq) {
+        if (threadIdx.x == 0) sh.srow[mm] = p.sx[m];
+        continue;
+      }
+      // quantize.zig:12-47: the row max spans all of K
+      const float* xr = p.x + (long long)m * p.ldx;
+      float amax = 0.0f;
+      for (int i = threadIdx.x; i < p.k; i += THREADS) amax = fmaxf(amax, fabsf(xr[i]));
+      amax = warp_max(amax);
+      if (lane == 0) sh.red[warp][mm][0] = amax;
+      consumer_sync();
+      if (threadIdx.x == 0) {
+        float a = sh.red[0][mm][0];
+        for (int i = 1; i < WARPS; i++) a = fmaxf(a, sh.red[i][mm][0]);
+        sh.srow[mm] = (a == 0.0f) ? 1.0f : __fdiv_rn(a, 127.0f);
+        sh.sinv[mm] = (a == 0.0f) ? 0.0f : __fdiv_rn(127.0f, a);
+      }
+      consumer_sync();
+    }
+    consumer_sync();
+    for (int mm = 0; mm < MT; mm++) {
+      const int m = m0 + mm;
+      const bool live = m < p.m;
+      const float inv = (live && !p.xq) ? sh.sinv[mm] : 0.0f;
+      prep_int8(p, m, live, inv, live && !p.xq && inv == 0.0f, wb0, wb1, act + mm * act_stride,
+                cb0);
+    }
+  } else {
+    for (int mm = 0; mm < MT; mm++) {
+      const int m = m0 + mm;
+      prep_blocks<FMT>(p.x + (long long)(m < p.m ? m : 0) * p.ldx, m < p.m, wb0, wb1,
+                       act + mm * act_stride, cb0);
+    }
+  }
+  consumer_sync();
+}
+
+// Reduces the CTA's warp partials (block formats: sh.red; INT8: csum) and
+// writes y or, with K split across CTAs, the CTA partials plus the ordered
+// final sum by the last CTA of the row group. Consumer threads only.
+template <int FMT, int MT>
+__device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, int ncc,
+                           const int* csum, CtaShared<MT>& sh) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = g * 32 + lane;
+  const bool split = p.nks > 1;
+  const long long G32 = (long long)p.groups * 32;
+  consumer_sync();
+  if (warp < MT) {
+    const int mm = warp, m = m0 + mm;
+    if (m < p.m) {
+      if constexpr (FMT == F_INT8) {
+        if (!split) {
+          if (row < p.n) {
+            const float sa = sh.srow[mm], sbv = p.sb[row];
+            float out = 0.0f;
+            if (p.chunked) {
+              for (int c = 0; c < ncc; c++)
+                out = __fadd_rn(
+                    out, __fmul_rn(__fmul_rn((float)csum[(mm * ncc + c) * 32 + lane], sa), sbv));
+            } else {
+              int tot = 0;
+              for (int c = 0; c < ncc; c++) tot += csum[(mm * ncc + c) * 32 + lane];
+              out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
+            }
+            p.y[(long long)m * p.ldy + row] = out;
+          }
+        } else {
+          float* dst = p.part + (long long)m * p.nchunks * G32;
+          for (int c = 0; c < ncc; c++)
+            dst[(long long)(cc0 + c) * G32 + row] = __int_as_float(csum[(mm * ncc + c) * 32 + lane]);
+        }
+      } else {
+        float v = 0.0f;
+#pragma unroll
+        for (int i = 0; i < WARPS; i++) v += sh.red[i][mm][lane];
+        if (!split) {
+          if (row < p.n) p.y[(long long)m * p.ldy + row] = v;
+        } else {
+          p.part[((long long)m * p.nks + ks) * G32 + row] = v;
+        }
+      }
+    }
+  }
+  if (!split) return;
+
+  // split K: the last CTA of this row group sums the partials in K order
+  __threadfence();
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    int* c = p.cnt + (long long)blockIdx.z * p.groups + g;
+    const int arrived = atomicAdd(c, 1);
+    sh.slast = (arrived == p.nks - 1);
+    if (sh.slast) *c = 0;  // self-reset for the next launch
+  }
+  consumer_sync();
+  if (!sh.slast) return;
+  __threadfence();
+  if (warp < MT) {
+    const int mm = warp, m = m0 + mm;
+    if (m < p.m && row < p.n) {
+      float out = 0.0f;
+      if constexpr (FMT == F_INT8) {
+        const float* src = p.part + (long long)m * p.nchunks * G32;
+        const float sa = sh.srow[mm], sbv = p.sb[row];
+        if (p.chunked) {
+          for (int c = 0; c < p.nchunks; c++) {
+            const int cv = __float_as_int(__ldcg(src + c * G32 + row));
+            out = __fadd_rn(out, __fmul_rn(__fmul_rn((float)cv, sa), sbv));
+          }
+        } else {
+          int tot = 0;
+          for (int c = 0; c < p.nchunks; c++) tot += __float_as_int(__ldcg(src + c * G32 + row));
+          out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
+        }
+      } else {
+        const float* src = p.part + (long long)m * p.nks * G32;
+        for (int s = 0; s < p.nks; s++) out += __ldcg(src + s * G32 + row);
+      }
+      p.y[(long long)m * p.ldy + row] = out;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
-// The kernel
+// k_qgemv_tma: repacked formats; weights through a TMA-filled smem ring.
+// Threads 0-255 consume, warp 8 (threads 256-287) produces.
+// ---------------------------------------------------------------------------
+template <int FMT, int MT>
+__global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) {
+  using S = Stage<FMT>;
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ __align__(8) uint64_t full[S::NS], empty[S::NS];
+  __shared__ CtaShared<MT> sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x, ks = blockIdx.y, m0 = blockIdx.z * MT;
+  const int cb0 = ks * p.kr, cb1 = min(p.nblk, cb0 + p.kr);
+  const int nst = (cb1 - cb0 + SB - 1) / SB;
+  uint8_t* ring = sm;
+  uint8_t* act = sm + S::NS * S::BYTES;
+  const int act_stride = p.kr * act_block_bytes(FMT);
+  const int cc0 = cb0 >> 4, ncc = ((cb1 + 15) >> 4) - cc0;
+  int* csum = reinterpret_cast<int*>(act + MT * act_stride);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::NS; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], WARPS);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == WARPS) {
+    // ---- producer: stream this CTA's weight bytes, stage by stage ----
+    griddep_launch();
+    if (lane == 0) {
+      const size_t tile0 = (size_t)g * p.nblk;  // first tile of this row group
+      const size_t stile0 = (size_t)g * p.nsb;  // first super-block tile
+      for (int s = 0; s < nst; s++) {
+        const int slot = s % S::NS;
+        if (s >= S::NS && !mbar_wait_bounded(&empty[slot], ((s / S::NS) - 1) & 1)) {
+          report(p, SYN_ERR_TIMEOUT);
+          break;
+        }
+        const int b0 = cb0 + s * SB, nbs = min(SB, cb1 - b0);
+        uint8_t* st = ring + slot * S::BYTES;
+        uint32_t bytes = nbs * S::QT + nbs * S::DT + (nbs / 8) * S::HT + nbs * S::QHT +
+                         nbs * S::SCT + (nbs / 8) * S::D6T;
+        mbar_expect_tx(&full[slot], bytes);
+        bulk_g2s(st, p.q + (tile0 + b0) * S::QT, nbs * S::QT, &full[slot]);
+        if constexpr (S::DT)
+          bulk_g2s(st + S::OFF_D, reinterpret_cast<const uint8_t*>(p.d) + (tile0 + b0) * 64,
+                   nbs * 64, &full[slot]);
+        if constexpr (S::HT)
+          bulk_g2s(st + S::OFF_H, p.hdr + (stile0 + b0 / 8) * 512, (nbs / 8) * 512, &full[slot]);
+        if constexpr (S::QHT) {
+          bulk_g2s(st + S::OFF_QH, p.qh + (tile0 + b0) * 256, nbs * 256, &full[slot]);
+          bulk_g2s(st + S::OFF_SC, reinterpret_cast<const uint8_t*>(p.sc) + (tile0 + b0) * 64,
+                   nbs * 64, &full[slot]);
+          bulk_g2s(st + S::OFF_D6, reinterpret_cast<const uint8_t*>(p.d) + (stile0 + b0 / 8) * 64,
+                   (nbs / 8) * 64, &full[slot]);
+        }
+      }
+    }
+    return;
+  }
+
+  // ---- consumers ----
+  griddep_wait();  // x may be written by the preceding kernel
+  griddep_launch();
+  cta_prologue<FMT, MT>(p, m0, cb0, cb1, act, csum, ncc, sh);
+
+  float facc[MT];
+#pragma unroll
+  for (int mm = 0; mm < MT; mm++) facc[mm] = 0.0f;
+  for (int s = 0; s < nst; s++) {
+    const int slot = s % S::NS;
+    const bool ok = mbar_wait_bounded(&full[slot], (s / S::NS) & 1);
+    if (!ok && lane == 0) report(p, SYN_ERR_TIMEOUT);
+    const int b0 = cb0 + s * SB, nbs = min(SB, cb1 - b0);
+    const uint8_t* st = ring + slot * S::BYTES;
+    int ich[MT];
+#pragma unroll
+    for (int mm = 0; mm < MT; mm++) ich[mm] = 0;
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      const int bl = warp * 2 + u;
+      if (!ok || bl >= nbs) break;
+      WB<FMT> w;
+      load_w_smem<FMT>(st, bl, lane, w);
+#pragma unroll
+      for (int mm = 0; mm < MT; mm++) {
+        AB a;
+        load_act<FMT>(act + mm * act_stride + (b0 + bl - cb0) * act_block_bytes(FMT), a);
+        if constexpr (FMT == F_INT8)
+          ich[mm] += dot_int8(w, a);
+        else
+          facc[mm] += dot_block<FMT>(w, a, b0 + bl);
+      }
+    }
+    if constexpr (FMT == F_INT8) {
+      // one stage = one 512-element chunk (stages start on chunk boundaries)
+#pragma unroll
+      for (int mm = 0; mm < MT; mm++)
+        if (warp * 2 < nbs) atomicAdd(&csum[(mm * ncc + (b0 >> 4) - cc0) * 32 + lane], ich[mm]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  if constexpr (FMT != F_INT8) {
+#pragma unroll
+    for (int mm = 0; mm < MT; mm++) sh.red[warp][mm][lane] = facc[mm];
+  }
+  cta_finish<FMT, MT>(p, g, ks, m0, cc0, ncc, csum, sh);
+}
+
+// ---------------------------------------------------------------------------
+// k_qgemv: direct global loads (the raw 18-byte Q4_0 layout).
 // ---------------------------------------------------------------------------
 template <int FMT, int MT>
 __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
   extern __shared__ __align__(16) uint8_t sm[];
-  __shared__ float red[WARPS][MT][32];
-  __shared__ float srow[MT];  // INT8: per-row activation scale sa
-  __shared__ float sinv[MT];  // INT8: 127 / max (0 for an all-zero row)
-  __shared__ int slast;
+  __shared__ CtaShared<MT> sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = blockIdx.x, ks = blockIdx.y, m0 = blockIdx.z * MT;
   const int cb0 = ks * p.kr, cb1 = min(p.nblk, cb0 + p.kr);
   const int per = (cb1 - cb0 + WARPS - 1) / WARPS;
   const int wb0 = min(cb1, cb0 + warp * per), wb1 = min(cb1, wb0 + per);
-  const int row = g * 32 + lane;
-  const int act_stride = p.kr * act_block_bytes(FMT);  // per activation row
-  // INT8 chunk sums live after the activations: [MT][chunks of this CTA][32]
+  const int act_stride = p.kr * act_block_bytes(FMT);
   const int cc0 = cb0 >> 4, ncc = ((cb1 + 15) >> 4) - cc0;
   int* csum = reinterpret_cast<int*>(sm + MT * act_stride);
 
@@ -382,50 +699,8 @@ __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
 
   griddep_wait();  // x may be written by the preceding kernel
   griddep_launch();
+  cta_prologue<FMT, MT>(p, m0, cb0, cb1, sm, csum, ncc, sh);
 
-  // ---- activation prologue ----
-  if constexpr (FMT == F_INT8) {
-    for (int i = threadIdx.x; i < MT * ncc * 32; i += THREADS) csum[i] = 0;
-    for (int mm = 0; mm < MT; mm++) {
-      const int m = m0 + mm;
-      if (m >= p.m) continue;  // uniform across the CTA
-      if (p.xq) {
-        if (threadIdx.x == 0) srow[mm] = p.sx[m];
-        continue;
-      }
-      // quantize.zig:12-47: the row max spans all of K
-      const float* xr = p.x + (long long)m * p.ldx;
-      float amax = 0.0f;
-      for (int i = threadIdx.x; i < p.k; i += THREADS) amax = fmaxf(amax, fabsf(xr[i]));
-      amax = warp_max(amax);
-      if (lane == 0) red[warp][mm][0] = amax;
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        float a = red[0][mm][0];
-        for (int i = 1; i < WARPS; i++) a = fmaxf(a, red[i][mm][0]);
-        srow[mm] = (a == 0.0f) ? 1.0f : __fdiv_rn(a, 127.0f);
-        sinv[mm] = (a == 0.0f) ? 0.0f : __fdiv_rn(127.0f, a);
-      }
-      __syncthreads();
-    }
-    __syncthreads();
-    for (int mm = 0; mm < MT; mm++) {
-      const int m = m0 + mm;
-      const bool live = m < p.m;
-      const float inv = (live && !p.xq) ? sinv[mm] : 0.0f;
-      prep_int8(p, m, live, inv, live && !p.xq && inv == 0.0f, wb0, wb1, sm + mm * act_stride,
-                cb0);
-    }
-  } else {
-    for (int mm = 0; mm < MT; mm++) {
-      const int m = m0 + mm;
-      prep_blocks<FMT>(p.x + (long long)(m < p.m ? m : 0) * p.ldx, m < p.m, wb0, wb1,
-                       sm + mm * act_stride, cb0);
-    }
-  }
-  __syncthreads();  // INT8 chunk sums zeroed, every warp's activations ready
-
-  // ---- main loop: U tiles per iteration ----
   float facc[MT];
   int ich[MT];
 #pragma unroll
@@ -434,7 +709,6 @@ __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
     ich[mm] = 0;
   }
   int cur_chunk = wb0 >> 4;
-
   for (int b0 = wb0; b0 < wb1; b0 += U) {
     if (b0 != wb0) {
 #pragma unroll
@@ -474,87 +748,9 @@ __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
     }
   } else {
 #pragma unroll
-    for (int mm = 0; mm < MT; mm++) red[warp][mm][lane] = facc[mm];
+    for (int mm = 0; mm < MT; mm++) sh.red[warp][mm][lane] = facc[mm];
   }
-  __syncthreads();
-
-  // ---- CTA result per (activation row, weight row) ----
-  const bool split = p.nks > 1;
-  const long long G32 = (long long)p.groups * 32;
-  if (warp < MT) {
-    const int mm = warp, m = m0 + mm;
-    if (m < p.m) {
-      if constexpr (FMT == F_INT8) {
-        if (!split) {
-          if (row < p.n) {
-            const float sa = srow[mm], sbv = p.sb[row];
-            float out = 0.0f;
-            if (p.chunked) {
-              for (int c = 0; c < ncc; c++)
-                out = __fadd_rn(
-                    out, __fmul_rn(__fmul_rn((float)csum[(mm * ncc + c) * 32 + lane], sa), sbv));
-            } else {
-              int tot = 0;
-              for (int c = 0; c < ncc; c++) tot += csum[(mm * ncc + c) * 32 + lane];
-              out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
-            }
-            p.y[(long long)m * p.ldy + row] = out;
-          }
-        } else {
-          float* dst = p.part + (long long)m * p.nchunks * G32;
-          for (int c = 0; c < ncc; c++)
-            dst[(long long)(cc0 + c) * G32 + row] = __int_as_float(csum[(mm * ncc + c) * 32 + lane]);
-        }
-      } else {
-        float v = 0.0f;
-#pragma unroll
-        for (int i = 0; i < WARPS; i++) v += red[i][mm][lane];
-        if (!split) {
-          if (row < p.n) p.y[(long long)m * p.ldy + row] = v;
-        } else {
-          p.part[((long long)m * p.nks + ks) * G32 + row] = v;
-        }
-      }
-    }
-  }
-  if (!split) return;
-
-  // ---- split K: the last CTA of this row group sums the partials in order ----
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int* c = p.cnt + (long long)blockIdx.z * p.groups + g;
-    const int arrived = atomicAdd(c, 1);
-    slast = (arrived == p.nks - 1);
-    if (slast) *c = 0;  // self-reset for the next launch
-  }
-  __syncthreads();
-  if (!slast) return;
-  __threadfence();
-  if (warp < MT) {
-    const int mm = warp, m = m0 + mm;
-    if (m < p.m && row < p.n) {
-      float out = 0.0f;
-      if constexpr (FMT == F_INT8) {
-        const float* src = p.part + (long long)m * p.nchunks * G32;
-        const float sa = srow[mm], sbv = p.sb[row];
-        if (p.chunked) {
-          for (int c = 0; c < p.nchunks; c++) {
-            const int cv = __float_as_int(__ldcg(src + c * G32 + row));
-            out = __fadd_rn(out, __fmul_rn(__fmul_rn((float)cv, sa), sbv));
-          }
-        } else {
-          int tot = 0;
-          for (int c = 0; c < p.nchunks; c++) tot += __float_as_int(__ldcg(src + c * G32 + row));
-          out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
-        }
-      } else {
-        const float* src = p.part + (long long)m * p.nks * G32;
-        for (int s = 0; s < p.nks; s++) out += __ldcg(src + s * G32 + row);
-      }
-      p.y[(long long)m * p.ldy + row] = out;
-    }
-  }
+  cta_finish<FMT, MT>(p, g, ks, m0, cc0, ncc, csum, sh);
 }
 
 // ---------------------------------------------------------------------------
@@ -562,10 +758,24 @@ __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
 // ---------------------------------------------------------------------------
 struct Plan {
   int groups, nblk, kr, nks, nchunks, mt;
-  size_t smem;
+  size_t act_smem;  // activations + INT8 chunk sums
 };
 
 int mt_for(size_t m) { return m == 1 ? 1 : (m == 2 ? 2 : 4); }
+
+// Launch-planning defaults, overridable through the environment for tuning
+// experiments (read once per process).
+int tune(const char* name, int dflt) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::string, int>> cache;
+  std::lock_guard<std::mutex> g(mu);
+  for (auto& kv : cache)
+    if (kv.first == name) return kv.second;
+  const char* v = getenv(name);
+  const int r = v ? atoi(v) : dflt;
+  cache.emplace_back(name, r);
+  return r;
+}
 
 Plan make_plan(int fmt, size_t m, size_t n, size_t kp) {
   Plan pl{};
@@ -575,22 +785,25 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp) {
   pl.mt = mt_for(m);
   const int sms = num_sms();
   // Aim at ~4 CTAs per SM: split K until the grid fills the GPU, keeping at
-  // least one block per warp (INT8: whole 512-element chunks per CTA).
-  const int target = sms * 4;
+  // least one 16-block stage (one 512-element chunk) per CTA.
+  const int target = sms * tune("SYN_GEMV_CTAS_PER_SM", 4);
   const int mslices = (int)((m + pl.mt - 1) / pl.mt);
   int nks = target / std::max(1, pl.groups * mslices);
-  const int maxks = fmt == F_INT8 ? std::max(1, pl.nblk / 16) : std::max(1, pl.nblk / WARPS);
-  nks = std::max(1, std::min(nks, maxks));
+  nks = std::max(1, std::min(nks, std::max(1, pl.nblk / SB)));
+  // K splits only pay off when each CTA still streams a sizeable range
+  // (measured on B200: the cross-CTA reduction costs more than it gains when
+  // a split CTA would stream fewer than 64 blocks)
+  const int min_split_blocks = tune("SYN_GEMV_MIN_SPLIT_BLOCKS", 64);
+  while (nks > 1 && pl.nblk / nks < min_split_blocks) nks--;
   int kr = (pl.nblk + nks - 1) / nks;
-  if (fmt == F_INT8) kr = (kr + 15) / 16 * 16;
+  kr = (kr + SB - 1) / SB * SB;
   // shared memory bound (activations of MT rows)
   const int abb = fmt == F_INT8 ? 32 : 80;
-  while ((size_t)pl.mt * kr * abb > 96 * 1024 && kr > 16) kr = (kr + 1) / 2;
-  if (fmt == F_INT8) kr = (kr + 15) / 16 * 16;
+  while ((size_t)pl.mt * kr * abb > 96 * 1024 && kr > SB) kr = ((kr + 1) / 2 + SB - 1) / SB * SB;
   pl.kr = kr;
   pl.nks = (pl.nblk + kr - 1) / kr;
-  const int ncc = (kr + 15) / 16 + 1;
-  pl.smem = (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
+  const int ncc = kr / 16 + 1;
+  pl.act_smem = (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
   return pl;
 }
 
@@ -604,28 +817,39 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = tune("SYN_GEMV_PDL", 1) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-template <int FMT, int MT>
-syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
+// Allows up to 200 KB of dynamic shared memory, once per kernel and device.
+// (Keyed by the kernel's address: all GEMV instantiations share one type.)
+template <typename K>
+void allow_smem(K kern) {
   static std::mutex mu;
-  static bool attr_set[64] = {false};
+  static std::set<std::pair<const void*, int>> done;
   int dev = 0;
   cudaGetDevice(&dev);
-  {
-    std::lock_guard<std::mutex> guard(mu);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      cudaFuncSetAttribute(k_qgemv<FMT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           200 * 1024);
-      attr_set[dev] = true;
-    }
-  }
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kern), dev);
+  std::lock_guard<std::mutex> guard(mu);
+  if (done.count(key)) return;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  done.insert(key);
+}
+
+template <int FMT, int MT>
+syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   dim3 grid((unsigned)pl.groups, (unsigned)pl.nks, (unsigned)((p.m + MT - 1) / MT));
-  cudaError_t e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.smem, st, p);
+  cudaError_t e;
+  if constexpr (FMT == F_Q4_0RAW) {
+    allow_smem(k_qgemv<FMT, MT>);
+    e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.act_smem, st, p);
+  } else {
+    allow_smem(k_qgemv_tma<FMT, MT>);
+    const size_t smem = (size_t)Stage<FMT>::NS * Stage<FMT>::BYTES + pl.act_smem;
+    e = launch_pdl(k_qgemv_tma<FMT, MT>, grid, dim3(THREADS + 32), smem, st, p);
+  }
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_qgemv");
     return SYN_ERR_CUDA;

@@ -14,7 +14,8 @@
 // data for that block are stored back to back, so one warp (lane = row)
 // reads a tile of 32 rows x one block as one contiguous run:
 //   tile index t = g * nblk + b, row-in-group l:
-//   q    : (t*32 + l) * QB bytes      (QB = 16 for 4-bit, 32 for 8-bit)
+//   q    : (t*32 + l) * 16 bytes      (4-bit formats)
+//          t*1024 + h*512 + l*16      (8-bit formats: half h of the block)
 //   d    : u16 [t*32 + l]             (Q4_0, Q8_0 block scale bits)
 //   hdr  : ((g*nsb + j)*32 + l) * 16  (Q4_K super-block j header: d, dmin,
 //                                      12 scale bytes, verbatim)
@@ -31,6 +32,13 @@ __device__ __forceinline__ size_t tile_row(size_t n, size_t b, size_t nblk) {
   return ((n >> 5) * nblk + b) * 32 + (n & 31);
 }
 
+// 8-bit formats: a tile of 32 rows x 32 bytes is stored as two half-planes
+// (elements 0-15 of the 32 rows, then elements 16-31), so lane l's 16-byte
+// reads are consecutive across lanes in both halves.
+__device__ __forceinline__ size_t q8_off(size_t t, size_t e) {
+  return (t >> 5) * 1024 + (e >> 4) * 512 + (t & 31) * 16 + (e & 15);
+}
+
 __global__ void k_repack_int8_kn(const int8_t* __restrict__ src, size_t ldsrc, size_t n,
                                  size_t k, size_t nblk, int8_t* __restrict__ dst) {
   // 32x32 tile transpose: src [k][n] -> dst tiles (zero padded)
@@ -45,7 +53,7 @@ __global__ void k_repack_int8_kn(const int8_t* __restrict__ src, size_t ldsrc, s
   // row n0 + r, block blockIdx.y, element tx
   for (int r = ty; r < 32; r += 8) {
     const size_t nn = n0 + r;
-    dst[tile_row(nn, blockIdx.y, nblk) * 32 + tx] = tile[tx][r];
+    dst[q8_off(tile_row(nn, blockIdx.y, nblk), tx)] = tile[tx][r];
   }
 }
 
@@ -68,7 +76,7 @@ __global__ void k_repack_q8_0(const uint8_t* __restrict__ src, size_t n, size_t 
   const uint8_t* s = src + idx * 34;
   const size_t t = tile_row(row, b, nblk);
   d[t] = (uint16_t)(s[0] | (s[1] << 8));
-  for (int i = 0; i < 32; i++) q[t * 32 + i] = s[2 + i];
+  for (int i = 0; i < 32; i++) q[q8_off(t, i)] = s[2 + i];
 }
 
 __global__ void k_repack_q4_k(const uint8_t* __restrict__ src, size_t n, size_t nsb,
@@ -136,7 +144,7 @@ __global__ void k_dequant(syn_cuda_weight_s w, float* __restrict__ out) {
   float v = 0.0f;
   switch (w.fmt) {
     case SYN_QFMT_INT8_KN: {  // quantize.zig:90-106
-      v = __fmul_rn((float)((const int8_t*)w.q)[t * 32 + e], w.sb[n]);
+      v = __fmul_rn((float)((const int8_t*)w.q)[q8_off(t, e)], w.sb[n]);
       break;
     }
     case SYN_QFMT_Q4_0: {  // gguf.rs:315-324
@@ -146,7 +154,7 @@ __global__ void k_dequant(syn_cuda_weight_s w, float* __restrict__ out) {
       break;
     }
     case SYN_QFMT_Q8_0: {  // gguf.rs:276-285
-      v = __fmul_rn(f16_loader(w.d[t]), (float)(int8_t)w.q[t * 32 + e]);
+      v = __fmul_rn(f16_loader(w.d[t]), (float)(int8_t)w.q[q8_off(t, e)]);
       break;
     }
     case SYN_QFMT_Q4_K: {  // gguf.rs:395-427
