@@ -157,17 +157,38 @@ def run_synapse(args, rank, world, local_rank):
                 c["w"].matmul(c["x"], out=c["y"])
         return run
 
-    def gemvs_e2e(cs):
+    # e2e buffers: per format, the step's activations live in one pinned host
+    # buffer and its outputs come back into one, as a caller batching a
+    # decode step would hold them; one H2D and one D2H copy per format.
+    e2e = {}
+    for nm in fmt_names:
+        cs = by_fmt[nm]
+        kx = sum(c["k"] for c in cs)
+        ny = sum(c["n"] for c in cs)
+        hx = torch.cat([c["x_pin"].reshape(-1) for c in cs]).pin_memory()
+        hy = torch.empty(ny, dtype=torch.float32).pin_memory()
+        dx = torch.empty(kx, dtype=torch.float32, device=dev)
+        dy = torch.empty(ny, dtype=torch.float32, device=dev)
+        views, ox, oy = [], 0, 0
+        for c in cs:
+            views.append((c, dx[ox:ox + c["k"]].view(1, -1), dy[oy:oy + c["n"]].view(1, -1)))
+            ox += c["k"]
+            oy += c["n"]
+        e2e[nm] = (hx, hy, dx, dy, views)
+
+    def gemvs_e2e(nm):
+        hx, hy, dx, dy, views = e2e[nm]
+
         def run():
-            for c in cs:
-                c["x"].copy_(c["x_pin"], non_blocking=True)
-                c["w"].matmul(c["x"], out=c["y"])
-                c["y_pin"].copy_(c["y"], non_blocking=True)
+            dx.copy_(hx, non_blocking=True)
+            for c, xv, yv in views:
+                c["w"].matmul(xv, out=yv)
+            hy.copy_(dy, non_blocking=True)
         return run
 
     # One CUDA graph per format (15 GEMVs each); a step replays the five.
     graphs = {nm: CapturedSequence(gemvs(by_fmt[nm]), dev) for nm in fmt_names}
-    graphs_e2e = {nm: CapturedSequence(gemvs_e2e(by_fmt[nm]), dev) for nm in fmt_names}
+    graphs_e2e = {nm: CapturedSequence(gemvs_e2e(nm), dev) for nm in fmt_names}
 
     def barrier():
         torch.cuda.synchronize(dev)

@@ -256,6 +256,7 @@ syn_status_t syn_cuda_context_destroy(syn_cuda_ctx_t* ctx) {
     cudaStreamDestroy(ctx->upload_stream);
     cudaFree(ctx->part);
     cudaFree(ctx->cnt);
+    cudaFree(ctx->abuf);
     cudaFree(ctx->err);
   }
   delete ctx;
@@ -292,15 +293,20 @@ syn_status_t syn_cuda_qgemm_int8(size_t m, size_t n, size_t k, const int8_t* a, 
   w.k = k;
   w.kp = (k + 31) / 32 * 32;
   const size_t wbytes = align256((n + 31) / 32 * 32 * w.kp);
+  const bool gemm = m >= kGemmMinRows;
+  const size_t abytes = gemm ? align256(gemm_a_bytes(w.fmt, m, w.kp)) : 0;
   CallScratch cs;
-  syn_status_t s = cs.init(w.fmt, m, n, w.kp, wbytes, st);
+  syn_status_t s = cs.init(w.fmt, m, n, w.kp, wbytes + abytes, st);
   if (s != SYN_OK) return cs.release(s, st);
   w.buf = cs.mem;
   w.bytes = wbytes;
   w.q = static_cast<uint8_t*>(cs.mem);
   w.sb = const_cast<float*>(scales_b);  // read only for rows < n
   s = repack_weight(&w, reinterpret_cast<const uint8_t*>(b), ldb, nullptr, st);
-  if (s == SYN_OK)
+  if (s == SYN_OK && gemm)
+    s = launch_qgemm(&w, nullptr, lda, a, scales_a, m, c, ldc, m > 16 ? 1 : 0,
+                     static_cast<uint8_t*>(cs.mem) + wbytes, nullptr, st);
+  else if (s == SYN_OK)
     s = launch_qgemv(&w, nullptr, lda, a, scales_a, m, c, ldc, m > 16 ? 1 : 0, cs.part, cs.cnt,
                      nullptr, st);
   return cs.release(s, st);
@@ -421,9 +427,16 @@ syn_status_t syn_cuda_qmatmul(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w, c
   DeviceGuard g(w->device);
   if (!g.ok) return SYN_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
+  const int chunked = (w->fmt == SYN_QFMT_INT8_KN && m > 16) ? 1 : 0;
+  if (m >= kGemmMinRows) {
+    syn_status_t s = grow(reinterpret_cast<void**>(&ctx->abuf), &ctx->abuf_bytes,
+                          gemm_a_bytes(w->fmt, m, w->kp), st);
+    if (s != SYN_OK) return s;
+    return launch_qgemm(w, x, w->k, nullptr, nullptr, m, y, w->n, chunked, ctx->abuf, ctx->err,
+                        st);
+  }
   syn_status_t s = ensure_scratch(ctx, w, m, st);
   if (s != SYN_OK) return s;
-  const int chunked = (w->fmt == SYN_QFMT_INT8_KN && m > 16) ? 1 : 0;
   return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, chunked, ctx->part, ctx->cnt,
                       ctx->err, st);
 }
@@ -437,6 +450,13 @@ syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t* ctx, const syn_cuda_
   DeviceGuard g(w->device);
   if (!g.ok) return SYN_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
+  if (m >= kGemmMinRows) {
+    syn_status_t s = grow(reinterpret_cast<void**>(&ctx->abuf), &ctx->abuf_bytes,
+                          gemm_a_bytes(w->fmt, m, w->kp), st);
+    if (s != SYN_OK) return s;
+    return launch_qgemm(w, nullptr, w->k, x_i8, scales_x, m, y, w->n, m > 16 ? 1 : 0, ctx->abuf,
+                        ctx->err, st);
+  }
   syn_status_t s = ensure_scratch(ctx, w, m, st);
   if (s != SYN_OK) return s;
   return launch_qgemv(w, nullptr, w->k, x_i8, scales_x, m, y, w->n, m > 16 ? 1 : 0, ctx->part,

@@ -1,0 +1,713 @@
+// gemm.cu -- prefill / batched path: quantized matmul on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in tensor memory).
+//
+//   y[M, N] = x[M, K] * W[N, K]^T, for M >= 8 (tokens), all five formats.
+//
+// Operands.
+//   A (activations) is prepared by k_prep_a into the canonical K-major
+//   no-swizzle layout of the MMA (core matrices of 8 rows x 16 bytes):
+//   global [m-tile][16-byte K column][128 rows][16 B], so one stage of A is
+//   one contiguous run for a 1-D bulk copy.
+//     INT8 weights: A = int8 codes of the reference's per-row quantisation
+//       (quantize.zig:12-47), bit-exact; products are exact int32
+//       (kind::i8). M <= 16: one int32 accumulator over K, then
+//       float(acc) * sa * sb (qmatmul.zig:52-66, 218-223). M > 16: the
+//       reference's per-512-K-chunk epilogue C += float(chunk) * sa * sb in
+//       chunk order (qmatmul.zig:68-98), every op rounded -- so the result
+//       is bit-exact for every M.
+//     Block formats: A = fp16(x); the weights are dequantised in shared
+//       memory with the reference's formulas (gguf.rs:255-487) to fp16 and
+//       multiplied with kind::f16, fp32 accumulation in tensor memory.
+//   B (weights) is the row-interleaved repack (repack.cu): a 32-row group's
+//   tiles for consecutive blocks are contiguous, and a tile [32 rows][16 B]
+//   is four core matrices, so each MMA is M=128 x N=32 x K (one row group)
+//   with SBO = 128 B (8 rows) and LBO = the distance to the next 16 bytes
+//   of K.
+//
+// CTA = 6 warps: warp 0 issues the bulk copies (TMA engine) of A and raw B
+// stages into a smem ring; warp 1 owns tensor memory and one of its threads
+// issues the MMAs; warps 2-5 dequantise B (block formats) and run the
+// epilogue (tensor memory -> registers -> y). Tile: 128 tokens x 128 weight
+// rows. Every wait is bounded and reports SYN_ERR_TIMEOUT instead of hanging.
+#include <mutex>
+#include <set>
+
+#include "internal.cuh"
+
+namespace syn {
+namespace {
+
+enum : int { F_INT8 = SYN_QFMT_INT8_KN, F_Q4_0 = SYN_QFMT_Q4_0, F_Q8_0 = SYN_QFMT_Q8_0,
+             F_Q4_K = SYN_QFMT_Q4_K, F_Q6_K = SYN_QFMT_Q6_K };
+
+constexpr int BM = 128;  // tokens per tile (MMA M)
+constexpr int BN = 128;  // weight rows per tile (4 row groups of 32)
+constexpr int NG = BN / 32;
+constexpr int GEMM_THREADS = 192;
+
+// ---------------------------------------------------------------------------
+// tcgen05 helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// smem matrix descriptor: K-major, no swizzle (core matrices 8 rows x 16 B).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  return d;                // base offset 0, legacy LBO mode, layout SWIZZLE_NONE
+}
+
+// Instruction descriptor: M=128, N=32, K-major A and B.
+template <bool I8>
+__host__ __device__ constexpr uint32_t idesc_128x32() {
+  // c_format (bits 4-5): 1 = F32, 2 = S32; a/b format (7-9, 10-12):
+  // kind::f16 -> 0 = F16; kind::i8 -> 1 = signed; n_dim (17-22) = N >> 3;
+  // m_dim (24-28) = M >> 4.
+  return (I8 ? (2u << 4) : (1u << 4)) | (I8 ? (1u << 7) : 0u) | (I8 ? (1u << 10) : 0u) |
+         ((32u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+template <bool I8>
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  constexpr uint32_t id = idesc_128x32<I8>();
+  if constexpr (I8) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(
+            tmem_d),
+        "l"(a), "l"(b), "r"(id), "r"(accumulate), "r"(0u));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(
+            tmem_d),
+        "l"(a), "l"(b), "r"(id), "r"(accumulate), "r"(0u));
+  }
+}
+
+// Arrives on `bar` once every MMA issued so far by this thread is complete.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns; thread i gets lane (base + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+      "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
+      "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Per-format stage geometry
+// ---------------------------------------------------------------------------
+template <int FMT>
+struct GS {
+  static constexpr bool I8 = FMT == F_INT8;
+  static constexpr int KB = I8 ? 8 : 4;                 // 32-element blocks per stage
+  static constexpr int A_BYTES = BM * KB * 32 * (I8 ? 1 : 2);  // 32 KB
+  // raw weight bytes per row group and block (q tile + per-block aux)
+  static constexpr int QT = (FMT == F_INT8 || FMT == F_Q8_0) ? 1024 : 512;
+  static constexpr int DT = (FMT == F_Q4_0 || FMT == F_Q8_0) ? 64 : 0;
+  static constexpr int QHT = (FMT == F_Q6_K) ? 256 : 0;
+  static constexpr int SCT = (FMT == F_Q6_K) ? 64 : 0;
+  static constexpr int HT = (FMT == F_Q4_K) ? 512 : 0;  // one super-block tile per stage
+  static constexpr int D6T = (FMT == F_Q6_K) ? 64 : 0;  // one super-block tile per stage
+  static constexpr int G_Q = 0;
+  static constexpr int G_D = G_Q + KB * QT;
+  static constexpr int G_QH = G_D + KB * DT;
+  static constexpr int G_SC = G_QH + KB * QHT;
+  static constexpr int G_H = G_SC + KB * SCT;
+  static constexpr int G_D6 = G_H + HT;
+  static constexpr int G_BYTES = (G_D6 + D6T + 127) / 128 * 128;  // per row group
+  static constexpr int RAW_BYTES = NG * G_BYTES;
+  static constexpr int STAGE_BYTES = A_BYTES + RAW_BYTES;
+  static constexpr int NS = I8 ? 3 : 2;                 // ring depth
+  static constexpr int BH_BYTES = I8 ? 0 : BN * KB * 32 * 2;  // dequantised fp16 B (32 KB)
+  static constexpr int NBH = I8 ? 0 : 2;
+  static constexpr int SMEM = NS * STAGE_BYTES + NBH * BH_BYTES;
+  static constexpr uint32_t TMEM_COLS = I8 ? 512 : 128;
+};
+
+struct GemmParams {
+  const uint8_t* q;
+  const uint16_t* d;
+  const float* sb;
+  const uint8_t* hdr;
+  const uint8_t* qh;
+  const uint16_t* sc;
+  int n, k, nblk, nsb, groups;
+  const uint8_t* a;  // prepared activations
+  int kcols;         // 16-byte K columns per A row (A row bytes / 16)
+  const float* sa;   // INT8: per-row activation scale
+  int m;
+  float* y;
+  long long ldy;
+  int chunked;
+  int* err;
+};
+
+__device__ __forceinline__ void greport(const GemmParams& p) {
+  if (p.err) atomicExch(p.err, SYN_ERR_TIMEOUT);
+}
+
+__device__ __forceinline__ bool bwait(const GemmParams& p, uint64_t* bar, uint32_t parity) {
+  if (mbar_wait_bounded(bar, parity)) return true;
+  greport(p);
+  return false;
+}
+
+// Dequantises the raw stage of one row group into fp16 B tiles:
+// out[b][c][32 rows][16 B] (c = 16-byte K column of the block, 8 halves).
+// Thread = one row (lane l of group gi). Reference formulas (gguf.rs).
+template <int FMT>
+__device__ void dequant_stage(const uint8_t* raw, uint8_t* out, int l, int nbs, int b0) {
+  using S = GS<FMT>;
+#pragma unroll 1
+  for (int bl = 0; bl < nbs; bl++) {
+    float v[32];
+    if constexpr (FMT == F_Q4_0) {
+      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+      const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        v[2 * i] = __fmul_rn(dd, (float)((int)(byte & 15) - 8));
+        v[2 * i + 1] = __fmul_rn(dd, (float)((int)(byte >> 4) - 8));
+      }
+    } else if constexpr (FMT == F_Q8_0) {
+      const uint4 q0 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024)[l];
+      const uint4 q1 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024 + 512)[l];
+      const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
+      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+      for (int i = 0; i < 32; i++)
+        v[i] = __fmul_rn(dd, (float)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFF));
+    } else if constexpr (FMT == F_Q4_K) {
+      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+      const uint4 h = reinterpret_cast<const uint4*>(raw + S::G_H)[l];
+      const int s = (b0 + bl) & 7;
+      const float dd = f16_loader((uint16_t)(h.x & 0xFFFF));
+      const float dmin = f16_loader((uint16_t)(h.x >> 16));
+      uint32_t scv, mnv;
+      if (s < 4) {
+        const int sh = 8 * s;
+        scv = (h.y >> sh) & 0x3F;
+        mnv = (((h.z >> sh) & 0xFF) >> 4) | (((h.w >> sh) & 0x0F) << 4);
+      } else {
+        const int sh = 8 * (s - 4);
+        const uint32_t ys = (h.y >> sh) & 0xFF;
+        scv = ((h.z >> sh) & 0x0F) | ((ys >> 6) << 4);
+        mnv = (((h.w >> sh) & 0xFF) >> 4) | (((ys >> 4) & 0x0C) << 4);
+      }
+      const float scl = __fmul_rn(dd, (float)scv), mv = __fmul_rn(dmin, (float)mnv);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        v[2 * i] = __fsub_rn(__fmul_rn((float)(byte & 15), scl), mv);
+        v[2 * i + 1] = __fsub_rn(__fmul_rn((float)(byte >> 4), scl), mv);
+      }
+    } else {  // F_Q6_K
+      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+      const uint2 hq = reinterpret_cast<const uint2*>(raw + S::G_QH + bl * 256)[l];
+      const uint32_t scp = reinterpret_cast<const uint16_t*>(raw + S::G_SC + bl * 64)[l];
+      const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D6)[l]);
+      const float s0 = __fmul_rn((float)(int8_t)(scp & 0xFF), dd);
+      const float s1 = __fmul_rn((float)(int8_t)(scp >> 8), dd);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int e = 0; e < 32; e++) {
+        const uint32_t byte = (w[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+        const uint32_t lo = (e & 1) ? (byte >> 4) : (byte & 15);
+        // invert the high-bit re-arrangement of repack.cu (k_repack_q6_k)
+        const int half = e >> 4, r = e & 15, f = 2 * (r >> 3) + (r & 1), tt = (r & 7) >> 1;
+        const uint32_t H = half ? hq.y : hq.x;
+        const uint32_t hi = (H >> (8 * tt + 2 * f)) & 3u;
+        v[e] = __fmul_rn((float)((int)(lo | (hi << 4)) - 32), half ? s1 : s0);
+      }
+    }
+    // 4 K columns of 8 halves each
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      uint4 o;
+      o.x = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 0])) |
+            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 1])) << 16);
+      o.y = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 2])) |
+            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 3])) << 16);
+      o.z = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 4])) |
+            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 5])) << 16);
+      o.w = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 6])) |
+            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 7])) << 16);
+      reinterpret_cast<uint4*>(out + bl * 2048 + c * 512)[l] = o;
+    }
+  }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
+  using S = GS<FMT>;
+  constexpr bool I8 = S::I8;
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ __align__(8) uint64_t full[S::NS], empty[S::NS];
+  __shared__ __align__(8) uint64_t bfull[2], bempty[2];    // fp16 B buffers
+  __shared__ __align__(8) uint64_t accfull[2], accempty[2];  // INT8 chunk accumulators
+  __shared__ uint32_t tmem_base_sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x, nt = blockIdx.y;
+  const int nst = (p.nblk + S::KB - 1) / S::KB;
+  // INT8 chunking: a 512-element chunk is 2 stages (16 blocks)
+  const bool chunked = I8 && p.chunked;
+  const int nchunks = (p.nblk + 15) / 16;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::NS; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], I8 ? 1 : 1 + 4);  // MMA commit (+ 4 dequant warps)
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&bfull[i], 4);
+      mbar_init(&bempty[i], 1);
+      mbar_init(&accfull[i], 1);
+      mbar_init(&accempty[i], 4);
+    }
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base_sh)),
+                 "r"(S::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_sh;
+  // A, sa (and y's previous readers) belong to the kernels launched before
+  griddep_wait();
+
+  if (warp == 0) {
+    // ---------------- producer: bulk copies of A and raw B stages ----------------
+    if (lane == 0) {
+      for (int s = 0; s < nst; s++) {
+        const int slot = s % S::NS;
+        if (s >= S::NS && !bwait(p, &empty[slot], ((s / S::NS) - 1) & 1)) break;
+        const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
+        uint8_t* st = sm + slot * S::STAGE_BYTES;
+        uint8_t* raw = st + S::A_BYTES;
+        // A: columns [b0 * cpb, (b0 + nbs) * cpb) of m-tile mt (cpb = 16-byte
+        // columns per block: 2 for int8, 4 for fp16)
+        constexpr int cpb = I8 ? 2 : 4;
+        const uint32_t a_bytes = nbs * cpb * 2048;
+        uint32_t bytes = a_bytes;
+        int ngr = 0;
+        for (int gi = 0; gi < NG; gi++)
+          if ((nt * NG + gi) < p.groups) ngr++;
+        bytes += ngr * (nbs * (S::QT + S::DT + S::QHT + S::SCT) + S::HT + S::D6T);
+        mbar_expect_tx(&full[slot], bytes);
+        bulk_g2s(st, p.a + ((size_t)mt * p.kcols + (size_t)b0 * cpb) * 2048, a_bytes, &full[slot]);
+        for (int gi = 0; gi < ngr; gi++) {
+          const size_t g = (size_t)nt * NG + gi;
+          uint8_t* gr = raw + gi * S::G_BYTES;
+          const size_t t0 = g * p.nblk + b0;
+          bulk_g2s(gr + S::G_Q, p.q + t0 * S::QT, nbs * S::QT, &full[slot]);
+          if constexpr (S::DT)
+            bulk_g2s(gr + S::G_D, reinterpret_cast<const uint8_t*>(p.d) + t0 * 64, nbs * 64,
+                     &full[slot]);
+          if constexpr (S::QHT) {
+            bulk_g2s(gr + S::G_QH, p.qh + t0 * 256, nbs * 256, &full[slot]);
+            bulk_g2s(gr + S::G_SC, reinterpret_cast<const uint8_t*>(p.sc) + t0 * 64, nbs * 64,
+                     &full[slot]);
+          }
+          if constexpr (S::HT)
+            bulk_g2s(gr + S::G_H, p.hdr + (g * p.nsb + b0 / 8) * 512, 512, &full[slot]);
+          if constexpr (S::D6T)
+            bulk_g2s(gr + S::G_D6, reinterpret_cast<const uint8_t*>(p.d) + (g * p.nsb + b0 / 8) * 64,
+                     64, &full[slot]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const int ngr_valid = min(NG, p.groups - nt * NG);
+      bool ok = true;
+      int chunk = 0;  // INT8 chunked: accumulator buffer = chunk & 1
+      for (int s = 0; s < nst && ok; s++) {
+        const int slot = s % S::NS;
+        if (!bwait(p, &full[slot], (s / S::NS) & 1)) { ok = false; break; }
+        const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
+        const uint8_t* st = sm + slot * S::STAGE_BYTES;
+        const uint32_t a_addr = smem_u32(st);
+        uint32_t b_addr;
+        if constexpr (I8) {
+          b_addr = smem_u32(st + S::A_BYTES);
+          if (chunked && (b0 & 15) == 0 && chunk >= 2) {
+            // reuse of accumulator buffer (chunk & 1): wait until drained
+            if (!bwait(p, &accempty[chunk & 1], ((chunk >> 1) - 1) & 1)) { ok = false; break; }
+          }
+        } else {
+          if (!bwait(p, &bfull[s & 1], (s >> 1) & 1)) { ok = false; break; }
+          b_addr = smem_u32(sm + S::NS * S::STAGE_BYTES + (s & 1) * S::BH_BYTES);
+        }
+        tc_fence_after();
+        const uint32_t dbase = tbase + (chunked ? (uint32_t)(chunk & 1) * BN : 0u);
+        for (int bl = 0; bl < nbs; bl++) {
+          const int b = b0 + bl;
+          if constexpr (I8) {
+            // one block = K of 32 int8 = one MMA per row group
+            const bool first = chunked ? ((b & 15) == 0) : (b == 0);
+            const uint64_t ad = sdesc(a_addr + bl * 2 * 2048, 2048, 128);
+            for (int gi = 0; gi < ngr_valid; gi++) {
+              const uint64_t bd = sdesc(b_addr + gi * S::G_BYTES + bl * 1024, 512, 128);
+              mma<true>(dbase + gi * 32, ad, bd, first ? 0u : 1u);
+            }
+          } else {
+            // one block = K of 32 halves = two MMAs (K = 16) per row group
+            for (int kh = 0; kh < 2; kh++) {
+              const uint64_t ad = sdesc(a_addr + (bl * 4 + kh * 2) * 2048, 2048, 128);
+              for (int gi = 0; gi < ngr_valid; gi++) {
+                const uint64_t bd =
+                    sdesc(b_addr + gi * (S::KB * 2048) + bl * 2048 + kh * 1024, 512, 128);
+                mma<false>(dbase + gi * 32, ad, bd, (b == 0 && kh == 0) ? 0u : 1u);
+              }
+            }
+          }
+        }
+        mma_commit(&empty[slot]);
+        if constexpr (!I8) mma_commit(&bempty[s & 1]);
+        if constexpr (I8) {
+          const bool chunk_end = chunked && (((b0 + nbs) & 15) == 0 || b0 + nbs == p.nblk);
+          if (chunk_end) {
+            mma_commit(&accfull[chunk & 1]);
+            chunk++;
+          }
+        }
+      }
+      if (!chunked) mma_commit(&accfull[0]);
+      if (!ok) {
+        // release the epilogue of any chunk it still waits for
+        for (int c = chunk; c < (chunked ? nchunks : 1); c++) mbar_arrive(&accfull[c & 1]);
+      }
+    }
+  } else {
+    // ---------------- warps 2-5: dequantise B / epilogue ----------------
+    const int ew = warp - 2;           // 0..3
+    const int quarter = warp & 3;      // tensor memory lane quarter of this warp
+    const int tok = mt * BM + quarter * 32 + lane;  // this thread's token row
+    const uint32_t tq = tbase + ((uint32_t)(quarter * 32) << 16);
+    if constexpr (!I8) {
+      // dequantise each stage's raw B into fp16 tiles
+      const int gi = ew, l = lane;
+      for (int s = 0; s < nst; s++) {
+        const int slot = s % S::NS;
+        const bool ok1 = bwait(p, &full[slot], (s / S::NS) & 1);
+        const bool ok2 = s < 2 || bwait(p, &bempty[s & 1], ((s >> 1) - 1) & 1);
+        const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
+        const uint8_t* raw = sm + slot * S::STAGE_BYTES + S::A_BYTES + gi * S::G_BYTES;
+        uint8_t* out = sm + S::NS * S::STAGE_BYTES + (s & 1) * S::BH_BYTES + gi * (S::KB * 2048);
+        if (ok1 && ok2 && nt * NG + gi < p.groups) dequant_stage<FMT>(raw, out, l, nbs, b0);
+        fence_async_smem();  // generic-proxy smem writes -> visible to the MMA
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bfull[s & 1]);
+          mbar_arrive(&empty[slot]);
+        }
+      }
+      // epilogue: fp32 accumulators -> y
+      bwait(p, &accfull[0], 0);
+      tc_fence_after();
+      for (int gi2 = 0; gi2 < NG; gi2++) {
+        uint32_t r[32];
+        tmem_ld32(tq + gi2 * 32, r);
+        const int n0 = (nt * NG + gi2) * 32;
+        if (tok < p.m) {
+          float* yr = p.y + (long long)tok * p.ldy;
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (n0 + j < p.n) yr[n0 + j] = __uint_as_float(r[j]);
+        }
+      }
+    } else {
+      const float sa = tok < p.m ? p.sa[tok] : 0.0f;
+      if (!chunked) {
+        // one int32 accumulator over all of K: float(acc) * sa * sb
+        bwait(p, &accfull[0], 0);
+        tc_fence_after();
+        for (int gi2 = 0; gi2 < NG; gi2++) {
+          uint32_t r[32];
+          tmem_ld32(tq + gi2 * 32, r);
+          const int n0 = (nt * NG + gi2) * 32;
+          if (tok < p.m) {
+            float* yr = p.y + (long long)tok * p.ldy;
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (n0 + j < p.n)
+                yr[n0 + j] = __fmul_rn(__fmul_rn((float)(int)r[j], sa), p.sb[n0 + j]);
+          }
+        }
+      } else {
+        // C = 0; per chunk C += float(acc) * sa * sb (running C in tensor
+        // memory columns 256..383)
+        for (int c = 0; c < nchunks; c++) {
+          bwait(p, &accfull[c & 1], (c >> 1) & 1);
+          tc_fence_after();
+          for (int gi2 = 0; gi2 < NG; gi2++) {
+            const int n0 = (nt * NG + gi2) * 32;
+            uint32_t r[32], cr[32];
+            tmem_ld32(tq + (c & 1) * BN + gi2 * 32, r);
+            if (c > 0) tmem_ld32(tq + 2 * BN + gi2 * 32, cr);
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              const float sbv = (n0 + j < p.n) ? p.sb[n0 + j] : 0.0f;
+              const float prev = c > 0 ? __uint_as_float(cr[j]) : 0.0f;
+              cr[j] = __float_as_uint(
+                  __fadd_rn(prev, __fmul_rn(__fmul_rn((float)(int)r[j], sa), sbv)));
+            }
+            tmem_st32(tq + 2 * BN + gi2 * 32, cr);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&accempty[c & 1]);
+        }
+        tc_fence_after();
+        for (int gi2 = 0; gi2 < NG; gi2++) {
+          uint32_t cr[32];
+          tmem_ld32(tq + 2 * BN + gi2 * 32, cr);
+          const int n0 = (nt * NG + gi2) * 32;
+          if (tok < p.m) {
+            float* yr = p.y + (long long)tok * p.ldy;
+#pragma unroll
+            for (int j = 0; j < 32; j++)
+              if (n0 + j < p.n) yr[n0 + j] = __uint_as_float(cr[j]);
+          }
+        }
+      }
+    }
+  }
+  griddep_launch();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase),
+                 "r"(S::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// A preparation: canonical K-major tiles [m-tile][16-byte column][128][16 B]
+// ---------------------------------------------------------------------------
+// INT8: per-row quantisation (quantize.zig:12-47) or copy of given codes.
+__global__ void __launch_bounds__(256) k_prep_a_i8(const float* __restrict__ x,
+                                                   const int8_t* __restrict__ xq,
+                                                   const float* __restrict__ sx, long long ldx,
+                                                   int m, int k, int kcols,
+                                                   uint8_t* __restrict__ a,
+                                                   float* __restrict__ sa) {
+  griddep_wait();
+  griddep_launch();
+  const int row = blockIdx.x;  // 0 .. mtiles*128
+  const int mt = row >> 7, rr = row & 127;
+  __shared__ float red[8];
+  float inv = 0.0f;
+  bool zero = true;
+  if (row < m && !xq) {
+    const float* xr = x + (long long)row * ldx;
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < k; i += 256) amax = fmaxf(amax, fabsf(xr[i]));
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+    for (int w = 1; w < 8; w++) amax = fmaxf(amax, red[w]);
+    zero = amax == 0.0f;
+    if (!zero) inv = __fdiv_rn(127.0f, amax);
+    if (threadIdx.x == 0) sa[row] = zero ? 1.0f : __fdiv_rn(amax, 127.0f);
+  } else if (row < m) {
+    zero = false;
+    if (threadIdx.x == 0) sa[row] = sx[row];
+  }
+  // each thread writes 16-byte columns of this row
+  for (int c = threadIdx.x; c < kcols; c += 256) {
+    uint32_t wv[4] = {0, 0, 0, 0};
+    if (row < m && !zero) {
+#pragma unroll
+      for (int e = 0; e < 16; e++) {
+        const int kk = c * 16 + e;
+        int8_t v = 0;
+        if (kk < k) {
+          if (xq) {
+            v = xq[(long long)row * ldx + kk];
+          } else {
+            float r = roundf(__fmul_rn(x[(long long)row * ldx + kk], inv));
+            r = fminf(127.0f, fmaxf(-127.0f, r));
+            v = (int8_t)(int)r;
+          }
+        }
+        wv[e >> 2] |= (uint32_t)(uint8_t)v << (8 * (e & 3));
+      }
+    }
+    reinterpret_cast<uint4*>(a + (((size_t)mt * kcols + c) * 128 + rr) * 16)[0] =
+        make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
+
+// Block formats: fp16(x).
+__global__ void __launch_bounds__(256) k_prep_a_f16(const float* __restrict__ x, long long ldx,
+                                                    int m, int k, int kcols,
+                                                    uint8_t* __restrict__ a) {
+  griddep_wait();
+  griddep_launch();
+  const int row = blockIdx.x;
+  const int mt = row >> 7, rr = row & 127;
+  for (int c = threadIdx.x; c < kcols; c += 256) {
+    uint32_t wv[4] = {0, 0, 0, 0};
+    if (row < m) {
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int kk = c * 8 + e;
+        const float v = kk < k ? x[(long long)row * ldx + kk] : 0.0f;
+        wv[e >> 1] |= (uint32_t)__half_as_ushort(__float2half_rn(v)) << (16 * (e & 1));
+      }
+    }
+    reinterpret_cast<uint4*>(a + (((size_t)mt * kcols + c) * 128 + rr) * 16)[0] =
+        make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl2(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                        cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+template <int FMT>
+syn_status_t launch_gemm_t(const GemmParams& p, int mtiles, int ntiles, cudaStream_t st) {
+  static std::mutex mu;
+  static std::set<int> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!done.count(dev)) {
+      cudaFuncSetAttribute(k_qgemm<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GS<FMT>::SMEM);
+      done.insert(dev);
+    }
+  }
+  cudaError_t e = launch_pdl2(k_qgemm<FMT>, dim3(mtiles, ntiles), dim3(GEMM_THREADS),
+                              (size_t)GS<FMT>::SMEM, st, p);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "k_qgemm");
+    return SYN_ERR_CUDA;
+  }
+  return SYN_OK;
+}
+
+}  // namespace
+
+size_t gemm_a_bytes(int fmt, size_t m, size_t kp) {
+  const size_t mtiles = (m + BM - 1) / BM;
+  const size_t kcols = (fmt == SYN_QFMT_INT8_KN) ? kp / 16 : kp / 8;
+  return mtiles * BM * kcols * 16 + mtiles * BM * sizeof(float) + 256;
+}
+
+syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx,
+                          const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
+                          int chunked, uint8_t* abuf, int* err, cudaStream_t st) {
+  if (w->n > 0x7FFFFFFFull || w->kp > 0x3FFFFFFFull || m > 0x7FFFFFFFull) return SYN_ERR_UNSUPPORTED;
+  const bool i8 = w->fmt == SYN_QFMT_INT8_KN;
+  const int mtiles = (int)((m + BM - 1) / BM);
+  const int groups = (int)((w->n + 31) / 32);
+  const int ntiles = (groups + NG - 1) / NG;
+  const int kcols = (int)(i8 ? w->kp / 16 : w->kp / 8);
+  uint8_t* a = abuf;
+  float* sa = reinterpret_cast<float*>(abuf + (size_t)mtiles * BM * kcols * 16);
+  cudaError_t e;
+  if (i8)
+    e = launch_pdl2(k_prep_a_i8, dim3(mtiles * BM), dim3(256), 0, st, x, xq, sx, (long long)ldx,
+                    (int)m, (int)w->k, kcols, a, sa);
+  else
+    e = launch_pdl2(k_prep_a_f16, dim3(mtiles * BM), dim3(256), 0, st, x, (long long)ldx, (int)m,
+                    (int)w->k, kcols, a);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "k_prep_a");
+    return SYN_ERR_CUDA;
+  }
+  GemmParams p{};
+  p.q = w->q;
+  p.d = w->d;
+  p.sb = w->sb;
+  p.hdr = w->hdr;
+  p.qh = w->qh;
+  p.sc = reinterpret_cast<const uint16_t*>(w->sc);
+  p.n = (int)w->n;
+  p.k = (int)w->k;
+  p.nblk = (int)(w->kp / 32);
+  p.nsb = (int)(w->k / 256);
+  p.groups = groups;
+  p.a = a;
+  p.kcols = kcols;
+  p.sa = sa;
+  p.m = (int)m;
+  p.y = y;
+  p.ldy = (long long)ldy;
+  p.chunked = chunked;
+  p.err = err;
+  switch (w->fmt) {
+    case SYN_QFMT_INT8_KN: return launch_gemm_t<F_INT8>(p, mtiles, ntiles, st);
+    case SYN_QFMT_Q4_0: return launch_gemm_t<F_Q4_0>(p, mtiles, ntiles, st);
+    case SYN_QFMT_Q8_0: return launch_gemm_t<F_Q8_0>(p, mtiles, ntiles, st);
+    case SYN_QFMT_Q4_K: return launch_gemm_t<F_Q4_K>(p, mtiles, ntiles, st);
+    case SYN_QFMT_Q6_K: return launch_gemm_t<F_Q6_K>(p, mtiles, ntiles, st);
+  }
+  return SYN_ERR_INVALID_ARG;
+}
+
+}  // namespace syn

@@ -13,6 +13,8 @@ struct syn_cuda_ctx_s {
   size_t part_bytes;
   int* cnt;          // per-row-group arrival counters; zero between launches
   size_t cnt_bytes;
+  uint8_t* abuf;     // activations prepared for the tensor-core GEMM
+  size_t abuf_bytes;
   int* err;          // device-side error word (e.g. SYN_ERR_TIMEOUT)
 };
 
@@ -56,6 +58,14 @@ size_t gemv_counter_bytes(size_t m, size_t n);
 syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx,
                           const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
                           int chunked, float* part, int* cnt, int* err, cudaStream_t st);
+
+// Tensor-core GEMM (gemm.cu) for m >= kGemmMinRows activation rows. abuf:
+// scratch of gemm_a_bytes(fmt, m, kp) bytes for the prepared activations.
+constexpr size_t kGemmMinRows = 8;
+size_t gemm_a_bytes(int fmt, size_t m, size_t kp);
+syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx,
+                          const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
+                          int chunked, uint8_t* abuf, int* err, cudaStream_t st);
 
 // Raw-layout Q4_0 GEMV over the reference's 18-byte blocks (M = 1).
 syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* b, float* c,
