@@ -3,32 +3,36 @@
 //
 //   y[M, N] = x[M, K] * W[N, K]^T, for M >= 8 (tokens), all five formats.
 //
-// Operands.
-//   A (activations) is prepared by k_prep_a into the canonical K-major
-//   no-swizzle layout of the MMA (core matrices of 8 rows x 16 bytes):
-//   global [m-tile][16-byte K column][128 rows][16 B], so one stage of A is
-//   one contiguous run for a 1-D bulk copy.
+// Operands (shared memory, K-major, no swizzle: core matrices of 8 rows x
+// 16 bytes; a [rows][16 B] column of 128 rows is 2 KB).
+//   A (activations) is prepared by k_prep_a_* into global memory already in
+//   that layout, [m-tile][16-byte K column][128 rows][16 B], so one stage of
+//   A is one contiguous run for a 1-D bulk copy.
 //     INT8 weights: A = int8 codes of the reference's per-row quantisation
 //       (quantize.zig:12-47), bit-exact; products are exact int32
 //       (kind::i8). M <= 16: one int32 accumulator over K, then
 //       float(acc) * sa * sb (qmatmul.zig:52-66, 218-223). M > 16: the
 //       reference's per-512-K-chunk epilogue C += float(chunk) * sa * sb in
-//       chunk order (qmatmul.zig:68-98), every op rounded -- so the result
-//       is bit-exact for every M.
+//       chunk order (qmatmul.zig:68-98), every op rounded -- bit-exact for
+//       every M.
 //     Block formats: A = fp16(x); the weights are dequantised in shared
-//       memory with the reference's formulas (gguf.rs:255-487) to fp16 and
-//       multiplied with kind::f16, fp32 accumulation in tensor memory.
-//   B (weights) is the row-interleaved repack (repack.cu): a 32-row group's
-//   tiles for consecutive blocks are contiguous, and a tile [32 rows][16 B]
-//   is four core matrices, so each MMA is M=128 x N=32 x K (one row group)
-//   with SBO = 128 B (8 rows) and LBO = the distance to the next 16 bytes
-//   of K.
+//       memory with the reference's formulas (gguf.rs:255-487), rounded to
+//       fp16 and multiplied with kind::f16, fp32 accumulation.
+//   B (weights) comes from the row-interleaved repack (repack.cu). For INT8
+//   a 4-D tensor map (TMA) gathers the 4 row groups' tiles of a stage into
+//   [16-byte K column][128 rows][16 B]; block formats bring the raw tiles in
+//   with 1-D bulk copies and 8 warps write the dequantised fp16 tiles in the
+//   same 128-row layout. Each K step is then one 128 x 128 MMA.
 //
-// CTA = 6 warps: warp 0 issues the bulk copies (TMA engine) of A and raw B
-// stages into a smem ring; warp 1 owns tensor memory and one of its threads
-// issues the MMAs; warps 2-5 dequantise B (block formats) and run the
-// epilogue (tensor memory -> registers -> y). Tile: 128 tokens x 128 weight
-// rows. Every wait is bounded and reports SYN_ERR_TIMEOUT instead of hanging.
+// CTA = 10 warps: warp 0 issues the copies into a smem ring; warp 1 owns
+// tensor memory and one of its threads issues the MMAs; warps 2-9
+// dequantise B (block formats) and run the epilogue (tensor memory ->
+// registers -> y). Tile: 128 tokens x 128 weight rows. Every wait is bounded
+// and reports SYN_ERR_TIMEOUT instead of hanging.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
 #include <mutex>
 #include <set>
 
@@ -41,9 +45,10 @@ enum : int { F_INT8 = SYN_QFMT_INT8_KN, F_Q4_0 = SYN_QFMT_Q4_0, F_Q8_0 = SYN_QFM
              F_Q4_K = SYN_QFMT_Q4_K, F_Q6_K = SYN_QFMT_Q6_K };
 
 constexpr int BM = 128;  // tokens per tile (MMA M)
-constexpr int BN = 128;  // weight rows per tile (4 row groups of 32)
+constexpr int BN = 128;  // weight rows per tile (4 row groups of 32) = MMA N
 constexpr int NG = BN / 32;
-constexpr int GEMM_THREADS = 192;
+constexpr int WORKERS = 8;                       // dequant / epilogue warps
+constexpr int GEMM_THREADS = 64 + WORKERS * 32;  // producer + MMA + workers
 
 // ---------------------------------------------------------------------------
 // tcgen05 helpers
@@ -59,6 +64,7 @@ __device__ __forceinline__ void fence_async_smem() {
 }
 
 // smem matrix descriptor: K-major, no swizzle (core matrices 8 rows x 16 B).
+// lbo = bytes to the next 16 bytes of K, sbo = bytes to the next 8 rows.
 __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = 0;
   d |= (uint64_t)((addr >> 4) & 0x3FFF);
@@ -68,19 +74,19 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t 
   return d;                // base offset 0, legacy LBO mode, layout SWIZZLE_NONE
 }
 
-// Instruction descriptor: M=128, N=32, K-major A and B.
+// Instruction descriptor: M = 128, N = 128, K-major A and B.
+// c_format (bits 4-5): 1 = F32, 2 = S32; a/b format (7-9, 10-12): kind::f16
+// -> 0 = F16, kind::i8 -> 1 = signed; n_dim (17-22) = N >> 3; m_dim (24-28)
+// = M >> 4.
 template <bool I8>
-__host__ __device__ constexpr uint32_t idesc_128x32() {
-  // c_format (bits 4-5): 1 = F32, 2 = S32; a/b format (7-9, 10-12):
-  // kind::f16 -> 0 = F16; kind::i8 -> 1 = signed; n_dim (17-22) = N >> 3;
-  // m_dim (24-28) = M >> 4.
+__host__ __device__ constexpr uint32_t idesc_tile() {
   return (I8 ? (2u << 4) : (1u << 4)) | (I8 ? (1u << 7) : 0u) | (I8 ? (1u << 10) : 0u) |
-         ((32u >> 3) << 17) | ((128u >> 4) << 24);
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 template <bool I8>
 __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
-  constexpr uint32_t id = idesc_128x32<I8>();
+  constexpr uint32_t id = idesc_tile<I8>();
   if constexpr (I8) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -101,6 +107,17 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
                : "memory");
+}
+
+// 4-D tiled TMA load (no multicast) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar))
+      : "memory");
 }
 
 // 32 lanes x 32 consecutive 32-bit columns; thread i gets lane (base + i).
@@ -136,10 +153,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 template <int FMT>
 struct GS {
   static constexpr bool I8 = FMT == F_INT8;
-  static constexpr int KB = I8 ? 8 : 4;                 // 32-element blocks per stage
+  static constexpr int KB = I8 ? 8 : 4;                        // 32-element blocks per stage
   static constexpr int A_BYTES = BM * KB * 32 * (I8 ? 1 : 2);  // 32 KB
-  // raw weight bytes per row group and block (q tile + per-block aux)
-  static constexpr int QT = (FMT == F_INT8 || FMT == F_Q8_0) ? 1024 : 512;
+  // INT8: B stage = [2*KB K columns][128 rows][16 B] (tensor-map gather)
+  static constexpr int B8_BYTES = I8 ? BN * KB * 32 : 0;       // 32 KB
+  // block formats: raw bytes per row group (q tiles + per-block aux)
+  static constexpr int QT = (FMT == F_Q8_0) ? 1024 : 512;
   static constexpr int DT = (FMT == F_Q4_0 || FMT == F_Q8_0) ? 64 : 0;
   static constexpr int QHT = (FMT == F_Q6_K) ? 256 : 0;
   static constexpr int SCT = (FMT == F_Q6_K) ? 64 : 0;
@@ -151,11 +170,12 @@ struct GS {
   static constexpr int G_SC = G_QH + KB * QHT;
   static constexpr int G_H = G_SC + KB * SCT;
   static constexpr int G_D6 = G_H + HT;
-  static constexpr int G_BYTES = (G_D6 + D6T + 127) / 128 * 128;  // per row group
-  static constexpr int RAW_BYTES = NG * G_BYTES;
+  static constexpr int G_BYTES = I8 ? 0 : (G_D6 + D6T + 127) / 128 * 128;  // per row group
+  static constexpr int RAW_BYTES = I8 ? B8_BYTES : NG * G_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + RAW_BYTES;
-  static constexpr int NS = I8 ? 3 : 2;                 // ring depth
-  static constexpr int BH_BYTES = I8 ? 0 : BN * KB * 32 * 2;  // dequantised fp16 B (32 KB)
+  static constexpr int NS = I8 ? 3 : 2;                        // ring depth
+  // block formats: dequantised fp16 B = [block][4 K columns][128 rows][16 B]
+  static constexpr int BH_BYTES = I8 ? 0 : BN * KB * 32 * 2;   // 32 KB
   static constexpr int NBH = I8 ? 0 : 2;
   static constexpr int SMEM = NS * STAGE_BYTES + NBH * BH_BYTES;
   static constexpr uint32_t TMEM_COLS = I8 ? 512 : 128;
@@ -170,7 +190,7 @@ struct GemmParams {
   const uint16_t* sc;
   int n, k, nblk, nsb, groups;
   const uint8_t* a;  // prepared activations
-  int kcols;         // 16-byte K columns per A row (A row bytes / 16)
+  int kcols;         // 16-byte K columns per A row
   const float* sa;   // INT8: per-row activation scale
   int m;
   float* y;
@@ -189,120 +209,117 @@ __device__ __forceinline__ bool bwait(const GemmParams& p, uint64_t* bar, uint32
   return false;
 }
 
-// Dequantises the raw stage of one row group into fp16 B tiles:
-// out[b][c][32 rows][16 B] (c = 16-byte K column of the block, 8 halves).
-// Thread = one row (lane l of group gi). Reference formulas (gguf.rs).
+// Dequantises block bl of one row group's raw stage (thread = row l of the
+// group) into fp16: 4 K columns of 8 halves, written as rows of the 128-row
+// tile. Reference formulas: gguf.rs:255-487.
 template <int FMT>
-__device__ void dequant_stage(const uint8_t* raw, uint8_t* out, int l, int nbs, int b0) {
+__device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, int l, int row,
+                                              int bl, int b) {
   using S = GS<FMT>;
-#pragma unroll 1
-  for (int bl = 0; bl < nbs; bl++) {
-    float v[32];
-    if constexpr (FMT == F_Q4_0) {
-      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
-      const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+  float v[32];
+  if constexpr (FMT == F_Q4_0) {
+    const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+    const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-        v[2 * i] = __fmul_rn(dd, (float)((int)(byte & 15) - 8));
-        v[2 * i + 1] = __fmul_rn(dd, (float)((int)(byte >> 4) - 8));
-      }
-    } else if constexpr (FMT == F_Q8_0) {
-      const uint4 q0 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024)[l];
-      const uint4 q1 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024 + 512)[l];
-      const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
-      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-      for (int i = 0; i < 32; i++)
-        v[i] = __fmul_rn(dd, (float)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFF));
-    } else if constexpr (FMT == F_Q4_K) {
-      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
-      const uint4 h = reinterpret_cast<const uint4*>(raw + S::G_H)[l];
-      const int s = (b0 + bl) & 7;
-      const float dd = f16_loader((uint16_t)(h.x & 0xFFFF));
-      const float dmin = f16_loader((uint16_t)(h.x >> 16));
-      uint32_t scv, mnv;
-      if (s < 4) {
-        const int sh = 8 * s;
-        scv = (h.y >> sh) & 0x3F;
-        mnv = (((h.z >> sh) & 0xFF) >> 4) | (((h.w >> sh) & 0x0F) << 4);
-      } else {
-        const int sh = 8 * (s - 4);
-        const uint32_t ys = (h.y >> sh) & 0xFF;
-        scv = ((h.z >> sh) & 0x0F) | ((ys >> 6) << 4);
-        mnv = (((h.w >> sh) & 0xFF) >> 4) | (((ys >> 4) & 0x0C) << 4);
-      }
-      const float scl = __fmul_rn(dd, (float)scv), mv = __fmul_rn(dmin, (float)mnv);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-        v[2 * i] = __fsub_rn(__fmul_rn((float)(byte & 15), scl), mv);
-        v[2 * i + 1] = __fsub_rn(__fmul_rn((float)(byte >> 4), scl), mv);
-      }
-    } else {  // F_Q6_K
-      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
-      const uint2 hq = reinterpret_cast<const uint2*>(raw + S::G_QH + bl * 256)[l];
-      const uint32_t scp = reinterpret_cast<const uint16_t*>(raw + S::G_SC + bl * 64)[l];
-      const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D6)[l]);
-      const float s0 = __fmul_rn((float)(int8_t)(scp & 0xFF), dd);
-      const float s1 = __fmul_rn((float)(int8_t)(scp >> 8), dd);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int e = 0; e < 32; e++) {
-        const uint32_t byte = (w[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
-        const uint32_t lo = (e & 1) ? (byte >> 4) : (byte & 15);
-        // invert the high-bit re-arrangement of repack.cu (k_repack_q6_k)
-        const int half = e >> 4, r = e & 15, f = 2 * (r >> 3) + (r & 1), tt = (r & 7) >> 1;
-        const uint32_t H = half ? hq.y : hq.x;
-        const uint32_t hi = (H >> (8 * tt + 2 * f)) & 3u;
-        v[e] = __fmul_rn((float)((int)(lo | (hi << 4)) - 32), half ? s1 : s0);
-      }
+    for (int i = 0; i < 16; i++) {
+      const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+      v[2 * i] = __fmul_rn(dd, (float)((int)(byte & 15) - 8));
+      v[2 * i + 1] = __fmul_rn(dd, (float)((int)(byte >> 4) - 8));
     }
-    // 4 K columns of 8 halves each
+  } else if constexpr (FMT == F_Q8_0) {
+    const uint4 q0 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024)[l];
+    const uint4 q1 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024 + 512)[l];
+    const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-      uint4 o;
-      o.x = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 0])) |
-            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 1])) << 16);
-      o.y = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 2])) |
-            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 3])) << 16);
-      o.z = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 4])) |
-            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 5])) << 16);
-      o.w = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 6])) |
-            ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 7])) << 16);
-      reinterpret_cast<uint4*>(out + bl * 2048 + c * 512)[l] = o;
+    for (int i = 0; i < 32; i++)
+      v[i] = __fmul_rn(dd, (float)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFF));
+  } else if constexpr (FMT == F_Q4_K) {
+    const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+    const uint4 h = reinterpret_cast<const uint4*>(raw + S::G_H)[l];
+    const int s = b & 7;
+    const float dd = f16_loader((uint16_t)(h.x & 0xFFFF));
+    const float dmin = f16_loader((uint16_t)(h.x >> 16));
+    uint32_t scv, mnv;
+    if (s < 4) {
+      const int sh = 8 * s;
+      scv = (h.y >> sh) & 0x3F;
+      mnv = (((h.z >> sh) & 0xFF) >> 4) | (((h.w >> sh) & 0x0F) << 4);
+    } else {
+      const int sh = 8 * (s - 4);
+      const uint32_t ys = (h.y >> sh) & 0xFF;
+      scv = ((h.z >> sh) & 0x0F) | ((ys >> 6) << 4);
+      mnv = (((h.w >> sh) & 0xFF) >> 4) | (((ys >> 4) & 0x0C) << 4);
     }
+    const float scl = __fmul_rn(dd, (float)scv), mv = __fmul_rn(dmin, (float)mnv);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+      v[2 * i] = __fsub_rn(__fmul_rn((float)(byte & 15), scl), mv);
+      v[2 * i + 1] = __fsub_rn(__fmul_rn((float)(byte >> 4), scl), mv);
+    }
+  } else {  // F_Q6_K
+    const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+    const uint2 hq = reinterpret_cast<const uint2*>(raw + S::G_QH + bl * 256)[l];
+    const uint32_t scp = reinterpret_cast<const uint16_t*>(raw + S::G_SC + bl * 64)[l];
+    const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D6)[l]);
+    const float s0 = __fmul_rn((float)(int8_t)(scp & 0xFF), dd);
+    const float s1 = __fmul_rn((float)(int8_t)(scp >> 8), dd);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int e = 0; e < 32; e++) {
+      const uint32_t byte = (w[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+      const uint32_t lo = (e & 1) ? (byte >> 4) : (byte & 15);
+      // invert the high-bit re-arrangement of repack.cu (k_repack_q6_k)
+      const int half = e >> 4, r = e & 15, f = 2 * (r >> 3) + (r & 1), tt = (r & 7) >> 1;
+      const uint32_t H = half ? hq.y : hq.x;
+      const uint32_t hi = (H >> (8 * tt + 2 * f)) & 3u;
+      v[e] = __fmul_rn((float)((int)(lo | (hi << 4)) - 32), half ? s1 : s0);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    uint4 o;
+    o.x = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 0])) |
+          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 1])) << 16);
+    o.y = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 2])) |
+          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 3])) << 16);
+    o.z = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 4])) |
+          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 5])) << 16);
+    o.w = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 6])) |
+          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 7])) << 16);
+    reinterpret_cast<uint4*>(out + bl * 8192 + c * 2048)[row] = o;
   }
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_qgemm(const GemmParams p, const __grid_constant__ CUtensorMap tmb) {
   using S = GS<FMT>;
   constexpr bool I8 = S::I8;
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ __align__(8) uint64_t full[S::NS], empty[S::NS];
-  __shared__ __align__(8) uint64_t bfull[2], bempty[2];    // fp16 B buffers
-  __shared__ __align__(8) uint64_t accfull[2], accempty[2];  // INT8 chunk accumulators
+  __shared__ __align__(8) uint64_t bfull[2], bempty[2];      // fp16 B buffers
+  __shared__ __align__(8) uint64_t accfull[2], accempty[2];  // accumulators
   __shared__ uint32_t tmem_base_sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = blockIdx.x, nt = blockIdx.y;
   const int nst = (p.nblk + S::KB - 1) / S::KB;
-  // INT8 chunking: a 512-element chunk is 2 stages (16 blocks)
-  const bool chunked = I8 && p.chunked;
+  const bool chunked = I8 && p.chunked;  // INT8: chunk = 16 blocks = 2 stages
   const int nchunks = (p.nblk + 15) / 16;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::NS; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], I8 ? 1 : 1 + 4);  // MMA commit (+ 4 dequant warps)
+      mbar_init(&empty[s], I8 ? 1 : 1 + WORKERS);  // MMA commit (+ dequant warps)
     }
     for (int i = 0; i < 2; i++) {
-      mbar_init(&bfull[i], 4);
+      mbar_init(&bfull[i], WORKERS);
       mbar_init(&bempty[i], 1);
       mbar_init(&accfull[i], 1);
-      mbar_init(&accempty[i], 4);
+      mbar_init(&accempty[i], WORKERS);
     }
     mbar_fence_init();
   }
@@ -321,53 +338,58 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
   griddep_wait();
 
   if (warp == 0) {
-    // ---------------- producer: bulk copies of A and raw B stages ----------------
+    // ---------------- producer ----------------
     if (lane == 0) {
+      constexpr int cpb = I8 ? 2 : 4;  // 16-byte A columns per block
+      int ngr = 0;
+      for (int gi = 0; gi < NG; gi++)
+        if (nt * NG + gi < p.groups) ngr++;
       for (int s = 0; s < nst; s++) {
         const int slot = s % S::NS;
         if (s >= S::NS && !bwait(p, &empty[slot], ((s / S::NS) - 1) & 1)) break;
         const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
         uint8_t* st = sm + slot * S::STAGE_BYTES;
         uint8_t* raw = st + S::A_BYTES;
-        // A: columns [b0 * cpb, (b0 + nbs) * cpb) of m-tile mt (cpb = 16-byte
-        // columns per block: 2 for int8, 4 for fp16)
-        constexpr int cpb = I8 ? 2 : 4;
         const uint32_t a_bytes = nbs * cpb * 2048;
         uint32_t bytes = a_bytes;
-        int ngr = 0;
-        for (int gi = 0; gi < NG; gi++)
-          if ((nt * NG + gi) < p.groups) ngr++;
-        bytes += ngr * (nbs * (S::QT + S::DT + S::QHT + S::SCT) + S::HT + S::D6T);
+        if constexpr (I8)
+          bytes += S::B8_BYTES;  // the full tensor-map box (out of range reads as zero)
+        else
+          bytes += ngr * (nbs * (S::QT + S::DT + S::QHT + S::SCT) + S::HT + S::D6T);
         mbar_expect_tx(&full[slot], bytes);
         bulk_g2s(st, p.a + ((size_t)mt * p.kcols + (size_t)b0 * cpb) * 2048, a_bytes, &full[slot]);
-        for (int gi = 0; gi < ngr; gi++) {
-          const size_t g = (size_t)nt * NG + gi;
-          uint8_t* gr = raw + gi * S::G_BYTES;
-          const size_t t0 = g * p.nblk + b0;
-          bulk_g2s(gr + S::G_Q, p.q + t0 * S::QT, nbs * S::QT, &full[slot]);
-          if constexpr (S::DT)
-            bulk_g2s(gr + S::G_D, reinterpret_cast<const uint8_t*>(p.d) + t0 * 64, nbs * 64,
-                     &full[slot]);
-          if constexpr (S::QHT) {
-            bulk_g2s(gr + S::G_QH, p.qh + t0 * 256, nbs * 256, &full[slot]);
-            bulk_g2s(gr + S::G_SC, reinterpret_cast<const uint8_t*>(p.sc) + t0 * 64, nbs * 64,
-                     &full[slot]);
+        if constexpr (I8) {
+          tma_load_4d(raw, &tmb, 0, 0, nt * NG, 2 * b0, &full[slot]);
+        } else {
+          for (int gi = 0; gi < ngr; gi++) {
+            const size_t g = (size_t)nt * NG + gi;
+            uint8_t* gr = raw + gi * S::G_BYTES;
+            const size_t t0 = g * p.nblk + b0;
+            bulk_g2s(gr + S::G_Q, p.q + t0 * S::QT, nbs * S::QT, &full[slot]);
+            if constexpr (S::DT)
+              bulk_g2s(gr + S::G_D, reinterpret_cast<const uint8_t*>(p.d) + t0 * 64, nbs * 64,
+                       &full[slot]);
+            if constexpr (S::QHT) {
+              bulk_g2s(gr + S::G_QH, p.qh + t0 * 256, nbs * 256, &full[slot]);
+              bulk_g2s(gr + S::G_SC, reinterpret_cast<const uint8_t*>(p.sc) + t0 * 64, nbs * 64,
+                       &full[slot]);
+            }
+            if constexpr (S::HT)
+              bulk_g2s(gr + S::G_H, p.hdr + (g * p.nsb + b0 / 8) * 512, 512, &full[slot]);
+            if constexpr (S::D6T)
+              bulk_g2s(gr + S::G_D6,
+                       reinterpret_cast<const uint8_t*>(p.d) + (g * p.nsb + b0 / 8) * 64, 64,
+                       &full[slot]);
           }
-          if constexpr (S::HT)
-            bulk_g2s(gr + S::G_H, p.hdr + (g * p.nsb + b0 / 8) * 512, 512, &full[slot]);
-          if constexpr (S::D6T)
-            bulk_g2s(gr + S::G_D6, reinterpret_cast<const uint8_t*>(p.d) + (g * p.nsb + b0 / 8) * 64,
-                     64, &full[slot]);
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const int ngr_valid = min(NG, p.groups - nt * NG);
       bool ok = true;
       int chunk = 0;  // INT8 chunked: accumulator buffer = chunk & 1
-      for (int s = 0; s < nst && ok; s++) {
+      for (int s = 0; s < nst; s++) {
         const int slot = s % S::NS;
         if (!bwait(p, &full[slot], (s / S::NS) & 1)) { ok = false; break; }
         const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
@@ -377,7 +399,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
         if constexpr (I8) {
           b_addr = smem_u32(st + S::A_BYTES);
           if (chunked && (b0 & 15) == 0 && chunk >= 2) {
-            // reuse of accumulator buffer (chunk & 1): wait until drained
+            // accumulator buffer (chunk & 1) must have been drained
             if (!bwait(p, &accempty[chunk & 1], ((chunk >> 1) - 1) & 1)) { ok = false; break; }
           }
         } else {
@@ -385,62 +407,54 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
           b_addr = smem_u32(sm + S::NS * S::STAGE_BYTES + (s & 1) * S::BH_BYTES);
         }
         tc_fence_after();
-        const uint32_t dbase = tbase + (chunked ? (uint32_t)(chunk & 1) * BN : 0u);
+        const uint32_t dcol = tbase + (chunked ? (uint32_t)(chunk & 1) * BN : 0u);
         for (int bl = 0; bl < nbs; bl++) {
           const int b = b0 + bl;
           if constexpr (I8) {
-            // one block = K of 32 int8 = one MMA per row group
+            // one block = K of 32 int8 = one 128 x 128 x 32 MMA
             const bool first = chunked ? ((b & 15) == 0) : (b == 0);
-            const uint64_t ad = sdesc(a_addr + bl * 2 * 2048, 2048, 128);
-            for (int gi = 0; gi < ngr_valid; gi++) {
-              const uint64_t bd = sdesc(b_addr + gi * S::G_BYTES + bl * 1024, 512, 128);
-              mma<true>(dbase + gi * 32, ad, bd, first ? 0u : 1u);
-            }
+            mma<true>(dcol, sdesc(a_addr + bl * 2 * 2048, 2048, 128),
+                      sdesc(b_addr + bl * 2 * 2048, 2048, 128), first ? 0u : 1u);
           } else {
-            // one block = K of 32 halves = two MMAs (K = 16) per row group
-            for (int kh = 0; kh < 2; kh++) {
-              const uint64_t ad = sdesc(a_addr + (bl * 4 + kh * 2) * 2048, 2048, 128);
-              for (int gi = 0; gi < ngr_valid; gi++) {
-                const uint64_t bd =
-                    sdesc(b_addr + gi * (S::KB * 2048) + bl * 2048 + kh * 1024, 512, 128);
-                mma<false>(dbase + gi * 32, ad, bd, (b == 0 && kh == 0) ? 0u : 1u);
-              }
-            }
+            // one block = K of 32 halves = two 128 x 128 x 16 MMAs
+            for (int kh = 0; kh < 2; kh++)
+              mma<false>(dcol, sdesc(a_addr + (bl * 4 + kh * 2) * 2048, 2048, 128),
+                         sdesc(b_addr + bl * 8192 + kh * 4096, 2048, 128),
+                         (b == 0 && kh == 0) ? 0u : 1u);
           }
         }
         mma_commit(&empty[slot]);
         if constexpr (!I8) mma_commit(&bempty[s & 1]);
         if constexpr (I8) {
-          const bool chunk_end = chunked && (((b0 + nbs) & 15) == 0 || b0 + nbs == p.nblk);
-          if (chunk_end) {
+          if (chunked && (((b0 + nbs) & 15) == 0 || b0 + nbs == p.nblk)) {
             mma_commit(&accfull[chunk & 1]);
             chunk++;
           }
         }
       }
       if (!chunked) mma_commit(&accfull[0]);
-      if (!ok) {
-        // release the epilogue of any chunk it still waits for
+      if (!ok)  // release the epilogue of any chunk it still waits for
         for (int c = chunk; c < (chunked ? nchunks : 1); c++) mbar_arrive(&accfull[c & 1]);
-      }
     }
   } else {
-    // ---------------- warps 2-5: dequantise B / epilogue ----------------
-    const int ew = warp - 2;           // 0..3
-    const int quarter = warp & 3;      // tensor memory lane quarter of this warp
-    const int tok = mt * BM + quarter * 32 + lane;  // this thread's token row
+    // ---------------- warps 2-9: dequantise B / epilogue ----------------
+    const int ew = warp - 2;          // 0..7
+    const int quarter = warp & 3;     // tensor memory lane quarter of this warp
+    const int chalf = ew >> 2;        // column half (64 columns) of the epilogue
+    const int tok = mt * BM + quarter * 32 + lane;
     const uint32_t tq = tbase + ((uint32_t)(quarter * 32) << 16);
     if constexpr (!I8) {
-      // dequantise each stage's raw B into fp16 tiles
-      const int gi = ew, l = lane;
+      const int gi = ew & 3, bpar = ew >> 2, row = gi * 32 + lane;
+      const bool gvalid = nt * NG + gi < p.groups;
       for (int s = 0; s < nst; s++) {
         const int slot = s % S::NS;
         const bool ok1 = bwait(p, &full[slot], (s / S::NS) & 1);
         const bool ok2 = s < 2 || bwait(p, &bempty[s & 1], ((s >> 1) - 1) & 1);
         const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
         const uint8_t* raw = sm + slot * S::STAGE_BYTES + S::A_BYTES + gi * S::G_BYTES;
-        uint8_t* out = sm + S::NS * S::STAGE_BYTES + (s & 1) * S::BH_BYTES + gi * (S::KB * 2048);
-        if (ok1 && ok2 && nt * NG + gi < p.groups) dequant_stage<FMT>(raw, out, l, nbs, b0);
+        uint8_t* out = sm + S::NS * S::STAGE_BYTES + (s & 1) * S::BH_BYTES;
+        if (ok1 && ok2 && gvalid)
+          for (int bl = bpar; bl < nbs; bl += 2) dequant_block<FMT>(raw, out, lane, row, bl, b0 + bl);
         fence_async_smem();  // generic-proxy smem writes -> visible to the MMA
         __syncwarp();
         if (lane == 0) {
@@ -451,10 +465,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
       // epilogue: fp32 accumulators -> y
       bwait(p, &accfull[0], 0);
       tc_fence_after();
-      for (int gi2 = 0; gi2 < NG; gi2++) {
+      for (int h = 0; h < 2; h++) {
+        const int cg = chalf * 2 + h;
         uint32_t r[32];
-        tmem_ld32(tq + gi2 * 32, r);
-        const int n0 = (nt * NG + gi2) * 32;
+        tmem_ld32(tq + cg * 32, r);
+        const int n0 = nt * BN + cg * 32;
         if (tok < p.m) {
           float* yr = p.y + (long long)tok * p.ldy;
 #pragma unroll
@@ -468,10 +483,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
         // one int32 accumulator over all of K: float(acc) * sa * sb
         bwait(p, &accfull[0], 0);
         tc_fence_after();
-        for (int gi2 = 0; gi2 < NG; gi2++) {
+        for (int h = 0; h < 2; h++) {
+          const int cg = chalf * 2 + h;
           uint32_t r[32];
-          tmem_ld32(tq + gi2 * 32, r);
-          const int n0 = (nt * NG + gi2) * 32;
+          tmem_ld32(tq + cg * 32, r);
+          const int n0 = nt * BN + cg * 32;
           if (tok < p.m) {
             float* yr = p.y + (long long)tok * p.ldy;
 #pragma unroll
@@ -486,11 +502,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
         for (int c = 0; c < nchunks; c++) {
           bwait(p, &accfull[c & 1], (c >> 1) & 1);
           tc_fence_after();
-          for (int gi2 = 0; gi2 < NG; gi2++) {
-            const int n0 = (nt * NG + gi2) * 32;
+          for (int h = 0; h < 2; h++) {
+            const int cg = chalf * 2 + h;
+            const int n0 = nt * BN + cg * 32;
             uint32_t r[32], cr[32];
-            tmem_ld32(tq + (c & 1) * BN + gi2 * 32, r);
-            if (c > 0) tmem_ld32(tq + 2 * BN + gi2 * 32, cr);
+            tmem_ld32(tq + (c & 1) * BN + cg * 32, r);
+            if (c > 0) tmem_ld32(tq + 2 * BN + cg * 32, cr);
 #pragma unroll
             for (int j = 0; j < 32; j++) {
               const float sbv = (n0 + j < p.n) ? p.sb[n0 + j] : 0.0f;
@@ -498,17 +515,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) k_qgemm(const GemmParams p) {
               cr[j] = __float_as_uint(
                   __fadd_rn(prev, __fmul_rn(__fmul_rn((float)(int)r[j], sa), sbv)));
             }
-            tmem_st32(tq + 2 * BN + gi2 * 32, cr);
+            tmem_st32(tq + 2 * BN + cg * 32, cr);
           }
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&accempty[c & 1]);
         }
         tc_fence_after();
-        for (int gi2 = 0; gi2 < NG; gi2++) {
+        for (int h = 0; h < 2; h++) {
+          const int cg = chalf * 2 + h;
           uint32_t cr[32];
-          tmem_ld32(tq + 2 * BN + gi2 * 32, cr);
-          const int n0 = (nt * NG + gi2) * 32;
+          tmem_ld32(tq + 2 * BN + cg * 32, cr);
+          const int n0 = nt * BN + cg * 32;
           if (tok < p.m) {
             float* yr = p.y + (long long)tok * p.ldy;
 #pragma unroll
@@ -563,7 +581,6 @@ __global__ void __launch_bounds__(256) k_prep_a_i8(const float* __restrict__ x,
     zero = false;
     if (threadIdx.x == 0) sa[row] = sx[row];
   }
-  // each thread writes 16-byte columns of this row
   for (int c = threadIdx.x; c < kcols; c += 256) {
     uint32_t wv[4] = {0, 0, 0, 0};
     if (row < m && !zero) {
@@ -627,8 +644,42 @@ cudaError_t launch_pdl2(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sm
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the
+// library does not link libcuda directly).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// INT8 weights: view of the row-interleaved tiles as a 4-D byte tensor
+// (256 B, 2 halves of a 512-B half-plane, row group, 16-byte K column) whose
+// box (256, 2, 4, 2 * KB) lands in shared memory as [K column][128 rows][16 B].
+bool make_int8_map(CUtensorMap* map, const syn_cuda_weight_s* w, int groups) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t nblk = w->kp / 32;
+  const cuuint64_t dims[4] = {256, 2, (cuuint64_t)groups, 2 * nblk};
+  const cuuint64_t strides[3] = {256, nblk * 1024, 512};
+  const cuuint32_t box[4] = {256, 2, (cuuint32_t)NG, (cuuint32_t)(2 * GS<F_INT8>::KB)};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w->q, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 template <int FMT>
-syn_status_t launch_gemm_t(const GemmParams& p, int mtiles, int ntiles, cudaStream_t st) {
+syn_status_t launch_gemm_t(const GemmParams& p, const CUtensorMap& map, int mtiles, int ntiles,
+                           cudaStream_t st) {
   static std::mutex mu;
   static std::set<int> done;
   int dev = 0;
@@ -642,7 +693,7 @@ syn_status_t launch_gemm_t(const GemmParams& p, int mtiles, int ntiles, cudaStre
     }
   }
   cudaError_t e = launch_pdl2(k_qgemm<FMT>, dim3(mtiles, ntiles), dim3(GEMM_THREADS),
-                              (size_t)GS<FMT>::SMEM, st, p);
+                              (size_t)GS<FMT>::SMEM, st, p, map);
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_qgemm");
     return SYN_ERR_CUDA;
@@ -667,6 +718,9 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
   const int groups = (int)((w->n + 31) / 32);
   const int ntiles = (groups + NG - 1) / NG;
   const int kcols = (int)(i8 ? w->kp / 16 : w->kp / 8);
+  alignas(64) CUtensorMap map;
+  memset(&map, 0, sizeof(map));
+  if (i8 && !make_int8_map(&map, w, groups)) return SYN_ERR_UNSUPPORTED;
   uint8_t* a = abuf;
   float* sa = reinterpret_cast<float*>(abuf + (size_t)mtiles * BM * kcols * 16);
   cudaError_t e;
@@ -701,11 +755,11 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
   p.chunked = chunked;
   p.err = err;
   switch (w->fmt) {
-    case SYN_QFMT_INT8_KN: return launch_gemm_t<F_INT8>(p, mtiles, ntiles, st);
-    case SYN_QFMT_Q4_0: return launch_gemm_t<F_Q4_0>(p, mtiles, ntiles, st);
-    case SYN_QFMT_Q8_0: return launch_gemm_t<F_Q8_0>(p, mtiles, ntiles, st);
-    case SYN_QFMT_Q4_K: return launch_gemm_t<F_Q4_K>(p, mtiles, ntiles, st);
-    case SYN_QFMT_Q6_K: return launch_gemm_t<F_Q6_K>(p, mtiles, ntiles, st);
+    case SYN_QFMT_INT8_KN: return launch_gemm_t<F_INT8>(p, map, mtiles, ntiles, st);
+    case SYN_QFMT_Q4_0: return launch_gemm_t<F_Q4_0>(p, map, mtiles, ntiles, st);
+    case SYN_QFMT_Q8_0: return launch_gemm_t<F_Q8_0>(p, map, mtiles, ntiles, st);
+    case SYN_QFMT_Q4_K: return launch_gemm_t<F_Q4_K>(p, map, mtiles, ntiles, st);
+    case SYN_QFMT_Q6_K: return launch_gemm_t<F_Q6_K>(p, map, mtiles, ntiles, st);
   }
   return SYN_ERR_INVALID_ARG;
 }
