@@ -203,6 +203,145 @@ syn_status_t syn_cuda_qmatmul_noalloc(const syn_cuda_weight_t *w,
                                       const float *x, size_t m, float *y,
                                       void *stream);
 
+/* ------------------------------------------------------------------ */
+/* Decoder-layer kernels around the matmuls (device pointers, stream-  */
+/* ordered). Reductions follow the reference's order so that greedy    */
+/* decoding reproduces its token ids.                                  */
+/* ------------------------------------------------------------------ */
+
+/* RoPE tables [max_pos, head_dim/2] on the host, as
+ * precompute_rope_tables (models/lm/builder.rs:88-133, no scaling). */
+syn_status_t syn_cuda_rope_tables(double base, size_t max_pos, size_t head_dim,
+                                  float *cos_out, float *sin_out);
+
+/* rmsnorm (ops/norm.rs:8-37; sum of squares in vecHsum order,
+ * zig/src/ffi/exports.zig:503-514): out = (x * w) * 1/sqrt(ms + eps). */
+syn_status_t syn_cuda_rmsnorm(const float *x, const float *weight, size_t rows,
+                              size_t hidden, float eps, float *out, void *stream);
+/* residual += delta (add_vecs, ops/vector.rs:1-9), then out = rmsnorm(residual). */
+syn_status_t syn_cuda_add_rmsnorm(float *residual, const float *delta,
+                                  const float *weight, size_t rows, size_t hidden,
+                                  float eps, float *out, void *stream);
+/* Embedding lookup (ids >= vocab give zeros, int8.rs:566-574) into x_out
+ * (optional), then out = rmsnorm(x). ids: device int32 [rows]. */
+syn_status_t syn_cuda_embed_rmsnorm(const float *table, size_t vocab,
+                                    const int32_t *ids, size_t rows, size_t hidden,
+                                    const float *weight, float eps, float *x_out,
+                                    float *out, void *stream);
+
+/* KV cache in HBM (zig/src/ops/kvcache.zig:13-170, syn_kvcache_* at
+ * exports.zig:1879-1940): per layer and sequence, K and V [max_seq,
+ * n_kv_heads*head_dim] f32. The length is per sequence and shared by all
+ * layers (LayerCaches). Appends write at the current length; _advance
+ * commits them. A call that would pass max_seq returns SYN_ERR_INVALID_ARG
+ * (CacheFull, mapError exports.zig:122-136). */
+typedef struct syn_cuda_kvcache_s syn_cuda_kvcache_t;
+syn_status_t syn_cuda_kvcache_create(syn_cuda_ctx_t *ctx, size_t max_seq,
+                                     size_t n_kv_heads, size_t head_dim,
+                                     size_t num_layers, size_t batch,
+                                     syn_cuda_kvcache_t **out);
+syn_status_t syn_cuda_kvcache_destroy(syn_cuda_kvcache_t *cache);
+syn_status_t syn_cuda_kvcache_len(const syn_cuda_kvcache_t *cache, size_t seq,
+                                  size_t *len);
+/* Device pointers of one layer's K and V arrays of one sequence. */
+syn_status_t syn_cuda_kvcache_view(const syn_cuda_kvcache_t *cache, size_t layer,
+                                   size_t seq, float **k, float **v);
+syn_status_t syn_cuda_kvcache_append(syn_cuda_kvcache_t *cache, size_t layer,
+                                     size_t seq, const float *k, const float *v,
+                                     size_t n_tokens, void *stream);
+syn_status_t syn_cuda_kvcache_advance(syn_cuda_kvcache_t *cache, size_t seq,
+                                      size_t n_tokens, void *stream);
+/* truncateTo (kvcache.zig:109-113): only shortens. */
+syn_status_t syn_cuda_kvcache_truncate(syn_cuda_kvcache_t *cache, size_t seq,
+                                       size_t new_len, void *stream);
+syn_status_t syn_cuda_kvcache_reset(syn_cuda_kvcache_t *cache, size_t seq,
+                                    void *stream);
+
+/* cached_attention_decode (ops/attention.rs:24-147) for sequences
+ * [0, batch), one new token each: headwise RMSNorm of q and k (q_norm /
+ * k_norm may be NULL = identity), RoPE at position len, K and raw V
+ * appended at len, GQA attention over the last `window` positions (0 =
+ * all). Rows: q/k/v of sequence b at q + b*ld etc.; out + b*ldo. The cache
+ * length is not advanced. */
+syn_status_t syn_cuda_attention_decode(syn_cuda_kvcache_t *cache, size_t layer,
+                                       size_t batch, float *q, const float *k,
+                                       const float *v, size_t ld, size_t n_heads,
+                                       const float *q_norm, const float *k_norm,
+                                       float eps, const float *rope_cos,
+                                       const float *rope_sin, size_t window,
+                                       float *out, size_t ldo, void *stream);
+/* The first half of cached_attention_prefill (ops/attention.rs:153-210):
+ * headwise norms and RoPE (offsets 0..n-1) of q in place and of k, K and
+ * raw V appended at the sequence's length. */
+syn_status_t syn_cuda_qk_norm_rope_kv_append(
+    syn_cuda_kvcache_t *cache, size_t layer, size_t seq, size_t n_tokens, float *q,
+    const float *k, const float *v, size_t ld, size_t n_heads, const float *q_norm,
+    const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
+    void *stream);
+/* cached_attention_prefill (ops/attention.rs:153-247): the above, then
+ * syn_fused_attention per head (exports.zig:1364-1478) over the prompt. */
+syn_status_t syn_cuda_attention_prefill(
+    syn_cuda_kvcache_t *cache, size_t layer, size_t seq, size_t n_tokens, float *q,
+    const float *k, const float *v, size_t ld, size_t n_heads, const float *q_norm,
+    const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
+    float *out, size_t ldo, void *stream);
+
+/* SwiGLU. variant 0: silu(g)*u of the INT8 model (int8.rs:500-503);
+ * variant 1: syn_swiglu / swigluFused (zig/src/ops/silu.zig:85-114). */
+syn_status_t syn_cuda_swiglu(const float *gate, const float *up, size_t ld_in,
+                             size_t rows, size_t n, int variant, float *out,
+                             size_t ldo, void *stream);
+/* Greedy argmax per row (generation/sampler.rs:217-224): last maximal index
+ * wins ties; NaN compares Equal. out_idx: device int32 [rows]. */
+syn_status_t syn_cuda_argmax(const float *logits, size_t rows, size_t n,
+                             int32_t *out_idx, void *stream);
+
+/* ------------------------------------------------------------------ */
+/* Model runner: QuantizedCausalLM / CausalLM on the GPU               */
+/* (quantization/lm/int8.rs:171-709, models/lm/causal_lm.rs:195-280).  */
+/* ------------------------------------------------------------------ */
+typedef struct syn_cuda_model_s syn_cuda_model_t;
+
+/* config_json: a model config in the reference's format (configs/*.json:
+ * architecture / attention / norm / ffn / position). max_seq: KV capacity
+ * per sequence; max_batch: sequences decoded together. */
+syn_status_t syn_cuda_model_create(syn_cuda_ctx_t *ctx, const char *config_json,
+                                   size_t max_seq, size_t max_batch,
+                                   syn_cuda_model_t **out);
+/* f32 tensors by Hugging Face name: model.embed_tokens.weight, model.norm.weight,
+ * model.layers.{i}.{input_layernorm,post_attention_layernorm}.weight,
+ * model.layers.{i}.self_attn.{q_norm,k_norm}.weight (optional). Host memory. */
+syn_status_t syn_cuda_model_set_tensor(syn_cuda_model_t *m, const char *name,
+                                       const float *host, size_t numel);
+/* Linear weights: model.layers.{i}.self_attn.{q,k,v,o}_proj.weight,
+ * model.layers.{i}.mlp.{gate,up,down}_proj.weight, lm_head.weight, in any
+ * syn_qformat_t (as syn_cuda_weight_upload). INT8 weights make the layer
+ * run the reference's W8A8 QuantizedDecoderLayer; block formats run the f32
+ * DecoderLayer semantics. */
+syn_status_t syn_cuda_model_set_linear(syn_cuda_model_t *m, const char *name,
+                                       syn_qformat_t fmt, const void *host, size_t n,
+                                       size_t k, const float *scales_or_null);
+/* Uploads and repacks everything (Q/K/V and gate/up fused along N) and
+ * allocates the KV cache. Synchronous. */
+syn_status_t syn_cuda_model_finalize(syn_cuda_model_t *m);
+/* forward_prefill (int8.rs:593-634) of sequence `seq` (must be empty):
+ * host tokens [n]; writes the greedy next token and, when logits_host is
+ * non-NULL, the last token's logits [vocab]. Synchronous. */
+syn_status_t syn_cuda_prefill(syn_cuda_model_t *m, size_t seq,
+                              const int32_t *tokens, size_t n,
+                              float *logits_host, int32_t *next_token);
+/* forward_one (int8.rs:637-709) of sequences [0, batch), one token each
+ * (host last_tokens[batch]); writes the greedy tokens and optionally the
+ * logits [batch, vocab]. Replays a CUDA graph of the whole step after the
+ * first call for a batch size. Synchronous. */
+syn_status_t syn_cuda_decode_step(syn_cuda_model_t *m, size_t batch,
+                                  const int32_t *last_tokens, int32_t *out_tokens,
+                                  float *logits_host);
+syn_status_t syn_cuda_model_seq_len(const syn_cuda_model_t *m, size_t seq, size_t *len);
+syn_status_t syn_cuda_model_reset(syn_cuda_model_t *m, size_t seq);
+syn_status_t syn_cuda_model_truncate(syn_cuda_model_t *m, size_t seq, size_t new_len);
+syn_status_t syn_cuda_model_destroy(syn_cuda_model_t *m);
+
 #ifdef __cplusplus
 }
 #endif

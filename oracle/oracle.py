@@ -39,6 +39,20 @@ def _load(fast=False):
         lib.orc_dequant.argtypes = [ctypes.c_int, vp, sz, vp]
         lib.orc_sgemm_nt.argtypes = [sz, sz, sz, vp, sz, vp, sz, vp, sz]
         lib.orc_block_matmul.argtypes = [ctypes.c_int, sz, sz, sz, vp, vp, vp, vp]
+        f32 = ctypes.c_float
+        lib.orc_exp.restype = f32
+        lib.orc_exp.argtypes = [f32]
+        lib.orc_rmsnorm.argtypes = [vp, vp, sz, sz, f32, vp]
+        lib.orc_rope_tables.argtypes = [ctypes.c_double, sz, sz, vp, vp]
+        lib.orc_rope_inplace.argtypes = [vp, vp, vp, sz, sz, sz, sz]
+        lib.orc_softmax.argtypes = [vp, sz]
+        lib.orc_sgemm_nn.argtypes = [sz, sz, sz, vp, sz, vp, sz, vp, sz]
+        lib.orc_attention_decode.argtypes = [vp, vp, vp, sz, sz, sz, sz, sz, vp]
+        lib.orc_fused_attention.argtypes = [sz, sz, sz, vp, vp, vp, vp]
+        lib.orc_silu_mul.argtypes = [vp, vp, sz, vp]
+        lib.orc_swiglu.argtypes = [vp, vp, sz, vp]
+        lib.orc_argmax.restype = ctypes.c_uint32
+        lib.orc_argmax.argtypes = [vp, sz]
         _LIBS[name] = lib
     return _LIBS[name]
 
@@ -121,3 +135,79 @@ def block_matmul(fmt, m, n, k, x, blocks):
     if st:
         return st, None
     return sgemm_nt(m, n, k, x, w)
+
+
+# ---- language-model epilogues (synapse_oracle_lm.c) ----------------------
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def exp32(x):
+    return _load().orc_exp(float(x))
+
+
+def rmsnorm(x, w, h, eps, fast=True):
+    x = _f32(x)
+    out = np.empty_like(x)
+    _load(fast).orc_rmsnorm(_p(x), _p(_f32(w)), x.size // h, h, eps, _p(out))
+    return out
+
+
+def rope_tables(base, max_pos, hd):
+    c = np.empty(max_pos * (hd // 2), dtype=np.float32)
+    s = np.empty_like(c)
+    _load().orc_rope_tables(float(base), max_pos, hd, _p(c), _p(s))
+    return c, s
+
+
+def rope_inplace(qk, cos_t, sin_t, seq, heads, hd, pos_off, fast=True):
+    assert qk.dtype == np.float32 and qk.flags.c_contiguous
+    _load(fast).orc_rope_inplace(_p(qk), _p(cos_t), _p(sin_t), seq, heads, hd, pos_off)
+
+
+def softmax(x):
+    x = _f32(x).copy()
+    _load().orc_softmax(_p(x), x.size)
+    return x
+
+
+def sgemm_nn(m, n, k, a, b, fast=False):
+    a, b = _f32(a), _f32(b)
+    c = np.empty(m * n, dtype=np.float32)
+    st = _load(fast).orc_sgemm_nn(m, n, k, _p(a), k, _p(b), n, _p(c), n)
+    return st, c
+
+
+def attention_decode(q, kc, vc, length, n_heads, n_kv, hd, window=0, fast=True):
+    q, kc, vc = _f32(q), _f32(kc), _f32(vc)
+    out = np.empty(n_heads * hd, dtype=np.float32)
+    _load(fast).orc_attention_decode(_p(q), _p(kc), _p(vc), length, n_heads, n_kv, hd,
+                                     window, _p(out))
+    return out
+
+
+def fused_attention(seq_q, seq_k, hd, q, k, v, fast=True):
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.empty(seq_q * hd, dtype=np.float32)
+    st = _load(fast).orc_fused_attention(seq_q, seq_k, hd, _p(q), _p(k), _p(v), _p(out))
+    return st, out
+
+
+def silu_mul(g, u):
+    g, u = _f32(g), _f32(u)
+    out = np.empty_like(g)
+    _load().orc_silu_mul(_p(g), _p(u), g.size, _p(out))
+    return out
+
+
+def swiglu(g, u):
+    g, u = _f32(g), _f32(u)
+    out = np.empty_like(g)
+    _load().orc_swiglu(_p(g), _p(u), g.size, _p(out))
+    return out
+
+
+def argmax(x):
+    x = _f32(x)
+    return int(_load().orc_argmax(_p(x), x.size))

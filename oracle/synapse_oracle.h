@@ -94,6 +94,37 @@ int orc_sgemm_nt(size_t m, size_t n, size_t k, const float *a, size_t lda,
 int orc_block_matmul(int fmt, size_t m, size_t n, size_t k, const float *x,
                      const uint8_t *w_blocks, float *w_f32, float *y);
 
+/* ---- language-model epilogues (synapse_oracle_lm.c) ---- */
+
+/* exp evaluated in double, rounded once to float (stand-in for the
+ * reference's f32 exp on both sides of every parity check). */
+float orc_exp(float x);
+/* ops/norm.rs:8-37 with vecHsum (zig/src/ffi/exports.zig:503-514). */
+void orc_rmsnorm(const float *x, const float *w, size_t rows, size_t h, float eps,
+                 float *out);
+/* models/lm/builder.rs:88-133 (no RoPE scaling). */
+void orc_rope_tables(double base, size_t max_pos, size_t hd, float *cos_t, float *sin_t);
+/* ops/rope.rs:13-60, RotateHalf. */
+void orc_rope_inplace(float *qk, const float *cos_t, const float *sin_t, size_t seq,
+                      size_t heads, size_t hd, size_t pos_off);
+/* ops/activation.rs:117-130. */
+void orc_softmax(float *x, size_t n);
+/* matmul_nn (ops/matmul.rs:82-101) -> sgemmTiled(trans_b=0). */
+int orc_sgemm_nn(size_t m, size_t n, size_t k, const float *a, size_t lda, const float *b,
+                 size_t ldb, float *c, size_t ldc);
+/* ops/attention.rs:70-147 (after the cache append); window 0 = none. */
+void orc_attention_decode(const float *q, const float *kc, const float *vc, size_t len,
+                          size_t n_heads, size_t n_kv, size_t hd, size_t window, float *out);
+/* syn_fused_attention (zig/src/ffi/exports.zig:1364-1478). */
+int orc_fused_attention(size_t seq_q, size_t seq_k, size_t hd, const float *q, const float *k,
+                        const float *v, float *out);
+/* quantization/lm/int8.rs:500-503. */
+void orc_silu_mul(const float *g, const float *u, size_t n, float *out);
+/* zig/src/ops/silu.zig:85-114. */
+void orc_swiglu(const float *g, const float *u, size_t n, float *out);
+/* generation/sampler.rs:217-224. */
+uint32_t orc_argmax(const float *x, size_t n);
+
 #ifdef __cplusplus
 }
 #endif

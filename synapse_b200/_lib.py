@@ -35,6 +35,46 @@ SIGNATURES = {
     "syn_cuda_qmatmul": (c_st, [c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
     "syn_cuda_qmatmul_int8_prequant": (c_st, [c_vp, c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
     "syn_cuda_qmatmul_noalloc": (c_st, [c_vp, c_vp, c_size, c_vp, c_vp]),
+    "syn_cuda_rope_tables": (c_st, [ctypes.c_double, c_size, c_size, c_vp, c_vp]),
+    "syn_cuda_rmsnorm": (c_st, [c_vp, c_vp, c_size, c_size, ctypes.c_float, c_vp, c_vp]),
+    "syn_cuda_add_rmsnorm": (c_st, [c_vp, c_vp, c_vp, c_size, c_size, ctypes.c_float, c_vp,
+                                    c_vp]),
+    "syn_cuda_embed_rmsnorm": (c_st, [c_vp, c_size, c_vp, c_size, c_size, c_vp, ctypes.c_float,
+                                      c_vp, c_vp, c_vp]),
+    "syn_cuda_kvcache_create": (c_st, [c_vp, c_size, c_size, c_size, c_size, c_size,
+                                       ctypes.POINTER(c_vp)]),
+    "syn_cuda_kvcache_destroy": (c_st, [c_vp]),
+    "syn_cuda_kvcache_len": (c_st, [c_vp, c_size, ctypes.POINTER(c_size)]),
+    "syn_cuda_kvcache_view": (c_st, [c_vp, c_size, c_size, ctypes.POINTER(c_vp),
+                                     ctypes.POINTER(c_vp)]),
+    "syn_cuda_kvcache_append": (c_st, [c_vp, c_size, c_size, c_vp, c_vp, c_size, c_vp]),
+    "syn_cuda_kvcache_advance": (c_st, [c_vp, c_size, c_size, c_vp]),
+    "syn_cuda_kvcache_truncate": (c_st, [c_vp, c_size, c_size, c_vp]),
+    "syn_cuda_kvcache_reset": (c_st, [c_vp, c_size, c_vp]),
+    "syn_cuda_attention_decode": (c_st, [c_vp, c_size, c_size, c_vp, c_vp, c_vp, c_size, c_size,
+                                         c_vp, c_vp, ctypes.c_float, c_vp, c_vp, c_size, c_vp,
+                                         c_size, c_vp]),
+    "syn_cuda_qk_norm_rope_kv_append": (c_st, [c_vp, c_size, c_size, c_size, c_vp, c_vp, c_vp,
+                                               c_size, c_size, c_vp, c_vp, ctypes.c_float, c_vp,
+                                               c_vp, c_vp]),
+    "syn_cuda_attention_prefill": (c_st, [c_vp, c_size, c_size, c_size, c_vp, c_vp, c_vp, c_size,
+                                          c_size, c_vp, c_vp, ctypes.c_float, c_vp, c_vp, c_vp,
+                                          c_size, c_vp]),
+    "syn_cuda_swiglu": (c_st, [c_vp, c_vp, c_size, c_size, c_size, ctypes.c_int, c_vp, c_size,
+                               c_vp]),
+    "syn_cuda_argmax": (c_st, [c_vp, c_size, c_size, c_vp, c_vp]),
+    "syn_cuda_model_create": (c_st, [c_vp, ctypes.c_char_p, c_size, c_size,
+                                     ctypes.POINTER(c_vp)]),
+    "syn_cuda_model_set_tensor": (c_st, [c_vp, ctypes.c_char_p, c_vp, c_size]),
+    "syn_cuda_model_set_linear": (c_st, [c_vp, ctypes.c_char_p, ctypes.c_int, c_vp, c_size,
+                                         c_size, c_vp]),
+    "syn_cuda_model_finalize": (c_st, [c_vp]),
+    "syn_cuda_prefill": (c_st, [c_vp, c_size, c_vp, c_size, c_vp, c_vp]),
+    "syn_cuda_decode_step": (c_st, [c_vp, c_size, c_vp, c_vp, c_vp]),
+    "syn_cuda_model_seq_len": (c_st, [c_vp, c_size, ctypes.POINTER(c_size)]),
+    "syn_cuda_model_reset": (c_st, [c_vp, c_size]),
+    "syn_cuda_model_truncate": (c_st, [c_vp, c_size, c_size]),
+    "syn_cuda_model_destroy": (c_st, [c_vp]),
 }
 
 

@@ -284,3 +284,278 @@ class QuantizedLinear:
 
     def memory_bytes(self):
         return self.weights_int8.size + 4 * self.scales.size
+
+
+# ---------------------------------------------------------------------------
+# Decoder-layer kernels (lm.cu) on torch CUDA tensors
+# ---------------------------------------------------------------------------
+
+def rope_tables(base, max_pos, head_dim):
+    """precompute_rope_tables (models/lm/builder.rs:88-133): (cos, sin) numpy
+    [max_pos, head_dim/2] computed on the host."""
+    import numpy as np
+    c = np.empty((max_pos, head_dim // 2), dtype=np.float32)
+    s = np.empty_like(c)
+    _check(lib().syn_cuda_rope_tables(float(base), max_pos, head_dim,
+                                      c.ctypes.data_as(ctypes.c_void_p),
+                                      s.ctypes.data_as(ctypes.c_void_p)), "rope_tables")
+    return c, s
+
+
+def rmsnorm(x, weight, eps, out=None):
+    """rmsnorm (ops/norm.rs:8-37) over the last dimension."""
+    _need_cuda(x, weight)
+    h = weight.numel()
+    out = torch.empty_like(x) if out is None else out
+    _check(lib().syn_cuda_rmsnorm(_ptr(x), _ptr(weight), x.numel() // h, h, float(eps), _ptr(out),
+                                  _stream(x)), "rmsnorm")
+    return out
+
+
+def add_rmsnorm(residual, delta, weight, eps, out=None):
+    """residual += delta; returns rmsnorm(residual)."""
+    _need_cuda(residual, delta, weight)
+    h = weight.numel()
+    out = torch.empty_like(residual) if out is None else out
+    _check(lib().syn_cuda_add_rmsnorm(_ptr(residual), _ptr(delta), _ptr(weight),
+                                      residual.numel() // h, h, float(eps), _ptr(out),
+                                      _stream(residual)), "add_rmsnorm")
+    return out
+
+
+def swiglu(gate, up, variant=0):
+    """variant 0: silu(g)*u (INT8 model); 1: syn_swiglu (f32 model)."""
+    _need_cuda(gate, up)
+    n = gate.shape[-1]
+    rows = gate.numel() // n
+    out = torch.empty_like(gate)
+    _check(lib().syn_cuda_swiglu(_ptr(gate), _ptr(up), n, rows, n, int(variant), _ptr(out), n,
+                                 _stream(gate)), "swiglu")
+    return out
+
+
+def argmax(logits):
+    """Greedy argmax per row (generation/sampler.rs:217-224)."""
+    _need_cuda(logits)
+    n = logits.shape[-1]
+    rows = logits.numel() // n
+    out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    _check(lib().syn_cuda_argmax(_ptr(logits), rows, n, _ptr(out), _stream(logits)), "argmax")
+    return out
+
+
+class KVCache:
+    """KV cache in HBM (syn_cuda_kvcache_*; kvcache.zig:13-170)."""
+
+    def __init__(self, ctx, max_seq, n_kv_heads, head_dim, num_layers, batch=1):
+        self.max_seq, self.n_kv, self.hd = max_seq, n_kv_heads, head_dim
+        self.layers, self.batch = num_layers, batch
+        h = ctypes.c_void_p()
+        _check(lib().syn_cuda_kvcache_create(ctx.handle, max_seq, n_kv_heads, head_dim,
+                                             num_layers, batch, ctypes.byref(h)),
+               "kvcache_create")
+        self.handle = h
+
+    def length(self, seq=0):
+        v = ctypes.c_size_t()
+        _check(lib().syn_cuda_kvcache_len(self.handle, seq, ctypes.byref(v)), "kvcache_len")
+        return v.value
+
+    def view(self, layer, seq=0):
+        """(K, V) torch views [max_seq, n_kv*hd] of one layer and sequence."""
+        k, v = ctypes.c_void_p(), ctypes.c_void_p()
+        _check(lib().syn_cuda_kvcache_view(self.handle, layer, seq, ctypes.byref(k),
+                                           ctypes.byref(v)), "kvcache_view")
+        n = self.max_seq * self.n_kv * self.hd
+        return _wrap_device(k.value, n, (self.max_seq, self.n_kv * self.hd)), \
+            _wrap_device(v.value, n, (self.max_seq, self.n_kv * self.hd))
+
+    def append(self, layer, k, v, seq=0):
+        _need_cuda(k, v)
+        n = k.numel() // (self.n_kv * self.hd)
+        _check(lib().syn_cuda_kvcache_append(self.handle, layer, seq, _ptr(k), _ptr(v), n,
+                                             _stream(k)), "kvcache_append")
+
+    def advance(self, n, seq=0):
+        _check(lib().syn_cuda_kvcache_advance(self.handle, seq, n,
+                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+               "kvcache_advance")
+
+    def truncate(self, new_len, seq=0):
+        _check(lib().syn_cuda_kvcache_truncate(self.handle, seq, new_len,
+                                               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+               "kvcache_truncate")
+
+    def reset(self, seq=0):
+        _check(lib().syn_cuda_kvcache_reset(self.handle, seq,
+                                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+               "kvcache_reset")
+
+    def close(self):
+        if self.handle:
+            lib().syn_cuda_kvcache_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _wrap_device(addr, numel, shape):
+    """A torch view of library-owned device memory (no copy, no ownership)."""
+    class _Iface:
+        pass
+    it = _Iface()
+    it.__cuda_array_interface__ = {"shape": (numel,), "typestr": "<f4", "data": (addr, False),
+                                   "version": 3, "strides": None}
+    return torch.as_tensor(it, device="cuda").view(*shape)
+
+
+def attention_decode(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, sin_t, window=0,
+                     batch=1):
+    """cached_attention_decode (ops/attention.rs:24-147) for sequences
+    [0, batch); qkv rows [q | k | v] (row stride = its last dim). Returns
+    [batch, n_heads*hd]; the cache length is not advanced."""
+    _need_cuda(qkv, cos_t, sin_t)
+    ld = qkv.shape[-1]
+    qd, kvd = n_heads * cache.hd, cache.n_kv * cache.hd
+    out = torch.empty(batch, qd, dtype=torch.float32, device=qkv.device)
+    base = qkv.data_ptr()
+    _check(lib().syn_cuda_attention_decode(
+        cache.handle, layer, batch, ctypes.c_void_p(base), ctypes.c_void_p(base + 4 * qd),
+        ctypes.c_void_p(base + 4 * (qd + kvd)), ld, n_heads, _ptr(q_norm), _ptr(k_norm),
+        float(eps), _ptr(cos_t), _ptr(sin_t), window, _ptr(out), qd, _stream(qkv)),
+        "attention_decode")
+    return out
+
+
+def attention_prefill(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, sin_t, seq=0):
+    """cached_attention_prefill (ops/attention.rs:153-247) for sequence
+    `seq`; qkv [n_tokens, q | k | v] (q rewritten in place). Returns
+    [n_tokens, n_heads*hd]; the cache length is not advanced."""
+    _need_cuda(qkv, cos_t, sin_t)
+    ld = qkv.shape[-1]
+    n = qkv.numel() // ld
+    qd, kvd = n_heads * cache.hd, cache.n_kv * cache.hd
+    out = torch.empty(n, qd, dtype=torch.float32, device=qkv.device)
+    base = qkv.data_ptr()
+    _check(lib().syn_cuda_attention_prefill(
+        cache.handle, layer, seq, n, ctypes.c_void_p(base), ctypes.c_void_p(base + 4 * qd),
+        ctypes.c_void_p(base + 4 * (qd + kvd)), ld, n_heads, _ptr(q_norm), _ptr(k_norm),
+        float(eps), _ptr(cos_t), _ptr(sin_t), _ptr(out), qd, _stream(qkv)), "attention_prefill")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Model runner (runner.cu): QuantizedCausalLM / CausalLM on the GPU
+# ---------------------------------------------------------------------------
+
+class Model:
+    """Decoder-only LM on the GPU (syn_cuda_model_*), mirroring
+    QuantizedCausalLM (quantization/lm/int8.rs:171-709) for INT8 weights and
+    CausalLM (models/lm/causal_lm.rs:195-280) for the block formats.
+
+    config: the reference's model config (dict or JSON text). weights: name ->
+    numpy f32 array (norms, embedding) or a linear spec
+    ("INT8_KN", q_kn int8 [K*N], scales [N]) / (fmt_name, block bytes).
+    """
+
+    def __init__(self, ctx, config, weights, max_seq, max_batch=1):
+        import json
+        import numpy as np
+        cfg = json.loads(config) if isinstance(config, str) else config
+        self.ctx = ctx
+        self.cfg = cfg
+        a, at = cfg["architecture"], cfg["attention"]
+        self.vocab = a["vocab_size"]
+        self.max_seq, self.max_batch = max_seq, max_batch
+        h = ctypes.c_void_p()
+        _check(lib().syn_cuda_model_create(ctx.handle, json.dumps(cfg).encode(), max_seq,
+                                           max_batch, ctypes.byref(h)), "model_create")
+        self.handle = h
+        hd = at["head_dim"]
+        qd, kvd = at["num_heads"] * hd, at["num_kv_heads"] * hd
+        hid, ff = a["hidden_size"], cfg["ffn"]["intermediate_size"]
+        shapes = {"q_proj": (qd, hid), "k_proj": (kvd, hid), "v_proj": (kvd, hid),
+                  "o_proj": (hid, qd), "gate_proj": (ff, hid), "up_proj": (ff, hid),
+                  "down_proj": (hid, ff)}
+        for name, val in weights.items():
+            if isinstance(val, tuple):
+                if name == "lm_head.weight":
+                    n, k = self.vocab, hid
+                else:
+                    n, k = shapes[name.split(".")[-2]]
+                fmt = QFormat[val[0]] if isinstance(val[0], str) else QFormat(val[0])
+                buf = np.ascontiguousarray(np.asarray(val[1]).view(np.uint8).reshape(-1))
+                sc = None
+                if fmt == QFormat.INT8_KN:
+                    sc = np.ascontiguousarray(np.asarray(val[2], dtype=np.float32))
+                _check(lib().syn_cuda_model_set_linear(
+                    self.handle, name.encode(), int(fmt), buf.ctypes.data_as(ctypes.c_void_p), n,
+                    k, sc.ctypes.data_as(ctypes.c_void_p) if sc is not None else None),
+                    "model_set_linear " + name)
+            else:
+                arr = np.ascontiguousarray(np.asarray(val, dtype=np.float32).reshape(-1))
+                _check(lib().syn_cuda_model_set_tensor(self.handle, name.encode(),
+                                                       arr.ctypes.data_as(ctypes.c_void_p),
+                                                       arr.size), "model_set_tensor " + name)
+        _check(lib().syn_cuda_model_finalize(self.handle), "model_finalize")
+
+    def forward_prefill(self, token_ids, seq=0, want_logits=True):
+        """Prefill of an empty sequence; returns (greedy next token, logits or None)."""
+        import numpy as np
+        ids = np.ascontiguousarray(np.asarray(token_ids, dtype=np.int32))
+        nxt = ctypes.c_int32()
+        logits = np.empty(self.vocab, dtype=np.float32) if want_logits else None
+        _check(lib().syn_cuda_prefill(self.handle, seq, ids.ctypes.data_as(ctypes.c_void_p),
+                                      ids.size,
+                                      logits.ctypes.data_as(ctypes.c_void_p) if want_logits else None,
+                                      ctypes.byref(nxt)), "prefill")
+        return nxt.value, logits
+
+    def forward_one(self, tokens, want_logits=True):
+        """One decode step of sequences [0, len(tokens)); returns (greedy
+        tokens, logits [batch, vocab] or None)."""
+        import numpy as np
+        ids = np.ascontiguousarray(np.atleast_1d(np.asarray(tokens, dtype=np.int32)))
+        b = ids.size
+        out = np.empty(b, dtype=np.int32)
+        logits = np.empty((b, self.vocab), dtype=np.float32) if want_logits else None
+        _check(lib().syn_cuda_decode_step(self.handle, b, ids.ctypes.data_as(ctypes.c_void_p),
+                                          out.ctypes.data_as(ctypes.c_void_p),
+                                          logits.ctypes.data_as(ctypes.c_void_p) if want_logits
+                                          else None), "decode_step")
+        return out, logits
+
+    def generate_greedy(self, prompt, steps, seq=0):
+        """generation/pipeline.rs:197-280 with GreedySampler (single sequence)."""
+        tok, _ = self.forward_prefill(prompt, seq, want_logits=False)
+        toks = [tok]
+        while len(toks) < steps:
+            nxt, _ = self.forward_one([toks[-1]], want_logits=False)
+            toks.append(int(nxt[0]))
+        return toks
+
+    def seq_len(self, seq=0):
+        v = ctypes.c_size_t()
+        _check(lib().syn_cuda_model_seq_len(self.handle, seq, ctypes.byref(v)), "model_seq_len")
+        return v.value
+
+    def reset(self, seq=0):
+        _check(lib().syn_cuda_model_reset(self.handle, seq), "model_reset")
+
+    def truncate(self, new_len, seq=0):
+        _check(lib().syn_cuda_model_truncate(self.handle, seq, new_len), "model_truncate")
+
+    def close(self):
+        if self.handle:
+            lib().syn_cuda_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

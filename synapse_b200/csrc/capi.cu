@@ -36,23 +36,6 @@ int num_sms() {
 
 namespace {
 
-// Keeps the caller's current device, switching to `dev` for the call.
-struct DeviceGuard {
-  int prev = -1;
-  bool ok = true;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) {
-      ok = false;
-      return;
-    }
-    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-  }
-};
-
 size_t block_elems(int fmt) {
   switch (fmt) {
     case SYN_QFMT_Q4_0:

@@ -15,7 +15,8 @@
 //       reference's per-512-K-chunk epilogue C += float(chunk) * sa * sb in
 //       chunk order (qmatmul.zig:68-98), every op rounded -- bit-exact for
 //       every M.
-//     Block formats: A = fp16(x); the weights are dequantised in shared
+//     Block formats: A = fp16(x * 2^-s) with a power-of-two scale per row (no
+//       fp16 overflow; undone exactly in the epilogue); the weights are dequantised in shared
 //       memory with the reference's formulas (gguf.rs:255-487), rounded to
 //       fp16 and multiplied with kind::f16, fp32 accumulation.
 //   B (weights) comes from the row-interleaved repack (repack.cu). For INT8
@@ -472,9 +473,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int n0 = nt * BN + cg * 32;
         if (tok < p.m) {
           float* yr = p.y + (long long)tok * p.ldy;
+          const float rs = p.sa[tok];  // 2^s of the row's fp16 scaling
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            if (n0 + j < p.n) yr[n0 + j] = __uint_as_float(r[j]);
+            if (n0 + j < p.n) yr[n0 + j] = __fmul_rn(__uint_as_float(r[j]), rs);
         }
       }
     } else {
@@ -605,21 +607,44 @@ __global__ void __launch_bounds__(256) k_prep_a_i8(const float* __restrict__ x,
   }
 }
 
-// Block formats: fp16(x).
+// Block formats: fp16(x * 2^-s) per row, with the power of two s chosen so
+// that the row's largest magnitude lands in [2^14, 2^15): no fp16 overflow
+// and full fp16 precision whatever the activations' range. The scaling is
+// exact; the epilogue multiplies the row's accumulators by 2^s (sa[row]).
 __global__ void __launch_bounds__(256) k_prep_a_f16(const float* __restrict__ x, long long ldx,
                                                     int m, int k, int kcols,
-                                                    uint8_t* __restrict__ a) {
+                                                    uint8_t* __restrict__ a,
+                                                    float* __restrict__ sa) {
+  __shared__ float red[8];
   griddep_wait();
   griddep_launch();
   const int row = blockIdx.x;
   const int mt = row >> 7, rr = row & 127;
+  float inv = 1.0f;
+  if (row < m) {
+    const float* xr = x + (long long)row * ldx;
+    float amax = 0.0f;
+    for (int i = threadIdx.x; i < k; i += 256) amax = fmaxf(amax, fabsf(xr[i]));
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+    for (int w = 1; w < 8; w++) amax = fmaxf(amax, red[w]);
+    int ex = 0;
+    if (amax > 0.0f && amax <= 3.0e38f) {
+      frexpf(amax, &ex);  // amax < 2^ex
+      ex -= 15;
+    }
+    inv = ldexpf(1.0f, -ex);
+    if (threadIdx.x == 0) sa[row] = ldexpf(1.0f, ex);
+  }
   for (int c = threadIdx.x; c < kcols; c += 256) {
     uint32_t wv[4] = {0, 0, 0, 0};
     if (row < m) {
 #pragma unroll
       for (int e = 0; e < 8; e++) {
         const int kk = c * 8 + e;
-        const float v = kk < k ? x[(long long)row * ldx + kk] : 0.0f;
+        const float v = kk < k ? __fmul_rn(x[(long long)row * ldx + kk], inv) : 0.0f;
         wv[e >> 1] |= (uint32_t)__half_as_ushort(__float2half_rn(v)) << (16 * (e & 1));
       }
     }
@@ -729,7 +754,7 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
                     (int)m, (int)w->k, kcols, a, sa);
   else
     e = launch_pdl2(k_prep_a_f16, dim3(mtiles * BM), dim3(256), 0, st, x, (long long)ldx, (int)m,
-                    (int)w->k, kcols, a);
+                    (int)w->k, kcols, a, sa);
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_prep_a");
     return SYN_ERR_CUDA;

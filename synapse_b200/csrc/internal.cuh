@@ -41,7 +41,40 @@ struct syn_cuda_weight_s {
   int8_t* sc;
 };
 
+// KV cache in HBM (zig/src/ops/kvcache.zig:13-170, kv_cache/cache.rs:26-340):
+// per layer and sequence, K and V rows of n_kv*hd f32 for max_seq positions.
+// One length per sequence, shared by all layers (LayerCaches advance, reset
+// and truncate together). The device copy of the lengths is what kernels
+// read (so that a captured graph replays at the current position); the host
+// copy mirrors it for the CacheFull check.
+struct syn_cuda_kvcache_s {
+  int device;
+  size_t max_seq, n_kv, hd, layers, batch;
+  float* k;     // [layers][batch][max_seq][n_kv*hd]
+  float* v;
+  int* d_len;   // [batch]
+  size_t* len;  // [batch], host mirror
+};
+
 namespace syn {
+
+// Makes `dev` current for the scope and restores the previous device.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      ok = false;
+      return;
+    }
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 
 // Scratch of a GEMV over m activation rows: partial sums (0 when K is not
 // split across CTAs) and per-row-group arrival counters (zero before the
@@ -84,5 +117,54 @@ syn_status_t launch_quantize_weights(const float* w, size_t n, size_t k, int8_t*
 syn_status_t repack_weight(syn_cuda_weight_s* w, const uint8_t* d_src, size_t ld_src,
                            const float* d_scales, cudaStream_t st);
 syn_status_t dequant_weight(const syn_cuda_weight_s* w, float* d_out, cudaStream_t st);
+
+// ---- decoder-layer kernels (lm.cu) ----
+// Residual add + RMSNorm: row r of out = rmsnorm(src_r (+ delta_r)), where
+// src_r is x_r or, when ids != nullptr, the embedding row table[ids[r]]
+// (zeros for ids outside the vocabulary). x_out (optional) receives the
+// normalised input (the updated residual stream); it may alias x.
+syn_status_t launch_add_rmsnorm(const float* x, size_t ldx, const float* delta, size_t ldd,
+                                const int32_t* ids, const float* table, size_t vocab,
+                                float* x_out, size_t ldxo, const float* w, size_t rows, size_t h,
+                                float eps, float* out, size_t ldo, cudaStream_t st);
+
+// Attention over the KV cache. q/k/v rows have stride ld (row b = sequence b
+// for decode, token t for prefill); out rows have stride ldo.
+struct AttnArgs {
+  float* q;
+  const float* k;
+  const float* v;
+  size_t ld;
+  size_t n_heads;
+  const float* qn;  // headwise norm weights or nullptr
+  const float* kn;
+  float eps;
+  const float* cos_t;
+  const float* sin_t;
+  size_t window;    // 0 = none
+  syn_cuda_kvcache_t* cache;
+  size_t layer;
+  float* out;
+  size_t ldo;
+};
+// Decode step of sequences [0, batch): norm/RoPE/append of the new token,
+// attention over positions [0, len] (the cache lengths are not advanced).
+syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, cudaStream_t st);
+// Prefill of ntok prompt tokens of sequence `seq` (appended from its current
+// length; RoPE at offsets 0..ntok-1 as the reference's prefill).
+syn_status_t launch_attn_prefill_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                      cudaStream_t st);
+// The two halves of the prefill: norm/RoPE/append, then attention.
+syn_status_t launch_norm_rope_append_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                          cudaStream_t st);
+syn_status_t launch_prefill_attention_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                           cudaStream_t st);
+syn_status_t launch_swiglu(const float* gate, const float* up, size_t ld_in, size_t rows, size_t n,
+                           int variant, float* out, size_t ldo, cudaStream_t st);
+// Greedy argmax per row; when len_adv != nullptr, len_adv[row] += adv after.
+syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
+                           int* len_adv, int adv, int max_len, cudaStream_t st);
+// Device length of sequence seq: set to value (add=0) or advanced by it.
+syn_status_t launch_kv_set(syn_cuda_kvcache_t* c, size_t seq, int value, int add, cudaStream_t st);
 
 }  // namespace syn

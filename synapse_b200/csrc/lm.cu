@@ -1,0 +1,980 @@
+// lm.cu -- the decoder-layer kernels around the quantized matmuls: RMSNorm
+// (fused with the residual add and, for layer 0, the embedding gather),
+// headwise q/k RMSNorm + RoPE + KV-cache append, cached GQA attention
+// (decode, fused with the norm/RoPE/append of its own heads; prefill), SwiGLU
+// and greedy argmax.
+//
+// Every reduction follows the reference's order, so that a greedy decode
+// reproduces the reference's token ids:
+//   * RMSNorm sums x*x in four lane accumulators of stride 4, adds the lanes
+//     in order, then the tail (vecHsum, zig/src/ffi/exports.zig:503-514);
+//   * attention dot products and weighted sums are sequential chains over the
+//     head dimension / positions, with fused multiply-add exactly where the
+//     reference's f32 GEMV/GEMM uses @mulAdd (zig/src/ops/matmul.zig:
+//     223-343, 452-515) and a rounded multiply then add where it writes
+//     `sum += a * b` (ops/attention.rs:118-144, the edge tiles);
+//   * the softmax sum is sequential (ops/activation.rs:117-130); the prefill
+//     online softmax keeps the reference's running (max, sum) recurrence
+//     (exports.zig:1420-1436), with the exponentials evaluated in parallel
+//     once the running maxima are known (a prefix-max scan);
+//   * exp is evaluated in double and rounded once to float (the correctly
+//     rounded expf except in rare ties), the same function as the CPU oracle.
+// Long-context attention therefore runs on the CUDA cores as sequential
+// chains; its cost is latency of the chain, not bandwidth.
+#include <math.h>
+
+#include <algorithm>
+#include <mutex>
+#include <new>
+#include <set>
+
+#include "internal.cuh"
+
+namespace syn {
+namespace {
+
+__device__ __forceinline__ float exp_f32(float x) { return (float)exp((double)x); }
+
+// one step of a sum-of-products chain: fused (@mulAdd) or two roundings
+__device__ __forceinline__ float chain(bool fused, float a, float b, float acc) {
+  return fused ? __fmaf_rn(a, b, acc) : __fadd_rn(acc, __fmul_rn(a, b));
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+syn_status_t allow_smem(const void* fn, size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  if (bytes <= 48 * 1024) return SYN_OK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> g(mu);
+  if (done.count({fn, dev})) return SYN_OK;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "cudaFuncSetAttribute");
+    return SYN_ERR_CUDA;
+  }
+  done.insert({fn, dev});
+  return SYN_OK;
+}
+
+constexpr size_t kMaxSmem = 200 * 1024;
+
+// ---------------------------------------------------------------------------
+// RMSNorm, fused with the residual add / embedding gather
+// ---------------------------------------------------------------------------
+constexpr int NORM_THREADS = 256;
+
+struct NormParams {
+  const float* x;      // input rows (unused when ids != nullptr)
+  long long ldx;
+  const float* delta;  // optional: x + delta is normalised (and stored in x_out)
+  long long ldd;
+  const int32_t* ids;  // optional: rows are embedding rows table[ids[r]]
+  const float* table;
+  unsigned vocab;
+  float* x_out;        // optional: the (residual) input row actually normalised
+  long long ldxo;
+  const float* w;
+  int h;
+  float eps;
+  float* out;
+  long long ldo;
+};
+
+// sum of squares in the reference's order; every thread returns the same value
+__device__ float norm_scale(const float* sx, int h, float eps, float* lane) {
+  if (threadIdx.x < 4) {
+    const int n4 = h & ~3;
+    float acc = 0.0f;
+    for (int i = threadIdx.x; i < n4; i += 4) acc = __fadd_rn(acc, __fmul_rn(sx[i], sx[i]));
+    lane[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(lane[0], lane[1]), lane[2]), lane[3]);
+  for (int i = h & ~3; i < h; i++) s = __fadd_rn(s, __fmul_rn(sx[i], sx[i]));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)h), eps)));
+}
+
+__global__ void __launch_bounds__(NORM_THREADS) k_add_rmsnorm(const NormParams p) {
+  extern __shared__ float sx[];
+  __shared__ float lane[4];
+  griddep_wait();
+  const int row = blockIdx.x;
+  const float* src = p.x + row * p.ldx;
+  bool zero = false;
+  if (p.ids) {
+    const unsigned id = (unsigned)p.ids[row];
+    zero = id >= p.vocab;  // ids outside the vocabulary embed as zeros
+    src = p.table + (size_t)(zero ? 0 : id) * p.h;
+  }
+  for (int j = threadIdx.x; j < p.h; j += NORM_THREADS) {
+    float v = zero ? 0.0f : src[j];
+    if (p.delta) v = __fadd_rn(v, p.delta[row * p.ldd + j]);
+    sx[j] = v;
+    if (p.x_out) p.x_out[row * p.ldxo + j] = v;
+  }
+  __syncthreads();
+  const float scale = norm_scale(sx, p.h, p.eps, lane);
+  griddep_launch();
+  for (int j = threadIdx.x; j < p.h; j += NORM_THREADS)
+    p.out[row * p.ldo + j] = __fmul_rn(__fmul_rn(sx[j], p.w[j]), scale);
+}
+
+// ---------------------------------------------------------------------------
+// Shared by the attention kernels: where q/k/v rows live, the cache, RoPE
+// ---------------------------------------------------------------------------
+struct AttnParams {
+  float* q;            // q rows (row stride ld); prefill rewrites them in place
+  const float* k;      // k rows (row stride ld)
+  const float* v;      // v rows (row stride ld)
+  long long ld;
+  int n_heads, n_kv, hd;
+  const float* qn;     // optional headwise norm weights [hd]
+  const float* kn;
+  float eps;
+  const float* cos_t;  // [max_pos, hd/2]
+  const float* sin_t;
+  int window;          // 0 = none
+  float* kc;           // cache of this layer: [batch][max_seq][n_kv*hd]
+  float* vc;
+  int max_seq;
+  const int* len;      // [batch] positions already committed
+  int seq0;            // prefill: the sequence; decode: row b is sequence b
+  int n_tokens;        // prefill tokens
+  float* out;          // [rows][n_heads*hd]
+  long long ldo;
+  float scale;
+  int* err;
+};
+
+// Headwise RMSNorm of `nv` vectors of length hd in smem (x, in place), with
+// weight w (nullptr = identity), then RotateHalf RoPE at position pos
+// (ops/norm.rs:78-92, ops/rope.rs:13-60). `lanes`: 4*nv floats, `scl`: nv.
+__device__ void norm_rope(float* x, int nv, int hd, const float* wq, const float* wk, int nq,
+                          float eps, const float* cos_t, const float* sin_t, int pos,
+                          float* lanes, float* scl, int nthreads) {
+  const int tid = threadIdx.x;
+  for (int t = tid; t < 4 * nv; t += nthreads) {
+    const int vi = t >> 2, l = t & 3;
+    const float* xv = x + vi * hd;
+    float acc = 0.0f;
+    for (int i = l; i < (hd & ~3); i += 4) acc = __fadd_rn(acc, __fmul_rn(xv[i], xv[i]));
+    lanes[t] = acc;
+  }
+  __syncthreads();
+  for (int vi = tid; vi < nv; vi += nthreads) {
+    const float* xv = x + vi * hd;
+    const float* ln = lanes + 4 * vi;
+    float s = __fadd_rn(__fadd_rn(__fadd_rn(ln[0], ln[1]), ln[2]), ln[3]);
+    for (int i = hd & ~3; i < hd; i++) s = __fadd_rn(s, __fmul_rn(xv[i], xv[i]));
+    scl[vi] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)hd), eps)));
+  }
+  __syncthreads();
+  const int half = hd >> 1;
+  for (int t = tid; t < nv * half; t += nthreads) {
+    const int vi = t / half, i = t - vi * half;
+    float* xv = x + vi * hd;
+    const float* w = vi < nq ? wq : wk;
+    float x1 = xv[i], x2 = xv[half + i];
+    if (w) {
+      x1 = __fmul_rn(__fmul_rn(x1, w[i]), scl[vi]);
+      x2 = __fmul_rn(__fmul_rn(x2, w[half + i]), scl[vi]);
+    }
+    const float c = cos_t[(size_t)pos * half + i], s = sin_t[(size_t)pos * half + i];
+    xv[i] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    xv[half + i] = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// Decode: one CTA per (sequence, KV head); threads = group size * hd.
+// cached_attention_decode (ops/attention.rs:24-147) for the group's heads.
+// ---------------------------------------------------------------------------
+constexpr int MAX_GROUPS = 8;
+
+__global__ void __launch_bounds__(1024) k_attn_decode(const AttnParams p) {
+  extern __shared__ float sm[];
+  const int b = blockIdx.x, kvh = blockIdx.y;
+  const int G = p.n_heads / p.n_kv, hd = p.hd, kvd = p.n_kv * hd;
+  const int nt = blockDim.x, tid = threadIdx.x;
+  float* xs = sm;                      // (G+1) vectors: q heads, then k
+  float* lanes = xs + (G + 1) * hd;    // 4*(G+1)
+  float* scl = lanes + 4 * (G + 1);    // G+1
+  float* sc = scl + (G + 1);           // G * eff scores
+  griddep_wait();
+  const int pos = p.len[b];
+  if (pos >= p.max_seq) {  // cache full: nothing is written (the host reports it)
+    if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
+    return;
+  }
+  const float* qrow = p.q + (long long)b * p.ld + (long long)kvh * G * hd;
+  const float* krow = p.k + (long long)b * p.ld + (long long)kvh * hd;
+  const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * hd;
+  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * hd;
+  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * hd;
+  for (int i = tid; i < G * hd; i += nt) xs[i] = qrow[i];
+  for (int i = tid; i < hd; i += nt) {
+    xs[G * hd + i] = krow[i];
+    vcb[(size_t)pos * kvd + i] = vrow[i];  // raw V
+  }
+  __syncthreads();
+  norm_rope(xs, G + 1, hd, p.qn, p.kn, G, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, nt);
+  for (int i = tid; i < hd; i += nt) kcb[(size_t)pos * kvd + i] = xs[G * hd + i];
+  __syncthreads();  // the appended row is visible to the whole CTA
+
+  const int L = pos + 1;
+  const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
+  const int eff = L - off;
+  // scores: below 64 positions the reference's scalar loop (sum += a*b);
+  // from 64 on matmul_t: @mulAdd except the last eff%8 columns
+  const int s_full = eff < 64 ? 0 : eff - (eff & 7);
+  for (int s = tid; s < eff; s += nt) {
+    const float* kr = kcb + (size_t)(off + s) * kvd;
+    const bool fused = s < s_full;
+    float acc[MAX_GROUPS];
+#pragma unroll
+    for (int g = 0; g < MAX_GROUPS; g++) acc[g] = 0.0f;
+    for (int d = 0; d < hd; d += 4) {
+      const float4 kv = *reinterpret_cast<const float4*>(kr + d);
+#pragma unroll
+      for (int g = 0; g < MAX_GROUPS; g++) {
+        if (g < G) {
+          const float* qg = xs + g * hd + d;
+          acc[g] = chain(fused, qg[0], kv.x, acc[g]);
+          acc[g] = chain(fused, qg[1], kv.y, acc[g]);
+          acc[g] = chain(fused, qg[2], kv.z, acc[g]);
+          acc[g] = chain(fused, qg[3], kv.w, acc[g]);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < MAX_GROUPS; g++)
+      if (g < G) sc[g * eff + s] = __fmul_rn(acc[g], p.scale);
+  }
+  __syncthreads();
+  // softmax_slice per head: warp g
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int g = warp; g < G; g += nt >> 5) {
+    float* r = sc + g * eff;
+    float mx = -INFINITY;
+    for (int s = lane; s < eff; s += 32) mx = fmaxf(mx, r[s]);
+    mx = warp_max(mx);
+    for (int s = lane; s < eff; s += 32) r[s] = exp_f32(__fsub_rn(r[s], mx));
+    __syncwarp();
+    float sum = 0.0f;
+    if (lane == 0)
+      for (int s = 0; s < eff; s++) sum = __fadd_rn(sum, r[s]);
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    if (sum > 0.0f)
+      for (int s = lane; s < eff; s += 32) r[s] = __fdiv_rn(r[s], sum);
+  }
+  __syncthreads();
+  griddep_launch();
+  // score * V: below 64 positions sum += p*v; from 64 on matmul_nn
+  // (f32GemvRow without trans_b: @mulAdd except the last hd%32 columns)
+  for (int t = tid; t < G * hd; t += nt) {
+    const int g = t / hd, d = t - g * hd;
+    const bool fused = eff >= 64 && d < hd - (hd & 31);
+    const float* pr = sc + g * eff;
+    const float* vcol = vcb + (size_t)off * kvd + d;
+    float acc = 0.0f;
+    for (int s = 0; s < eff; s++) acc = chain(fused, pr[s], vcol[(size_t)s * kvd], acc);
+    p.out[(long long)b * p.ldo + (long long)(kvh * G + g) * hd + d] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Prefill step 1: headwise norm + RoPE of every q/k head in place, K and raw
+// V appended to the cache at positions len[seq] + t.
+// grid (tokens, n_heads + n_kv), block hd/2 (>= 32)
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) k_norm_rope_append(const AttnParams p) {
+  extern __shared__ float sm[];
+  const int t = blockIdx.x, hh = blockIdx.y, hd = p.hd, kvd = p.n_kv * hd;
+  const bool is_q = hh < p.n_heads;
+  float* xs = sm;
+  float* lanes = xs + hd;
+  float* scl = lanes + 4;
+  griddep_wait();
+  const int slot = p.len[p.seq0] + t;  // cache slot; RoPE uses offset 0 (attention.rs:171-190)
+  if (slot >= p.max_seq) {
+    if (threadIdx.x == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
+    return;
+  }
+  float* src = is_q ? p.q + (long long)t * p.ld + (long long)hh * hd
+                    : const_cast<float*>(p.k) + (long long)t * p.ld + (long long)(hh - p.n_heads) * hd;
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) xs[i] = src[i];
+  __syncthreads();
+  norm_rope(xs, 1, hd, is_q ? p.qn : p.kn, nullptr, 1, p.eps, p.cos_t, p.sin_t, t, lanes, scl,
+            blockDim.x);
+  griddep_launch();
+  if (is_q) {
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) src[i] = xs[i];
+  } else {
+    const int kh = hh - p.n_heads;
+    float* kd = p.kc + ((size_t)p.seq0 * p.max_seq + slot) * kvd + kh * hd;
+    float* vd = p.vc + ((size_t)p.seq0 * p.max_seq + slot) * kvd + kh * hd;
+    const float* vs = p.v + (long long)t * p.ld + (long long)kh * hd;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+      kd[i] = xs[i];
+      vd[i] = vs[i];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Prefill step 2: syn_fused_attention (zig/src/ffi/exports.zig:1364-1478) per
+// head over the prompt: CTA = (head, PR query rows), 256 threads.
+// Chain kinds follow sgemmTiled per 32-row query tile (TILE_Q,
+// zig/src/ops/attention.zig:25): tiles of <= 16 rows use the per-row GEMV
+// (@mulAdd except trailing columns), larger tiles the 8x8 micro-kernels
+// (@mulAdd in full tiles, sum += a*b in edge tiles).
+// ---------------------------------------------------------------------------
+constexpr int PF_THREADS = 256;
+
+__device__ __forceinline__ void tile_of(int q, int S, int& tqs, int& i) {
+  const int tq = q & ~31;
+  tqs = min(32, S - tq);
+  i = q - tq;
+}
+__device__ __forceinline__ bool s_fused(int q, int j, int S) {
+  int tqs, i;
+  tile_of(q, S, tqs, i);
+  const bool jfull = j < S - (S & 7);
+  if (tqs <= 16) return jfull;
+  return i < tqs - (tqs & 7) && jfull;
+}
+__device__ __forceinline__ bool o_fused(int q, int d, int S, int hd) {
+  int tqs, i;
+  tile_of(q, S, tqs, i);
+  if (tqs <= 16) return d < hd - (hd & 31);
+  return i < tqs - (tqs & 7) && d < hd - (hd & 7);
+}
+
+__global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p, int PR) {
+  extern __shared__ float sm[];
+  const int hh = blockIdx.x, r0 = blockIdx.y * PR;
+  const int G = p.n_heads / p.n_kv, kvh = hh / G, hd = p.hd, kvd = p.n_kv * hd;
+  const int S = p.n_tokens, rows = min(PR, S - r0), jn = r0 + rows;  // keys [0, jn)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* qs = sm;                 // [rows][hd]
+  float* sc = qs + PR * hd;       // [rows][jn]
+  float* chv = sc + (size_t)PR * jn;  // per warp: 32 values + 32 flags
+  griddep_wait();
+  // the prompt's own K/V: cache slots from the sequence's first free one on
+  const int base = p.len[p.seq0];
+  const float* kcb = p.kc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * hd;
+  const float* vcb = p.vc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * hd;
+  for (int t = tid; t < rows * hd; t += PF_THREADS) {
+    const int i = t / hd, d = t - i * hd;
+    qs[t] = p.q[(long long)(r0 + i) * p.ld + (long long)hh * hd + d];
+  }
+  __syncthreads();
+  // S = Q K^T * scale (masked entries are not needed: set to 0 below)
+  for (int t = tid; t < rows * jn; t += PF_THREADS) {
+    const int i = t / jn, j = t - i * jn, q = r0 + i;
+    if (j > q) {
+      sc[t] = 0.0f;
+      continue;
+    }
+    const bool fused = s_fused(q, j, S);
+    const float* kr = kcb + (size_t)j * kvd;
+    const float* qr = qs + i * hd;
+    float acc = 0.0f;
+    for (int d = 0; d < hd; d += 4) {
+      const float4 kv = *reinterpret_cast<const float4*>(kr + d);
+      acc = chain(fused, qr[d], kv.x, acc);
+      acc = chain(fused, qr[d + 1], kv.y, acc);
+      acc = chain(fused, qr[d + 2], kv.z, acc);
+      acc = chain(fused, qr[d + 3], kv.w, acc);
+    }
+    sc[t] = __fmul_rn(acc, p.scale);
+  }
+  __syncthreads();
+  // online softmax per row (warp per row): running max known from a prefix
+  // scan, exponentials in parallel, the (se) recurrence sequential
+  float* wv = chv + warp * 64;
+  for (int i = warp; i < rows; i += PF_THREADS / 32) {
+    const int q = r0 + i;
+    float* r = sc + (size_t)i * jn;
+    float M = -INFINITY, se = 0.0f;
+    for (int c0 = 0; c0 <= q; c0 += 32) {
+      const int j = c0 + lane;
+      const float x = j <= q ? r[j] : -INFINITY;
+      float incl = x;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl = fmaxf(incl, y);
+      }
+      float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+      const float mprev = lane == 0 ? M : fmaxf(M, excl);
+      const bool up = x > mprev;
+      wv[lane] = up ? exp_f32(__fsub_rn(mprev, x)) : exp_f32(__fsub_rn(x, mprev));
+      wv[32 + lane] = up ? 1.0f : 0.0f;
+      __syncwarp();
+      if (lane == 0) {
+        const int cn = min(32, q + 1 - c0);
+        for (int l = 0; l < cn; l++)
+          se = wv[32 + l] != 0.0f ? __fadd_rn(__fmul_rn(se, wv[l]), 1.0f) : __fadd_rn(se, wv[l]);
+      }
+      __syncwarp();
+      M = fmaxf(M, __shfl_sync(0xffffffffu, incl, 31));
+    }
+    se = __shfl_sync(0xffffffffu, se, 0);
+    const float inv = __fdiv_rn(1.0f, se);
+    for (int j = lane; j <= q; j += 32) r[j] = __fmul_rn(exp_f32(__fsub_rn(r[j], M)), inv);
+  }
+  __syncthreads();
+  griddep_launch();
+  // O = P V: each thread owns up to 16 outputs, chains advanced together
+  constexpr int NPER = 16;
+  float acc[NPER];
+  int oi[NPER];
+  bool fz[NPER];
+  int nown = 0;
+#pragma unroll
+  for (int u = 0; u < NPER; u++) {
+    const int t = tid + u * PF_THREADS;
+    acc[u] = 0.0f;
+    oi[u] = t < rows * hd ? t : -1;
+    fz[u] = false;
+    if (oi[u] >= 0) {
+      const int i = t / hd, d = t - i * hd;
+      fz[u] = o_fused(r0 + i, d, S, hd);
+      nown = u + 1;
+    }
+  }
+  for (int j = 0; j < jn; j++) {
+    const float* vr = vcb + (size_t)j * kvd;
+#pragma unroll
+    for (int u = 0; u < NPER; u++) {
+      if (u < nown && oi[u] >= 0) {
+        const int i = oi[u] / hd, d = oi[u] - i * hd;
+        acc[u] = chain(fz[u], sc[(size_t)i * jn + j], vr[d], acc[u]);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < NPER; u++) {
+    if (u < nown && oi[u] >= 0) {
+      const int i = oi[u] / hd, d = oi[u] - i * hd;
+      p.out[(long long)(r0 + i) * p.ldo + (long long)hh * hd + d] = acc[u];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU: variant 0 = the INT8 model's silu(g) * u with silu = g/(1+exp(-g))
+// (quantization/lm/int8.rs:500-503, ops/activation.rs:30-32); variant 1 =
+// swigluFused (zig/src/ops/silu.zig:85-114): g * (1/(1+exp(-g))) * u for the
+// first n - n%4 elements, (g/(1+exp(-g))) * u for the tail.
+// ---------------------------------------------------------------------------
+__global__ void k_swiglu(const float* __restrict__ gate, const float* __restrict__ up,
+                         long long ld_in, int rows, int n, int variant, float* __restrict__ out,
+                         long long ldo) {
+  griddep_wait();
+  griddep_launch();
+  const long long total = (long long)rows * n;
+  const int n4 = n & ~3;
+  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+       t += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(t / n), i = (int)(t - (long long)r * n);
+    const float g = gate[r * ld_in + i], u = up[r * ld_in + i];
+    const float e = __fadd_rn(1.0f, exp_f32(-g));
+    float y;
+    if (variant == 1 && i < n4)
+      y = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, e)), u);
+    else
+      y = __fmul_rn(__fdiv_rn(g, e), u);
+    out[r * ldo + i] = y;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// argmax (generation/sampler.rs:217-224): Iterator::max_by with partial_cmp,
+// NaN comparing Equal. The running best is replaced unless it is strictly
+// greater, so: the answer is the last index of the maximum over the elements
+// after the last NaN (or that NaN itself when it is the last element).
+// One CTA per row; optionally advances the KV-cache lengths afterwards.
+// ---------------------------------------------------------------------------
+constexpr int AM_THREADS = 1024;
+
+__global__ void __launch_bounds__(AM_THREADS) k_argmax(const float* __restrict__ x, long long ldx,
+                                                       int n, int32_t* __restrict__ out,
+                                                       int* len_adv, int adv, int max_len) {
+  __shared__ int s_i[AM_THREADS / 32];
+  __shared__ float s_v[AM_THREADS / 32];
+  __shared__ int s_nan;
+  griddep_wait();
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* xr = x + row * ldx;
+  int lastnan = -1;
+  for (int i = tid; i < n; i += AM_THREADS)
+    if (isnan(xr[i])) lastnan = i;
+  for (int o = 16; o; o >>= 1) lastnan = max(lastnan, __shfl_xor_sync(0xffffffffu, lastnan, o));
+  if (lane == 0) s_i[warp] = lastnan;
+  __syncthreads();
+  if (tid == 0) {
+    int m = -1;
+    for (int w = 0; w < AM_THREADS / 32; w++) m = max(m, s_i[w]);
+    s_nan = m;
+  }
+  __syncthreads();
+  const int ln = s_nan;
+  float bv = -INFINITY;
+  int bi = -1;
+  for (int i = ln + 1 + tid; i < n; i += AM_THREADS) {
+    const float v = xr[i];
+    if (bi < 0 || v >= bv) {  // later index wins ties (+0 == -0)
+      bv = v;
+      bi = i;
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi > bi))) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __syncthreads();
+  if (lane == 0) {
+    s_i[warp] = bi;
+    s_v[warp] = bv;
+  }
+  __syncthreads();
+  griddep_launch();
+  if (tid == 0) {
+    int ri = -1;
+    float rv = -INFINITY;
+    for (int w = 0; w < AM_THREADS / 32; w++) {
+      const int oi = s_i[w];
+      const float ov = s_v[w];
+      if (oi >= 0 && (ri < 0 || ov > rv || (ov == rv && oi > ri))) {
+        rv = ov;
+        ri = oi;
+      }
+    }
+    if (ri < 0) ri = ln >= 0 ? ln : 0;  // nothing after the last NaN: the NaN itself
+    out[row] = ri;
+    if (len_adv) {
+      const int nl = len_adv[row] + adv;
+      len_adv[row] = nl <= max_len ? nl : max_len;
+    }
+  }
+}
+
+__global__ void k_kv_set(int* len, int seq, int value, int add) {
+  griddep_wait();
+  griddep_launch();
+  if (threadIdx.x == 0) len[seq] = add ? len[seq] + value : value;
+}
+
+syn_status_t cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return SYN_OK;
+  set_last_cuda_error(e, where);
+  return SYN_ERR_CUDA;
+}
+
+}  // namespace
+
+// ---- internal launchers (also used by the runner) --------------------------
+syn_status_t launch_add_rmsnorm(const float* x, size_t ldx, const float* delta, size_t ldd,
+                                const int32_t* ids, const float* table, size_t vocab,
+                                float* x_out, size_t ldxo, const float* w, size_t rows, size_t h,
+                                float eps, float* out, size_t ldo, cudaStream_t st) {
+  if (h == 0 || rows == 0) return SYN_OK;
+  if (h > 40000 || rows > 0x7FFFFFFF) return SYN_ERR_UNSUPPORTED;
+  NormParams p{x, (long long)ldx, delta, (long long)ldd, ids, table, (unsigned)vocab,
+               x_out, (long long)ldxo, w, (int)h, eps, out, (long long)ldo};
+  const size_t smem = h * sizeof(float);
+  syn_status_t s = allow_smem((const void*)k_add_rmsnorm, smem);
+  if (s) return s;
+  return cuda_status(launch_pdl(k_add_rmsnorm, dim3((unsigned)rows), dim3(NORM_THREADS), smem, st, p),
+                     "k_add_rmsnorm");
+}
+
+syn_status_t launch_swiglu(const float* gate, const float* up, size_t ld_in, size_t rows, size_t n,
+                           int variant, float* out, size_t ldo, cudaStream_t st) {
+  if (!rows || !n) return SYN_OK;
+  const long long total = (long long)rows * n;
+  const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+  return cuda_status(launch_pdl(k_swiglu, dim3(blocks), dim3(256), 0, st, gate, up,
+                                (long long)ld_in, (int)rows, (int)n, variant, out, (long long)ldo),
+                     "k_swiglu");
+}
+
+syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
+                           int* len_adv, int adv, int max_len, cudaStream_t st) {
+  if (!rows || !n) return SYN_OK;
+  return cuda_status(launch_pdl(k_argmax, dim3((unsigned)rows), dim3(AM_THREADS), 0, st, x,
+                                (long long)ldx, (int)n, out, len_adv, adv, max_len),
+                     "k_argmax");
+}
+
+}  // namespace syn
+
+// ---------------------------------------------------------------------------
+// decode / prefill launchers (need AttnParams, defined in the unnamed space)
+// ---------------------------------------------------------------------------
+namespace syn {
+namespace {
+
+size_t decode_smem(int G, int hd, int eff) {
+  return ((size_t)(G + 1) * hd + 4 * (G + 1) + (G + 1) + (size_t)G * eff) * sizeof(float);
+}
+
+int prefill_rows(int S, int hd) {
+  for (int pr = 16; pr >= 1; pr >>= 1) {
+    const size_t smem = ((size_t)pr * hd + (size_t)pr * S + 8 * 64) * sizeof(float);
+    if (smem <= kMaxSmem && pr * hd <= 16 * PF_THREADS) return pr;
+  }
+  return 0;
+}
+
+
+syn_status_t make_params(const AttnArgs& a, AttnParams& p, int seq0, int ntok) {
+  const syn_cuda_kvcache_t* c = a.cache;
+  if (a.n_heads == 0 || a.n_heads % c->n_kv) return SYN_ERR_SHAPE_MISMATCH;
+  if (a.layer >= c->layers) return SYN_ERR_INVALID_ARG;
+  if (c->hd % 4 || c->hd < 8 || c->hd > 1024) return SYN_ERR_UNSUPPORTED;
+  p.q = a.q;
+  p.k = a.k;
+  p.v = a.v;
+  p.ld = (long long)a.ld;
+  p.n_heads = (int)a.n_heads;
+  p.n_kv = (int)c->n_kv;
+  p.hd = (int)c->hd;
+  p.qn = a.qn;
+  p.kn = a.kn;
+  p.eps = a.eps;
+  p.cos_t = a.cos_t;
+  p.sin_t = a.sin_t;
+  p.window = (int)a.window;
+  const size_t kvd = c->n_kv * c->hd;
+  p.kc = c->k + a.layer * c->batch * c->max_seq * kvd;
+  p.vc = c->v + a.layer * c->batch * c->max_seq * kvd;
+  p.max_seq = (int)c->max_seq;
+  p.len = c->d_len;
+  p.seq0 = seq0;
+  p.n_tokens = ntok;
+  p.out = a.out;
+  p.ldo = (long long)a.ldo;
+  p.scale = 1.0f / sqrtf((float)c->hd);  // host: 1 / sqrt(hd) in f32
+  p.err = nullptr;
+  return SYN_OK;
+}
+
+}  // namespace
+
+syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, cudaStream_t st) {
+  AttnParams p;
+  syn_status_t s = make_params(a, p, 0, 1);
+  if (s) return s;
+  p.err = err;
+  const int G = p.n_heads / p.n_kv;
+  if (G > MAX_GROUPS || G * p.hd > 1024) return SYN_ERR_UNSUPPORTED;
+  if (batch > a.cache->batch) return SYN_ERR_INVALID_ARG;
+  for (size_t b = 0; b < batch; b++)
+    if (a.cache->len[b] >= a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  size_t maxlen = 0;
+  for (size_t b = 0; b < batch; b++) maxlen = std::max(maxlen, a.cache->len[b] + 1);
+  // The graph replays at growing positions: size smem for the whole window.
+  size_t eff = a.cache->max_seq;
+  if (a.window && a.window < eff) eff = a.window;
+  const size_t smem = decode_smem(G, p.hd, (int)eff);
+  if (smem > kMaxSmem) return SYN_ERR_UNSUPPORTED;
+  (void)maxlen;
+  s = allow_smem((const void*)k_attn_decode, smem);
+  if (s) return s;
+  return cuda_status(launch_pdl(k_attn_decode, dim3((unsigned)batch, (unsigned)p.n_kv),
+                                dim3(G * p.hd), smem, st, p),
+                     "k_attn_decode");
+}
+
+syn_status_t launch_norm_rope_append_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                          cudaStream_t st) {
+  AttnParams p;
+  syn_status_t s = make_params(a, p, (int)seq, (int)ntok);
+  if (s) return s;
+  p.err = err;
+  if (seq >= a.cache->batch) return SYN_ERR_INVALID_ARG;
+  if (a.cache->len[seq] + ntok > a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  if (ntok == 0) return SYN_OK;
+  const int thr = std::max(32, p.hd / 2);
+  const size_t smem = (p.hd + 8) * sizeof(float);
+  return cuda_status(
+      launch_pdl(k_norm_rope_append, dim3((unsigned)ntok, (unsigned)(p.n_heads + p.n_kv)),
+                 dim3(thr), smem, st, p),
+      "k_norm_rope_append");
+}
+
+syn_status_t launch_prefill_attention_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                           cudaStream_t st) {
+  AttnParams p;
+  syn_status_t s = make_params(a, p, (int)seq, (int)ntok);
+  if (s) return s;
+  p.err = err;
+  if (seq >= a.cache->batch) return SYN_ERR_INVALID_ARG;
+  if (a.cache->len[seq] + ntok > a.cache->max_seq) return SYN_ERR_INVALID_ARG;
+  if (ntok == 0) return SYN_OK;
+  const int pr = prefill_rows((int)ntok, p.hd);
+  if (!pr) return SYN_ERR_UNSUPPORTED;
+  const size_t smem = ((size_t)pr * p.hd + (size_t)pr * ntok + 8 * 64) * sizeof(float);
+  s = allow_smem((const void*)k_attn_prefill, smem);
+  if (s) return s;
+  return cuda_status(launch_pdl(k_attn_prefill,
+                                dim3((unsigned)p.n_heads, (unsigned)((ntok + pr - 1) / pr)),
+                                dim3(PF_THREADS), smem, st, p, pr),
+                     "k_attn_prefill");
+}
+
+syn_status_t launch_attn_prefill_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                      cudaStream_t st) {
+  syn_status_t s = launch_norm_rope_append_args(a, seq, ntok, err, st);
+  if (s) return s;
+  return launch_prefill_attention_args(a, seq, ntok, err, st);
+}
+
+syn_status_t launch_kv_set(syn_cuda_kvcache_t* c, size_t seq, int value, int add, cudaStream_t st) {
+  return cuda_status(launch_pdl(k_kv_set, dim3(1), dim3(32), 0, st, c->d_len, (int)seq, value, add),
+                     "k_kv_set");
+}
+
+}  // namespace syn
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+using namespace syn;
+
+extern "C" {
+
+syn_status_t syn_cuda_rope_tables(double base, size_t max_pos, size_t head_dim, float* cos_out,
+                                  float* sin_out) {
+  if (!cos_out || !sin_out) return SYN_ERR_NULL_PTR;
+  if (head_dim == 0 || head_dim % 2) return SYN_ERR_INVALID_ARG;
+  const size_t half = head_dim / 2;
+  for (size_t pos = 0; pos < max_pos; pos++)
+    for (size_t i = 0; i < half; i++) {
+      const float freq = 1.0f / powf((float)base, (2.0f * (float)i) / (float)head_dim);
+      const float scaled = freq / 1.0f;
+      const float angle = (float)pos * scaled;
+      cos_out[pos * half + i] = cosf(angle);
+      sin_out[pos * half + i] = sinf(angle);
+    }
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_rmsnorm(const float* x, const float* weight, size_t rows, size_t hidden,
+                              float eps, float* out, void* stream) {
+  if (!x || !weight || !out) return SYN_ERR_NULL_PTR;
+  return launch_add_rmsnorm(x, hidden, nullptr, 0, nullptr, nullptr, 0, nullptr, 0, weight, rows,
+                            hidden, eps, out, hidden, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_add_rmsnorm(float* residual, const float* delta, const float* weight,
+                                  size_t rows, size_t hidden, float eps, float* out,
+                                  void* stream) {
+  if (!residual || !delta || !weight || !out) return SYN_ERR_NULL_PTR;
+  return launch_add_rmsnorm(residual, hidden, delta, hidden, nullptr, nullptr, 0, residual, hidden,
+                            weight, rows, hidden, eps, out, hidden, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_embed_rmsnorm(const float* table, size_t vocab, const int32_t* ids,
+                                    size_t rows, size_t hidden, const float* weight, float eps,
+                                    float* x_out, float* out, void* stream) {
+  if (!table || !ids || !weight || !out) return SYN_ERR_NULL_PTR;
+  return launch_add_rmsnorm(nullptr, 0, nullptr, 0, ids, table, vocab, x_out, hidden, weight, rows,
+                            hidden, eps, out, hidden, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_kvcache_create(syn_cuda_ctx_t* ctx, size_t max_seq, size_t n_kv_heads,
+                                     size_t head_dim, size_t num_layers, size_t batch,
+                                     syn_cuda_kvcache_t** out) {
+  if (!ctx || !out) return SYN_ERR_NULL_PTR;
+  *out = nullptr;
+  if (!max_seq || !n_kv_heads || !head_dim || !num_layers || !batch)
+    return SYN_ERR_INVALID_DIMENSIONS;  // kvcache.zig:31-34
+  if (max_seq > 0x7FFFFFF || head_dim % 4) return SYN_ERR_UNSUPPORTED;
+  DeviceGuard g(ctx->device);
+  if (!g.ok) return SYN_ERR_CUDA;
+  auto* c = new (std::nothrow) syn_cuda_kvcache_s();
+  if (!c) return SYN_ERR_OUT_OF_MEMORY;
+  c->device = ctx->device;
+  c->max_seq = max_seq;
+  c->n_kv = n_kv_heads;
+  c->hd = head_dim;
+  c->layers = num_layers;
+  c->batch = batch;
+  const size_t elems = num_layers * batch * max_seq * n_kv_heads * head_dim;
+  c->len = new (std::nothrow) size_t[batch]();
+  cudaError_t e = c->len ? cudaMalloc(&c->k, elems * sizeof(float)) : cudaErrorMemoryAllocation;
+  if (e == cudaSuccess) e = cudaMalloc(&c->v, elems * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_len, batch * sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->k, 0, elems * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemset(c->v, 0, elems * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemset(c->d_len, 0, batch * sizeof(int));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "syn_cuda_kvcache_create");
+    cudaFree(c->k);
+    cudaFree(c->v);
+    cudaFree(c->d_len);
+    delete[] c->len;
+    delete c;
+    return SYN_ERR_OUT_OF_MEMORY;
+  }
+  *out = c;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_kvcache_destroy(syn_cuda_kvcache_t* c) {
+  if (!c) return SYN_ERR_NULL_PTR;
+  DeviceGuard g(c->device);
+  cudaDeviceSynchronize();
+  cudaFree(c->k);
+  cudaFree(c->v);
+  cudaFree(c->d_len);
+  delete[] c->len;
+  delete c;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_kvcache_len(const syn_cuda_kvcache_t* c, size_t seq, size_t* len) {
+  if (!c || !len) return SYN_ERR_NULL_PTR;
+  if (seq >= c->batch) return SYN_ERR_INVALID_ARG;
+  *len = c->len[seq];
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_kvcache_view(const syn_cuda_kvcache_t* c, size_t layer, size_t seq,
+                                   float** k, float** v) {
+  if (!c) return SYN_ERR_NULL_PTR;
+  if (layer >= c->layers || seq >= c->batch) return SYN_ERR_INVALID_ARG;
+  const size_t off = (layer * c->batch + seq) * c->max_seq * c->n_kv * c->hd;
+  if (k) *k = c->k + off;
+  if (v) *v = c->v + off;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_kvcache_append(syn_cuda_kvcache_t* c, size_t layer, size_t seq,
+                                     const float* k, const float* v, size_t n_tokens,
+                                     void* stream) {
+  if (!c || !k || !v) return SYN_ERR_NULL_PTR;
+  if (layer >= c->layers || seq >= c->batch) return SYN_ERR_INVALID_ARG;
+  if (c->len[seq] + n_tokens > c->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  if (!n_tokens) return SYN_OK;
+  DeviceGuard g(c->device);
+  float *kd, *vd;
+  syn_cuda_kvcache_view(c, layer, seq, &kd, &vd);
+  const size_t row = c->n_kv * c->hd, off = c->len[seq] * row, bytes = n_tokens * row * 4;
+  cudaStream_t st = (cudaStream_t)stream;
+  SYN_CUDA_TRY(cudaMemcpyAsync(kd + off, k, bytes, cudaMemcpyDeviceToDevice, st));
+  SYN_CUDA_TRY(cudaMemcpyAsync(vd + off, v, bytes, cudaMemcpyDeviceToDevice, st));
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_kvcache_advance(syn_cuda_kvcache_t* c, size_t seq, size_t n, void* stream) {
+  if (!c) return SYN_ERR_NULL_PTR;
+  if (seq >= c->batch) return SYN_ERR_INVALID_ARG;
+  if (c->len[seq] + n > c->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  DeviceGuard g(c->device);
+  syn_status_t s = launch_kv_set(c, seq, (int)n, 1, (cudaStream_t)stream);
+  if (s == SYN_OK) c->len[seq] += n;
+  return s;
+}
+
+syn_status_t syn_cuda_kvcache_truncate(syn_cuda_kvcache_t* c, size_t seq, size_t new_len,
+                                       void* stream) {
+  if (!c) return SYN_ERR_NULL_PTR;
+  if (seq >= c->batch) return SYN_ERR_INVALID_ARG;
+  if (new_len >= c->len[seq]) return SYN_OK;  // kvcache.zig:109-113
+  DeviceGuard g(c->device);
+  syn_status_t s = launch_kv_set(c, seq, (int)new_len, 0, (cudaStream_t)stream);
+  if (s == SYN_OK) c->len[seq] = new_len;
+  return s;
+}
+
+syn_status_t syn_cuda_kvcache_reset(syn_cuda_kvcache_t* c, size_t seq, void* stream) {
+  if (!c) return SYN_ERR_NULL_PTR;
+  if (seq >= c->batch) return SYN_ERR_INVALID_ARG;
+  DeviceGuard g(c->device);
+  syn_status_t s = launch_kv_set(c, seq, 0, 0, (cudaStream_t)stream);
+  if (s == SYN_OK) c->len[seq] = 0;
+  return s;
+}
+
+syn_status_t syn_cuda_attention_decode(syn_cuda_kvcache_t* cache, size_t layer, size_t batch,
+                                       float* q, const float* k, const float* v, size_t ld,
+                                       size_t n_heads, const float* q_norm, const float* k_norm,
+                                       float eps, const float* rope_cos, const float* rope_sin,
+                                       size_t window, float* out, size_t ldo, void* stream) {
+  if (!cache || !q || !k || !v || !rope_cos || !rope_sin || !out) return SYN_ERR_NULL_PTR;
+  if (!batch) return SYN_OK;
+  DeviceGuard g(cache->device);
+  AttnArgs a{q, k, v, ld, n_heads, q_norm, k_norm, eps, rope_cos, rope_sin, window, cache, layer,
+             out, ldo};
+  return launch_attn_decode_args(a, batch, nullptr, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_qk_norm_rope_kv_append(syn_cuda_kvcache_t* cache, size_t layer, size_t seq,
+                                             size_t n_tokens, float* q, const float* k,
+                                             const float* v, size_t ld, size_t n_heads,
+                                             const float* q_norm, const float* k_norm, float eps,
+                                             const float* rope_cos, const float* rope_sin,
+                                             void* stream) {
+  if (!cache || !q || !k || !v || !rope_cos || !rope_sin) return SYN_ERR_NULL_PTR;
+  DeviceGuard g(cache->device);
+  AttnArgs a{q, k, v, ld, n_heads, q_norm, k_norm, eps, rope_cos, rope_sin, 0, cache, layer,
+             nullptr, 0};
+  return launch_norm_rope_append_args(a, seq, n_tokens, nullptr, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_attention_prefill(syn_cuda_kvcache_t* cache, size_t layer, size_t seq,
+                                        size_t n_tokens, float* q, const float* k, const float* v,
+                                        size_t ld, size_t n_heads, const float* q_norm,
+                                        const float* k_norm, float eps, const float* rope_cos,
+                                        const float* rope_sin, float* out, size_t ldo,
+                                        void* stream) {
+  if (!cache || !q || !k || !v || !rope_cos || !rope_sin || !out) return SYN_ERR_NULL_PTR;
+  DeviceGuard g(cache->device);
+  AttnArgs a{q, k, v, ld, n_heads, q_norm, k_norm, eps, rope_cos, rope_sin, 0, cache, layer,
+             out, ldo};
+  return launch_attn_prefill_args(a, seq, n_tokens, nullptr, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_swiglu(const float* gate, const float* up, size_t ld_in, size_t rows,
+                             size_t n, int variant, float* out, size_t ldo, void* stream) {
+  if (!gate || !up || !out) return SYN_ERR_NULL_PTR;
+  if (variant != 0 && variant != 1) return SYN_ERR_INVALID_ARG;
+  return launch_swiglu(gate, up, ld_in, rows, n, variant, out, ldo, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_argmax(const float* logits, size_t rows, size_t n, int32_t* out_idx,
+                             void* stream) {
+  if (!logits || !out_idx) return SYN_ERR_NULL_PTR;
+  if (n > 0x7FFFFFFF) return SYN_ERR_UNSUPPORTED;
+  return launch_argmax(logits, n, rows, n, out_idx, nullptr, 0, 0, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,619 @@
+// runner.cu -- the decoder-only LM runner on the GPU: QuantizedCausalLM
+// (quantization/lm/int8.rs:171-709) for INT8 weights and CausalLM
+// (models/lm/causal_lm.rs:195-280, models/lm/decoder_layer.rs:590-730) for
+// the block formats, with the weights repacked in HBM, the KV cache in HBM
+// and each decode step replayed as one CUDA graph.
+//
+// Per layer (rows = tokens of a prefill, or one per sequence in a decode):
+//   add_rmsnorm(resid += down_prev; x = norm(resid))      [layer 0: embedding]
+//   qkv  = x * [Wq;Wk;Wv]^T                               (one fused matmul)
+//   att  = attention(qkv)            (headwise norm, RoPE, KV append, GQA)
+//   o    = att * Wo^T
+//   add_rmsnorm(resid += o; x = ffn_norm(resid))
+//   gu   = x * [Wgate;Wup]^T                              (one fused matmul)
+//   hid  = swiglu(gu)
+//   down = hid * Wdown^T
+// then add_rmsnorm with the final norm, the LM head and argmax. Fusing the
+// weights along N is exact: every output column is computed independently.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "internal.cuh"
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// Minimal JSON reader for the model config: flattens objects into
+// "section.key" -> scalar text.
+// ---------------------------------------------------------------------------
+struct Json {
+  const char* s;
+  size_t i = 0;
+  bool ok = true;
+  std::map<std::string, std::string> flat;
+  explicit Json(const char* t) : s(t) {}
+  void ws() {
+    while (s[i] == ' ' || s[i] == '\n' || s[i] == '\t' || s[i] == '\r') i++;
+  }
+  std::string str() {
+    std::string out;
+    if (s[i] != '"') {
+      ok = false;
+      return out;
+    }
+    i++;
+    while (s[i] && s[i] != '"') {
+      if (s[i] == '\\' && s[i + 1]) i++;
+      out += s[i++];
+    }
+    if (s[i] != '"') ok = false;
+    else i++;
+    return out;
+  }
+  void value(const std::string& path) {
+    ws();
+    if (s[i] == '{') {
+      i++;
+      ws();
+      if (s[i] == '}') {
+        i++;
+        return;
+      }
+      while (ok) {
+        ws();
+        std::string k = str();
+        ws();
+        if (s[i] != ':') {
+          ok = false;
+          return;
+        }
+        i++;
+        value(path.empty() ? k : path + "." + k);
+        ws();
+        if (s[i] == ',') {
+          i++;
+          continue;
+        }
+        if (s[i] == '}') {
+          i++;
+          return;
+        }
+        ok = false;
+      }
+    } else if (s[i] == '[') {
+      int depth = 0;  // arrays are not needed by the config: skip them
+      do {
+        if (s[i] == '[') depth++;
+        else if (s[i] == ']') depth--;
+        else if (!s[i]) {
+          ok = false;
+          return;
+        }
+        i++;
+      } while (depth > 0);
+    } else if (s[i] == '"') {
+      flat[path] = str();
+    } else {
+      size_t j = i;
+      while (s[i] && s[i] != ',' && s[i] != '}' && s[i] != ']' && s[i] != ' ' && s[i] != '\n' &&
+             s[i] != '\r' && s[i] != '\t')
+        i++;
+      if (i == j) ok = false;
+      flat[path] = std::string(s + j, i - j);
+    }
+  }
+  bool parse() {
+    value("");
+    return ok;
+  }
+  bool num(const char* key, double* out) const {
+    auto it = flat.find(key);
+    if (it == flat.end()) return false;
+    char* end = nullptr;
+    *out = strtod(it->second.c_str(), &end);
+    return end && *end == 0;
+  }
+  std::string text(const char* key) const {
+    auto it = flat.find(key);
+    return it == flat.end() ? std::string() : it->second;
+  }
+};
+
+struct HostLinear {
+  int fmt = -1;
+  size_t n = 0, k = 0;
+  std::vector<uint8_t> data;
+  std::vector<float> scales;
+};
+
+size_t row_bytes(int fmt, size_t k) {
+  switch (fmt) {
+    case SYN_QFMT_Q4_0: return k / 32 * 18;
+    case SYN_QFMT_Q8_0: return k / 32 * 34;
+    case SYN_QFMT_Q4_K: return k / 256 * 144;
+    case SYN_QFMT_Q6_K: return k / 256 * 210;
+  }
+  return 0;
+}
+
+size_t weight_bytes(int fmt, size_t n, size_t k) {
+  return fmt == SYN_QFMT_INT8_KN ? n * k : n * row_bytes(fmt, k);
+}
+
+// Concatenates linears along N (output rows): INT8 [K,N] column blocks, block
+// formats row blocks.
+bool concat(const std::vector<const HostLinear*>& parts, HostLinear& out) {
+  out = HostLinear();
+  out.fmt = parts[0]->fmt;
+  out.k = parts[0]->k;
+  for (auto* p : parts) {
+    if (p->fmt != out.fmt || p->k != out.k) return false;
+    out.n += p->n;
+  }
+  out.data.resize(weight_bytes(out.fmt, out.n, out.k));
+  if (out.fmt == SYN_QFMT_INT8_KN) {
+    size_t c0 = 0;
+    for (auto* p : parts) {
+      for (size_t kk = 0; kk < out.k; kk++)
+        memcpy(out.data.data() + kk * out.n + c0, p->data.data() + kk * p->n, p->n);
+      out.scales.insert(out.scales.end(), p->scales.begin(), p->scales.end());
+      c0 += p->n;
+    }
+  } else {
+    size_t off = 0;
+    for (auto* p : parts) {
+      memcpy(out.data.data() + off, p->data.data(), p->data.size());
+      off += p->data.size();
+    }
+  }
+  return true;
+}
+
+struct LayerDev {
+  float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  syn_cuda_weight_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+};
+
+}  // namespace
+
+struct syn_cuda_model_s {
+  syn_cuda_ctx_t* ctx = nullptr;
+  int device = 0;
+  // config
+  size_t h = 0, L = 0, V = 0, Hq = 0, Hkv = 0, hd = 0, ff = 0, window = 0;
+  size_t qd = 0, kvd = 0, qkv_n = 0;
+  float eps = 1e-6f;
+  double rope_base = 10000.0;
+  size_t max_seq = 0, max_batch = 0, max_rows = 0;
+  bool int8 = false;
+  bool finalized = false;
+  // staged host weights
+  std::map<std::string, HostLinear> lin;
+  std::map<std::string, std::vector<float>> ten;
+  // device
+  cudaStream_t st = nullptr;
+  std::vector<LayerDev> layers;
+  syn_cuda_weight_t* lm_head = nullptr;
+  float *embed = nullptr, *final_norm = nullptr, *cos_t = nullptr, *sin_t = nullptr;
+  syn_cuda_kvcache_t* cache = nullptr;
+  std::vector<void*> allocs;
+  int32_t* ids = nullptr;
+  int32_t* tok = nullptr;
+  float *resid = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *o = nullptr,
+        *gu = nullptr, *hid = nullptr, *dn = nullptr, *logits = nullptr;
+  // pinned host staging
+  int32_t* ids_h = nullptr;
+  int32_t* tok_h = nullptr;
+  float* logits_h = nullptr;
+  int32_t* err_h = nullptr;
+  // decode graphs per (batch, with logits)
+  std::map<std::pair<size_t, int>, cudaGraphExec_t> graphs;
+  std::map<std::pair<size_t, int>, int> eager_runs;
+};
+
+namespace {
+
+using namespace syn;
+
+syn_status_t dev_alloc(syn_cuda_model_s* m, void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "cudaMalloc(model)");
+    return SYN_ERR_OUT_OF_MEMORY;
+  }
+  m->allocs.push_back(*p);
+  return SYN_OK;
+}
+
+template <typename T>
+syn_status_t dev_alloc_t(syn_cuda_model_s* m, T** p, size_t count) {
+  return dev_alloc(m, reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+syn_status_t upload_tensor(syn_cuda_model_s* m, const std::string& name, size_t numel, float** out,
+                           bool optional) {
+  auto it = m->ten.find(name);
+  if (it == m->ten.end()) {
+    if (optional) {
+      *out = nullptr;
+      return SYN_OK;
+    }
+    set_last_cuda_error(cudaErrorInvalidValue, ("missing tensor " + name).c_str());
+    return SYN_ERR_INVALID_ARG;
+  }
+  if (it->second.size() != numel) return SYN_ERR_SHAPE_MISMATCH;
+  syn_status_t s = dev_alloc_t(m, out, numel);
+  if (s) return s;
+  SYN_CUDA_TRY(cudaMemcpy(*out, it->second.data(), numel * 4, cudaMemcpyHostToDevice));
+  return SYN_OK;
+}
+
+syn_status_t upload_linear(syn_cuda_model_s* m, const HostLinear& hl, syn_cuda_weight_t** out) {
+  return syn_cuda_weight_upload(m->ctx, (syn_qformat_t)hl.fmt, hl.data.data(), hl.n, hl.k,
+                                hl.fmt == SYN_QFMT_INT8_KN ? hl.scales.data() : nullptr, out);
+}
+
+const HostLinear* find_lin(syn_cuda_model_s* m, const std::string& name, size_t n, size_t k) {
+  auto it = m->lin.find(name);
+  if (it == m->lin.end() || it->second.n != n || it->second.k != k) return nullptr;
+  return &it->second;
+}
+
+std::string lname(size_t i, const char* rest) {
+  return "model.layers." + std::to_string(i) + "." + rest;
+}
+
+// y[rows, w.n] = x[rows, w.k] * W^T through the public matmul entry point
+syn_status_t mm(syn_cuda_model_s* m, const syn_cuda_weight_t* w, const float* x, size_t rows,
+                float* y) {
+  return syn_cuda_qmatmul(m->ctx, w, x, rows, y, m->st);
+}
+
+// One forward over `rows` rows. Prefill: rows tokens of sequence `seq`.
+// Decode: rows sequences [0, rows), one token each.
+syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq, bool want_logits) {
+  cudaStream_t st = m->st;
+  syn_status_t s;
+  const size_t h = m->h;
+  const int variant = m->int8 ? 0 : 1;
+  AttnArgs a{};
+  a.ld = m->qkv_n;
+  a.n_heads = m->Hq;
+  a.eps = m->eps;
+  a.cos_t = m->cos_t;
+  a.sin_t = m->sin_t;
+  a.window = m->window;
+  a.cache = m->cache;
+  a.ldo = m->qd;
+  for (size_t li = 0; li < m->L; li++) {
+    LayerDev& ly = m->layers[li];
+    if (li == 0)
+      s = launch_add_rmsnorm(nullptr, 0, nullptr, 0, m->ids, m->embed, m->V, m->resid, h,
+                             ly.attn_norm, rows, h, m->eps, m->x, h, st);
+    else
+      s = launch_add_rmsnorm(m->resid, h, m->dn, h, nullptr, nullptr, 0, m->resid, h,
+                             ly.attn_norm, rows, h, m->eps, m->x, h, st);
+    if (s) return s;
+    if ((s = mm(m, ly.qkv, m->x, rows, m->qkv))) return s;
+    a.q = m->qkv;
+    a.k = m->qkv + m->qd;
+    a.v = m->qkv + m->qd + m->kvd;
+    a.qn = ly.q_norm;
+    a.kn = ly.k_norm;
+    a.layer = li;
+    a.out = m->att;
+    s = prefill ? launch_attn_prefill_args(a, seq, rows, m->ctx->err, st)
+                : launch_attn_decode_args(a, rows, m->ctx->err, st);
+    if (s) return s;
+    if ((s = mm(m, ly.o, m->att, rows, m->o))) return s;
+    s = launch_add_rmsnorm(m->resid, h, m->o, h, nullptr, nullptr, 0, m->resid, h, ly.ffn_norm,
+                           rows, h, m->eps, m->x, h, st);
+    if (s) return s;
+    if ((s = mm(m, ly.gu, m->x, rows, m->gu))) return s;
+    s = launch_swiglu(m->gu, m->gu + m->ff, 2 * m->ff, rows, m->ff, variant, m->hid, m->ff, st);
+    if (s) return s;
+    if ((s = mm(m, ly.down, m->hid, rows, m->dn))) return s;
+  }
+  // final norm and LM head: prefill keeps only the last token (int8.rs:619-627)
+  const size_t r0 = prefill ? rows - 1 : 0, nr = prefill ? 1 : rows;
+  s = launch_add_rmsnorm(m->resid + r0 * h, h, m->dn + r0 * h, h, nullptr, nullptr, 0,
+                         m->resid + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st);
+  if (s) return s;
+  if ((s = mm(m, m->lm_head, m->x, nr, m->logits))) return s;
+  s = launch_argmax(m->logits, m->V, nr, m->V, m->tok, m->cache->d_len + (prefill ? seq : 0),
+                    prefill ? (int)rows : 1, (int)m->max_seq, st);
+  if (s) return s;
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->tok_h, m->tok, nr * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->err_h, m->ctx->err, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  if (want_logits)
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->logits_h, m->logits, nr * m->V * sizeof(float),
+                                 cudaMemcpyDeviceToHost, st));
+  return SYN_OK;
+}
+
+syn_status_t finish(syn_cuda_model_s* m, size_t nr, int32_t* out_tokens, float* logits_host) {
+  SYN_CUDA_TRY(cudaStreamSynchronize(m->st));
+  if (*m->err_h != SYN_OK) {
+    const syn_status_t e = *m->err_h;
+    int32_t zero = 0;
+    cudaMemcpy(m->ctx->err, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    *m->err_h = 0;
+    return e;
+  }
+  if (out_tokens) memcpy(out_tokens, m->tok_h, nr * sizeof(int32_t));
+  if (logits_host) memcpy(logits_host, m->logits_h, nr * m->V * sizeof(float));
+  return SYN_OK;
+}
+
+bool use_graphs() {
+  const char* e = getenv("SYN_RUNNER_GRAPH");
+  return !(e && e[0] == '0');
+}
+
+}  // namespace
+
+extern "C" {
+
+syn_status_t syn_cuda_model_create(syn_cuda_ctx_t* ctx, const char* config_json, size_t max_seq,
+                                   size_t max_batch, syn_cuda_model_t** out) {
+  if (!ctx || !config_json || !out) return SYN_ERR_NULL_PTR;
+  *out = nullptr;
+  if (!max_seq || !max_batch) return SYN_ERR_INVALID_ARG;
+  Json j(config_json);
+  if (!j.parse()) return SYN_ERR_INVALID_ARG;
+  double v;
+  auto* m = new (std::nothrow) syn_cuda_model_s();
+  if (!m) return SYN_ERR_OUT_OF_MEMORY;
+  m->ctx = ctx;
+  m->device = ctx->device;
+  bool ok = true;
+  ok &= j.num("architecture.hidden_size", &v), m->h = (size_t)v;
+  ok &= j.num("architecture.num_layers", &v), m->L = (size_t)v;
+  ok &= j.num("architecture.vocab_size", &v), m->V = (size_t)v;
+  ok &= j.num("attention.num_heads", &v), m->Hq = (size_t)v;
+  m->Hkv = j.num("attention.num_kv_heads", &v) ? (size_t)v : m->Hq;
+  m->hd = j.num("attention.head_dim", &v) ? (size_t)v : (m->Hq ? m->h / m->Hq : 0);
+  ok &= j.num("ffn.intermediate_size", &v), m->ff = (size_t)v;
+  m->eps = j.num("norm.eps", &v) ? (float)v : 1e-6f;  // NormVariant::eps() as f32
+  m->rope_base = j.num("position.base", &v) ? v : 10000.0;
+  if (j.text("attention.type") == "SlidingWindow" && j.num("attention.window_size", &v))
+    m->window = (size_t)v;
+  if (!ok || !m->h || !m->L || !m->V || !m->Hq || !m->Hkv || !m->hd || !m->ff ||
+      m->Hq % m->Hkv || j.text("ffn.type") != "SwiGLU" ||
+      (!j.text("norm.type").empty() && j.text("norm.type") != "RMSNorm")) {
+    delete m;
+    return SYN_ERR_INVALID_ARG;
+  }
+  m->qd = m->Hq * m->hd;
+  m->kvd = m->Hkv * m->hd;
+  m->qkv_n = m->qd + 2 * m->kvd;
+  m->max_seq = max_seq;
+  m->max_batch = max_batch;
+  m->max_rows = std::max(max_seq, max_batch);
+  *out = m;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_set_tensor(syn_cuda_model_t* m, const char* name, const float* host,
+                                       size_t numel) {
+  if (!m || !name || (!host && numel)) return SYN_ERR_NULL_PTR;
+  if (m->finalized) return SYN_ERR_INVALID_ARG;
+  m->ten[name].assign(host, host + numel);
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_set_linear(syn_cuda_model_t* m, const char* name, syn_qformat_t fmt,
+                                       const void* host, size_t n, size_t k,
+                                       const float* scales_or_null) {
+  if (!m || !name || !host) return SYN_ERR_NULL_PTR;
+  if (m->finalized) return SYN_ERR_INVALID_ARG;
+  if ((int)fmt < 0 || (int)fmt > SYN_QFMT_Q6_K) return SYN_ERR_INVALID_ARG;
+  if (fmt == SYN_QFMT_INT8_KN && !scales_or_null) return SYN_ERR_NULL_PTR;
+  if (fmt != SYN_QFMT_INT8_KN && k % ((fmt == SYN_QFMT_Q4_K || fmt == SYN_QFMT_Q6_K) ? 256 : 32))
+    return SYN_ERR_SHAPE_MISMATCH;
+  HostLinear& hl = m->lin[name];
+  hl.fmt = fmt;
+  hl.n = n;
+  hl.k = k;
+  const uint8_t* p = static_cast<const uint8_t*>(host);
+  hl.data.assign(p, p + weight_bytes(fmt, n, k));
+  if (fmt == SYN_QFMT_INT8_KN) hl.scales.assign(scales_or_null, scales_or_null + n);
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
+  if (!m) return SYN_ERR_NULL_PTR;
+  if (m->finalized) return SYN_OK;
+  DeviceGuard g(m->device);
+  if (!g.ok) return SYN_ERR_CUDA;
+  syn_status_t s;
+  const size_t h = m->h;
+  SYN_CUDA_TRY(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
+  if ((s = upload_tensor(m, "model.embed_tokens.weight", m->V * h, &m->embed, false))) return s;
+  if ((s = upload_tensor(m, "model.norm.weight", h, &m->final_norm, false))) return s;
+  m->layers.resize(m->L);
+  for (size_t i = 0; i < m->L; i++) {
+    LayerDev& ly = m->layers[i];
+    if ((s = upload_tensor(m, lname(i, "input_layernorm.weight"), h, &ly.attn_norm, false))) return s;
+    if ((s = upload_tensor(m, lname(i, "post_attention_layernorm.weight"), h, &ly.ffn_norm, false)))
+      return s;
+    if ((s = upload_tensor(m, lname(i, "self_attn.q_norm.weight"), m->hd, &ly.q_norm, true))) return s;
+    if ((s = upload_tensor(m, lname(i, "self_attn.k_norm.weight"), m->hd, &ly.k_norm, true))) return s;
+    const HostLinear* q = find_lin(m, lname(i, "self_attn.q_proj.weight"), m->qd, h);
+    const HostLinear* k = find_lin(m, lname(i, "self_attn.k_proj.weight"), m->kvd, h);
+    const HostLinear* v = find_lin(m, lname(i, "self_attn.v_proj.weight"), m->kvd, h);
+    const HostLinear* o = find_lin(m, lname(i, "self_attn.o_proj.weight"), h, m->qd);
+    const HostLinear* ga = find_lin(m, lname(i, "mlp.gate_proj.weight"), m->ff, h);
+    const HostLinear* up = find_lin(m, lname(i, "mlp.up_proj.weight"), m->ff, h);
+    const HostLinear* dn = find_lin(m, lname(i, "mlp.down_proj.weight"), h, m->ff);
+    if (!q || !k || !v || !o || !ga || !up || !dn) return SYN_ERR_SHAPE_MISMATCH;
+    if (i == 0) m->int8 = q->fmt == SYN_QFMT_INT8_KN;
+    HostLinear cat;
+    if (!concat({q, k, v}, cat)) return SYN_ERR_INVALID_ARG;
+    if ((s = upload_linear(m, cat, &ly.qkv))) return s;
+    if (!concat({ga, up}, cat)) return SYN_ERR_INVALID_ARG;
+    if ((s = upload_linear(m, cat, &ly.gu))) return s;
+    if ((s = upload_linear(m, *o, &ly.o))) return s;
+    if ((s = upload_linear(m, *dn, &ly.down))) return s;
+  }
+  const HostLinear* lm = find_lin(m, "lm_head.weight", m->V, h);
+  if (!lm) return SYN_ERR_SHAPE_MISMATCH;
+  if ((s = upload_linear(m, *lm, &m->lm_head))) return s;
+  m->lin.clear();
+  m->ten.clear();
+  // RoPE tables for the cache's positions
+  std::vector<float> c(m->max_seq * (m->hd / 2)), sn(c.size());
+  if ((s = syn_cuda_rope_tables(m->rope_base, m->max_seq, m->hd, c.data(), sn.data()))) return s;
+  if ((s = dev_alloc_t(m, &m->cos_t, c.size()))) return s;
+  if ((s = dev_alloc_t(m, &m->sin_t, c.size()))) return s;
+  SYN_CUDA_TRY(cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+  SYN_CUDA_TRY(cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  if ((s = syn_cuda_kvcache_create(m->ctx, m->max_seq, m->Hkv, m->hd, m->L, m->max_batch,
+                                   &m->cache)))
+    return s;
+  const size_t R = m->max_rows;
+  if ((s = dev_alloc_t(m, &m->ids, R))) return s;
+  if ((s = dev_alloc_t(m, &m->tok, m->max_batch))) return s;
+  if ((s = dev_alloc_t(m, &m->resid, R * h))) return s;
+  if ((s = dev_alloc_t(m, &m->x, R * h))) return s;
+  if ((s = dev_alloc_t(m, &m->qkv, R * m->qkv_n))) return s;
+  if ((s = dev_alloc_t(m, &m->att, R * m->qd))) return s;
+  if ((s = dev_alloc_t(m, &m->o, R * h))) return s;
+  if ((s = dev_alloc_t(m, &m->gu, R * 2 * m->ff))) return s;
+  if ((s = dev_alloc_t(m, &m->hid, R * m->ff))) return s;
+  if ((s = dev_alloc_t(m, &m->dn, R * h))) return s;
+  if ((s = dev_alloc_t(m, &m->logits, m->max_batch * m->V))) return s;
+  SYN_CUDA_TRY(cudaMallocHost(&m->ids_h, R * sizeof(int32_t)));
+  SYN_CUDA_TRY(cudaMallocHost(&m->tok_h, m->max_batch * sizeof(int32_t)));
+  SYN_CUDA_TRY(cudaMallocHost(&m->logits_h, m->max_batch * m->V * sizeof(float)));
+  SYN_CUDA_TRY(cudaMallocHost(&m->err_h, sizeof(int32_t)));
+  *m->err_h = 0;
+  SYN_CUDA_TRY(cudaDeviceSynchronize());
+  m->finalized = true;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_prefill(syn_cuda_model_t* m, size_t seq, const int32_t* tokens, size_t n,
+                              float* logits_host, int32_t* next_token) {
+  if (!m || !tokens || !next_token) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  if (seq >= m->max_batch || n == 0) return SYN_ERR_INVALID_ARG;
+  if (m->cache->len[seq] != 0) return SYN_ERR_INVALID_ARG;  // prefill starts a sequence
+  if (n > m->max_seq) return SYN_ERR_INVALID_ARG;           // CacheFull
+  DeviceGuard g(m->device);
+  memcpy(m->ids_h, tokens, n * sizeof(int32_t));
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->ids, m->ids_h, n * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+  syn_status_t s = forward(m, n, true, seq, logits_host != nullptr);
+  if (s) return s;
+  s = finish(m, 1, next_token, logits_host);
+  if (s == SYN_OK) m->cache->len[seq] += n;
+  return s;
+}
+
+syn_status_t syn_cuda_decode_step(syn_cuda_model_t* m, size_t batch, const int32_t* last_tokens,
+                                  int32_t* out_tokens, float* logits_host) {
+  if (!m || !last_tokens || !out_tokens) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  if (batch == 0 || batch > m->max_batch) return SYN_ERR_INVALID_ARG;
+  for (size_t b = 0; b < batch; b++)
+    if (m->cache->len[b] + 1 > m->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  DeviceGuard g(m->device);
+  memcpy(m->ids_h, last_tokens, batch * sizeof(int32_t));
+  const auto key = std::make_pair(batch, logits_host ? 1 : 0);
+  syn_status_t s = SYN_OK;
+  auto it = m->graphs.find(key);
+  if (it != m->graphs.end()) {
+    SYN_CUDA_TRY(cudaGraphLaunch(it->second, m->st));
+  } else if (!use_graphs() || m->eager_runs[key] == 0) {
+    // first step of this shape runs eagerly (it sizes the scratch buffers)
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->ids, m->ids_h, batch * sizeof(int32_t),
+                                 cudaMemcpyHostToDevice, m->st));
+    s = forward(m, batch, false, 0, logits_host != nullptr);
+    if (s) return s;
+    m->eager_runs[key]++;
+  } else {
+    cudaGraph_t graph = nullptr;
+    SYN_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+    cudaError_t ce = cudaMemcpyAsync(m->ids, m->ids_h, batch * sizeof(int32_t),
+                                     cudaMemcpyHostToDevice, m->st);
+    s = ce == cudaSuccess ? forward(m, batch, false, 0, logits_host != nullptr) : SYN_ERR_CUDA;
+    cudaError_t e = cudaStreamEndCapture(m->st, &graph);
+    if (s == SYN_OK && e != cudaSuccess) {
+      set_last_cuda_error(e, "cudaStreamEndCapture");
+      s = SYN_ERR_CUDA;
+    }
+    if (s) {
+      if (graph) cudaGraphDestroy(graph);
+      return s;
+    }
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e, "cudaGraphInstantiate");
+      return SYN_ERR_CUDA;
+    }
+    m->graphs[key] = exec;
+    SYN_CUDA_TRY(cudaGraphLaunch(exec, m->st));
+  }
+  s = finish(m, batch, out_tokens, logits_host);
+  if (s == SYN_OK)
+    for (size_t b = 0; b < batch; b++) m->cache->len[b] += 1;
+  return s;
+}
+
+syn_status_t syn_cuda_model_seq_len(const syn_cuda_model_t* m, size_t seq, size_t* len) {
+  if (!m || !len) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  return syn_cuda_kvcache_len(m->cache, seq, len);
+}
+
+syn_status_t syn_cuda_model_reset(syn_cuda_model_t* m, size_t seq) {
+  if (!m) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  DeviceGuard g(m->device);
+  syn_status_t s = syn_cuda_kvcache_reset(m->cache, seq, m->st);
+  if (s) return s;
+  SYN_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_truncate(syn_cuda_model_t* m, size_t seq, size_t new_len) {
+  if (!m) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  DeviceGuard g(m->device);
+  syn_status_t s = syn_cuda_kvcache_truncate(m->cache, seq, new_len, m->st);
+  if (s) return s;
+  SYN_CUDA_TRY(cudaStreamSynchronize(m->st));
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_destroy(syn_cuda_model_t* m) {
+  if (!m) return SYN_ERR_NULL_PTR;
+  DeviceGuard g(m->device);
+  if (m->st) cudaStreamSynchronize(m->st);
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& ly : m->layers) {
+    if (ly.qkv) syn_cuda_weight_destroy(ly.qkv);
+    if (ly.o) syn_cuda_weight_destroy(ly.o);
+    if (ly.gu) syn_cuda_weight_destroy(ly.gu);
+    if (ly.down) syn_cuda_weight_destroy(ly.down);
+  }
+  if (m->lm_head) syn_cuda_weight_destroy(m->lm_head);
+  if (m->cache) syn_cuda_kvcache_destroy(m->cache);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->ids_h) cudaFreeHost(m->ids_h);
+  if (m->tok_h) cudaFreeHost(m->tok_h);
+  if (m->logits_h) cudaFreeHost(m->logits_h);
+  if (m->err_h) cudaFreeHost(m->err_h);
+  if (m->st) cudaStreamDestroy(m->st);
+  delete m;
+  return SYN_OK;
+}
+
+}  // extern "C"

@@ -59,3 +59,110 @@ def format_bytes(fmt, n, k):
     """Algorithmic weight bytes of one [n, k] matrix in its reference format."""
     fmt = QFormat(fmt)
     return n * row_bytes(fmt, k) + (4 * n if fmt == QFormat.INT8_KN else 0)
+
+
+# ---------------------------------------------------------------------------
+# Random-init language models with the shapes of the benchmark configs
+# ---------------------------------------------------------------------------
+
+def lm_config(name):
+    """Model configs in the reference's JSON schema (configs/*.json) with the
+    shapes of the benchmark configs: qwen3-0.6b (head_dim 128, as the real
+    checkpoint), llama-3.2-1b, mistral-7b (vocab 32000, RoPE base 1e6, sliding
+    window 4096), and small test shapes."""
+    def cfg(h, L, V, hq, hkv, hd, ff, eps, base, window=0):
+        att = {"type": "SlidingWindow" if window else "GQA", "num_heads": hq,
+               "num_kv_heads": hkv, "head_dim": hd}
+        if window:
+            att["window_size"] = window
+        return {"name": name,
+                "architecture": {"hidden_size": h, "num_layers": L, "vocab_size": V,
+                                 "max_sequence_length": 32768, "tie_word_embeddings": True},
+                "attention": att, "norm": {"type": "RMSNorm", "eps": eps},
+                "ffn": {"type": "SwiGLU", "intermediate_size": ff},
+                "position": {"type": "RoPE", "base": base, "max_position_embeddings": 32768},
+                "quantization": {"type": "F32"}}
+    table = {
+        "qwen3-0.6b": cfg(1024, 28, 151936, 16, 8, 128, 3072, 1e-6, 1e6),
+        "llama-3.2-1b": cfg(2048, 16, 128256, 32, 8, 64, 8192, 1e-5, 5e5),
+        "mistral-7b": cfg(4096, 32, 32000, 32, 8, 128, 14336, 1e-5, 1e6, window=4096),
+        # test shapes
+        "tiny": cfg(128, 2, 512, 4, 2, 32, 256, 1e-6, 1e6),
+        "tiny-hd64": cfg(256, 2, 640, 4, 1, 64, 512, 1e-5, 5e5),
+        "tiny-window": cfg(256, 2, 640, 8, 2, 32, 512, 1e-5, 1e6, window=24),
+    }
+    return table[name]
+
+
+def quantize_rows_int8(w):
+    """Per-output-row INT8 weight quantisation (MinMaxCalibration +
+    QuantizedLinear::from_f32_with_scales, int8_linear.rs:21-70): scale =
+    max|row|/127 (1 for a zero row), q = clamp(round(w * (1/scale)), -128,
+    127) with round half away from zero; returns (q [K, N], scales [N])."""
+    w = np.asarray(w, dtype=np.float32)
+    amax = np.abs(w).max(axis=1)
+    scale = np.where(amax == 0, np.float32(1.0), amax / np.float32(127.0)).astype(np.float32)
+    inv = (np.float32(1.0) / scale).astype(np.float32)
+    x = (w * inv[:, None]).astype(np.float32).astype(np.float64)
+    r = np.sign(x) * np.floor(np.abs(x) + 0.5)
+    q = np.clip(r, -128, 127).astype(np.int8)
+    q[amax == 0] = 0
+    return np.ascontiguousarray(q.T), scale
+
+
+def gen_lm_weights(cfg, fmt, seed=1234, dequant=None, qk_norm=None):
+    """Random-init weights of a decoder-only LM in the runner's naming.
+
+    INT8_KN: every linear is N(0, 0.02) f32 quantised per output row; the tied
+    LM head is quantised from the N(0, 0.02) embedding. Block formats: random
+    blocks as in the matmul sweep for every linear including the LM head,
+    and the embedding is the dequantised LM head (`dequant(fmt, blocks, n*k)`
+    must return the f32 values). Norm weights are 1.0. qk_norm (default: for
+    Qwen-style configs with head_dim 128 or the test shapes) adds q/k norms.
+    """
+    fmt = QFormat[fmt] if isinstance(fmt, str) else QFormat(fmt)
+    rng = np.random.default_rng(seed)
+    a, at = cfg["architecture"], cfg["attention"]
+    h, L, V = a["hidden_size"], a["num_layers"], a["vocab_size"]
+    hd = at["head_dim"]
+    qd, kvd = at["num_heads"] * hd, at["num_kv_heads"] * hd
+    ff = cfg["ffn"]["intermediate_size"]
+    if qk_norm is None:
+        qk_norm = cfg.get("name", "").startswith(("qwen", "tiny"))
+    shapes = {"self_attn.q_proj": (qd, h), "self_attn.k_proj": (kvd, h),
+              "self_attn.v_proj": (kvd, h), "self_attn.o_proj": (h, qd),
+              "mlp.gate_proj": (ff, h), "mlp.up_proj": (ff, h), "mlp.down_proj": (h, ff)}
+    w = {}
+
+    def linear(n, k):
+        if fmt == QFormat.INT8_KN:
+            f = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+            q, s = quantize_rows_int8(f)
+            return ("INT8_KN", q, s)
+        blocks, _ = gen_weight(fmt, n, k, rng)
+        return (fmt.name, blocks)
+
+    ones = np.ones(h, np.float32)
+    for i in range(L):
+        p = f"model.layers.{i}."
+        w[p + "input_layernorm.weight"] = ones
+        w[p + "post_attention_layernorm.weight"] = ones
+        if qk_norm:
+            w[p + "self_attn.q_norm.weight"] = np.ones(hd, np.float32)
+            w[p + "self_attn.k_norm.weight"] = np.ones(hd, np.float32)
+        for nm, (n, k) in shapes.items():
+            w[p + nm + ".weight"] = linear(n, k)
+    w["model.norm.weight"] = ones
+    if fmt == QFormat.INT8_KN:
+        emb = rng.standard_normal((V, h), dtype=np.float32) * np.float32(0.02)
+        w["model.embed_tokens.weight"] = emb
+        q, s = quantize_rows_int8(emb)
+        w["lm_head.weight"] = ("INT8_KN", q, s)
+    else:
+        blocks, _ = gen_weight(fmt, V, h, rng)
+        w["lm_head.weight"] = (fmt.name, blocks)
+        if dequant is None:
+            raise ValueError("block-format models need dequant() for the tied embedding")
+        w["model.embed_tokens.weight"] = np.asarray(dequant(fmt, blocks, V * h),
+                                                    dtype=np.float32).reshape(V, h)
+    return w

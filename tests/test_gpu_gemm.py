@@ -59,3 +59,26 @@ def test_gemm_error_word_clear(ctx):
     v = ctypes.c_int32(-1)
     assert sb.lib.syn_cuda_context_get_error(ctx.handle, ctypes.byref(v)) == 0
     assert v.value == 0
+
+
+@pytest.mark.parametrize("fmt", ["Q4_0", "Q4_K", "Q6_K"])
+@pytest.mark.parametrize("scale", [1e6, 1e-6])
+def test_gemm_block_formats_activation_range(ctx, fmt, scale):
+    """Rows far outside fp16 range (and tiny rows) keep the 1e-3 bound: the
+    fp16 operand is scaled per row by an exact power of two."""
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    m, n, k = 24, 256, 512
+    rng = np.random.default_rng(int(scale * 7) % 1000 + 3)
+    f = sb.QFormat[fmt]
+    blocks, _ = synth.gen_weight(f, n, k, rng)
+    x = synth.gen_activations(m, k, rng)
+    x[::2] *= np.float32(scale)
+    w = sb.QuantizedWeight(ctx, f, blocks, n, k)
+    y = w.matmul(torch.from_numpy(x).cuda()).cpu().numpy().reshape(m, n)
+    st, yo = oracle.block_matmul(fmt, m, n, k, x, blocks)
+    yo = yo.reshape(m, n)
+    assert np.all(np.isfinite(y))
+    errs = [max_rel_err(y[i], yo[i]) for i in range(m)]
+    assert max(errs) <= TOL, max(errs)
+    w.close()

@@ -1,0 +1,283 @@
+"""GPU parity of the decoder-layer kernels and the model runner against the
+CPU oracle (oracle/synapse_oracle_lm.c, oracle/lm.py) on seeded inputs.
+
+Bit-exact: RMSNorm, SwiGLU, argmax, RoPE tables, KV-cache contents,
+attention (decode and prefill), and the whole INT8 model (logits and greedy
+tokens). Block-format models compute their matmuls on tensor cores with fp16
+activations, so their logits are compared with a normwise tolerance and
+their tokens wherever the oracle's top-2 margin exceeds the observed error.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from oracle.lm import OracleLM
+
+pytestmark = pytest.mark.gpu
+
+sb = pytest.importorskip("synapse_b200")
+from synapse_b200 import synth  # noqa: E402
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def exact(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    return a.shape == b.shape and np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("h", [4, 7, 128, 1024, 1027, 4096])
+@pytest.mark.parametrize("rows", [1, 3])
+def test_rmsnorm_bit_exact(h, rows):
+    rng = np.random.default_rng(h + rows)
+    x = rng.standard_normal((rows, h)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(h)).astype(np.float32)
+    got = sb.rmsnorm(cuda(x), cuda(w), 1e-6).cpu().numpy()
+    assert exact(got, O.rmsnorm(x, w, h, 1e-6).reshape(rows, h))
+    d = rng.standard_normal((rows, h)).astype(np.float32)
+    r = cuda(x)
+    got = sb.add_rmsnorm(r, cuda(d), cuda(w), 1e-5).cpu().numpy()
+    xs = (x + d).astype(np.float32)
+    assert exact(r.cpu().numpy(), xs)
+    assert exact(got, O.rmsnorm(xs, w, h, 1e-5).reshape(rows, h))
+
+
+@pytest.mark.parametrize("n", [1, 6, 1030, 3072])
+def test_swiglu_bit_exact(n):
+    rng = np.random.default_rng(n)
+    g = (4 * rng.standard_normal((2, n))).astype(np.float32)
+    u = rng.standard_normal((2, n)).astype(np.float32)
+    got0 = sb.swiglu(cuda(g), cuda(u), 0).cpu().numpy()
+    got1 = sb.swiglu(cuda(g), cuda(u), 1).cpu().numpy()
+    for r in range(2):
+        assert exact(got0[r], O.silu_mul(g[r], u[r]))
+        assert exact(got1[r], O.swiglu(g[r], u[r]))
+
+
+def test_argmax_bit_exact():
+    rng = np.random.default_rng(1)
+    cases = [rng.standard_normal(151936).astype(np.float32),
+             np.array([1, 3, 3, 2], np.float32),
+             np.array([5, np.nan, 3, 1], np.float32),
+             np.array([5, 1, np.nan], np.float32),
+             np.array([0.0, -0.0, -1.0], np.float32),
+             np.full(5000, 2.0, np.float32)]
+    big = rng.standard_normal(128256).astype(np.float32)
+    big[[7, 90000, 128000]] = 50.0
+    cases.append(big)
+    for c in cases:
+        got = int(sb.argmax(cuda(c[None, :])).cpu()[0])
+        assert got == O.argmax(c), (c[:8], got)
+
+
+def test_rope_tables_match_oracle():
+    for base, hd in ((1e6, 128), (5e5, 64), (10000.0, 32)):
+        c, s = sb.rope_tables(base, 300, hd)
+        oc, os_ = O.rope_tables(base, 300, hd)
+        assert exact(c.reshape(-1), oc) and exact(s.reshape(-1), os_)
+
+
+def _oracle_head_norm_rope(x, w, heads, hd, eps, cos, sin, pos):
+    x = x.astype(np.float32).copy()
+    if w is not None:
+        x = O.rmsnorm(x, w, hd, eps)
+    O.rope_inplace(x, cos, sin, 1, heads, hd, pos)
+    return x
+
+
+@pytest.mark.parametrize("hq,hkv,hd", [(4, 2, 32), (8, 2, 64), (16, 8, 128), (32, 8, 128)])
+@pytest.mark.parametrize("lengths", [(1, 5), (63, 64), (65, 130)])
+@pytest.mark.parametrize("window,norm", [(0, True), (24, False)])
+def test_attention_decode_bit_exact(ctx, hq, hkv, hd, lengths, window, norm):
+    rng = np.random.default_rng(hq * 1000 + hd + lengths[0] + window)
+    max_seq, B = 160, 2
+    qd, kvd = hq * hd, hkv * hd
+    eps = 1e-6
+    cache = sb.KVCache(ctx, max_seq, hkv, hd, 1, batch=B)
+    cos, sin = sb.rope_tables(1e6, max_seq, hd)
+    oc, os_ = O.rope_tables(1e6, max_seq, hd)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) if norm else None
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32) if norm else None
+    hist = []
+    for b, L in enumerate(lengths):
+        prev = L - 1
+        kh = rng.standard_normal((max(prev, 1), kvd)).astype(np.float32)
+        vh = rng.standard_normal((max(prev, 1), kvd)).astype(np.float32)
+        if prev:
+            cache.append(0, cuda(kh[:prev]), cuda(vh[:prev]), seq=b)
+            cache.advance(prev, seq=b)
+        hist.append((kh[:prev], vh[:prev]))
+    qkv = rng.standard_normal((B, qd + 2 * kvd)).astype(np.float32)
+    out = sb.attention_decode(cache, 0, cuda(qkv), hq, cuda(qn) if norm else None,
+                              cuda(kn) if norm else None, eps, cuda(cos), cuda(sin),
+                              window=window, batch=B).cpu().numpy()
+    for b, L in enumerate(lengths):
+        pos = L - 1
+        q = _oracle_head_norm_rope(qkv[b, :qd], qn, hq, hd, eps, oc, os_, pos)
+        k = _oracle_head_norm_rope(qkv[b, qd:qd + kvd], kn, hkv, hd, eps, oc, os_, pos)
+        v = qkv[b, qd + kvd:]
+        kc = np.concatenate([hist[b][0], k[None, :]])
+        vc = np.concatenate([hist[b][1], v[None, :]])
+        want = O.attention_decode(q, kc, vc, L, hq, hkv, hd, window)
+        assert exact(out[b], want), (b, L, np.abs(out[b] - want).max())
+        kv, vv = cache.view(0, b)
+        assert exact(kv[pos].cpu().numpy(), k) and exact(vv[pos].cpu().numpy(), v)
+        assert cache.length(b) == L - 1  # not advanced
+    cache.close()
+
+
+@pytest.mark.parametrize("S", [1, 5, 16, 17, 33, 40, 70])
+@pytest.mark.parametrize("hq,hkv,hd", [(4, 2, 32), (8, 2, 128)])
+def test_attention_prefill_bit_exact(ctx, S, hq, hkv, hd):
+    rng = np.random.default_rng(S * 7 + hd)
+    qd, kvd = hq * hd, hkv * hd
+    eps = 1e-6
+    cache = sb.KVCache(ctx, 96, hkv, hd, 2, batch=2)
+    cos, sin = sb.rope_tables(1e6, 96, hd)
+    oc, os_ = O.rope_tables(1e6, 96, hd)
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    qkv = rng.standard_normal((S, qd + 2 * kvd)).astype(np.float32)
+    out = sb.attention_prefill(cache, 1, cuda(qkv), hq, cuda(qn), cuda(kn), eps, cuda(cos),
+                               cuda(sin), seq=1).cpu().numpy()
+    q = O.rmsnorm(qkv[:, :qd], qn, hd, eps)
+    k = O.rmsnorm(qkv[:, qd:qd + kvd], kn, hd, eps)
+    O.rope_inplace(q, oc, os_, S, hq, hd, 0)
+    O.rope_inplace(k, oc, os_, S, hkv, hd, 0)
+    q3, k3 = q.reshape(S, hq, hd), k.reshape(S, hkv, hd)
+    v3 = qkv[:, qd + kvd:].reshape(S, hkv, hd)
+    g = hq // hkv
+    for h in range(hq):
+        st, o = O.fused_attention(S, S, hd, q3[:, h], k3[:, h // g], v3[:, h // g])
+        assert exact(out[:, h * hd:(h + 1) * hd], o.reshape(S, hd)), h
+    kv, vv = cache.view(1, 1)
+    assert exact(kv[:S].cpu().numpy(), k.reshape(S, kvd))
+    assert exact(vv[:S].cpu().numpy(), qkv[:, qd + kvd:])
+    cache.close()
+
+
+def test_kvcache_lengths_and_full(ctx):
+    c = sb.KVCache(ctx, 4, 1, 8, 2, batch=2)
+    z = torch.zeros(3, 8, device="cuda")
+    c.append(0, z, z, seq=1)
+    c.advance(3, seq=1)
+    assert c.length(1) == 3 and c.length(0) == 0
+    with pytest.raises(sb.SynapseError) as e:
+        c.advance(2, seq=1)  # CacheFull -> INVALID_ARG (mapError)
+    assert e.value.status == 2
+    c.truncate(5, seq=1)
+    assert c.length(1) == 3  # truncateTo only shortens
+    c.truncate(1, seq=1)
+    assert c.length(1) == 1
+    c.reset(seq=1)
+    assert c.length(1) == 0
+    c.close()
+
+
+def _gpu_model(ctx, cfg, w, max_seq, max_batch=1):
+    return sb.Model(ctx, cfg, w, max_seq, max_batch)
+
+
+@pytest.mark.parametrize("name", ["tiny", "tiny-hd64", "tiny-window"])
+def test_int8_model_bit_exact_tokens_and_logits(ctx, name):
+    cfg = synth.lm_config(name)
+    w = synth.gen_lm_weights(cfg, "INT8_KN", seed=21)
+    prompt = [3, 77, 140, 9, 255, 31, 64]
+    steps = 40
+    ref = OracleLM(cfg, w, 64)
+    m = _gpu_model(ctx, cfg, w, 64)
+    lref = ref.forward_prefill(prompt)
+    tok, lg = m.forward_prefill(prompt)
+    assert exact(lg, lref)
+    assert tok == O.argmax(lref)
+    for i in range(steps):
+        lref = ref.forward_one(tok)
+        nxt, lg = m.forward_one([tok])
+        assert exact(lg[0], lref), (i, np.abs(lg[0] - lref).max())
+        assert int(nxt[0]) == O.argmax(lref)
+        tok = int(nxt[0])
+    assert m.seq_len() == len(prompt) + steps
+    m.close()
+
+
+def test_int8_model_batch_matches_single_sequences(ctx):
+    cfg = synth.lm_config("tiny")
+    w = synth.gen_lm_weights(cfg, "INT8_KN", seed=5)
+    prompts = [[1, 2, 3, 4, 5], [400, 300, 200]]
+    m = _gpu_model(ctx, cfg, w, 64, max_batch=2)
+    toks = [m.forward_prefill(p, seq=i, want_logits=False)[0] for i, p in enumerate(prompts)]
+    refs = [OracleLM(cfg, w, 64) for _ in prompts]
+    rt = [refs[i].forward_prefill(p) for i, p in enumerate(prompts)]
+    assert toks == [O.argmax(x) for x in rt]
+    for step in range(12):
+        nxt, lg = m.forward_one(toks)
+        for i in range(2):
+            lr = refs[i].forward_one(toks[i])
+            assert exact(lg[i], lr), (step, i)
+        toks = [int(t) for t in nxt]
+    m.close()
+
+
+def test_int8_model_greedy_generation_and_reset(ctx):
+    cfg = synth.lm_config("tiny")
+    w = synth.gen_lm_weights(cfg, "INT8_KN", seed=9)
+    m = _gpu_model(ctx, cfg, w, 64)
+    t1 = m.generate_greedy([10, 20, 30], 24)
+    ref, _ = OracleLM(cfg, w, 64).generate_greedy([10, 20, 30], 24)
+    assert t1 == ref
+    with pytest.raises(sb.SynapseError):
+        m.forward_prefill([1, 2])  # the sequence is not empty
+    m.reset()
+    assert m.seq_len() == 0
+    assert m.generate_greedy([10, 20, 30], 24) == ref
+    m.truncate(5)
+    assert m.seq_len() == 5
+    m.close()
+
+
+@pytest.mark.parametrize("fmt,name", [("Q4_0", "tiny"), ("Q8_0", "tiny"), ("Q4_K", "tiny-hd64"),
+                                      ("Q6_K", "tiny-hd64")])
+def test_block_model_logits_within_tolerance(ctx, fmt, name):
+    cfg = synth.lm_config(name)
+    w = synth.gen_lm_weights(cfg, fmt, seed=13,
+                             dequant=lambda f, b, n: O.dequant(f.name, b, n)[1])
+    prompt = [7, 8, 9, 100, 200, 11, 12, 13, 14, 15]
+    ref = OracleLM(cfg, w, 64)
+    m = _gpu_model(ctx, cfg, w, 64)
+    lref = ref.forward_prefill(prompt)
+    tok, lg = m.forward_prefill(prompt)
+    err = np.linalg.norm(lg - lref) / np.linalg.norm(lref)
+    assert err < 5e-3, err
+    agree = 0
+    for i in range(16):
+        srt = np.sort(lref)
+        if O.argmax(lref) != tok:
+            # a disagreement is only allowed where the oracle's margin is tiny
+            assert srt[-1] - srt[-2] < 20 * np.abs(lg - lref).max() + 1e-6
+            break
+        agree += 1
+        lref = ref.forward_one(tok)
+        nxt, lgs = m.forward_one([tok])
+        lg = lgs[0]
+        err = np.linalg.norm(lg - lref) / np.linalg.norm(lref)
+        assert err < 5e-3, (i, err)
+        tok = int(nxt[0])
+    assert agree >= 4
+    m.close()
+
+
+def test_qwen3_0p6b_int8_greedy_64_tokens_identical(ctx):
+    """Config 1 at full size: 16-token prompt, 64 greedy tokens, token ids and
+    final logits identical to the oracle (int8.rs:593-709)."""
+    cfg = synth.lm_config("qwen3-0.6b")
+    w = synth.gen_lm_weights(cfg, "INT8_KN", seed=1234)
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, cfg["architecture"]["vocab_size"], 16).tolist()
+    m = _gpu_model(ctx, cfg, w, 128)
+    got = m.generate_greedy(prompt, 64)
+    m.close()
+    ref, margins = OracleLM(cfg, w, 128).generate_greedy(prompt, 64)
+    assert got == ref, (got, ref, margins)
