@@ -102,7 +102,15 @@ __device__ float norm_scale(const float* sx, int h, float eps, float* lane) {
   if (threadIdx.x < 4) {
     const int n4 = h & ~3;
     float acc = 0.0f;
-    for (int i = threadIdx.x; i < n4; i += 4) acc = __fadd_rn(acc, __fmul_rn(sx[i], sx[i]));
+    int i = threadIdx.x;
+    for (; i + 60 < n4; i += 64) {  // 16 loads in flight, then the add chain
+      float v[16];
+#pragma unroll
+      for (int u = 0; u < 16; u++) v[u] = sx[i + 4 * u];
+#pragma unroll
+      for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+    }
+    for (; i < n4; i += 4) acc = __fadd_rn(acc, __fmul_rn(sx[i], sx[i]));
     lane[threadIdx.x] = acc;
   }
   __syncthreads();
@@ -123,17 +131,43 @@ __global__ void __launch_bounds__(NORM_THREADS) k_add_rmsnorm(const NormParams p
     zero = id >= p.vocab;  // ids outside the vocabulary embed as zeros
     src = p.table + (size_t)(zero ? 0 : id) * p.h;
   }
-  for (int j = threadIdx.x; j < p.h; j += NORM_THREADS) {
-    float v = zero ? 0.0f : src[j];
-    if (p.delta) v = __fadd_rn(v, p.delta[row * p.ldd + j]);
-    sx[j] = v;
-    if (p.x_out) p.x_out[row * p.ldxo + j] = v;
+  // all loads of a batch are issued before any store (x_out may alias x)
+  constexpr int NV = 8;
+  const int tid = threadIdx.x;
+  for (int j0 = 0; j0 < p.h; j0 += NORM_THREADS * NV) {
+    float v[NV], dl[NV];
+#pragma unroll
+    for (int u = 0; u < NV; u++) {
+      const int j = j0 + tid + u * NORM_THREADS;
+      v[u] = (j < p.h && !zero) ? src[j] : 0.0f;
+      dl[u] = (j < p.h && p.delta) ? p.delta[row * p.ldd + j] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < NV; u++) {
+      const int j = j0 + tid + u * NORM_THREADS;
+      if (j < p.h) {
+        const float x = p.delta ? __fadd_rn(v[u], dl[u]) : v[u];
+        sx[j] = x;
+        if (p.x_out) p.x_out[row * p.ldxo + j] = x;
+      }
+    }
   }
   __syncthreads();
   const float scale = norm_scale(sx, p.h, p.eps, lane);
   griddep_launch();
-  for (int j = threadIdx.x; j < p.h; j += NORM_THREADS)
-    p.out[row * p.ldo + j] = __fmul_rn(__fmul_rn(sx[j], p.w[j]), scale);
+  for (int j0 = 0; j0 < p.h; j0 += NORM_THREADS * NV) {
+    float wv[NV];
+#pragma unroll
+    for (int u = 0; u < NV; u++) {
+      const int j = j0 + tid + u * NORM_THREADS;
+      wv[u] = j < p.h ? p.w[j] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < NV; u++) {
+      const int j = j0 + tid + u * NORM_THREADS;
+      if (j < p.h) p.out[row * p.ldo + j] = __fmul_rn(__fmul_rn(sx[j], wv[u]), scale);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -203,101 +237,163 @@ __device__ void norm_rope(float* x, int nv, int hd, const float* wq, const float
   __syncthreads();
 }
 
-// ---------------------------------------------------------------------------
-// Decode: one CTA per (sequence, KV head); threads = group size * hd.
-// cached_attention_decode (ops/attention.rs:24-147) for the group's heads.
-// ---------------------------------------------------------------------------
-constexpr int MAX_GROUPS = 8;
+// Sequential left-to-right sum (the reference's `sum += x`), with the smem
+// loads issued in batches so that only the add chain is serial.
+__device__ __forceinline__ float serial_sum(const float* r, int n) {
+  float sum = 0.0f;
+  int s = 0;
+  for (; s + 16 <= n; s += 16) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) v[u] = r[s + u];
+#pragma unroll
+    for (int u = 0; u < 16; u++) sum = __fadd_rn(sum, v[u]);
+  }
+  for (; s < n; s++) sum = __fadd_rn(sum, r[s]);
+  return sum;
+}
 
-__global__ void __launch_bounds__(1024) k_attn_decode(const AttnParams p) {
-  extern __shared__ float sm[];
-  const int b = blockIdx.x, kvh = blockIdx.y;
-  const int G = p.n_heads / p.n_kv, hd = p.hd, kvd = p.n_kv * hd;
-  const int nt = blockDim.x, tid = threadIdx.x;
-  float* xs = sm;                      // (G+1) vectors: q heads, then k
-  float* lanes = xs + (G + 1) * hd;    // 4*(G+1)
-  float* scl = lanes + 4 * (G + 1);    // G+1
-  float* sc = scl + (G + 1);           // G * eff scores
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float m = red[0];
+  for (int i = 1; i < nw; i++) m = fmaxf(m, red[i]);
+  return m;
+}
+
+// ---------------------------------------------------------------------------
+// Decode: one CTA of DEC_THREADS per (sequence, query head):
+// cached_attention_decode (ops/attention.rs:24-147). Every CTA of a KV group
+// normalises and rotates the new K itself (same bits), the group's first
+// CTA appends K and V to the cache, and the new position is read from smem,
+// so no CTA waits for another.
+// ---------------------------------------------------------------------------
+constexpr int DEC_THREADS = 128;
+constexpr int DEC_CH = 64;  // V rows staged per chunk
+
+template <int HD>
+__global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p) {
+  extern __shared__ __align__(16) float sm[];
+  constexpr int Q4 = HD / 4;
+  constexpr int VS = HD + 4;             // staged row stride
+  float* xs = sm;                        // q (HD) then k (HD), then v (HD)
+  float* vb = sm + 3 * HD;               // DEC_CH staged V rows
+  float* lanes = vb + DEC_CH * VS;       // 8
+  float* scl = lanes + 8;                // 2 (+2 pad)
+  float* red = scl + 4;                  // DEC_THREADS / 32
+  float* sc = red + DEC_THREADS / 32;    // scores, eff
+  const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int G = p.n_heads / p.n_kv, kvh = h / G, kvd = p.n_kv * HD;
   griddep_wait();
   const int pos = p.len[b];
   if (pos >= p.max_seq) {  // cache full: nothing is written (the host reports it)
     if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
     return;
   }
-  const float* qrow = p.q + (long long)b * p.ld + (long long)kvh * G * hd;
-  const float* krow = p.k + (long long)b * p.ld + (long long)kvh * hd;
-  const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * hd;
-  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * hd;
-  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * hd;
-  for (int i = tid; i < G * hd; i += nt) xs[i] = qrow[i];
-  for (int i = tid; i < hd; i += nt) {
-    xs[G * hd + i] = krow[i];
-    vcb[(size_t)pos * kvd + i] = vrow[i];  // raw V
+  const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
+  const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
+  const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
+  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
+  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
+  for (int i = tid; i < HD; i += DEC_THREADS) {
+    xs[i] = qrow[i];
+    xs[HD + i] = krow[i];
+    xs[2 * HD + i] = vrow[i];
   }
   __syncthreads();
-  norm_rope(xs, G + 1, hd, p.qn, p.kn, G, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, nt);
-  for (int i = tid; i < hd; i += nt) kcb[(size_t)pos * kvd + i] = xs[G * hd + i];
-  __syncthreads();  // the appended row is visible to the whole CTA
+  norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, DEC_THREADS);
+  if (h % G == 0)
+    for (int i = tid; i < HD; i += DEC_THREADS) {
+      kcb[(size_t)pos * kvd + i] = xs[HD + i];
+      vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
+    }
 
   const int L = pos + 1;
   const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
   const int eff = L - off;
   // scores: below 64 positions the reference's scalar loop (sum += a*b);
-  // from 64 on matmul_t: @mulAdd except the last eff%8 columns
+  // from 64 on matmul_t (@mulAdd except the last eff%8 columns). Each thread
+  // holds one K row in registers (all loads in flight at once).
   const int s_full = eff < 64 ? 0 : eff - (eff & 7);
-  for (int s = tid; s < eff; s += nt) {
-    const float* kr = kcb + (size_t)(off + s) * kvd;
+  for (int s = tid; s < eff; s += DEC_THREADS) {
+    const int row = off + s;
+    const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
+    float4 kv[Q4];
+#pragma unroll
+    for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
     const bool fused = s < s_full;
-    float acc[MAX_GROUPS];
+    float acc = 0.0f;
 #pragma unroll
-    for (int g = 0; g < MAX_GROUPS; g++) acc[g] = 0.0f;
-    for (int d = 0; d < hd; d += 4) {
-      const float4 kv = *reinterpret_cast<const float4*>(kr + d);
+    for (int c = 0; c < Q4; c++) {
+      const float4 q = reinterpret_cast<const float4*>(xs)[c];
+      acc = chain(fused, q.x, kv[c].x, acc);
+      acc = chain(fused, q.y, kv[c].y, acc);
+      acc = chain(fused, q.z, kv[c].z, acc);
+      acc = chain(fused, q.w, kv[c].w, acc);
+    }
+    sc[s] = __fmul_rn(acc, p.scale);
+  }
+  __syncthreads();
+  // softmax_slice (ops/activation.rs:117-130)
+  float mx = -INFINITY;
+  for (int s = tid; s < eff; s += DEC_THREADS) mx = fmaxf(mx, sc[s]);
+  mx = block_max(mx, red);
+  for (int s = tid; s < eff; s += DEC_THREADS) sc[s] = exp_f32(__fsub_rn(sc[s], mx));
+  __syncthreads();
+  if (tid == 0) red[0] = serial_sum(sc, eff);
+  __syncthreads();
+  const float sum = red[0];
+  if (sum > 0.0f)
+    for (int s = tid; s < eff; s += DEC_THREADS) sc[s] = __fdiv_rn(sc[s], sum);
+  griddep_launch();
+  // score * V: below 64 positions sum += p*v; from 64 on matmul_nn
+  // (@mulAdd except the last hd%32 columns). V rows staged DEC_CH at a time.
+  const bool vfused = eff >= 64 && tid < HD - (HD & 31);
+  float acc = 0.0f;
+  constexpr int PER = (DEC_CH * Q4 + DEC_THREADS - 1) / DEC_THREADS;  // float4 per thread
+  for (int c0 = 0; c0 < eff; c0 += DEC_CH) {
+    const int cn = min(DEC_CH, eff - c0);
+    __syncthreads();  // previous chunk consumed (and sc final on the first pass)
+    float4 tmp[PER];
 #pragma unroll
-      for (int g = 0; g < MAX_GROUPS; g++) {
-        if (g < G) {
-          const float* qg = xs + g * hd + d;
-          acc[g] = chain(fused, qg[0], kv.x, acc[g]);
-          acc[g] = chain(fused, qg[1], kv.y, acc[g]);
-          acc[g] = chain(fused, qg[2], kv.z, acc[g]);
-          acc[g] = chain(fused, qg[3], kv.w, acc[g]);
-        }
+    for (int u = 0; u < PER; u++) {
+      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
+      if (r < cn) {
+        const int row = off + c0 + r;
+        tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
+                            : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
       }
     }
 #pragma unroll
-    for (int g = 0; g < MAX_GROUPS; g++)
-      if (g < G) sc[g * eff + s] = __fmul_rn(acc[g], p.scale);
+    for (int u = 0; u < PER; u++) {
+      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
+      if (r < cn) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
+    }
+    __syncthreads();
+    if (tid < HD) {
+      const float* pr = sc + c0;
+      int s = 0;
+      for (; s + 8 <= cn; s += 8) {
+        float pv[8], vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+          pv[u] = pr[s + u];
+          vv[u] = vb[(s + u) * VS + tid];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) acc = chain(vfused, pv[u], vv[u], acc);
+      }
+      for (; s < cn; s++) acc = chain(vfused, pr[s], vb[s * VS + tid], acc);
+    }
   }
-  __syncthreads();
-  // softmax_slice per head: warp g
-  const int warp = tid >> 5, lane = tid & 31;
-  for (int g = warp; g < G; g += nt >> 5) {
-    float* r = sc + g * eff;
-    float mx = -INFINITY;
-    for (int s = lane; s < eff; s += 32) mx = fmaxf(mx, r[s]);
-    mx = warp_max(mx);
-    for (int s = lane; s < eff; s += 32) r[s] = exp_f32(__fsub_rn(r[s], mx));
-    __syncwarp();
-    float sum = 0.0f;
-    if (lane == 0)
-      for (int s = 0; s < eff; s++) sum = __fadd_rn(sum, r[s]);
-    sum = __shfl_sync(0xffffffffu, sum, 0);
-    if (sum > 0.0f)
-      for (int s = lane; s < eff; s += 32) r[s] = __fdiv_rn(r[s], sum);
-  }
-  __syncthreads();
-  griddep_launch();
-  // score * V: below 64 positions sum += p*v; from 64 on matmul_nn
-  // (f32GemvRow without trans_b: @mulAdd except the last hd%32 columns)
-  for (int t = tid; t < G * hd; t += nt) {
-    const int g = t / hd, d = t - g * hd;
-    const bool fused = eff >= 64 && d < hd - (hd & 31);
-    const float* pr = sc + g * eff;
-    const float* vcol = vcb + (size_t)off * kvd + d;
-    float acc = 0.0f;
-    for (int s = 0; s < eff; s++) acc = chain(fused, pr[s], vcol[(size_t)s * kvd], acc);
-    p.out[(long long)b * p.ldo + (long long)(kvh * G + g) * hd + d] = acc;
-  }
+  if (tid < HD) p.out[(long long)b * p.ldo + (long long)h * HD + tid] = acc;
+}
+
+size_t decode_smem_floats(int hd, int eff) {
+  return (size_t)3 * hd + (size_t)DEC_CH * (hd + 4) + 8 + 4 + DEC_THREADS / 32 + eff;
 }
 
 // ---------------------------------------------------------------------------
@@ -511,71 +607,88 @@ __global__ void k_swiglu(const float* __restrict__ gate, const float* __restrict
 // ---------------------------------------------------------------------------
 // argmax (generation/sampler.rs:217-224): Iterator::max_by with partial_cmp,
 // NaN comparing Equal. The running best is replaced unless it is strictly
-// greater, so: the answer is the last index of the maximum over the elements
-// after the last NaN (or that NaN itself when it is the last element).
-// One CTA per row; optionally advances the KV-cache lengths afterwards.
+// greater, so the answer is the last index of the maximum over the elements
+// after the last NaN (or that NaN itself when nothing follows it).
+// That rule is a fold over contiguous segments with an associative combine,
+// so the row is split over CTAs of AM_THREADS * AM_PER elements, reduced in
+// index order inside each CTA, and the last CTA of a row (arrival counter)
+// combines the CTA states in order. It can also advance the KV-cache lengths.
 // ---------------------------------------------------------------------------
-constexpr int AM_THREADS = 1024;
+constexpr int AM_THREADS = 256, AM_PER = 8, AM_SEG = AM_THREADS * AM_PER;
+
+struct AmState {
+  int nan;  // last NaN index in the segment, -1 if none
+  int i;    // best index after `nan`, -1 if none
+  float v;
+};
+
+__device__ __forceinline__ AmState am_combine(AmState l, const AmState& r) {
+  if (r.nan >= 0) return r;  // nothing before r's NaN survives
+  if (r.i >= 0 && (l.i < 0 || r.v >= l.v)) {  // the later segment wins ties
+    l.i = r.i;
+    l.v = r.v;
+  }
+  return l;
+}
+
+__device__ __forceinline__ AmState am_shfl_down(const AmState& s, int o) {
+  AmState r;
+  r.nan = __shfl_down_sync(0xffffffffu, s.nan, o);
+  r.i = __shfl_down_sync(0xffffffffu, s.i, o);
+  r.v = __shfl_down_sync(0xffffffffu, s.v, o);
+  return r;
+}
 
 __global__ void __launch_bounds__(AM_THREADS) k_argmax(const float* __restrict__ x, long long ldx,
                                                        int n, int32_t* __restrict__ out,
-                                                       int* len_adv, int adv, int max_len) {
-  __shared__ int s_i[AM_THREADS / 32];
-  __shared__ float s_v[AM_THREADS / 32];
-  __shared__ int s_nan;
+                                                       int* len_adv, int adv, int max_len,
+                                                       AmState* __restrict__ part,
+                                                       int* __restrict__ cnt) {
+  __shared__ AmState ws[AM_THREADS / 32];
+  __shared__ int last;
   griddep_wait();
-  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.y, c = blockIdx.x, nct = gridDim.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* xr = x + row * ldx;
-  int lastnan = -1;
-  for (int i = tid; i < n; i += AM_THREADS)
-    if (isnan(xr[i])) lastnan = i;
-  for (int o = 16; o; o >>= 1) lastnan = max(lastnan, __shfl_xor_sync(0xffffffffu, lastnan, o));
-  if (lane == 0) s_i[warp] = lastnan;
+  const int base = c * AM_SEG + tid * AM_PER;
+  float v[AM_PER];
+#pragma unroll
+  for (int u = 0; u < AM_PER; u++) v[u] = base + u < n ? xr[base + u] : 0.0f;
+  AmState st{-1, -1, 0.0f};
+#pragma unroll
+  for (int u = 0; u < AM_PER; u++) {
+    if (base + u < n) {
+      if (isnan(v[u])) {
+        st.nan = base + u;
+        st.i = -1;
+      } else if (st.i < 0 || v[u] >= st.v) {
+        st.i = base + u;
+        st.v = v[u];
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const AmState r = am_shfl_down(st, o);
+    if ((lane & (2 * o - 1)) == 0) st = am_combine(st, r);
+  }
+  if (lane == 0) ws[warp] = st;
   __syncthreads();
   if (tid == 0) {
-    int m = -1;
-    for (int w = 0; w < AM_THREADS / 32; w++) m = max(m, s_i[w]);
-    s_nan = m;
-  }
-  __syncthreads();
-  const int ln = s_nan;
-  float bv = -INFINITY;
-  int bi = -1;
-  for (int i = ln + 1 + tid; i < n; i += AM_THREADS) {
-    const float v = xr[i];
-    if (bi < 0 || v >= bv) {  // later index wins ties (+0 == -0)
-      bv = v;
-      bi = i;
-    }
-  }
-  for (int o = 16; o; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi > bi))) {
-      bv = ov;
-      bi = oi;
-    }
-  }
-  __syncthreads();
-  if (lane == 0) {
-    s_i[warp] = bi;
-    s_v[warp] = bv;
+    AmState t = ws[0];
+    for (int w = 1; w < AM_THREADS / 32; w++) t = am_combine(t, ws[w]);
+    part[row * nct + c] = t;
+    __threadfence();
+    last = atomicAdd(&cnt[row], 1) == nct - 1;
   }
   __syncthreads();
   griddep_launch();
-  if (tid == 0) {
-    int ri = -1;
-    float rv = -INFINITY;
-    for (int w = 0; w < AM_THREADS / 32; w++) {
-      const int oi = s_i[w];
-      const float ov = s_v[w];
-      if (oi >= 0 && (ri < 0 || ov > rv || (ov == rv && oi > ri))) {
-        rv = ov;
-        ri = oi;
-      }
-    }
-    if (ri < 0) ri = ln >= 0 ? ln : 0;  // nothing after the last NaN: the NaN itself
-    out[row] = ri;
+  if (last && tid == 0) {
+    __threadfence();
+    AmState t = part[row * nct];
+    for (int k = 1; k < nct; k++) t = am_combine(t, part[row * nct + k]);
+    out[row] = t.i >= 0 ? t.i : (t.nan >= 0 ? t.nan : 0);
+    cnt[row] = 0;  // ready for the next launch
     if (len_adv) {
       const int nl = len_adv[row] + adv;
       len_adv[row] = nl <= max_len ? nl : max_len;
@@ -623,11 +736,22 @@ syn_status_t launch_swiglu(const float* gate, const float* up, size_t ld_in, siz
                      "k_swiglu");
 }
 
+size_t argmax_scratch_bytes(size_t rows, size_t n) {
+  const size_t nct = (n + AM_SEG - 1) / AM_SEG;
+  return rows * nct * sizeof(AmState) + rows * sizeof(int) + 64;
+}
+
 syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
-                           int* len_adv, int adv, int max_len, cudaStream_t st) {
+                           int* len_adv, int adv, int max_len, void* scratch, cudaStream_t st) {
   if (!rows || !n) return SYN_OK;
-  return cuda_status(launch_pdl(k_argmax, dim3((unsigned)rows), dim3(AM_THREADS), 0, st, x,
-                                (long long)ldx, (int)n, out, len_adv, adv, max_len),
+  const size_t nct = (n + AM_SEG - 1) / AM_SEG;
+  if (nct > 65535 || rows > 65535) return SYN_ERR_UNSUPPORTED;
+  int* cnt = static_cast<int*>(scratch);  // zero before the first launch; left zero
+  AmState* part = reinterpret_cast<AmState*>(static_cast<uint8_t*>(scratch) +
+                                             ((rows * sizeof(int) + 63) & ~size_t(63)));
+  return cuda_status(launch_pdl(k_argmax, dim3((unsigned)nct, (unsigned)rows), dim3(AM_THREADS), 0,
+                                st, x, (long long)ldx, (int)n, out, len_adv, adv, max_len, part,
+                                cnt),
                      "k_argmax");
 }
 
@@ -639,9 +763,6 @@ syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, in
 namespace syn {
 namespace {
 
-size_t decode_smem(int G, int hd, int eff) {
-  return ((size_t)(G + 1) * hd + 4 * (G + 1) + (G + 1) + (size_t)G * eff) * sizeof(float);
-}
 
 int prefill_rows(int S, int hd) {
   for (int pr = 16; pr >= 1; pr >>= 1) {
@@ -691,23 +812,25 @@ syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, 
   syn_status_t s = make_params(a, p, 0, 1);
   if (s) return s;
   p.err = err;
-  const int G = p.n_heads / p.n_kv;
-  if (G > MAX_GROUPS || G * p.hd > 1024) return SYN_ERR_UNSUPPORTED;
   if (batch > a.cache->batch) return SYN_ERR_INVALID_ARG;
   for (size_t b = 0; b < batch; b++)
     if (a.cache->len[b] >= a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
-  size_t maxlen = 0;
-  for (size_t b = 0; b < batch; b++) maxlen = std::max(maxlen, a.cache->len[b] + 1);
-  // The graph replays at growing positions: size smem for the whole window.
+  // A captured graph replays at growing positions: size smem for the window.
   size_t eff = a.cache->max_seq;
   if (a.window && a.window < eff) eff = a.window;
-  const size_t smem = decode_smem(G, p.hd, (int)eff);
+  const size_t smem = decode_smem_floats(p.hd, (int)eff) * sizeof(float);
   if (smem > kMaxSmem) return SYN_ERR_UNSUPPORTED;
-  (void)maxlen;
-  s = allow_smem((const void*)k_attn_decode, smem);
+  void (*kern)(const AttnParams) = nullptr;
+  switch (p.hd) {
+    case 32: kern = k_attn_decode<32>; break;
+    case 64: kern = k_attn_decode<64>; break;
+    case 128: kern = k_attn_decode<128>; break;
+    default: return SYN_ERR_UNSUPPORTED;
+  }
+  s = allow_smem((const void*)kern, smem);
   if (s) return s;
-  return cuda_status(launch_pdl(k_attn_decode, dim3((unsigned)batch, (unsigned)p.n_kv),
-                                dim3(G * p.hd), smem, st, p),
+  return cuda_status(launch_pdl(kern, dim3((unsigned)batch, (unsigned)p.n_heads), dim3(DEC_THREADS),
+                                smem, st, p),
                      "k_attn_decode");
 }
 
@@ -974,7 +1097,19 @@ syn_status_t syn_cuda_argmax(const float* logits, size_t rows, size_t n, int32_t
                              void* stream) {
   if (!logits || !out_idx) return SYN_ERR_NULL_PTR;
   if (n > 0x7FFFFFFF) return SYN_ERR_UNSUPPORTED;
-  return launch_argmax(logits, n, rows, n, out_idx, nullptr, 0, 0, (cudaStream_t)stream);
+  if (!rows || !n) return SYN_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  // stream-ordered scratch: zeroed arrival counters + per-CTA states
+  void* scratch = nullptr;
+  const size_t bytes = argmax_scratch_bytes(rows, n);
+  SYN_CUDA_TRY(cudaMallocAsync(&scratch, bytes, st));
+  cudaError_t e = cudaMemsetAsync(scratch, 0, bytes, st);
+  syn_status_t s = e == cudaSuccess
+                       ? launch_argmax(logits, n, rows, n, out_idx, nullptr, 0, 0, scratch, st)
+                       : cuda_status(e, "cudaMemsetAsync");
+  e = cudaFreeAsync(scratch, st);
+  if (s == SYN_OK && e != cudaSuccess) s = cuda_status(e, "cudaFreeAsync");
+  return s;
 }
 
 }  // extern "C"

@@ -204,6 +204,7 @@ struct syn_cuda_model_s {
   std::vector<void*> allocs;
   int32_t* ids = nullptr;
   int32_t* tok = nullptr;
+  void* am_scratch = nullptr;
   float *resid = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *o = nullptr,
         *gu = nullptr, *hid = nullptr, *dn = nullptr, *logits = nullptr;
   // pinned host staging
@@ -326,7 +327,7 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   if (s) return s;
   if ((s = mm(m, m->lm_head, m->x, nr, m->logits))) return s;
   s = launch_argmax(m->logits, m->V, nr, m->V, m->tok, m->cache->d_len + (prefill ? seq : 0),
-                    prefill ? (int)rows : 1, (int)m->max_seq, st);
+                    prefill ? (int)rows : 1, (int)m->max_seq, m->am_scratch, st);
   if (s) return s;
   SYN_CUDA_TRY(cudaMemcpyAsync(m->tok_h, m->tok, nr * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
   SYN_CUDA_TRY(cudaMemcpyAsync(m->err_h, m->ctx->err, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
@@ -488,6 +489,11 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   if ((s = dev_alloc_t(m, &m->hid, R * m->ff))) return s;
   if ((s = dev_alloc_t(m, &m->dn, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->logits, m->max_batch * m->V))) return s;
+  {
+    const size_t ab = argmax_scratch_bytes(m->max_batch, m->V);
+    if ((s = dev_alloc(m, &m->am_scratch, ab))) return s;
+    SYN_CUDA_TRY(cudaMemset(m->am_scratch, 0, ab));
+  }
   SYN_CUDA_TRY(cudaMallocHost(&m->ids_h, R * sizeof(int32_t)));
   SYN_CUDA_TRY(cudaMallocHost(&m->tok_h, m->max_batch * sizeof(int32_t)));
   SYN_CUDA_TRY(cudaMallocHost(&m->logits_h, m->max_batch * m->V * sizeof(float)));
