@@ -337,6 +337,13 @@ syn_status_t syn_cuda_prefill(syn_cuda_model_t *m, size_t seq,
 syn_status_t syn_cuda_decode_step(syn_cuda_model_t *m, size_t batch,
                                   const int32_t *last_tokens, int32_t *out_tokens,
                                   float *logits_host);
+/* Greedy generation of n_steps further tokens for sequences [0, batch)
+ * entirely on the device: each step's input is the previous step's argmax
+ * (the last token produced by syn_cuda_prefill / syn_cuda_decode_step /
+ * syn_cuda_generate), one captured CUDA graph replayed n_steps times, one
+ * synchronisation at the end. out_tokens: host [batch][n_steps]. */
+syn_status_t syn_cuda_generate(syn_cuda_model_t *m, size_t batch, size_t n_steps,
+                               int32_t *out_tokens);
 syn_status_t syn_cuda_model_seq_len(const syn_cuda_model_t *m, size_t seq, size_t *len);
 syn_status_t syn_cuda_model_reset(syn_cuda_model_t *m, size_t seq);
 syn_status_t syn_cuda_model_truncate(syn_cuda_model_t *m, size_t seq, size_t new_len);

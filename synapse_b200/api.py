@@ -538,6 +538,15 @@ class Model:
             toks.append(int(nxt[0]))
         return toks
 
+    def generate(self, n_steps, batch=1):
+        """n_steps greedy tokens for sequences [0, batch), chained on the
+        device (syn_cuda_generate); returns int32 [batch, n_steps]."""
+        import numpy as np
+        out = np.empty((batch, n_steps), dtype=np.int32)
+        _check(lib().syn_cuda_generate(self.handle, batch, n_steps,
+                                       out.ctypes.data_as(ctypes.c_void_p)), "generate")
+        return out
+
     def seq_len(self, seq=0):
         v = ctypes.c_size_t()
         _check(lib().syn_cuda_model_seq_len(self.handle, seq, ctypes.byref(v)), "model_seq_len")

@@ -161,12 +161,14 @@ syn_status_t launch_prefill_attention_args(const AttnArgs& a, size_t seq, size_t
                                            cudaStream_t st);
 syn_status_t launch_swiglu(const float* gate, const float* up, size_t ld_in, size_t rows, size_t n,
                            int variant, float* out, size_t ldo, cudaStream_t st);
-// Greedy argmax per row; when len_adv != nullptr, len_adv[row] += adv after.
+// Greedy argmax per row; when len_adv != nullptr, len_adv[row] += adv after
+// and (hist != nullptr) the token is recorded at hist[row*hist_ld + new len].
 // scratch: argmax_scratch_bytes(rows, n) bytes, zero before the first launch
 // (each launch leaves it reusable).
 size_t argmax_scratch_bytes(size_t rows, size_t n);
 syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
-                           int* len_adv, int adv, int max_len, void* scratch, cudaStream_t st);
+                           int* len_adv, int adv, int max_len, int32_t* hist, int hist_ld,
+                           void* scratch, cudaStream_t st);
 // Device length of sequence seq: set to value (add=0) or advanced by it.
 syn_status_t launch_kv_set(syn_cuda_kvcache_t* c, size_t seq, int value, int add, cudaStream_t st);
 

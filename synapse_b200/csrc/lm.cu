@@ -642,6 +642,7 @@ __device__ __forceinline__ AmState am_shfl_down(const AmState& s, int o) {
 __global__ void __launch_bounds__(AM_THREADS) k_argmax(const float* __restrict__ x, long long ldx,
                                                        int n, int32_t* __restrict__ out,
                                                        int* len_adv, int adv, int max_len,
+                                                       int32_t* hist, int hist_ld,
                                                        AmState* __restrict__ part,
                                                        int* __restrict__ cnt) {
   __shared__ AmState ws[AM_THREADS / 32];
@@ -687,11 +688,15 @@ __global__ void __launch_bounds__(AM_THREADS) k_argmax(const float* __restrict__
     __threadfence();
     AmState t = part[row * nct];
     for (int k = 1; k < nct; k++) t = am_combine(t, part[row * nct + k]);
-    out[row] = t.i >= 0 ? t.i : (t.nan >= 0 ? t.nan : 0);
+    const int r = t.i >= 0 ? t.i : (t.nan >= 0 ? t.nan : 0);
+    out[row] = r;
     cnt[row] = 0;  // ready for the next launch
     if (len_adv) {
-      const int nl = len_adv[row] + adv;
-      len_adv[row] = nl <= max_len ? nl : max_len;
+      int nl = len_adv[row] + adv;
+      nl = nl <= max_len ? nl : max_len;
+      len_adv[row] = nl;
+      // token history: the generated token will occupy position nl
+      if (hist) hist[(size_t)row * hist_ld + nl] = r;
     }
   }
 }
@@ -742,7 +747,8 @@ size_t argmax_scratch_bytes(size_t rows, size_t n) {
 }
 
 syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
-                           int* len_adv, int adv, int max_len, void* scratch, cudaStream_t st) {
+                           int* len_adv, int adv, int max_len, int32_t* hist, int hist_ld,
+                           void* scratch, cudaStream_t st) {
   if (!rows || !n) return SYN_OK;
   const size_t nct = (n + AM_SEG - 1) / AM_SEG;
   if (nct > 65535 || rows > 65535) return SYN_ERR_UNSUPPORTED;
@@ -750,7 +756,8 @@ syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, in
   AmState* part = reinterpret_cast<AmState*>(static_cast<uint8_t*>(scratch) +
                                              ((rows * sizeof(int) + 63) & ~size_t(63)));
   return cuda_status(launch_pdl(k_argmax, dim3((unsigned)nct, (unsigned)rows), dim3(AM_THREADS), 0,
-                                st, x, (long long)ldx, (int)n, out, len_adv, adv, max_len, part,
+                                st, x, (long long)ldx, (int)n, out, len_adv, adv, max_len, hist,
+                                hist_ld, part,
                                 cnt),
                      "k_argmax");
 }
@@ -1105,7 +1112,7 @@ syn_status_t syn_cuda_argmax(const float* logits, size_t rows, size_t n, int32_t
   SYN_CUDA_TRY(cudaMallocAsync(&scratch, bytes, st));
   cudaError_t e = cudaMemsetAsync(scratch, 0, bytes, st);
   syn_status_t s = e == cudaSuccess
-                       ? launch_argmax(logits, n, rows, n, out_idx, nullptr, 0, 0, scratch, st)
+                       ? launch_argmax(logits, n, rows, n, out_idx, nullptr, 0, 0, nullptr, 0, scratch, st)
                        : cuda_status(e, "cudaMemsetAsync");
   e = cudaFreeAsync(scratch, st);
   if (s == SYN_OK && e != cudaSuccess) s = cuda_status(e, "cudaFreeAsync");

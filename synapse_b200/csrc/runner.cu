@@ -204,6 +204,7 @@ struct syn_cuda_model_s {
   std::vector<void*> allocs;
   int32_t* ids = nullptr;
   int32_t* tok = nullptr;
+  int32_t* hist = nullptr;  // [max_batch][max_seq + 1] generated token per position
   void* am_scratch = nullptr;
   float *resid = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *o = nullptr,
         *gu = nullptr, *hid = nullptr, *dn = nullptr, *logits = nullptr;
@@ -215,6 +216,7 @@ struct syn_cuda_model_s {
   // decode graphs per (batch, with logits)
   std::map<std::pair<size_t, int>, cudaGraphExec_t> graphs;
   std::map<std::pair<size_t, int>, int> eager_runs;
+  std::map<size_t, cudaGraphExec_t> chain_graphs;  // chained decode step per batch
 };
 
 namespace {
@@ -277,7 +279,10 @@ syn_status_t mm(syn_cuda_model_s* m, const syn_cuda_weight_t* w, const float* x,
 
 // One forward over `rows` rows. Prefill: rows tokens of sequence `seq`.
 // Decode: rows sequences [0, rows), one token each.
-syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq, bool want_logits) {
+// chained: the step's input tokens are the previous step's outputs (m->tok),
+// and nothing is copied to the host.
+syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq, bool want_logits,
+                     bool chained = false) {
   cudaStream_t st = m->st;
   syn_status_t s;
   const size_t h = m->h;
@@ -294,7 +299,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   for (size_t li = 0; li < m->L; li++) {
     LayerDev& ly = m->layers[li];
     if (li == 0)
-      s = launch_add_rmsnorm(nullptr, 0, nullptr, 0, m->ids, m->embed, m->V, m->resid, h,
+      s = launch_add_rmsnorm(nullptr, 0, nullptr, 0, chained ? m->tok : m->ids, m->embed, m->V,
+                             m->resid, h,
                              ly.attn_norm, rows, h, m->eps, m->x, h, st);
     else
       s = launch_add_rmsnorm(m->resid, h, m->dn, h, nullptr, nullptr, 0, m->resid, h,
@@ -326,10 +332,15 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
                          m->resid + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st);
   if (s) return s;
   if ((s = mm(m, m->lm_head, m->x, nr, m->logits))) return s;
-  s = launch_argmax(m->logits, m->V, nr, m->V, m->tok, m->cache->d_len + (prefill ? seq : 0),
-                    prefill ? (int)rows : 1, (int)m->max_seq, m->am_scratch, st);
+  // the generated token of sequence b lands in tok[b] (prefill: tok[seq])
+  s = launch_argmax(m->logits, m->V, nr, m->V, m->tok + (prefill ? seq : 0),
+                    m->cache->d_len + (prefill ? seq : 0), prefill ? (int)rows : 1,
+                    (int)m->max_seq, m->hist + (prefill ? seq : 0) * (m->max_seq + 1),
+                    (int)(m->max_seq + 1), m->am_scratch, st);
   if (s) return s;
-  SYN_CUDA_TRY(cudaMemcpyAsync(m->tok_h, m->tok, nr * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+  if (chained) return SYN_OK;
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->tok_h, m->tok + (prefill ? seq : 0), nr * sizeof(int32_t),
+                               cudaMemcpyDeviceToHost, st));
   SYN_CUDA_TRY(cudaMemcpyAsync(m->err_h, m->ctx->err, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
   if (want_logits)
     SYN_CUDA_TRY(cudaMemcpyAsync(m->logits_h, m->logits, nr * m->V * sizeof(float),
@@ -349,6 +360,12 @@ syn_status_t finish(syn_cuda_model_s* m, size_t nr, int32_t* out_tokens, float* 
   if (out_tokens) memcpy(out_tokens, m->tok_h, nr * sizeof(int32_t));
   if (logits_host) memcpy(logits_host, m->logits_h, nr * m->V * sizeof(float));
   return SYN_OK;
+}
+
+syn_status_t cuda_status_r(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return SYN_OK;
+  set_last_cuda_error(e, where);
+  return SYN_ERR_CUDA;
 }
 
 bool use_graphs() {
@@ -480,6 +497,7 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   const size_t R = m->max_rows;
   if ((s = dev_alloc_t(m, &m->ids, R))) return s;
   if ((s = dev_alloc_t(m, &m->tok, m->max_batch))) return s;
+  if ((s = dev_alloc_t(m, &m->hist, m->max_batch * (m->max_seq + 1)))) return s;
   if ((s = dev_alloc_t(m, &m->resid, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->x, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->qkv, R * m->qkv_n))) return s;
@@ -573,6 +591,67 @@ syn_status_t syn_cuda_decode_step(syn_cuda_model_t* m, size_t batch, const int32
   return s;
 }
 
+syn_status_t syn_cuda_generate(syn_cuda_model_t* m, size_t batch, size_t n_steps,
+                               int32_t* out_tokens) {
+  if (!m || !out_tokens) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  if (batch == 0 || batch > m->max_batch) return SYN_ERR_INVALID_ARG;
+  if (n_steps == 0) return SYN_OK;
+  for (size_t b = 0; b < batch; b++)
+    if (m->cache->len[b] == 0 || m->cache->len[b] + n_steps > m->max_seq)
+      return SYN_ERR_INVALID_ARG;  // not started, or CacheFull
+  DeviceGuard g(m->device);
+  std::vector<size_t> len0(m->cache->len, m->cache->len + batch);
+  syn_status_t s = SYN_OK;
+  size_t done = 0;
+  auto it = m->chain_graphs.find(batch);
+  if (it == m->chain_graphs.end()) {
+    // one eager step sizes the scratch buffers, then the step is captured
+    if ((s = forward(m, batch, false, 0, false, true))) return s;
+    done = 1;
+    if (use_graphs()) {
+      cudaGraph_t graph = nullptr;
+      SYN_CUDA_TRY(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+      s = forward(m, batch, false, 0, false, true);
+      cudaError_t e = cudaStreamEndCapture(m->st, &graph);
+      if (s == SYN_OK && e != cudaSuccess) s = cuda_status_r(e, "cudaStreamEndCapture");
+      if (s) {
+        if (graph) cudaGraphDestroy(graph);
+        return s;
+      }
+      cudaGraphExec_t exec = nullptr;
+      e = cudaGraphInstantiate(&exec, graph, 0);
+      cudaGraphDestroy(graph);
+      if (e != cudaSuccess) return cuda_status_r(e, "cudaGraphInstantiate");
+      it = m->chain_graphs.emplace(batch, exec).first;
+    }
+  }
+  for (; done < n_steps; done++) {
+    if (it != m->chain_graphs.end()) {
+      SYN_CUDA_TRY(cudaGraphLaunch(it->second, m->st));
+    } else if ((s = forward(m, batch, false, 0, false, true))) {
+      return s;
+    }
+  }
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->err_h, m->ctx->err, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                               m->st));
+  SYN_CUDA_TRY(cudaStreamSynchronize(m->st));
+  if (*m->err_h != SYN_OK) {
+    const syn_status_t e = *m->err_h;
+    int32_t zero = 0;
+    cudaMemcpy(m->ctx->err, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    *m->err_h = 0;
+    return e;
+  }
+  for (size_t b = 0; b < batch; b++) {
+    // tokens generated by these steps occupy positions len0+1 .. len0+n_steps
+    SYN_CUDA_TRY(cudaMemcpy(out_tokens + b * n_steps, m->hist + b * (m->max_seq + 1) + len0[b] + 1,
+                            n_steps * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    m->cache->len[b] += n_steps;
+  }
+  return SYN_OK;
+}
+
 syn_status_t syn_cuda_model_seq_len(const syn_cuda_model_t* m, size_t seq, size_t* len) {
   if (!m || !len) return SYN_ERR_NULL_PTR;
   if (!m->finalized) return SYN_ERR_INVALID_ARG;
@@ -604,6 +683,7 @@ syn_status_t syn_cuda_model_destroy(syn_cuda_model_t* m) {
   DeviceGuard g(m->device);
   if (m->st) cudaStreamSynchronize(m->st);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : m->chain_graphs) cudaGraphExecDestroy(kv.second);
   for (auto& ly : m->layers) {
     if (ly.qkv) syn_cuda_weight_destroy(ly.qkv);
     if (ly.o) syn_cuda_weight_destroy(ly.o);

@@ -235,6 +235,26 @@ def test_int8_model_greedy_generation_and_reset(ctx):
     assert m.generate_greedy([10, 20, 30], 24) == ref
     m.truncate(5)
     assert m.seq_len() == 5
+    # chained on-device generation gives the same tokens
+    m.reset()
+    first, _ = m.forward_prefill([10, 20, 30], want_logits=False)
+    assert first == ref[0]
+    assert m.generate(23)[0].tolist() == ref[1:]
+    assert m.seq_len() == 3 + 23
+    m.close()
+
+
+def test_int8_model_generate_batch(ctx):
+    cfg = synth.lm_config("tiny-window")
+    w = synth.gen_lm_weights(cfg, "INT8_KN", seed=17)
+    prompts = [[5, 6, 7, 8], [99, 98]]
+    m = _gpu_model(ctx, cfg, w, 96, max_batch=2)
+    for i, p in enumerate(prompts):
+        m.forward_prefill(p, seq=i, want_logits=False)
+    got = m.generate(40, batch=2)
+    for i, p in enumerate(prompts):
+        ref, _ = OracleLM(cfg, w, 96).generate_greedy(p, 41)
+        assert got[i].tolist() == ref[1:], i
     m.close()
 
 
