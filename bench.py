@@ -118,6 +118,131 @@ def traffic_from_profile(fmt_name):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+DECODE_MODEL = "qwen3-0.6b"
+DECODE_PROMPT, DECODE_STEPS = 16, 128
+
+
+def decode_bytes_per_token(cfg, ctx_len):
+    """HBM bytes one decode step must read: every linear weight in its
+    reference INT8 format (+ f32 per-row scales), the LM head, one embedding
+    row, and the f32 K/V of `ctx_len` cached positions in every layer."""
+    a, at = cfg["architecture"], cfg["attention"]
+    h, L, V = a["hidden_size"], a["num_layers"], a["vocab_size"]
+    hd = at["head_dim"]
+    qd, kvd = at["num_heads"] * hd, at["num_kv_heads"] * hd
+    ff = cfg["ffn"]["intermediate_size"]
+    per_layer = sum(n * k + 4 * n for n, k in ((qd + 2 * kvd, h), (h, qd), (2 * ff, h), (h, ff)))
+    return L * per_layer + V * h + 4 * V + 4 * h + L * 2 * kvd * 4 * ctx_len
+
+
+def run_decode(args, local_rank, dist, cpu_leg):
+    """Config 1 (Qwen3-0.6B shape, INT8 per-row weights, random init): a
+    16-token prompt, then 128 greedy decode steps at batch 1.
+    device: syn_cuda_generate (each step one CUDA graph, chained on the
+    device); e2e: syn_cuda_decode_step per token (host token in, host token
+    out, synchronous)."""
+    import torch
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    cfg = synth.lm_config(DECODE_MODEL)
+    w = synth.gen_lm_weights(cfg, "INT8_KN", seed=1234)
+    ctx = sb.Context(local_rank)
+    max_seq = DECODE_PROMPT + DECODE_STEPS + 8
+    m = sb.Model(ctx, cfg, w, max_seq)
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, cfg["architecture"]["vocab_size"], DECODE_PROMPT).tolist()
+    res = {}
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    for rep in range(max(1, args.warmup // 3) + 1):  # first passes warm up (graph capture)
+        m.reset()
+        sync_all()
+        t0 = time.perf_counter()
+        m.forward_prefill(prompt, want_logits=False)
+        t1 = time.perf_counter()
+        toks = m.generate(DECODE_STEPS - 1)
+        t2 = time.perf_counter()
+        res = {"prefill_s": t1 - t0, "decode_s": t2 - t1}
+    dec_s = res["decode_s"]
+    if dist is not None:
+        tt = torch.tensor([dec_s], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dec_s = float(tt.item())
+    world = dist.get_world_size() if dist is not None else 1
+    n_dec = DECODE_STEPS - 1
+    tok_s = world * n_dec / dec_s
+    # e2e: one public-API call per token with host buffers
+    m.reset()
+    tok, _ = m.forward_prefill(prompt, want_logits=False)
+    seq = [tok]
+    for _ in range(3):
+        nxt, _ = m.forward_one([seq[-1]], want_logits=False)
+        seq.append(int(nxt[0]))
+    m.reset()
+    tok, _ = m.forward_prefill(prompt, want_logits=False)
+    sync_all()
+    t0 = time.perf_counter()
+    seq = [tok]
+    for _ in range(n_dec):
+        nxt, _ = m.forward_one([seq[-1]], want_logits=False)
+        seq.append(int(nxt[0]))
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        tt = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    same = seq[1:] == toks[0].tolist()
+    avg_ctx = DECODE_PROMPT + (n_dec + 1) / 2.0
+    bpt = decode_bytes_per_token(cfg, avg_ctx)
+    peak, src = peaks()
+    out = {
+        "model": "Qwen3-0.6B shape (28 layers, d 1024, 16/8 heads x 128, ff 3072, vocab 151936), "
+                 "random-init N(0,0.02), INT8 per-row W8A8",
+        "prompt_tokens": DECODE_PROMPT, "decode_steps": n_dec, "batch": 1,
+        "tok_s": round(tok_s, 1), "ms_per_token": round(dec_s / n_dec * 1e3, 4),
+        "prefill_tok_s": round(world * DECODE_PROMPT / res["prefill_s"], 1),
+        "e2e_tok_s": round(world * n_dec / e2e_s, 1),
+        "e2e": {"api": "syn_cuda_decode_step per token", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "device_and_e2e_tokens_identical": bool(same),
+        "hbm_bytes_per_token": int(bpt),
+        "roofline": {"bound": "hbm", "achieved": round(bpt * n_dec / dec_s / 1e9, 1),
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(bpt * n_dec / dec_s / 1e9 / peak, 4), "peak_source": src},
+        "gpu_launches_per_token": 8 * cfg["architecture"]["num_layers"] + 3,
+    }
+    if cpu_leg:
+        out["cpu_baseline"] = cpu_decode_sample(cfg, w, prompt)
+    m.close()
+    ctx.close()
+    return out
+
+
+def cpu_decode_sample(cfg, w, prompt, budget_s=20.0):
+    """The oracle restatement of QuantizedCausalLM (oracle/lm.py) on 1 core:
+    the same prompt, then decode steps until ~budget_s."""
+    from oracle.lm import OracleLM
+    lm = OracleLM(cfg, w, DECODE_PROMPT + 64)
+    t0 = time.perf_counter()
+    logits = lm.forward_prefill(prompt)
+    t1 = time.perf_counter()
+    tok = int(np.argmax(logits))
+    n = 0
+    while time.perf_counter() - t1 < budget_s and n < 32:
+        logits = lm.forward_one(tok)
+        tok = int(np.argmax(logits))
+        n += 1
+    t2 = time.perf_counter()
+    return {"value": round(n / (t2 - t1), 3), "unit": "tok/s", "cores": 1, "kind": "port",
+            "prefill_tok_s": round(len(prompt) / (t1 - t0), 3),
+            "sample": f"oracle QuantizedCausalLM restatement, {len(prompt)}-token prefill then "
+                      f"{n} decode steps, 1 thread"}
+
+
 def run_synapse(args, rank, world, local_rank):
     import torch
     import synapse_b200 as sb
@@ -257,6 +382,10 @@ def run_synapse(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample()
+    decode = None
+    if not args.no_decode:
+        decode = run_decode(args, local_rank, dist,
+                            cpu_leg=rank == 0 and world == 1 and not args.no_cpu_baseline)
 
     if rank == 0:
         line = {
@@ -282,6 +411,7 @@ def run_synapse(args, rank, world, local_rank):
             "launch": "one CUDA graph per format (15 GEMVs), 5 replays per step",
             "clocks": clk,
             "cpu_baseline": cpu,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -418,12 +548,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="synapse", choices=["synapse", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the model decode leg")
     ap.add_argument("--case", default=None, help="FMT:N:K -- time one GEMV only (profiling)")
     args = ap.parse_args()
     global CASE_FILTER
     CASE_FILTER = args.case
     if args.case:
         args.no_cpu_baseline = True
+        args.no_decode = True
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
