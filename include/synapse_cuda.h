@@ -302,7 +302,7 @@ syn_status_t syn_cuda_argmax(const float *logits, size_t rows, size_t n,
 /* ------------------------------------------------------------------ */
 typedef struct syn_cuda_model_s syn_cuda_model_t;
 
-/* config_json: a model config in the reference's format (configs/*.json:
+/* config_json: a model config in the reference's format (configs/<name>.json:
  * architecture / attention / norm / ffn / position). max_seq: KV capacity
  * per sequence; max_batch: sequences decoded together. */
 syn_status_t syn_cuda_model_create(syn_cuda_ctx_t *ctx, const char *config_json,
@@ -348,6 +348,33 @@ syn_status_t syn_cuda_model_seq_len(const syn_cuda_model_t *m, size_t seq, size_
 syn_status_t syn_cuda_model_reset(syn_cuda_model_t *m, size_t seq);
 syn_status_t syn_cuda_model_truncate(syn_cuda_model_t *m, size_t seq, size_t new_len);
 syn_status_t syn_cuda_model_destroy(syn_cuda_model_t *m);
+
+/* ------------------------------------------------------------------ */
+/* Tensor parallelism (Megatron column/row split; the reference has no */
+/* multi-GPU code). One process per GPU; every rank passes the full    */
+/* weights to its model and keeps its own shard: Q/K/V by heads and    */
+/* gate/up by FFN rows (column-parallel), O and down by input columns  */
+/* (row-parallel, whole quant blocks) with one sum all-reduce after    */
+/* each, the LM head by vocabulary rows with an all-gather of the      */
+/* logits. Block formats only (the INT8 W8A8 row-parallel split would  */
+/* need the activation scale of the whole row).                        */
+/* ------------------------------------------------------------------ */
+#define SYN_CUDA_TP_ID_BYTES 128
+/* Rank 0 creates the group id (ncclGetUniqueId) and shares it. */
+syn_status_t syn_cuda_tp_unique_id(uint8_t *id_out);
+/* Joins the TP group: every model created on ctx afterwards is sharded. */
+syn_status_t syn_cuda_tp_init(syn_cuda_ctx_t *ctx, int rank, int world, const uint8_t *id);
+/* In-place sum all-reduce of device floats over the group. */
+syn_status_t syn_cuda_tp_allreduce_sum(syn_cuda_ctx_t *ctx, float *buf, size_t count,
+                                       void *stream);
+/* Host-side shard of a linear weight in its reference storage format:
+ * axis 0 = output rows [rank*n/world, ...), axis 1 = input columns
+ * [rank*k/world, ...) (block-aligned). out: n_out*k_out weights in the same
+ * format; INT8_KN also slices (axis 0) or copies (axis 1) the scales. */
+syn_status_t syn_cuda_tp_shard_linear(syn_qformat_t fmt, const void *host, size_t n,
+                                      size_t k, const float *scales, int axis, int rank,
+                                      int world, void *out, float *out_scales,
+                                      size_t *n_out, size_t *k_out);
 
 #ifdef __cplusplus
 }

@@ -30,9 +30,11 @@ from .api import (  # noqa: E402
     attention_decode,
     attention_prefill,
     Model,
+    tp_unique_id,
+    tp_shard_linear,
 )
 
 __all__ = ["lib", "QFormat", "SynapseError", "Context", "QuantizedWeight", "QuantizedLinear",
            "capability_summary", "quantize_per_channel_int8", "quantize_weights_int8",
            "qgemm_int8", "q4_0_gemv", "row_bytes", "rope_tables", "rmsnorm", "add_rmsnorm",
-           "swiglu", "argmax", "KVCache", "attention_decode", "attention_prefill", "Model"]
+           "swiglu", "argmax", "KVCache", "attention_decode", "attention_prefill", "Model", "tp_unique_id", "tp_shard_linear"]

@@ -76,6 +76,12 @@ SIGNATURES = {
     "syn_cuda_model_reset": (c_st, [c_vp, c_size]),
     "syn_cuda_model_truncate": (c_st, [c_vp, c_size, c_size]),
     "syn_cuda_model_destroy": (c_st, [c_vp]),
+    "syn_cuda_tp_unique_id": (c_st, [c_vp]),
+    "syn_cuda_tp_init": (c_st, [c_vp, ctypes.c_int, ctypes.c_int, c_vp]),
+    "syn_cuda_tp_allreduce_sum": (c_st, [c_vp, c_vp, c_size, c_vp]),
+    "syn_cuda_tp_shard_linear": (c_st, [ctypes.c_int, c_vp, c_size, c_size, c_vp, ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_int, c_vp, c_vp,
+                                        ctypes.POINTER(c_size), ctypes.POINTER(c_size)]),
 }
 
 

@@ -163,6 +163,19 @@ class Context:
         _check(lib().syn_cuda_context_create(self.device, ctypes.byref(h)), "context_create")
         self.handle = h
 
+    def tp_init(self, rank, world, unique_id):
+        """Joins a tensor-parallel group (syn_cuda_tp_init); unique_id: the
+        bytes of tp_unique_id() from rank 0."""
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(bytes(unique_id))
+        _check(lib().syn_cuda_tp_init(self.handle, int(rank), int(world), buf), "tp_init")
+        self.tp_rank, self.tp_world = int(rank), int(world)
+
+    def tp_allreduce_sum(self, t):
+        _need_cuda(t)
+        _check(lib().syn_cuda_tp_allreduce_sum(self.handle, _ptr(t), t.numel(), _stream(t)),
+               "tp_allreduce_sum")
+        return t
+
     def close(self):
         if self.handle:
             lib().syn_cuda_context_destroy(self.handle)
@@ -173,6 +186,35 @@ class Context:
             self.close()
         except Exception:
             pass
+
+
+def tp_unique_id():
+    """A new tensor-parallel group id (rank 0; ncclGetUniqueId), as bytes."""
+    buf = (ctypes.c_uint8 * 128)()
+    _check(lib().syn_cuda_tp_unique_id(buf), "tp_unique_id")
+    return bytes(buf)
+
+
+def tp_shard_linear(fmt, data, n, k, rank, world, axis, scales=None):
+    """This rank's shard of a linear weight in its storage format
+    (syn_cuda_tp_shard_linear; host only). Returns (data, n, k, scales)."""
+    import numpy as np
+    fmt = QFormat[fmt] if isinstance(fmt, str) else QFormat(fmt)
+    buf = np.ascontiguousarray(np.asarray(data).view(np.uint8).reshape(-1))
+    out = np.empty(buf.size // world, dtype=np.uint8)
+    sc = None
+    osc = None
+    if fmt == QFormat.INT8_KN:
+        sc = np.ascontiguousarray(np.asarray(scales, dtype=np.float32))
+        osc = np.empty(n // world if axis == 0 else n, dtype=np.float32)
+    no, ko = ctypes.c_size_t(), ctypes.c_size_t()
+    _check(lib().syn_cuda_tp_shard_linear(
+        int(fmt), buf.ctypes.data_as(ctypes.c_void_p), n, k,
+        sc.ctypes.data_as(ctypes.c_void_p) if sc is not None else None, axis, rank, world,
+        out.ctypes.data_as(ctypes.c_void_p),
+        osc.ctypes.data_as(ctypes.c_void_p) if osc is not None else None, ctypes.byref(no),
+        ctypes.byref(ko)), "tp_shard_linear")
+    return out, no.value, ko.value, osc
 
 
 class QuantizedWeight:

@@ -241,6 +241,7 @@ syn_status_t syn_cuda_context_destroy(syn_cuda_ctx_t* ctx) {
     cudaFree(ctx->cnt);
     cudaFree(ctx->abuf);
     cudaFree(ctx->err);
+    tp_release(ctx);
   }
   delete ctx;
   return SYN_OK;

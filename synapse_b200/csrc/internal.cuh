@@ -16,6 +16,8 @@ struct syn_cuda_ctx_s {
   uint8_t* abuf;     // activations prepared for the tensor-core GEMM
   size_t abuf_bytes;
   int* err;          // device-side error word (e.g. SYN_ERR_TIMEOUT)
+  void* nccl;        // tensor-parallel communicator (ncclComm_t) or nullptr
+  int tp_rank, tp_world;
 };
 
 // Repacked weight in HBM. One allocation; the views below point into it.
@@ -171,5 +173,15 @@ syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, in
                            void* scratch, cudaStream_t st);
 // Device length of sequence seq: set to value (add=0) or advanced by it.
 syn_status_t launch_kv_set(syn_cuda_kvcache_t* c, size_t seq, int value, int add, cudaStream_t st);
+
+// ---- tensor parallelism (tp.cu) ----
+// Releases the context's communicator (context destroy).
+void tp_release(syn_cuda_ctx_s* ctx);
+// Sum all-reduce of count floats in place over the context's TP group.
+syn_status_t tp_allreduce_sum(syn_cuda_ctx_s* ctx, float* buf, size_t count, cudaStream_t st);
+// All-gather: every rank contributes count floats; recv holds world*count
+// in rank order.
+syn_status_t tp_allgather(syn_cuda_ctx_s* ctx, const float* send, float* recv, size_t count,
+                          cudaStream_t st);
 
 }  // namespace syn

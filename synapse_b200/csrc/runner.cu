@@ -187,6 +187,9 @@ struct syn_cuda_model_s {
   // config
   size_t h = 0, L = 0, V = 0, Hq = 0, Hkv = 0, hd = 0, ff = 0, window = 0;
   size_t qd = 0, kvd = 0, qkv_n = 0;
+  // this rank's shard (tensor parallelism; equal to the full sizes at tp = 1)
+  int tp = 1, tp_rank = 0;
+  size_t hq_l = 0, hkv_l = 0, ff_l = 0, v_l = 0, qd_l = 0, kvd_l = 0;
   float eps = 1e-6f;
   double rope_base = 10000.0;
   size_t max_seq = 0, max_batch = 0, max_rows = 0;
@@ -206,6 +209,7 @@ struct syn_cuda_model_s {
   int32_t* tok = nullptr;
   int32_t* hist = nullptr;  // [max_batch][max_seq + 1] generated token per position
   void* am_scratch = nullptr;
+  float* logits_l = nullptr;  // this rank's vocabulary slice of the logits (tp > 1)
   float *resid = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *o = nullptr,
         *gu = nullptr, *hid = nullptr, *dn = nullptr, *logits = nullptr;
   // pinned host staging
@@ -289,13 +293,14 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   const int variant = m->int8 ? 0 : 1;
   AttnArgs a{};
   a.ld = m->qkv_n;
-  a.n_heads = m->Hq;
+  a.n_heads = m->hq_l;
   a.eps = m->eps;
   a.cos_t = m->cos_t;
   a.sin_t = m->sin_t;
   a.window = m->window;
   a.cache = m->cache;
-  a.ldo = m->qd;
+  a.ldo = m->qd_l;
+  const bool tp = m->tp > 1;
   for (size_t li = 0; li < m->L; li++) {
     LayerDev& ly = m->layers[li];
     if (li == 0)
@@ -308,8 +313,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
     if (s) return s;
     if ((s = mm(m, ly.qkv, m->x, rows, m->qkv))) return s;
     a.q = m->qkv;
-    a.k = m->qkv + m->qd;
-    a.v = m->qkv + m->qd + m->kvd;
+    a.k = m->qkv + m->qd_l;
+    a.v = m->qkv + m->qd_l + m->kvd_l;
     a.qn = ly.q_norm;
     a.kn = ly.k_norm;
     a.layer = li;
@@ -318,20 +323,30 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
                 : launch_attn_decode_args(a, rows, m->ctx->err, st);
     if (s) return s;
     if ((s = mm(m, ly.o, m->att, rows, m->o))) return s;
+    if (tp && (s = tp_allreduce_sum(m->ctx, m->o, rows * h, st))) return s;  // row-parallel O
     s = launch_add_rmsnorm(m->resid, h, m->o, h, nullptr, nullptr, 0, m->resid, h, ly.ffn_norm,
                            rows, h, m->eps, m->x, h, st);
     if (s) return s;
     if ((s = mm(m, ly.gu, m->x, rows, m->gu))) return s;
-    s = launch_swiglu(m->gu, m->gu + m->ff, 2 * m->ff, rows, m->ff, variant, m->hid, m->ff, st);
+    s = launch_swiglu(m->gu, m->gu + m->ff_l, 2 * m->ff_l, rows, m->ff_l, variant, m->hid,
+                      m->ff_l, st);
     if (s) return s;
     if ((s = mm(m, ly.down, m->hid, rows, m->dn))) return s;
+    if (tp && (s = tp_allreduce_sum(m->ctx, m->dn, rows * h, st))) return s;  // row-parallel down
   }
   // final norm and LM head: prefill keeps only the last token (int8.rs:619-627)
   const size_t r0 = prefill ? rows - 1 : 0, nr = prefill ? 1 : rows;
   s = launch_add_rmsnorm(m->resid + r0 * h, h, m->dn + r0 * h, h, nullptr, nullptr, 0,
                          m->resid + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st);
   if (s) return s;
-  if ((s = mm(m, m->lm_head, m->x, nr, m->logits))) return s;
+  if (tp) {  // vocab-parallel LM head: gather each row's logits in rank (= vocab) order
+    if ((s = mm(m, m->lm_head, m->x, nr, m->logits_l))) return s;
+    for (size_t b = 0; b < nr; b++)
+      if ((s = tp_allgather(m->ctx, m->logits_l + b * m->v_l, m->logits + b * m->V, m->v_l, st)))
+        return s;
+  } else if ((s = mm(m, m->lm_head, m->x, nr, m->logits))) {
+    return s;
+  }
   // the generated token of sequence b lands in tok[b] (prefill: tok[seq])
   s = launch_argmax(m->logits, m->V, nr, m->V, m->tok + (prefill ? seq : 0),
                     m->cache->d_len + (prefill ? seq : 0), prefill ? (int)rows : 1,
@@ -454,6 +469,31 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   SYN_CUDA_TRY(cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking));
   if ((s = upload_tensor(m, "model.embed_tokens.weight", m->V * h, &m->embed, false))) return s;
   if ((s = upload_tensor(m, "model.norm.weight", h, &m->final_norm, false))) return s;
+  // tensor parallelism: this rank's shard of every linear
+  m->tp = m->ctx->tp_world > 1 ? m->ctx->tp_world : 1;
+  m->tp_rank = m->tp > 1 ? m->ctx->tp_rank : 0;
+  const size_t W = (size_t)m->tp;
+  if (m->Hq % W || m->Hkv % W || m->ff % W || m->V % W) return SYN_ERR_SHAPE_MISMATCH;
+  m->hq_l = m->Hq / W;
+  m->hkv_l = m->Hkv / W;
+  m->ff_l = m->ff / W;
+  m->v_l = m->V / W;
+  m->qd_l = m->hq_l * m->hd;
+  m->kvd_l = m->hkv_l * m->hd;
+  m->qkv_n = m->qd_l + 2 * m->kvd_l;
+  auto shard = [&](const HostLinear& full, int axis, HostLinear& out) -> syn_status_t {
+    if (W == 1) {
+      out = full;
+      return SYN_OK;
+    }
+    if (full.fmt == SYN_QFMT_INT8_KN) return SYN_ERR_UNSUPPORTED;  // W8A8 row-parallel
+    out = HostLinear();
+    out.fmt = full.fmt;
+    out.data.resize(full.data.size() / W);
+    return syn_cuda_tp_shard_linear((syn_qformat_t)full.fmt, full.data.data(), full.n, full.k,
+                                    nullptr, axis, m->tp_rank, (int)W, out.data.data(), nullptr,
+                                    &out.n, &out.k);
+  };
   m->layers.resize(m->L);
   for (size_t i = 0; i < m->L; i++) {
     LayerDev& ly = m->layers[i];
@@ -471,17 +511,25 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
     const HostLinear* dn = find_lin(m, lname(i, "mlp.down_proj.weight"), h, m->ff);
     if (!q || !k || !v || !o || !ga || !up || !dn) return SYN_ERR_SHAPE_MISMATCH;
     if (i == 0) m->int8 = q->fmt == SYN_QFMT_INT8_KN;
-    HostLinear cat;
-    if (!concat({q, k, v}, cat)) return SYN_ERR_INVALID_ARG;
+    HostLinear qs, ks, vs, os, gs, us, ds, cat;
+    if ((s = shard(*q, 0, qs)) || (s = shard(*k, 0, ks)) || (s = shard(*v, 0, vs)) ||
+        (s = shard(*o, 1, os)) || (s = shard(*ga, 0, gs)) || (s = shard(*up, 0, us)) ||
+        (s = shard(*dn, 1, ds)))
+      return s;
+    if (!concat({&qs, &ks, &vs}, cat)) return SYN_ERR_INVALID_ARG;
     if ((s = upload_linear(m, cat, &ly.qkv))) return s;
-    if (!concat({ga, up}, cat)) return SYN_ERR_INVALID_ARG;
+    if (!concat({&gs, &us}, cat)) return SYN_ERR_INVALID_ARG;
     if ((s = upload_linear(m, cat, &ly.gu))) return s;
-    if ((s = upload_linear(m, *o, &ly.o))) return s;
-    if ((s = upload_linear(m, *dn, &ly.down))) return s;
+    if ((s = upload_linear(m, os, &ly.o))) return s;
+    if ((s = upload_linear(m, ds, &ly.down))) return s;
   }
   const HostLinear* lm = find_lin(m, "lm_head.weight", m->V, h);
   if (!lm) return SYN_ERR_SHAPE_MISMATCH;
-  if ((s = upload_linear(m, *lm, &m->lm_head))) return s;
+  {
+    HostLinear ls;
+    if ((s = shard(*lm, 0, ls))) return s;
+    if ((s = upload_linear(m, ls, &m->lm_head))) return s;
+  }
   m->lin.clear();
   m->ten.clear();
   // RoPE tables for the cache's positions
@@ -491,7 +539,7 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   if ((s = dev_alloc_t(m, &m->sin_t, c.size()))) return s;
   SYN_CUDA_TRY(cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
   SYN_CUDA_TRY(cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
-  if ((s = syn_cuda_kvcache_create(m->ctx, m->max_seq, m->Hkv, m->hd, m->L, m->max_batch,
+  if ((s = syn_cuda_kvcache_create(m->ctx, m->max_seq, m->hkv_l, m->hd, m->L, m->max_batch,
                                    &m->cache)))
     return s;
   const size_t R = m->max_rows;
@@ -501,10 +549,11 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   if ((s = dev_alloc_t(m, &m->resid, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->x, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->qkv, R * m->qkv_n))) return s;
-  if ((s = dev_alloc_t(m, &m->att, R * m->qd))) return s;
+  if ((s = dev_alloc_t(m, &m->att, R * m->qd_l))) return s;
   if ((s = dev_alloc_t(m, &m->o, R * h))) return s;
-  if ((s = dev_alloc_t(m, &m->gu, R * 2 * m->ff))) return s;
-  if ((s = dev_alloc_t(m, &m->hid, R * m->ff))) return s;
+  if ((s = dev_alloc_t(m, &m->gu, R * 2 * m->ff_l))) return s;
+  if ((s = dev_alloc_t(m, &m->hid, R * m->ff_l))) return s;
+  if (m->tp > 1 && (s = dev_alloc_t(m, &m->logits_l, m->max_batch * m->v_l))) return s;
   if ((s = dev_alloc_t(m, &m->dn, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->logits, m->max_batch * m->V))) return s;
   {

@@ -90,6 +90,7 @@ def lm_config(name):
         "tiny": cfg(128, 2, 512, 4, 2, 32, 256, 1e-6, 1e6),
         "tiny-hd64": cfg(256, 2, 640, 4, 1, 64, 512, 1e-5, 5e5),
         "tiny-window": cfg(256, 2, 640, 8, 2, 32, 512, 1e-5, 1e6, window=24),
+        "tiny-k-tp": cfg(256, 2, 640, 8, 2, 64, 512, 1e-5, 5e5),
     }
     return table[name]
 
