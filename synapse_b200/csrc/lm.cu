@@ -444,6 +444,34 @@ __global__ void __launch_bounds__(512) k_norm_rope_append(const AttnParams p) {
 // (@mulAdd in full tiles, sum += a*b in edge tiles).
 // ---------------------------------------------------------------------------
 constexpr int PF_THREADS = 256;
+constexpr int PF_CH = 32;  // keys staged per chunk
+
+// Copies rows [0, cn) of hd floats (global row stride gs) into smem rows of
+// stride ss, all loads of a thread issued before its stores.
+__device__ __forceinline__ void stage_rows_pf(float* dst, int ss, const float* src, size_t gs,
+                                              int cn, int hd, int tid) {
+  const int q = hd >> 2, tot = cn * q;
+  constexpr int U = 8;
+  for (int t0 = 0; t0 < tot; t0 += U * PF_THREADS) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int t = t0 + tid + u * PF_THREADS;
+      if (t < tot) {
+        const int r = t / q, c4 = t - r * q;
+        v[u] = *reinterpret_cast<const float4*>(src + (size_t)r * gs + 4 * c4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int t = t0 + tid + u * PF_THREADS;
+      if (t < tot) {
+        const int r = t / q, c4 = t - r * q;
+        *reinterpret_cast<float4*>(dst + r * ss + 4 * c4) = v[u];
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ void tile_of(int q, int S, int& tqs, int& i) {
   const int tq = q & ~31;
@@ -470,9 +498,11 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
   const int G = p.n_heads / p.n_kv, kvh = hh / G, hd = p.hd, kvd = p.n_kv * hd;
   const int S = p.n_tokens, rows = min(PR, S - r0), jn = r0 + rows;  // keys [0, jn)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* qs = sm;                 // [rows][hd]
-  float* sc = qs + PR * hd;       // [rows][jn]
-  float* chv = sc + (size_t)PR * jn;  // per warp: 32 values + 32 flags
+  const int ks = hd + 4;
+  float* qs = sm;                      // [rows][hd]
+  float* kb = qs + PR * hd;            // PF_CH staged K or V rows (16-byte aligned)
+  float* sc = kb + PF_CH * ks;         // [rows][jn]
+  float* chv = sc + (size_t)PR * jn;   // per warp: 32 values + 32 flags
   griddep_wait();
   // the prompt's own K/V: cache slots from the sequence's first free one on
   const int base = p.len[p.seq0];
@@ -482,26 +512,34 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
     const int i = t / hd, d = t - i * hd;
     qs[t] = p.q[(long long)(r0 + i) * p.ld + (long long)hh * hd + d];
   }
-  __syncthreads();
-  // S = Q K^T * scale (masked entries are not needed: set to 0 below)
-  for (int t = tid; t < rows * jn; t += PF_THREADS) {
-    const int i = t / jn, j = t - i * jn, q = r0 + i;
-    if (j > q) {
-      sc[t] = 0.0f;
-      continue;
+  // S = Q K^T * scale, K rows staged through smem PF_CH keys at a time
+  // (masked entries are not needed: set to 0, a no-op in P V)
+  for (int j0 = 0; j0 < jn; j0 += PF_CH) {
+    const int cn = min(PF_CH, jn - j0);
+    __syncthreads();
+    stage_rows_pf(kb, ks, kcb + (size_t)j0 * kvd, kvd, cn, hd, tid);
+    __syncthreads();
+    for (int t = tid; t < rows * cn; t += PF_THREADS) {
+      const int i = t / cn, jj = t - i * cn, j = j0 + jj, q = r0 + i;
+      float* dst = sc + (size_t)i * jn + j;
+      if (j > q) {
+        *dst = 0.0f;
+        continue;
+      }
+      const bool fused = s_fused(q, j, S);
+      const float* kr = kb + jj * ks;
+      const float* qr = qs + i * hd;
+      float acc = 0.0f;
+      for (int d = 0; d < hd; d += 4) {
+        const float4 kv = *reinterpret_cast<const float4*>(kr + d);
+        const float4 qv = *reinterpret_cast<const float4*>(qr + d);
+        acc = chain(fused, qv.x, kv.x, acc);
+        acc = chain(fused, qv.y, kv.y, acc);
+        acc = chain(fused, qv.z, kv.z, acc);
+        acc = chain(fused, qv.w, kv.w, acc);
+      }
+      *dst = __fmul_rn(acc, p.scale);
     }
-    const bool fused = s_fused(q, j, S);
-    const float* kr = kcb + (size_t)j * kvd;
-    const float* qr = qs + i * hd;
-    float acc = 0.0f;
-    for (int d = 0; d < hd; d += 4) {
-      const float4 kv = *reinterpret_cast<const float4*>(kr + d);
-      acc = chain(fused, qr[d], kv.x, acc);
-      acc = chain(fused, qr[d + 1], kv.y, acc);
-      acc = chain(fused, qr[d + 2], kv.z, acc);
-      acc = chain(fused, qr[d + 3], kv.w, acc);
-    }
-    sc[t] = __fmul_rn(acc, p.scale);
   }
   __syncthreads();
   // online softmax per row (warp per row): running max known from a prefix
@@ -558,14 +596,24 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
       nown = u + 1;
     }
   }
-  for (int j = 0; j < jn; j++) {
-    const float* vr = vcb + (size_t)j * kvd;
+  int srow[NPER], vcol[NPER];
 #pragma unroll
-    for (int u = 0; u < NPER; u++) {
-      if (u < nown && oi[u] >= 0) {
-        const int i = oi[u] / hd, d = oi[u] - i * hd;
-        acc[u] = chain(fz[u], sc[(size_t)i * jn + j], vr[d], acc[u]);
-      }
+  for (int u = 0; u < NPER; u++) {
+    const int i = oi[u] >= 0 ? oi[u] / hd : 0;
+    srow[u] = i * jn;
+    vcol[u] = oi[u] >= 0 ? oi[u] - i * hd : 0;
+  }
+  for (int j0 = 0; j0 < jn; j0 += PF_CH) {
+    const int cn = min(PF_CH, jn - j0);
+    __syncthreads();
+    stage_rows_pf(kb, ks, vcb + (size_t)j0 * kvd, kvd, cn, hd, tid);
+    __syncthreads();
+    for (int jj = 0; jj < cn; jj++) {
+      const float* vr = kb + jj * ks;
+#pragma unroll
+      for (int u = 0; u < NPER; u++)
+        if (u < nown && oi[u] >= 0)
+          acc[u] = chain(fz[u], sc[srow[u] + j0 + jj], vr[vcol[u]], acc[u]);
     }
   }
 #pragma unroll
@@ -771,9 +819,13 @@ namespace syn {
 namespace {
 
 
+size_t prefill_smem(int pr, int S, int hd) {
+  return ((size_t)pr * hd + (size_t)PF_CH * (hd + 4) + (size_t)pr * S + 8 * 64) * sizeof(float);
+}
+
 int prefill_rows(int S, int hd) {
   for (int pr = 16; pr >= 1; pr >>= 1) {
-    const size_t smem = ((size_t)pr * hd + (size_t)pr * S + 8 * 64) * sizeof(float);
+    const size_t smem = prefill_smem(pr, S, hd);
     if (smem <= kMaxSmem && pr * hd <= 16 * PF_THREADS) return pr;
   }
   return 0;
@@ -869,7 +921,7 @@ syn_status_t launch_prefill_attention_args(const AttnArgs& a, size_t seq, size_t
   if (ntok == 0) return SYN_OK;
   const int pr = prefill_rows((int)ntok, p.hd);
   if (!pr) return SYN_ERR_UNSUPPORTED;
-  const size_t smem = ((size_t)pr * p.hd + (size_t)pr * ntok + 8 * 64) * sizeof(float);
+  const size_t smem = prefill_smem(pr, (int)ntok, p.hd);
   s = allow_smem((const void*)k_attn_prefill, smem);
   if (s) return s;
   return cuda_status(launch_pdl(k_attn_prefill,
