@@ -286,6 +286,25 @@ syn_status_t syn_cuda_attention_prefill(
     const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
     float *out, size_t ldo, void *stream);
 
+/* The same two attention operations with a parallel reduction order (split
+ * over positions with max/sum rescaling; flash-style tiles for the prefill):
+ * identical inputs, outputs and cache effects, results within f32
+ * reassociation of the reference order. The runner uses them for
+ * block-format models, whose matmuls carry a 1e-3 tolerance; head_dim 32,
+ * 64 or 128 (prefill: 64 or 128; other sizes fall back to the exact order). */
+syn_status_t syn_cuda_attention_decode_flash(syn_cuda_kvcache_t *cache, size_t layer,
+                                             size_t batch, float *q, const float *k,
+                                             const float *v, size_t ld, size_t n_heads,
+                                             const float *q_norm, const float *k_norm,
+                                             float eps, const float *rope_cos,
+                                             const float *rope_sin, size_t window,
+                                             float *out, size_t ldo, void *stream);
+syn_status_t syn_cuda_attention_prefill_flash(
+    syn_cuda_kvcache_t *cache, size_t layer, size_t seq, size_t n_tokens, float *q,
+    const float *k, const float *v, size_t ld, size_t n_heads, const float *q_norm,
+    const float *k_norm, float eps, const float *rope_cos, const float *rope_sin,
+    float *out, size_t ldo, void *stream);
+
 /* SwiGLU. variant 0: silu(g)*u of the INT8 model (int8.rs:500-503);
  * variant 1: syn_swiglu / swigluFused (zig/src/ops/silu.zig:85-114). */
 syn_status_t syn_cuda_swiglu(const float *gate, const float *up, size_t ld_in,

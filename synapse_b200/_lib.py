@@ -60,6 +60,12 @@ SIGNATURES = {
     "syn_cuda_attention_prefill": (c_st, [c_vp, c_size, c_size, c_size, c_vp, c_vp, c_vp, c_size,
                                           c_size, c_vp, c_vp, ctypes.c_float, c_vp, c_vp, c_vp,
                                           c_size, c_vp]),
+    "syn_cuda_attention_decode_flash": (c_st, [c_vp, c_size, c_size, c_vp, c_vp, c_vp, c_size,
+                                               c_size, c_vp, c_vp, ctypes.c_float, c_vp, c_vp,
+                                               c_size, c_vp, c_size, c_vp]),
+    "syn_cuda_attention_prefill_flash": (c_st, [c_vp, c_size, c_size, c_size, c_vp, c_vp, c_vp,
+                                                c_size, c_size, c_vp, c_vp, ctypes.c_float, c_vp,
+                                                c_vp, c_vp, c_size, c_vp]),
     "syn_cuda_swiglu": (c_st, [c_vp, c_vp, c_size, c_size, c_size, ctypes.c_int, c_vp, c_size,
                                c_vp]),
     "syn_cuda_argmax": (c_st, [c_vp, c_size, c_size, c_vp, c_vp]),

@@ -456,7 +456,7 @@ def _wrap_device(addr, numel, shape):
 
 
 def attention_decode(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, sin_t, window=0,
-                     batch=1):
+                     batch=1, flash=False):
     """cached_attention_decode (ops/attention.rs:24-147) for sequences
     [0, batch); qkv rows [q | k | v] (row stride = its last dim). Returns
     [batch, n_heads*hd]; the cache length is not advanced."""
@@ -465,7 +465,8 @@ def attention_decode(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, sin
     qd, kvd = n_heads * cache.hd, cache.n_kv * cache.hd
     out = torch.empty(batch, qd, dtype=torch.float32, device=qkv.device)
     base = qkv.data_ptr()
-    _check(lib().syn_cuda_attention_decode(
+    fn = lib().syn_cuda_attention_decode_flash if flash else lib().syn_cuda_attention_decode
+    _check(fn(
         cache.handle, layer, batch, ctypes.c_void_p(base), ctypes.c_void_p(base + 4 * qd),
         ctypes.c_void_p(base + 4 * (qd + kvd)), ld, n_heads, _ptr(q_norm), _ptr(k_norm),
         float(eps), _ptr(cos_t), _ptr(sin_t), window, _ptr(out), qd, _stream(qkv)),
@@ -473,7 +474,8 @@ def attention_decode(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, sin
     return out
 
 
-def attention_prefill(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, sin_t, seq=0):
+def attention_prefill(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, sin_t, seq=0,
+                      flash=False):
     """cached_attention_prefill (ops/attention.rs:153-247) for sequence
     `seq`; qkv [n_tokens, q | k | v] (q rewritten in place). Returns
     [n_tokens, n_heads*hd]; the cache length is not advanced."""
@@ -483,7 +485,8 @@ def attention_prefill(cache, layer, qkv, n_heads, q_norm, k_norm, eps, cos_t, si
     qd, kvd = n_heads * cache.hd, cache.n_kv * cache.hd
     out = torch.empty(n, qd, dtype=torch.float32, device=qkv.device)
     base = qkv.data_ptr()
-    _check(lib().syn_cuda_attention_prefill(
+    fn = lib().syn_cuda_attention_prefill_flash if flash else lib().syn_cuda_attention_prefill
+    _check(fn(
         cache.handle, layer, seq, n, ctypes.c_void_p(base), ctypes.c_void_p(base + 4 * qd),
         ctypes.c_void_p(base + 4 * (qd + kvd)), ld, n_heads, _ptr(q_norm), _ptr(k_norm),
         float(eps), _ptr(cos_t), _ptr(sin_t), _ptr(out), qd, _stream(qkv)), "attention_prefill")

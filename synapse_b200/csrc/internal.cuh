@@ -56,6 +56,8 @@ struct syn_cuda_kvcache_s {
   float* v;
   int* d_len;   // [batch]
   size_t* len;  // [batch], host mirror
+  float* part;  // split-attention partials (grown on demand)
+  size_t part_bytes;
 };
 
 namespace syn {
@@ -148,6 +150,7 @@ struct AttnArgs {
   size_t layer;
   float* out;
   size_t ldo;
+  int flash;        // 1: parallel reduction order (block-format models)
 };
 // Decode step of sequences [0, batch): norm/RoPE/append of the new token,
 // attention over positions [0, len] (the cache lengths are not advanced).

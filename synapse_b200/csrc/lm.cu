@@ -626,6 +626,294 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
 }
 
 // ---------------------------------------------------------------------------
+// Parallel ("flash") attention for the block-format models, whose matmuls
+// already carry the 1e-3 tolerance: same inputs, outputs and cache effects
+// as the exact kernels above, but reductions in a parallel order (split over
+// positions with a max/sum rescaling combine), so long contexts are not
+// latency-bound. The exact kernels stay the reference-order path (INT8).
+// ---------------------------------------------------------------------------
+constexpr int FD_THREADS = 128, FD_CH = 256;  // decode: positions per split CTA
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.0f;
+  for (int i = 0; i < nw; i++) s += red[i];
+  return s;
+}
+
+// grid (batch, heads, splits): partial (max, sum, o[HD]) of one position range
+template <int HD>
+__global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnParams p, float* part,
+                                                                  int nsplit) {
+  extern __shared__ __align__(16) float sm[];
+  constexpr int Q4 = HD / 4, VS = HD + 4, VCH = 32;
+  float* xs = sm;                   // q, k, v (3*HD)
+  float* vb = sm + 3 * HD;          // VCH staged V rows
+  float* lanes = vb + VCH * VS;     // 8
+  float* scl = lanes + 8;           // 4
+  float* red = scl + 4;             // 4
+  float* sc = red + 4;              // FD_CH
+  const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
+  const int G = p.n_heads / p.n_kv, kvh = h / G, kvd = p.n_kv * HD;
+  float* dst = part + (((size_t)b * p.n_heads + h) * nsplit + sp) * (HD + 2);
+  griddep_wait();
+  const int pos = p.len[b];
+  if (pos >= p.max_seq) {
+    if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
+    return;
+  }
+  const int L = pos + 1;
+  const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
+  const int eff = L - off, c0 = sp * FD_CH;
+  const bool owner = sp == 0 && h % G == 0;
+  if (c0 >= eff && !owner) {
+    if (tid == 0) {
+      dst[0] = -INFINITY;
+      dst[1] = 0.0f;
+    }
+    return;
+  }
+  const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
+  const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
+  const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
+  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
+  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
+  for (int i = tid; i < HD; i += FD_THREADS) {
+    xs[i] = qrow[i];
+    xs[HD + i] = krow[i];
+    xs[2 * HD + i] = vrow[i];
+  }
+  __syncthreads();
+  norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, FD_THREADS);
+  if (owner)
+    for (int i = tid; i < HD; i += FD_THREADS) {
+      kcb[(size_t)pos * kvd + i] = xs[HD + i];
+      vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
+    }
+  const int cn = min(FD_CH, eff - c0);
+  if (cn <= 0) {  // the owner with an empty range
+    if (tid == 0) {
+      dst[0] = -INFINITY;
+      dst[1] = 0.0f;
+    }
+    return;
+  }
+  for (int t = tid; t < cn; t += FD_THREADS) {
+    const int row = off + c0 + t;
+    const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
+    float4 kv[Q4];
+#pragma unroll
+    for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+    for (int c = 0; c < Q4; c++) {
+      const float4 q = reinterpret_cast<const float4*>(xs)[c];
+      a0 = fmaf(q.x, kv[c].x, a0);
+      a1 = fmaf(q.y, kv[c].y, a1);
+      a2 = fmaf(q.z, kv[c].z, a2);
+      a3 = fmaf(q.w, kv[c].w, a3);
+    }
+    sc[t] = ((a0 + a1) + (a2 + a3)) * p.scale;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int t = tid; t < cn; t += FD_THREADS) mx = fmaxf(mx, sc[t]);
+  mx = block_max(mx, red);
+  float ls = 0.0f;
+  for (int t = tid; t < cn; t += FD_THREADS) {
+    const float e = expf(sc[t] - mx);
+    sc[t] = e;
+    ls += e;
+  }
+  ls = block_sum(ls, red);
+  griddep_launch();
+  float acc = 0.0f;
+  constexpr int PER = (VCH * Q4 + FD_THREADS - 1) / FD_THREADS;
+  for (int v0 = 0; v0 < cn; v0 += VCH) {
+    const int vn = min(VCH, cn - v0);
+    __syncthreads();
+    float4 tmp[PER];
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+      const int t = tid + u * FD_THREADS, r = t / Q4, c4 = t - r * Q4;
+      if (r < vn) {
+        const int row = off + c0 + v0 + r;
+        tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
+                            : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+      const int t = tid + u * FD_THREADS, r = t / Q4, c4 = t - r * Q4;
+      if (r < vn) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
+    }
+    __syncthreads();
+    if (tid < HD)
+      for (int s = 0; s < vn; s++) acc = fmaf(sc[v0 + s], vb[s * VS + tid], acc);
+  }
+  if (tid < HD) dst[2 + tid] = acc;
+  if (tid == 0) {
+    dst[0] = mx;
+    dst[1] = ls;
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(HD) k_attn_decode_combine(const AttnParams p, const float* part,
+                                                            int nsplit) {
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  griddep_wait();
+  griddep_launch();
+  if (p.len[b] >= p.max_seq) return;
+  const float* src = part + ((size_t)b * p.n_heads + h) * nsplit * (HD + 2);
+  float M = -INFINITY;
+  for (int c = 0; c < nsplit; c++) M = fmaxf(M, src[c * (HD + 2)]);
+  float l = 0.0f, o = 0.0f;
+  for (int c = 0; c < nsplit; c++) {
+    const float m = src[c * (HD + 2)];
+    if (m == -INFINITY) continue;
+    const float f = expf(m - M);
+    l += src[c * (HD + 2) + 1] * f;
+    o += src[c * (HD + 2) + 2 + d] * f;
+  }
+  p.out[(long long)b * p.ldo + (long long)h * HD + d] = o / l;
+}
+
+size_t flash_decode_smem(int hd) {
+  return ((size_t)3 * hd + 32 * (hd + 4) + 8 + 4 + 4 + FD_CH) * sizeof(float);
+}
+
+// Prefill: CTA = (head, 64 queries), 256 threads; key tiles of 64 staged in
+// smem; 4x4 score tile and 4 rows x HD/16 output columns per thread; online
+// softmax with rescaling.
+constexpr int FP_B = 64, FP_THREADS = 256;
+
+template <int HD>
+__global__ void __launch_bounds__(FP_THREADS) k_attn_prefill_flash(const AttnParams p) {
+  extern __shared__ __align__(16) float sm[];
+  constexpr int S4 = HD + 4, PS = FP_B + 4, OC = HD / 16;
+  float* qs = sm;                 // [64][S4]
+  float* ks = qs + FP_B * S4;     // [64][S4]
+  float* vs = ks + FP_B * S4;     // [64][S4]
+  float* ps = vs + FP_B * S4;     // [64][PS]
+  const int hh = blockIdx.x, q0 = blockIdx.y * FP_B, tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;  // rows 4ty..4ty+3; score cols 4tx..; out cols tx*OC..
+  const int G = p.n_heads / p.n_kv, kvh = hh / G, kvd = p.n_kv * HD, S = p.n_tokens;
+  griddep_wait();
+  const int base = p.len[p.seq0];
+  const float* kcb = p.kc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * HD;
+  const float* vcb = p.vc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * HD;
+  for (int t = tid; t < FP_B * (HD / 4); t += FP_THREADS) {
+    const int r = t / (HD / 4), c4 = t - r * (HD / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + r < S)
+      v = reinterpret_cast<const float4*>(p.q + (long long)(q0 + r) * p.ld + (long long)hh * HD)[c4];
+    reinterpret_cast<float4*>(qs + r * S4)[c4] = v;
+  }
+  float m[4], l[4], o[4][OC];
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < OC; c++) o[r][c] = 0.0f;
+  }
+  const int kend = min(S, q0 + FP_B);  // causal: keys < kend
+  for (int k0 = 0; k0 < kend; k0 += FP_B) {
+    __syncthreads();
+    for (int t = tid; t < FP_B * (HD / 4); t += FP_THREADS) {
+      const int r = t / (HD / 4), c4 = t - r * (HD / 4);
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (k0 + r < S) {
+        kv = reinterpret_cast<const float4*>(kcb + (size_t)(k0 + r) * kvd)[c4];
+        vv = reinterpret_cast<const float4*>(vcb + (size_t)(k0 + r) * kvd)[c4];
+      }
+      reinterpret_cast<float4*>(ks + r * S4)[c4] = kv;
+      reinterpret_cast<float4*>(vs + r * S4)[c4] = vv;
+    }
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) sc[i][j] = 0.0f;
+    for (int d = 0; d < HD; d += 4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const float4*>(qs + (4 * ty + i) * S4 + d);
+#pragma unroll
+      for (int j = 0; j < 4; j++) kv[j] = *reinterpret_cast<const float4*>(ks + (4 * tx + j) * S4 + d);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          sc[i][j] = fmaf(qv[i].x, kv[j].x, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].y, kv[j].y, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].z, kv[j].z, sc[i][j]);
+          sc[i][j] = fmaf(qv[i].w, kv[j].w, sc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int q = q0 + 4 * ty + i;
+      float rm = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int k = k0 + 4 * tx + j;
+        sc[i][j] = (k <= q && k < S) ? sc[i][j] * p.scale : -INFINITY;
+        rm = fmaxf(rm, sc[i][j]);
+      }
+      for (int off = 1; off < 16; off <<= 1) rm = fmaxf(rm, __shfl_xor_sync(0xffffffffu, rm, off));
+      const float mn = fmaxf(m[i], rm);
+      const float corr = mn == -INFINITY ? 1.0f : expf(m[i] - mn);
+      float rs = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float e = mn == -INFINITY ? 0.0f : expf(sc[i][j] - mn);
+        rs += e;
+        ps[(4 * ty + i) * PS + 4 * tx + j] = e;
+      }
+      for (int off = 1; off < 16; off <<= 1) rs += __shfl_xor_sync(0xffffffffu, rs, off);
+      l[i] = l[i] * corr + rs;
+      m[i] = mn;
+#pragma unroll
+      for (int c = 0; c < OC; c++) o[i][c] *= corr;
+    }
+    __syncthreads();
+    for (int j = 0; j < FP_B; j++) {
+      float pv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) pv[i] = ps[(4 * ty + i) * PS + j];
+      const float* vr = vs + j * S4 + tx * OC;
+#pragma unroll
+      for (int c = 0; c < OC; c++) {
+        const float v = vr[c];
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[i][c] = fmaf(pv[i], v, o[i][c]);
+      }
+    }
+  }
+  griddep_launch();
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int q = q0 + 4 * ty + i;
+    if (q < S) {
+      float* orow = p.out + (long long)q * p.ldo + (long long)hh * HD + tx * OC;
+#pragma unroll
+      for (int c = 0; c < OC; c++) orow[c] = o[i][c] / l[i];
+    }
+  }
+}
+
+size_t flash_prefill_smem(int hd) {
+  return ((size_t)3 * FP_B * (hd + 4) + (size_t)FP_B * (FP_B + 4)) * sizeof(float);
+}
+
+// ---------------------------------------------------------------------------
 // SwiGLU: variant 0 = the INT8 model's silu(g) * u with silu = g/(1+exp(-g))
 // (quantization/lm/int8.rs:500-503, ops/activation.rs:30-32); variant 1 =
 // swigluFused (zig/src/ops/silu.zig:85-114): g * (1/(1+exp(-g))) * u for the
@@ -866,6 +1154,42 @@ syn_status_t make_params(const AttnArgs& a, AttnParams& p, int seq0, int ntok) {
 
 }  // namespace
 
+syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t batch, size_t eff,
+                                 cudaStream_t st) {
+  syn_cuda_kvcache_t* c = a.cache;
+  const int nsplit = (int)((eff + FD_CH - 1) / FD_CH);
+  const size_t need = batch * p.n_heads * (size_t)nsplit * (p.hd + 2) * sizeof(float);
+  if (need > c->part_bytes) {  // grows outside graph capture only
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs != cudaStreamCaptureStatusNone) return SYN_ERR_UNSUPPORTED;
+    cudaStreamSynchronize(st);
+    cudaFree(c->part);
+    c->part = nullptr;
+    c->part_bytes = 0;
+    if (cudaMalloc(&c->part, need) != cudaSuccess) return SYN_ERR_OUT_OF_MEMORY;
+    c->part_bytes = need;
+  }
+  void (*split)(const AttnParams, float*, int) = nullptr;
+  void (*comb)(const AttnParams, const float*, int) = nullptr;
+  switch (p.hd) {
+    case 32: split = k_attn_decode_split<32>; comb = k_attn_decode_combine<32>; break;
+    case 64: split = k_attn_decode_split<64>; comb = k_attn_decode_combine<64>; break;
+    case 128: split = k_attn_decode_split<128>; comb = k_attn_decode_combine<128>; break;
+    default: return SYN_ERR_UNSUPPORTED;
+  }
+  const size_t smem = flash_decode_smem(p.hd);
+  syn_status_t s = allow_smem((const void*)split, smem);
+  if (s) return s;
+  s = cuda_status(launch_pdl(split, dim3((unsigned)batch, (unsigned)p.n_heads, (unsigned)nsplit),
+                             dim3(FD_THREADS), smem, st, p, c->part, nsplit),
+                  "k_attn_decode_split");
+  if (s) return s;
+  return cuda_status(launch_pdl(comb, dim3((unsigned)batch, (unsigned)p.n_heads), dim3(p.hd), 0, st,
+                                p, (const float*)c->part, nsplit),
+                     "k_attn_decode_combine");
+}
+
 syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, cudaStream_t st) {
   AttnParams p;
   syn_status_t s = make_params(a, p, 0, 1);
@@ -874,9 +1198,10 @@ syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, 
   if (batch > a.cache->batch) return SYN_ERR_INVALID_ARG;
   for (size_t b = 0; b < batch; b++)
     if (a.cache->len[b] >= a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
-  // A captured graph replays at growing positions: size smem for the window.
+  // A captured graph replays at growing positions: size for the window.
   size_t eff = a.cache->max_seq;
   if (a.window && a.window < eff) eff = a.window;
+  if (a.flash) return launch_decode_flash(a, p, batch, eff, st);
   const size_t smem = decode_smem_floats(p.hd, (int)eff) * sizeof(float);
   if (smem > kMaxSmem) return SYN_ERR_UNSUPPORTED;
   void (*kern)(const AttnParams) = nullptr;
@@ -919,6 +1244,14 @@ syn_status_t launch_prefill_attention_args(const AttnArgs& a, size_t seq, size_t
   if (seq >= a.cache->batch) return SYN_ERR_INVALID_ARG;
   if (a.cache->len[seq] + ntok > a.cache->max_seq) return SYN_ERR_INVALID_ARG;
   if (ntok == 0) return SYN_OK;
+  if (a.flash && (p.hd == 64 || p.hd == 128)) {
+    void (*kern)(const AttnParams) = p.hd == 64 ? k_attn_prefill_flash<64> : k_attn_prefill_flash<128>;
+    const size_t fs = flash_prefill_smem(p.hd);
+    if ((s = allow_smem((const void*)kern, fs))) return s;
+    return cuda_status(launch_pdl(kern, dim3((unsigned)p.n_heads, (unsigned)((ntok + FP_B - 1) / FP_B)),
+                                  dim3(FP_THREADS), fs, st, p),
+                       "k_attn_prefill_flash");
+  }
   const int pr = prefill_rows((int)ntok, p.hd);
   if (!pr) return SYN_ERR_UNSUPPORTED;
   const size_t smem = prefill_smem(pr, (int)ntok, p.hd);
@@ -1037,6 +1370,7 @@ syn_status_t syn_cuda_kvcache_destroy(syn_cuda_kvcache_t* c) {
   cudaFree(c->k);
   cudaFree(c->v);
   cudaFree(c->d_len);
+  cudaFree(c->part);
   delete[] c->len;
   delete c;
   return SYN_OK;
@@ -1142,6 +1476,30 @@ syn_status_t syn_cuda_attention_prefill(syn_cuda_kvcache_t* cache, size_t layer,
   DeviceGuard g(cache->device);
   AttnArgs a{q, k, v, ld, n_heads, q_norm, k_norm, eps, rope_cos, rope_sin, 0, cache, layer,
              out, ldo};
+  return launch_attn_prefill_args(a, seq, n_tokens, nullptr, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_attention_decode_flash(
+    syn_cuda_kvcache_t* cache, size_t layer, size_t batch, float* q, const float* k,
+    const float* v, size_t ld, size_t n_heads, const float* q_norm, const float* k_norm, float eps,
+    const float* rope_cos, const float* rope_sin, size_t window, float* out, size_t ldo,
+    void* stream) {
+  if (!cache || !q || !k || !v || !rope_cos || !rope_sin || !out) return SYN_ERR_NULL_PTR;
+  if (!batch) return SYN_OK;
+  DeviceGuard g(cache->device);
+  AttnArgs a{q, k, v, ld, n_heads, q_norm, k_norm, eps, rope_cos, rope_sin, window, cache, layer,
+             out, ldo, 1};
+  return launch_attn_decode_args(a, batch, nullptr, (cudaStream_t)stream);
+}
+
+syn_status_t syn_cuda_attention_prefill_flash(
+    syn_cuda_kvcache_t* cache, size_t layer, size_t seq, size_t n_tokens, float* q, const float* k,
+    const float* v, size_t ld, size_t n_heads, const float* q_norm, const float* k_norm, float eps,
+    const float* rope_cos, const float* rope_sin, float* out, size_t ldo, void* stream) {
+  if (!cache || !q || !k || !v || !rope_cos || !rope_sin || !out) return SYN_ERR_NULL_PTR;
+  DeviceGuard g(cache->device);
+  AttnArgs a{q, k, v, ld, n_heads, q_norm, k_norm, eps, rope_cos, rope_sin, 0, cache, layer,
+             out, ldo, 1};
   return launch_attn_prefill_args(a, seq, n_tokens, nullptr, (cudaStream_t)stream);
 }
 

@@ -300,6 +300,9 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   a.window = m->window;
   a.cache = m->cache;
   a.ldo = m->qd_l;
+  // block-format models carry a 1e-3 tolerance: parallel-order attention;
+  // INT8 models keep the reference's reduction order (bit-exact tokens)
+  a.flash = m->int8 ? 0 : 1;
   const bool tp = m->tp > 1;
   for (size_t li = 0; li < m->L; li++) {
     LayerDev& ly = m->layers[li];

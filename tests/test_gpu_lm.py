@@ -29,6 +29,15 @@ def exact(a, b):
     return a.shape == b.shape and np.array_equal(a, b)
 
 
+def close(a, b, flash):
+    """Bit-exact for the reference-order kernels; within f32 reassociation
+    (1e-5 of the row's magnitude) for the parallel-order ones."""
+    if not flash:
+        return exact(a, b)
+    a, b = np.asarray(a), np.asarray(b)
+    return a.shape == b.shape and np.allclose(a, b, rtol=1e-5, atol=1e-5 * np.abs(b).max())
+
+
 @pytest.mark.parametrize("h", [4, 7, 128, 1024, 1027, 4096])
 @pytest.mark.parametrize("rows", [1, 3])
 def test_rmsnorm_bit_exact(h, rows):
@@ -91,7 +100,8 @@ def _oracle_head_norm_rope(x, w, heads, hd, eps, cos, sin, pos):
 @pytest.mark.parametrize("hq,hkv,hd", [(4, 2, 32), (8, 2, 64), (16, 8, 128), (32, 8, 128)])
 @pytest.mark.parametrize("lengths", [(1, 5), (63, 64), (65, 130)])
 @pytest.mark.parametrize("window,norm", [(0, True), (24, False)])
-def test_attention_decode_bit_exact(ctx, hq, hkv, hd, lengths, window, norm):
+@pytest.mark.parametrize("flash", [False, True])
+def test_attention_decode_bit_exact(ctx, hq, hkv, hd, lengths, window, norm, flash):
     rng = np.random.default_rng(hq * 1000 + hd + lengths[0] + window)
     max_seq, B = 160, 2
     qd, kvd = hq * hd, hkv * hd
@@ -113,7 +123,7 @@ def test_attention_decode_bit_exact(ctx, hq, hkv, hd, lengths, window, norm):
     qkv = rng.standard_normal((B, qd + 2 * kvd)).astype(np.float32)
     out = sb.attention_decode(cache, 0, cuda(qkv), hq, cuda(qn) if norm else None,
                               cuda(kn) if norm else None, eps, cuda(cos), cuda(sin),
-                              window=window, batch=B).cpu().numpy()
+                              window=window, batch=B, flash=flash).cpu().numpy()
     for b, L in enumerate(lengths):
         pos = L - 1
         q = _oracle_head_norm_rope(qkv[b, :qd], qn, hq, hd, eps, oc, os_, pos)
@@ -122,27 +132,28 @@ def test_attention_decode_bit_exact(ctx, hq, hkv, hd, lengths, window, norm):
         kc = np.concatenate([hist[b][0], k[None, :]])
         vc = np.concatenate([hist[b][1], v[None, :]])
         want = O.attention_decode(q, kc, vc, L, hq, hkv, hd, window)
-        assert exact(out[b], want), (b, L, np.abs(out[b] - want).max())
+        assert close(out[b], want, flash), (b, L, np.abs(out[b] - want).max())
         kv, vv = cache.view(0, b)
         assert exact(kv[pos].cpu().numpy(), k) and exact(vv[pos].cpu().numpy(), v)
         assert cache.length(b) == L - 1  # not advanced
     cache.close()
 
 
-@pytest.mark.parametrize("S", [1, 5, 16, 17, 33, 40, 70])
-@pytest.mark.parametrize("hq,hkv,hd", [(4, 2, 32), (8, 2, 128)])
-def test_attention_prefill_bit_exact(ctx, S, hq, hkv, hd):
+@pytest.mark.parametrize("S", [1, 5, 16, 17, 33, 40, 70, 130])
+@pytest.mark.parametrize("hq,hkv,hd,flash", [(4, 2, 32, False), (8, 2, 128, False),
+                                             (4, 2, 64, True), (8, 2, 128, True)])
+def test_attention_prefill_bit_exact(ctx, S, hq, hkv, hd, flash):
     rng = np.random.default_rng(S * 7 + hd)
     qd, kvd = hq * hd, hkv * hd
     eps = 1e-6
-    cache = sb.KVCache(ctx, 96, hkv, hd, 2, batch=2)
-    cos, sin = sb.rope_tables(1e6, 96, hd)
-    oc, os_ = O.rope_tables(1e6, 96, hd)
+    cache = sb.KVCache(ctx, 160, hkv, hd, 2, batch=2)
+    cos, sin = sb.rope_tables(1e6, 160, hd)
+    oc, os_ = O.rope_tables(1e6, 160, hd)
     qn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
     kn = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
     qkv = rng.standard_normal((S, qd + 2 * kvd)).astype(np.float32)
     out = sb.attention_prefill(cache, 1, cuda(qkv), hq, cuda(qn), cuda(kn), eps, cuda(cos),
-                               cuda(sin), seq=1).cpu().numpy()
+                               cuda(sin), seq=1, flash=flash).cpu().numpy()
     q = O.rmsnorm(qkv[:, :qd], qn, hd, eps)
     k = O.rmsnorm(qkv[:, qd:qd + kvd], kn, hd, eps)
     O.rope_inplace(q, oc, os_, S, hq, hd, 0)
@@ -152,7 +163,7 @@ def test_attention_prefill_bit_exact(ctx, S, hq, hkv, hd):
     g = hq // hkv
     for h in range(hq):
         st, o = O.fused_attention(S, S, hd, q3[:, h], k3[:, h // g], v3[:, h // g])
-        assert exact(out[:, h * hd:(h + 1) * hd], o.reshape(S, hd)), h
+        assert close(out[:, h * hd:(h + 1) * hd], o.reshape(S, hd), flash), h
     kv, vv = cache.view(1, 1)
     assert exact(kv[:S].cpu().numpy(), k.reshape(S, kvd))
     assert exact(vv[:S].cpu().numpy(), qkv[:, qd + kvd:])
