@@ -126,11 +126,12 @@ syn_status_t dequant_weight(const syn_cuda_weight_s* w, float* d_out, cudaStream
 // Residual add + RMSNorm: row r of out = rmsnorm(src_r (+ delta_r)), where
 // src_r is x_r or, when ids != nullptr, the embedding row table[ids[r]]
 // (zeros for ids outside the vocabulary). x_out (optional) receives the
-// normalised input (the updated residual stream); it may alias x.
+// normalised input (the updated residual stream); it may alias x. fast=1
+// sums the squares in a parallel order (models with a tolerance).
 syn_status_t launch_add_rmsnorm(const float* x, size_t ldx, const float* delta, size_t ldd,
                                 const int32_t* ids, const float* table, size_t vocab,
                                 float* x_out, size_t ldxo, const float* w, size_t rows, size_t h,
-                                float eps, float* out, size_t ldo, cudaStream_t st);
+                                float eps, float* out, size_t ldo, cudaStream_t st, int fast = 0);
 
 // Attention over the KV cache. q/k/v rows have stride ld (row b = sequence b
 // for decode, token t for prefill); out rows have stride ldo.

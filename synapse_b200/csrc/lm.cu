@@ -95,6 +95,7 @@ struct NormParams {
   float eps;
   float* out;
   long long ldo;
+  int fast;            // 1: parallel sum of squares (block-format models)
 };
 
 // sum of squares in the reference's order; every thread returns the same value
@@ -153,7 +154,20 @@ __global__ void __launch_bounds__(NORM_THREADS) k_add_rmsnorm(const NormParams p
     }
   }
   __syncthreads();
-  const float scale = norm_scale(sx, p.h, p.eps, lane);
+  float scale;
+  if (p.fast) {  // tree sum: a parallel order, for models with a tolerance
+    __shared__ float red[NORM_THREADS / 32];
+    float a = 0.0f;
+    for (int j = tid; j < p.h; j += NORM_THREADS) a = fmaf(sx[j], sx[j], a);
+    for (int o = 16; o; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if ((tid & 31) == 0) red[tid >> 5] = a;
+    __syncthreads();
+    float ss = 0.0f;
+    for (int w = 0; w < NORM_THREADS / 32; w++) ss += red[w];
+    scale = 1.0f / sqrtf(ss / (float)p.h + p.eps);
+  } else {
+    scale = norm_scale(sx, p.h, p.eps, lane);
+  }
   griddep_launch();
   for (int j0 = 0; j0 < p.h; j0 += NORM_THREADS * NV) {
     float wv[NV];
@@ -632,7 +646,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
 // positions with a max/sum rescaling combine), so long contexts are not
 // latency-bound. The exact kernels stay the reference-order path (INT8).
 // ---------------------------------------------------------------------------
-constexpr int FD_THREADS = 128, FD_CH = 256;  // decode: positions per split CTA
+constexpr int FD_THREADS = 128, FD_CH = 64;  // decode: positions per split CTA
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -645,10 +659,12 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
-// grid (batch, heads, splits): partial (max, sum, o[HD]) of one position range
+// grid (batch, heads, splits): partial (max, sum, o[HD]) of one position
+// range; the last CTA of a head to finish (arrival counter, left at zero)
+// combines the partials with the max/sum rescaling.
 template <int HD>
 __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnParams p, float* part,
-                                                                  int nsplit) {
+                                                                  int* cnt, int nsplit) {
   extern __shared__ __align__(16) float sm[];
   constexpr int Q4 = HD / 4, VS = HD + 4, VCH = 32;
   float* xs = sm;                   // q, k, v (3*HD)
@@ -657,9 +673,11 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
   float* scl = lanes + 8;           // 4
   float* red = scl + 4;             // 4
   float* sc = red + 4;              // FD_CH
+  __shared__ int last;
   const int b = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
   const int G = p.n_heads / p.n_kv, kvh = h / G, kvd = p.n_kv * HD;
-  float* dst = part + (((size_t)b * p.n_heads + h) * nsplit + sp) * (HD + 2);
+  float* base = part + ((size_t)b * p.n_heads + h) * nsplit * (HD + 2);
+  float* dst = base + (size_t)sp * (HD + 2);
   griddep_wait();
   const int pos = p.len[b];
   if (pos >= p.max_seq) {
@@ -670,117 +688,104 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
   const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
   const int eff = L - off, c0 = sp * FD_CH;
   const bool owner = sp == 0 && h % G == 0;
-  if (c0 >= eff && !owner) {
-    if (tid == 0) {
-      dst[0] = -INFINITY;
-      dst[1] = 0.0f;
-    }
-    return;
-  }
-  const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
-  const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
-  const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
-  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
-  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
-  for (int i = tid; i < HD; i += FD_THREADS) {
-    xs[i] = qrow[i];
-    xs[HD + i] = krow[i];
-    xs[2 * HD + i] = vrow[i];
-  }
-  __syncthreads();
-  norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, FD_THREADS);
-  if (owner)
-    for (int i = tid; i < HD; i += FD_THREADS) {
-      kcb[(size_t)pos * kvd + i] = xs[HD + i];
-      vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
-    }
   const int cn = min(FD_CH, eff - c0);
-  if (cn <= 0) {  // the owner with an empty range
-    if (tid == 0) {
-      dst[0] = -INFINITY;
-      dst[1] = 0.0f;
+  float mx = -INFINITY, ls = 0.0f, acc = 0.0f;
+  if (cn > 0 || owner) {
+    const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
+    const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
+    const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
+    float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
+    float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
+    for (int i = tid; i < HD; i += FD_THREADS) {
+      xs[i] = qrow[i];
+      xs[HD + i] = krow[i];
+      xs[2 * HD + i] = vrow[i];
     }
-    return;
-  }
-  for (int t = tid; t < cn; t += FD_THREADS) {
-    const int row = off + c0 + t;
-    const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
-    float4 kv[Q4];
-#pragma unroll
-    for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-    for (int c = 0; c < Q4; c++) {
-      const float4 q = reinterpret_cast<const float4*>(xs)[c];
-      a0 = fmaf(q.x, kv[c].x, a0);
-      a1 = fmaf(q.y, kv[c].y, a1);
-      a2 = fmaf(q.z, kv[c].z, a2);
-      a3 = fmaf(q.w, kv[c].w, a3);
-    }
-    sc[t] = ((a0 + a1) + (a2 + a3)) * p.scale;
-  }
-  __syncthreads();
-  float mx = -INFINITY;
-  for (int t = tid; t < cn; t += FD_THREADS) mx = fmaxf(mx, sc[t]);
-  mx = block_max(mx, red);
-  float ls = 0.0f;
-  for (int t = tid; t < cn; t += FD_THREADS) {
-    const float e = expf(sc[t] - mx);
-    sc[t] = e;
-    ls += e;
-  }
-  ls = block_sum(ls, red);
-  griddep_launch();
-  float acc = 0.0f;
-  constexpr int PER = (VCH * Q4 + FD_THREADS - 1) / FD_THREADS;
-  for (int v0 = 0; v0 < cn; v0 += VCH) {
-    const int vn = min(VCH, cn - v0);
     __syncthreads();
-    float4 tmp[PER];
+    norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, FD_THREADS);
+    if (owner)
+      for (int i = tid; i < HD; i += FD_THREADS) {
+        kcb[(size_t)pos * kvd + i] = xs[HD + i];
+        vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
+      }
+    if (cn > 0) {
+      for (int t = tid; t < cn; t += FD_THREADS) {
+        const int row = off + c0 + t;
+        const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
+        float4 kv[Q4];
 #pragma unroll
-    for (int u = 0; u < PER; u++) {
-      const int t = tid + u * FD_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < vn) {
-        const int row = off + c0 + v0 + r;
-        tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
-                            : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+        for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int c = 0; c < Q4; c++) {
+          const float4 q = reinterpret_cast<const float4*>(xs)[c];
+          a0 = fmaf(q.x, kv[c].x, a0);
+          a1 = fmaf(q.y, kv[c].y, a1);
+          a2 = fmaf(q.z, kv[c].z, a2);
+          a3 = fmaf(q.w, kv[c].w, a3);
+        }
+        sc[t] = ((a0 + a1) + (a2 + a3)) * p.scale;
+      }
+      __syncthreads();
+      for (int t = tid; t < cn; t += FD_THREADS) mx = fmaxf(mx, sc[t]);
+      mx = block_max(mx, red);
+      for (int t = tid; t < cn; t += FD_THREADS) {
+        const float e = expf(sc[t] - mx);
+        sc[t] = e;
+        ls += e;
+      }
+      ls = block_sum(ls, red);
+      constexpr int PER = (VCH * Q4 + FD_THREADS - 1) / FD_THREADS;
+      for (int v0 = 0; v0 < cn; v0 += VCH) {
+        const int vn = min(VCH, cn - v0);
+        __syncthreads();
+        float4 tmp[PER];
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+          const int t = tid + u * FD_THREADS, r = t / Q4, c4 = t - r * Q4;
+          if (r < vn) {
+            const int row = off + c0 + v0 + r;
+            tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
+                                : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+          const int t = tid + u * FD_THREADS, r = t / Q4, c4 = t - r * Q4;
+          if (r < vn) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
+        }
+        __syncthreads();
+        if (tid < HD)
+          for (int s2 = 0; s2 < vn; s2++) acc = fmaf(sc[v0 + s2], vb[s2 * VS + tid], acc);
       }
     }
-#pragma unroll
-    for (int u = 0; u < PER; u++) {
-      const int t = tid + u * FD_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < vn) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
-    }
-    __syncthreads();
-    if (tid < HD)
-      for (int s = 0; s < vn; s++) acc = fmaf(sc[v0 + s], vb[s * VS + tid], acc);
   }
   if (tid < HD) dst[2 + tid] = acc;
   if (tid == 0) {
     dst[0] = mx;
     dst[1] = ls;
   }
-}
-
-template <int HD>
-__global__ void __launch_bounds__(HD) k_attn_decode_combine(const AttnParams p, const float* part,
-                                                            int nsplit) {
-  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  griddep_wait();
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(&cnt[b * p.n_heads + h], 1) == nsplit - 1;
+  __syncthreads();
   griddep_launch();
-  if (p.len[b] >= p.max_seq) return;
-  const float* src = part + ((size_t)b * p.n_heads + h) * nsplit * (HD + 2);
-  float M = -INFINITY;
-  for (int c = 0; c < nsplit; c++) M = fmaxf(M, src[c * (HD + 2)]);
-  float l = 0.0f, o = 0.0f;
-  for (int c = 0; c < nsplit; c++) {
-    const float m = src[c * (HD + 2)];
-    if (m == -INFINITY) continue;
-    const float f = expf(m - M);
-    l += src[c * (HD + 2) + 1] * f;
-    o += src[c * (HD + 2) + 2 + d] * f;
+  if (!last) return;
+  __threadfence();
+  if (tid < HD) {
+    float M = -INFINITY;
+    for (int c = 0; c < nsplit; c++) M = fmaxf(M, base[c * (HD + 2)]);
+    float l = 0.0f, o = 0.0f;
+    for (int c = 0; c < nsplit; c++) {
+      const float m = base[c * (HD + 2)];
+      if (m == -INFINITY) continue;
+      const float f = expf(m - M);
+      l += base[c * (HD + 2) + 1] * f;
+      o += base[c * (HD + 2) + 2 + tid] * f;
+    }
+    p.out[(long long)b * p.ldo + (long long)h * HD + tid] = o / l;
   }
-  p.out[(long long)b * p.ldo + (long long)h * HD + d] = o / l;
+  if (tid == 0) cnt[b * p.n_heads + h] = 0;  // ready for the next launch
 }
 
 size_t flash_decode_smem(int hd) {
@@ -1055,11 +1060,11 @@ syn_status_t cuda_status(cudaError_t e, const char* where) {
 syn_status_t launch_add_rmsnorm(const float* x, size_t ldx, const float* delta, size_t ldd,
                                 const int32_t* ids, const float* table, size_t vocab,
                                 float* x_out, size_t ldxo, const float* w, size_t rows, size_t h,
-                                float eps, float* out, size_t ldo, cudaStream_t st) {
+                                float eps, float* out, size_t ldo, cudaStream_t st, int fast) {
   if (h == 0 || rows == 0) return SYN_OK;
   if (h > 40000 || rows > 0x7FFFFFFF) return SYN_ERR_UNSUPPORTED;
   NormParams p{x, (long long)ldx, delta, (long long)ldd, ids, table, (unsigned)vocab,
-               x_out, (long long)ldxo, w, (int)h, eps, out, (long long)ldo};
+               x_out, (long long)ldxo, w, (int)h, eps, out, (long long)ldo, fast};
   const size_t smem = h * sizeof(float);
   syn_status_t s = allow_smem((const void*)k_add_rmsnorm, smem);
   if (s) return s;
@@ -1158,8 +1163,10 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
                                  cudaStream_t st) {
   syn_cuda_kvcache_t* c = a.cache;
   const int nsplit = (int)((eff + FD_CH - 1) / FD_CH);
-  const size_t need = batch * p.n_heads * (size_t)nsplit * (p.hd + 2) * sizeof(float);
-  if (need > c->part_bytes) {  // grows outside graph capture only
+  const size_t pbytes = (batch * p.n_heads * (size_t)nsplit * (p.hd + 2) * sizeof(float) + 255) &
+                        ~size_t(255);
+  const size_t need = pbytes + batch * p.n_heads * sizeof(int);
+  if (need > c->part_bytes) {  // grows outside graph capture only; counters start at zero
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cs);
     if (cs != cudaStreamCaptureStatusNone) return SYN_ERR_UNSUPPORTED;
@@ -1168,26 +1175,23 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
     c->part = nullptr;
     c->part_bytes = 0;
     if (cudaMalloc(&c->part, need) != cudaSuccess) return SYN_ERR_OUT_OF_MEMORY;
+    if (cudaMemset(c->part, 0, need) != cudaSuccess) return SYN_ERR_CUDA;
     c->part_bytes = need;
   }
-  void (*split)(const AttnParams, float*, int) = nullptr;
-  void (*comb)(const AttnParams, const float*, int) = nullptr;
+  int* cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(c->part) + pbytes);
+  void (*split)(const AttnParams, float*, int*, int) = nullptr;
   switch (p.hd) {
-    case 32: split = k_attn_decode_split<32>; comb = k_attn_decode_combine<32>; break;
-    case 64: split = k_attn_decode_split<64>; comb = k_attn_decode_combine<64>; break;
-    case 128: split = k_attn_decode_split<128>; comb = k_attn_decode_combine<128>; break;
+    case 32: split = k_attn_decode_split<32>; break;
+    case 64: split = k_attn_decode_split<64>; break;
+    case 128: split = k_attn_decode_split<128>; break;
     default: return SYN_ERR_UNSUPPORTED;
   }
   const size_t smem = flash_decode_smem(p.hd);
   syn_status_t s = allow_smem((const void*)split, smem);
   if (s) return s;
-  s = cuda_status(launch_pdl(split, dim3((unsigned)batch, (unsigned)p.n_heads, (unsigned)nsplit),
-                             dim3(FD_THREADS), smem, st, p, c->part, nsplit),
-                  "k_attn_decode_split");
-  if (s) return s;
-  return cuda_status(launch_pdl(comb, dim3((unsigned)batch, (unsigned)p.n_heads), dim3(p.hd), 0, st,
-                                p, (const float*)c->part, nsplit),
-                     "k_attn_decode_combine");
+  return cuda_status(launch_pdl(split, dim3((unsigned)batch, (unsigned)p.n_heads, (unsigned)nsplit),
+                                dim3(FD_THREADS), smem, st, p, c->part, cnt, nsplit),
+                     "k_attn_decode_split");
 }
 
 syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, cudaStream_t st) {

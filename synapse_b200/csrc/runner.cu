@@ -309,10 +309,10 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
     if (li == 0)
       s = launch_add_rmsnorm(nullptr, 0, nullptr, 0, chained ? m->tok : m->ids, m->embed, m->V,
                              m->resid, h,
-                             ly.attn_norm, rows, h, m->eps, m->x, h, st);
+                             ly.attn_norm, rows, h, m->eps, m->x, h, st, a.flash);
     else
       s = launch_add_rmsnorm(m->resid, h, m->dn, h, nullptr, nullptr, 0, m->resid, h,
-                             ly.attn_norm, rows, h, m->eps, m->x, h, st);
+                             ly.attn_norm, rows, h, m->eps, m->x, h, st, a.flash);
     if (s) return s;
     if ((s = mm(m, ly.qkv, m->x, rows, m->qkv))) return s;
     a.q = m->qkv;
@@ -328,7 +328,7 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
     if ((s = mm(m, ly.o, m->att, rows, m->o))) return s;
     if (tp && (s = tp_allreduce_sum(m->ctx, m->o, rows * h, st))) return s;  // row-parallel O
     s = launch_add_rmsnorm(m->resid, h, m->o, h, nullptr, nullptr, 0, m->resid, h, ly.ffn_norm,
-                           rows, h, m->eps, m->x, h, st);
+                           rows, h, m->eps, m->x, h, st, a.flash);
     if (s) return s;
     if ((s = mm(m, ly.gu, m->x, rows, m->gu))) return s;
     s = launch_swiglu(m->gu, m->gu + m->ff_l, 2 * m->ff_l, rows, m->ff_l, variant, m->hid,
@@ -340,7 +340,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   // final norm and LM head: prefill keeps only the last token (int8.rs:619-627)
   const size_t r0 = prefill ? rows - 1 : 0, nr = prefill ? 1 : rows;
   s = launch_add_rmsnorm(m->resid + r0 * h, h, m->dn + r0 * h, h, nullptr, nullptr, 0,
-                         m->resid + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st);
+                         m->resid + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st,
+                         a.flash);
   if (s) return s;
   if (tp) {  // vocab-parallel LM head: gather each row's logits in rank (= vocab) order
     if ((s = mm(m, m->lm_head, m->x, nr, m->logits_l))) return s;
