@@ -566,18 +566,22 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
 // k_qgemv_tma: repacked formats; weights through a TMA-filled smem ring.
 // Threads 0-255 consume, warp 8 (threads 256-287) produces.
 // ---------------------------------------------------------------------------
-template <int FMT, int MT>
+template <int FMT, int MT, int RG>
 __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) {
   using S = Stage<FMT>;
+  static_assert(RG == 1 || (FMT != F_INT8 && MT == 1), "row-group pairs: block formats, M=1");
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) uint64_t full[S::NS], empty[S::NS];
   __shared__ CtaShared<MT> sh;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = blockIdx.x, ks = blockIdx.y, m0 = blockIdx.z * MT;
+  // RG row groups per CTA: their stages share the activation blocks
+  const int g = blockIdx.x * RG, ks = blockIdx.y, m0 = blockIdx.z * MT;
+  const int ng = min(RG, p.groups - g);
   const int cb0 = ks * p.kr, cb1 = min(p.nblk, cb0 + p.kr);
   const int nst = (cb1 - cb0 + SB - 1) / SB;
+  constexpr int SBYTES = RG * S::BYTES;  // one stage: RG sub-stages
   uint8_t* ring = sm;
-  uint8_t* act = sm + S::NS * S::BYTES;
+  uint8_t* act = sm + S::NS * SBYTES;
   const int act_stride = p.kr * act_block_bytes(FMT);
   const int cc0 = cb0 >> 4, ncc = ((cb1 + 15) >> 4) - cc0;
   int* csum = reinterpret_cast<int*>(act + MT * act_stride);
@@ -595,8 +599,6 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
     // ---- producer: stream this CTA's weight bytes, stage by stage ----
     griddep_launch();
     if (lane == 0) {
-      const size_t tile0 = (size_t)g * p.nblk;  // first tile of this row group
-      const size_t stile0 = (size_t)g * p.nsb;  // first super-block tile
       for (int s = 0; s < nst; s++) {
         const int slot = s % S::NS;
         if (s >= S::NS && !mbar_wait_bounded(&empty[slot], ((s / S::NS) - 1) & 1)) {
@@ -604,10 +606,13 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
           break;
         }
         const int b0 = cb0 + s * SB, nbs = min(SB, cb1 - b0);
-        uint8_t* st = ring + slot * S::BYTES;
-        uint32_t bytes = nbs * S::QT + nbs * S::DT + (nbs / 8) * S::HT + nbs * S::QHT +
-                         nbs * S::SCT + (nbs / 8) * S::D6T;
-        mbar_expect_tx(&full[slot], bytes);
+        const uint32_t bytes = nbs * S::QT + nbs * S::DT + (nbs / 8) * S::HT + nbs * S::QHT +
+                               nbs * S::SCT + (nbs / 8) * S::D6T;
+        mbar_expect_tx(&full[slot], bytes * ng);
+        for (int r = 0; r < ng; r++) {
+        const size_t tile0 = (size_t)(g + r) * p.nblk;  // first tile of this row group
+        const size_t stile0 = (size_t)(g + r) * p.nsb;  // first super-block tile
+        uint8_t* st = ring + slot * SBYTES + r * S::BYTES;
         bulk_g2s(st, p.q + (tile0 + b0) * S::QT, nbs * S::QT, &full[slot]);
         if constexpr (S::DT)
           bulk_g2s(st + S::OFF_D, reinterpret_cast<const uint8_t*>(p.d) + (tile0 + b0) * 64,
@@ -621,6 +626,7 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
           bulk_g2s(st + S::OFF_D6, reinterpret_cast<const uint8_t*>(p.d) + (stile0 + b0 / 8) * 64,
                    (nbs / 8) * 64, &full[slot]);
         }
+        }
       }
     }
     return;
@@ -631,15 +637,17 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
   griddep_launch();
   cta_prologue<FMT, MT>(p, m0, cb0, cb1, act, csum, ncc, sh);
 
-  float facc[MT];
+  float facc[MT][RG];
 #pragma unroll
-  for (int mm = 0; mm < MT; mm++) facc[mm] = 0.0f;
+  for (int mm = 0; mm < MT; mm++)
+#pragma unroll
+    for (int r = 0; r < RG; r++) facc[mm][r] = 0.0f;
   for (int s = 0; s < nst; s++) {
     const int slot = s % S::NS;
     const bool ok = mbar_wait_bounded(&full[slot], (s / S::NS) & 1);
     if (!ok && lane == 0) report(p, SYN_ERR_TIMEOUT);
     const int b0 = cb0 + s * SB, nbs = min(SB, cb1 - b0);
-    const uint8_t* st = ring + slot * S::BYTES;
+    const uint8_t* st = ring + slot * SBYTES;
     int ich[MT];
 #pragma unroll
     for (int mm = 0; mm < MT; mm++) ich[mm] = 0;
@@ -647,16 +655,21 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
     for (int u = 0; u < 2; u++) {
       const int bl = warp * 2 + u;
       if (!ok || bl >= nbs) break;
-      WB<FMT> w;
-      load_w_smem<FMT>(st, bl, lane, w);
+      WB<FMT> w[RG];
+#pragma unroll
+      for (int r = 0; r < RG; r++)
+        if (r < ng) load_w_smem<FMT>(st + r * S::BYTES, bl, lane, w[r]);
 #pragma unroll
       for (int mm = 0; mm < MT; mm++) {
         AB a;
         load_act<FMT>(act + mm * act_stride + (b0 + bl - cb0) * act_block_bytes(FMT), a);
-        if constexpr (FMT == F_INT8)
-          ich[mm] += dot_int8(w, a);
-        else
-          facc[mm] += dot_block<FMT>(w, a, b0 + bl);
+        if constexpr (FMT == F_INT8) {
+          ich[mm] += dot_int8(w[0], a);
+        } else {
+#pragma unroll
+          for (int r = 0; r < RG; r++)
+            if (r < ng) facc[mm][r] += dot_block<FMT>(w[r], a, b0 + bl);
+        }
       }
     }
     if constexpr (FMT == F_INT8) {
@@ -668,11 +681,16 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
-  if constexpr (FMT != F_INT8) {
 #pragma unroll
-    for (int mm = 0; mm < MT; mm++) sh.red[warp][mm][lane] = facc[mm];
+  for (int r = 0; r < RG; r++) {
+    if (r >= ng) break;
+    consumer_sync();  // the previous group's finish has read sh.red
+    if constexpr (FMT != F_INT8) {
+#pragma unroll
+      for (int mm = 0; mm < MT; mm++) sh.red[warp][mm][lane] = facc[mm][r];
+    }
+    cta_finish<FMT, MT>(p, g + r, ks, m0, cc0, ncc, csum, sh);
   }
-  cta_finish<FMT, MT>(p, g, ks, m0, cc0, ncc, csum, sh);
 }
 
 // ---------------------------------------------------------------------------
@@ -757,7 +775,7 @@ __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
 // Host-side planning and launch
 // ---------------------------------------------------------------------------
 struct Plan {
-  int groups, nblk, kr, nks, nchunks, mt;
+  int groups, nblk, kr, nks, nchunks, mt, rg;
   size_t act_smem;  // activations + INT8 chunk sums
 };
 
@@ -802,6 +820,16 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp) {
   while ((size_t)pl.mt * kr * abb > 96 * 1024 && kr > SB) kr = ((kr + 1) / 2 + SB - 1) / SB * SB;
   pl.kr = kr;
   pl.nks = (pl.nblk + kr - 1) / kr;
+  // Row-group pairs (block formats, M = 1, K not split): two groups share
+  // each activation block, which saves about a third of the instructions per
+  // weight; taken when the busiest SM's load goes down (per-SM CTA counts).
+  pl.rg = 1;
+  if (fmt != F_INT8 && fmt != F_Q4_0RAW && pl.mt == 1 && pl.nks == 1 &&
+      tune("SYN_GEMV_ROW_PAIRS", 1)) {
+    const double t1 = (double)((pl.groups + sms - 1) / sms);
+    const double t2 = 2.0 * 0.7 * (double)(((pl.groups + 1) / 2 + sms - 1) / sms);
+    if (t2 < t1) pl.rg = 2;
+  }
   const int ncc = kr / 16 + 1;
   pl.act_smem = (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
   return pl;
@@ -845,10 +873,21 @@ syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   if constexpr (FMT == F_Q4_0RAW) {
     allow_smem(k_qgemv<FMT, MT>);
     e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.act_smem, st, p);
+  } else if constexpr (FMT != F_INT8 && MT == 1) {
+    if (pl.rg == 2) {
+      allow_smem(k_qgemv_tma<FMT, 1, 2>);
+      grid.x = (unsigned)((pl.groups + 1) / 2);
+      const size_t smem = (size_t)Stage<FMT>::NS * 2 * Stage<FMT>::BYTES + pl.act_smem;
+      e = launch_pdl(k_qgemv_tma<FMT, 1, 2>, grid, dim3(THREADS + 32), smem, st, p);
+    } else {
+      allow_smem(k_qgemv_tma<FMT, 1, 1>);
+      const size_t smem = (size_t)Stage<FMT>::NS * Stage<FMT>::BYTES + pl.act_smem;
+      e = launch_pdl(k_qgemv_tma<FMT, 1, 1>, grid, dim3(THREADS + 32), smem, st, p);
+    }
   } else {
-    allow_smem(k_qgemv_tma<FMT, MT>);
+    allow_smem(k_qgemv_tma<FMT, MT, 1>);
     const size_t smem = (size_t)Stage<FMT>::NS * Stage<FMT>::BYTES + pl.act_smem;
-    e = launch_pdl(k_qgemv_tma<FMT, MT>, grid, dim3(THREADS + 32), smem, st, p);
+    e = launch_pdl(k_qgemv_tma<FMT, MT, 1>, grid, dim3(THREADS + 32), smem, st, p);
   }
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_qgemv");
