@@ -243,6 +243,35 @@ def cpu_decode_sample(cfg, w, prompt, budget_s=20.0):
                       f"{n} decode steps, 1 thread"}
 
 
+def run_gemm_case(args):
+    """--gemm FMT:M:N:K: times one prefill matmul (tcgen05 GEMM) on cuda:0 and
+    prints its TFLOP/s (profiling aid; not the benchmark line)."""
+    import torch
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    f, m, n, k = args.gemm.split(":")
+    m, n, k = int(m), int(n), int(k)
+    fmt = sb.QFormat[f]
+    ctx = sb.Context(0)
+    rng = np.random.default_rng(1234)
+    data, scales = synth.gen_weight(fmt, n, k, rng)
+    w = sb.QuantizedWeight(ctx, fmt, data, n, k, scales)
+    x = torch.from_numpy(synth.gen_activations(m, k, rng)).cuda()
+    y = torch.empty(m, n, device="cuda")
+    for _ in range(args.warmup):
+        w.matmul(x, out=y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(args.steps):
+        w.matmul(x, out=y)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    print(json.dumps({"gemm": args.gemm, "us": round(us, 2),
+                      "tflops": round(2 * m * n * k / us / 1e6, 1)}), flush=True)
+
+
 def run_synapse(args, rank, world, local_rank):
     import torch
     import synapse_b200 as sb
@@ -550,6 +579,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the model decode leg")
     ap.add_argument("--case", default=None, help="FMT:N:K -- time one GEMV only (profiling)")
+    ap.add_argument("--gemm", default=None, help="FMT:M:N:K -- time one GEMM only (profiling)")
     args = ap.parse_args()
     global CASE_FILTER
     CASE_FILTER = args.case
@@ -561,7 +591,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.gemm:
+        run_gemm_case(args)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_synapse(args, rank, world, local_rank)

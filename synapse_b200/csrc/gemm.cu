@@ -225,8 +225,8 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
 #pragma unroll
     for (int i = 0; i < 16; i++) {
       const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-      v[2 * i] = __fmul_rn(dd, (float)((int)(byte & 15) - 8));
-      v[2 * i + 1] = __fmul_rn(dd, (float)((int)(byte >> 4) - 8));
+      v[2 * i] = __fmul_rn(dd, i2f_small((int)(byte & 15) - 8));
+      v[2 * i + 1] = __fmul_rn(dd, i2f_small((int)(byte >> 4) - 8));
     }
   } else if constexpr (FMT == F_Q8_0) {
     const uint4 q0 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024)[l];
@@ -235,7 +235,7 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
     const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
     for (int i = 0; i < 32; i++)
-      v[i] = __fmul_rn(dd, (float)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFF));
+      v[i] = __fmul_rn(dd, i2f_small((int)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFF)));
   } else if constexpr (FMT == F_Q4_K) {
     const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
     const uint4 h = reinterpret_cast<const uint4*>(raw + S::G_H)[l];
@@ -258,8 +258,8 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
 #pragma unroll
     for (int i = 0; i < 16; i++) {
       const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-      v[2 * i] = __fsub_rn(__fmul_rn((float)(byte & 15), scl), mv);
-      v[2 * i + 1] = __fsub_rn(__fmul_rn((float)(byte >> 4), scl), mv);
+      v[2 * i] = __fsub_rn(__fmul_rn(i2f_small((int)(byte & 15)), scl), mv);
+      v[2 * i + 1] = __fsub_rn(__fmul_rn(i2f_small((int)(byte >> 4)), scl), mv);
     }
   } else {  // F_Q6_K
     const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
@@ -277,20 +277,20 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
       const int half = e >> 4, r = e & 15, f = 2 * (r >> 3) + (r & 1), tt = (r & 7) >> 1;
       const uint32_t H = half ? hq.y : hq.x;
       const uint32_t hi = (H >> (8 * tt + 2 * f)) & 3u;
-      v[e] = __fmul_rn((float)((int)(lo | (hi << 4)) - 32), half ? s1 : s0);
+      v[e] = __fmul_rn(i2f_small((int)(lo | (hi << 4)) - 32), half ? s1 : s0);
     }
   }
 #pragma unroll
-  for (int c = 0; c < 4; c++) {
+  for (int c = 0; c < 4; c++) {  // paired f32 -> f16 conversions (round to nearest)
     uint4 o;
-    o.x = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 0])) |
-          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 1])) << 16);
-    o.y = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 2])) |
-          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 3])) << 16);
-    o.z = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 4])) |
-          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 5])) << 16);
-    o.w = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 6])) |
-          ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * c + 7])) << 16);
+    const __half2 h0 = __floats2half2_rn(v[8 * c + 0], v[8 * c + 1]);
+    const __half2 h1 = __floats2half2_rn(v[8 * c + 2], v[8 * c + 3]);
+    const __half2 h2 = __floats2half2_rn(v[8 * c + 4], v[8 * c + 5]);
+    const __half2 h3 = __floats2half2_rn(v[8 * c + 6], v[8 * c + 7]);
+    o.x = *reinterpret_cast<const uint32_t*>(&h0);
+    o.y = *reinterpret_cast<const uint32_t*>(&h1);
+    o.z = *reinterpret_cast<const uint32_t*>(&h2);
+    o.w = *reinterpret_cast<const uint32_t*>(&h3);
     reinterpret_cast<uint4*>(out + bl * 8192 + c * 2048)[row] = o;
   }
 }
