@@ -351,14 +351,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
         uint8_t* st = sm + slot * S::STAGE_BYTES;
         uint8_t* raw = st + S::A_BYTES;
-        const uint32_t a_bytes = nbs * cpb * 2048;
+        // A: a short m-tile (few tokens) copies only its valid rows of every
+        // 16-byte K column (the rows beyond are never stored to y)
+        const int rv = (min(BM, p.m - mt * BM) + 7) & ~7;
+        const bool short_a = rv <= 64;
+        const uint32_t a_bytes = short_a ? (uint32_t)(nbs * cpb * rv * 16) : nbs * cpb * 2048;
         uint32_t bytes = a_bytes;
         if constexpr (I8)
           bytes += S::B8_BYTES;  // the full tensor-map box (out of range reads as zero)
         else
           bytes += ngr * (nbs * (S::QT + S::DT + S::QHT + S::SCT) + S::HT + S::D6T);
         mbar_expect_tx(&full[slot], bytes);
-        bulk_g2s(st, p.a + ((size_t)mt * p.kcols + (size_t)b0 * cpb) * 2048, a_bytes, &full[slot]);
+        const uint8_t* asrc = p.a + ((size_t)mt * p.kcols + (size_t)b0 * cpb) * 2048;
+        if (short_a) {
+          for (int c = 0; c < nbs * cpb; c++)
+            bulk_g2s(st + c * 2048, asrc + (size_t)c * 2048, rv * 16, &full[slot]);
+        } else {
+          bulk_g2s(st, asrc, a_bytes, &full[slot]);
+        }
         if constexpr (I8) {
           tma_load_4d(raw, &tmb, 0, 0, nt * NG, 2 * b0, &full[slot]);
         } else {
