@@ -222,6 +222,98 @@ def run_decode(args, local_rank, dist, cpu_leg):
     return out
 
 
+TP_MODEL, TP_FMT, TP_PROMPT, TP_STEPS = "mistral-7b", "Q4_0", 2048, 512
+
+
+def run_tp_decode(args, rank, world, local_rank, dist):
+    """Config 4 (the Mistral-7B shape, Q4_0 weights, random init): a
+    2048-token prefill, then 511 greedy decode steps at batch 1, with the
+    model tensor-parallel over all ranks (Megatron split, NCCL all-reduce
+    after O and down, logits all-gather). Weak in weights per GPU, strong in
+    work: the same model on 1, 2, 4, 8 GPUs."""
+    import torch
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    cfg = synth.lm_config(TP_MODEL)
+    a = cfg["architecture"]
+    ctx = sb.Context(local_rank)
+    if world > 1:
+        obj = [sb.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.tp_init(rank, world, obj[0])
+
+    def gpu_dequant(f, b, n):
+        w = sb.QuantizedWeight(ctx, f, b, a["vocab_size"], a["hidden_size"])
+        out = w.dequant()
+        w.close()
+        return out
+    w = synth.gen_lm_weights(cfg, TP_FMT, seed=1234, dequant=gpu_dequant)
+    m = sb.Model(ctx, cfg, w, TP_PROMPT + TP_STEPS + 8)
+    del w
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, a["vocab_size"], TP_PROMPT).tolist()
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def maxr(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    res = None
+    for _ in range(2):  # the first pass captures the decode graph
+        m.reset()
+        sync_all()
+        t0 = time.perf_counter()
+        m.forward_prefill(prompt, want_logits=False)
+        t1 = time.perf_counter()
+        toks = m.generate(TP_STEPS - 1)
+        t2 = time.perf_counter()
+        res = (maxr(t1 - t0), maxr(t2 - t1), toks)
+    pre_s, dec_s, toks = res
+    n_dec = TP_STEPS - 1
+    # e2e: one public-API call per token (host token in / out)
+    m.reset()
+    tok, _ = m.forward_prefill(prompt, want_logits=False)
+    sync_all()
+    t0 = time.perf_counter()
+    seq = [tok]
+    for _ in range(n_dec):
+        nxt, _ = m.forward_one([seq[-1]], want_logits=False)
+        seq.append(int(nxt[0]))
+    e2e_s = maxr(time.perf_counter() - t0)
+    h, L, ff = a["hidden_size"], a["num_layers"], cfg["ffn"]["intermediate_size"]
+    at = cfg["attention"]
+    qd, kvd = at["num_heads"] * at["head_dim"], at["num_kv_heads"] * at["head_dim"]
+    wbytes = (L * ((qd + 2 * kvd) * h + h * qd + 2 * ff * h + h * ff) + a["vocab_size"] * h) \
+        * 18 // 32
+    ctx_avg = TP_PROMPT + (n_dec + 1) / 2.0
+    kv = L * 2 * kvd * 4 * ctx_avg
+    per_gpu = (wbytes + kv) / world
+    peak, src = peaks()
+    out = {
+        "model": "Mistral-7B shape (32 layers, d 4096, 32/8 heads x 128, ff 14336, vocab 32000, "
+                 "window 4096), random-init Q4_0 blocks",
+        "tp": world, "prompt_tokens": TP_PROMPT, "decode_steps": n_dec, "batch": 1,
+        "prefill_tok_s": round(TP_PROMPT / pre_s, 1),
+        "tok_s": round(n_dec / dec_s, 1), "ms_per_token": round(dec_s / n_dec * 1e3, 4),
+        "e2e_tok_s": round(n_dec / e2e_s, 1),
+        "device_and_e2e_tokens_identical": bool(seq[1:] == toks[0].tolist()),
+        "hbm_bytes_per_token_per_gpu": int(per_gpu),
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu * n_dec / dec_s / 1e9, 1),
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(per_gpu * n_dec / dec_s / 1e9 / peak, 4), "peak_source": src},
+    }
+    m.close()
+    ctx.close()
+    return out
+
+
 def cpu_decode_sample(cfg, w, prompt, budget_s=20.0):
     """The oracle restatement of QuantizedCausalLM (oracle/lm.py) on 1 core:
     the same prompt, then decode steps until ~budget_s."""
@@ -412,9 +504,11 @@ def run_synapse(args, rank, world, local_rank):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample()
     decode = None
+    tp_decode = None
     if not args.no_decode:
         decode = run_decode(args, local_rank, dist,
                             cpu_leg=rank == 0 and world == 1 and not args.no_cpu_baseline)
+        tp_decode = run_tp_decode(args, rank, world, local_rank, dist)
 
     if rank == 0:
         line = {
@@ -441,6 +535,7 @@ def run_synapse(args, rank, world, local_rank):
             "clocks": clk,
             "cpu_baseline": cpu,
             "decode": decode,
+            "tp_decode": tp_decode,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
