@@ -293,51 +293,87 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   extern __shared__ __align__(16) float sm[];
   constexpr int Q4 = HD / 4;
   constexpr int VS = HD + 4;             // staged row stride
+  constexpr int PER = (DEC_CH * Q4 + DEC_THREADS - 1) / DEC_THREADS;  // V float4 per thread
   float* xs = sm;                        // q (HD) then k (HD), then v (HD)
-  float* vb = sm + 3 * HD;               // DEC_CH staged V rows
+  float* cs = xs + 3 * HD;               // RoPE cos (HD/2) then sin (HD/2) at pos
+  float* vb = cs + HD;                   // DEC_CH staged V rows
   float* lanes = vb + DEC_CH * VS;       // 8
   float* scl = lanes + 8;                // 2 (+2 pad)
   float* red = scl + 4;                  // DEC_THREADS / 32
   float* sc = red + DEC_THREADS / 32;    // scores, eff
   const int b = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int G = p.n_heads / p.n_kv, kvh = h / G, kvd = p.n_kv * HD;
-  griddep_wait();
+  // Before griddepcontrol.wait only data written two or more kernels back is
+  // read: the committed length (argmax of the previous step), the cached
+  // rows below it (previous steps' attention) and the RoPE tables. Their
+  // loads overlap the tail of the Q/K/V matmul.
   const int pos = p.len[b];
   if (pos >= p.max_seq) {  // cache full: nothing is written (the host reports it)
+    griddep_wait();
     if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
     return;
   }
+  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
+  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
+  const int L = pos + 1;
+  const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
+  const int eff = L - off;
+  for (int i = tid; i < HD / 2; i += DEC_THREADS) {
+    cs[i] = p.cos_t[(size_t)pos * (HD / 2) + i];
+    cs[HD / 2 + i] = p.sin_t[(size_t)pos * (HD / 2) + i];
+  }
+  float4 kv[Q4];  // K row of position `tid` (first pass of the score loop)
+  const bool kpre = tid < eff && off + tid != pos;
+  if (kpre) {
+#pragma unroll
+    for (int c = 0; c < Q4; c++)
+      kv[c] = reinterpret_cast<const float4*>(kcb + (size_t)(off + tid) * kvd)[c];
+  }
+  const int cn0 = min(DEC_CH, eff);
+  {  // first V chunk (the new position is filled in after its RoPE/append)
+    float4 tmp[PER];
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
+      if (r < cn0 && off + r != pos)
+        tmp[u] = reinterpret_cast<const float4*>(vcb + (size_t)(off + r) * kvd)[c4];
+    }
+#pragma unroll
+    for (int u = 0; u < PER; u++) {
+      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
+      if (r < cn0 && off + r != pos) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
+    }
+  }
+  griddep_wait();
   const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
   const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
   const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
-  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
-  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
   for (int i = tid; i < HD; i += DEC_THREADS) {
     xs[i] = qrow[i];
     xs[HD + i] = krow[i];
     xs[2 * HD + i] = vrow[i];
   }
   __syncthreads();
-  norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, DEC_THREADS);
+  norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, cs, cs + HD / 2, 0, lanes, scl, DEC_THREADS);
   if (h % G == 0)
     for (int i = tid; i < HD; i += DEC_THREADS) {
       kcb[(size_t)pos * kvd + i] = xs[HD + i];
       vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
     }
+  if (pos - off < cn0)  // the new V row in the first chunk
+    for (int i = tid; i < HD; i += DEC_THREADS) vb[(pos - off) * VS + i] = xs[2 * HD + i];
 
-  const int L = pos + 1;
-  const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
-  const int eff = L - off;
   // scores: below 64 positions the reference's scalar loop (sum += a*b);
   // from 64 on matmul_t (@mulAdd except the last eff%8 columns). Each thread
   // holds one K row in registers (all loads in flight at once).
   const int s_full = eff < 64 ? 0 : eff - (eff & 7);
   for (int s = tid; s < eff; s += DEC_THREADS) {
     const int row = off + s;
-    const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
-    float4 kv[Q4];
+    if (!(s == tid && kpre)) {
+      const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
 #pragma unroll
-    for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
+      for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
+    }
     const bool fused = s < s_full;
     float acc = 0.0f;
 #pragma unroll
@@ -364,29 +400,31 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
     for (int s = tid; s < eff; s += DEC_THREADS) sc[s] = __fdiv_rn(sc[s], sum);
   griddep_launch();
   // score * V: below 64 positions sum += p*v; from 64 on matmul_nn
-  // (@mulAdd except the last hd%32 columns). V rows staged DEC_CH at a time.
+  // (@mulAdd except the last hd%32 columns). V rows staged DEC_CH at a time
+  // (the first chunk was staged before the wait).
   const bool vfused = eff >= 64 && tid < HD - (HD & 31);
   float acc = 0.0f;
-  constexpr int PER = (DEC_CH * Q4 + DEC_THREADS - 1) / DEC_THREADS;  // float4 per thread
   for (int c0 = 0; c0 < eff; c0 += DEC_CH) {
     const int cn = min(DEC_CH, eff - c0);
     __syncthreads();  // previous chunk consumed (and sc final on the first pass)
-    float4 tmp[PER];
+    if (c0 > 0) {
+      float4 tmp[PER];
 #pragma unroll
-    for (int u = 0; u < PER; u++) {
-      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < cn) {
-        const int row = off + c0 + r;
-        tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
-                            : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+      for (int u = 0; u < PER; u++) {
+        const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
+        if (r < cn) {
+          const int row = off + c0 + r;
+          tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
+                              : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+        }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < PER; u++) {
-      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < cn) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
+      for (int u = 0; u < PER; u++) {
+        const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
+        if (r < cn) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
+      }
+      __syncthreads();
     }
-    __syncthreads();
     if (tid < HD) {
       const float* pr = sc + c0;
       int s = 0;
@@ -407,7 +445,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
 }
 
 size_t decode_smem_floats(int hd, int eff) {
-  return (size_t)3 * hd + (size_t)DEC_CH * (hd + 4) + 8 + 4 + DEC_THREADS / 32 + eff;
+  return (size_t)4 * hd + (size_t)DEC_CH * (hd + 4) + 8 + 4 + DEC_THREADS / 32 + eff;
 }
 
 // ---------------------------------------------------------------------------
