@@ -174,7 +174,7 @@ struct GS {
   static constexpr int G_BYTES = I8 ? 0 : (G_D6 + D6T + 127) / 128 * 128;  // per row group
   static constexpr int RAW_BYTES = I8 ? B8_BYTES : NG * G_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + RAW_BYTES;
-  static constexpr int NS = I8 ? 3 : 2;                        // ring depth
+  static constexpr int NS = 3;                                 // ring depth
   // block formats: dequantised fp16 B = [block][4 K columns][128 rows][16 B]
   static constexpr int BH_BYTES = I8 ? 0 : BN * KB * 32 * 2;   // 32 KB
   static constexpr int NBH = I8 ? 0 : 2;
@@ -217,6 +217,52 @@ template <int FMT>
 __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, int l, int row,
                                               int bl, int b) {
   using S = GS<FMT>;
+  if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0) {
+    // fp16 arithmetic, same values: (q - 8) and q are exact in fp16, d is an
+    // fp16 value, and the product of two fp16 values rounded once to fp16
+    // equals the reference's exact f32 product (gguf.rs:276-285, 318-324)
+    // rounded to fp16. The loader's subnormal quirk (a halved scale) is kept
+    // by halving q first, which is exact. Codes become fp16 with the
+    // 0x6400 (1024.0) mantissa trick: no int-to-float conversions.
+    const uint16_t dbits = reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l];
+    const __half2 d2 = __half2half2(__ushort_as_half(dbits));
+    const bool sub = (dbits & 0x7C00u) == 0;
+    const __half2 half2_05 = __float2half2_rn(0.5f);
+    uint32_t o[16];
+    if constexpr (FMT == F_Q4_0) {
+      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      const __half2 bias = __float2half2_rn(1032.0f);  // 1024 + 8
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+        const uint32_t pr = (byte & 0x0Fu) | ((byte & 0xF0u) << 12) | 0x64006400u;
+        __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&pr), bias);  // (lo-8, hi-8)
+        if (sub) h = __hmul2(h, half2_05);
+        h = __hmul2(h, d2);
+        o[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    } else {
+      const uint4 q0 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024)[l];
+      const uint4 q1 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024 + 512)[l];
+      const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const uint32_t two = (w[i >> 1] >> (16 * (i & 1))) & 0xFFFFu;  // codes 2i, 2i+1
+        const uint32_t pr = (((two & 0xFFu) ^ 0x80u) | (((two >> 8) ^ 0x80u) << 16)) | 0x64006400u;
+        __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&pr), bias);
+        if (sub) h = __hmul2(h, half2_05);
+        h = __hmul2(h, d2);
+        o[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      reinterpret_cast<uint4*>(out + bl * 8192 + c * 2048)[row] =
+          make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+    return;
+  }
   float v[32];
   if constexpr (FMT == F_Q4_0) {
     const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
