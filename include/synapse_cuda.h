@@ -184,6 +184,18 @@ syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t *ctx,
                                             const float *scales_x, size_t m,
                                             float *y, void *stream);
 
+/* One decode row through RMSNorm and a matmul in one launch:
+ * x = rmsnorm(residual (+ delta), norm_weight) (ops/norm.rs:8-37, same
+ * arithmetic as syn_cuda_add_rmsnorm; parallel_sum != 0 sums the squares in a
+ * parallel order instead of vecHsum's), then y[1,N] = x * W^T as
+ * syn_cuda_qmatmul. residual_out (optional, must not alias residual)
+ * receives residual + delta. delta may be NULL. M = 1. */
+syn_status_t syn_cuda_qmatmul_rmsnorm(syn_cuda_ctx_t *ctx, const syn_cuda_weight_t *w,
+                                      const float *residual, const float *delta,
+                                      const float *norm_weight, float eps,
+                                      float *residual_out, int parallel_sum, float *y,
+                                      void *stream);
+
 /* Allocation-free variant of syn_cuda_qmatmul. It has no counterpart in the
  * reference: it is for callers that must not allocate device memory while
  * they run (latency-critical decode loops, processes whose device memory is

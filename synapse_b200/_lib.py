@@ -35,6 +35,8 @@ SIGNATURES = {
     "syn_cuda_qmatmul": (c_st, [c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
     "syn_cuda_qmatmul_int8_prequant": (c_st, [c_vp, c_vp, c_vp, c_vp, c_size, c_vp, c_vp]),
     "syn_cuda_qmatmul_noalloc": (c_st, [c_vp, c_vp, c_size, c_vp, c_vp]),
+    "syn_cuda_qmatmul_rmsnorm": (c_st, [c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.c_float, c_vp,
+                                        ctypes.c_int, c_vp, c_vp]),
     "syn_cuda_rope_tables": (c_st, [ctypes.c_double, c_size, c_size, c_vp, c_vp]),
     "syn_cuda_rmsnorm": (c_st, [c_vp, c_vp, c_size, c_size, ctypes.c_float, c_vp, c_vp]),
     "syn_cuda_add_rmsnorm": (c_st, [c_vp, c_vp, c_vp, c_size, c_size, ctypes.c_float, c_vp,

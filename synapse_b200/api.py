@@ -272,6 +272,19 @@ class QuantizedWeight:
                                       _stream(x)), "qmatmul")
         return out
 
+    def matmul_rmsnorm(self, residual, norm_weight, eps, delta=None, residual_out=None,
+                       parallel_sum=False, out=None):
+        """y [1, n] = rmsnorm(residual (+ delta)) @ W^T in one launch
+        (syn_cuda_qmatmul_rmsnorm); residual_out receives residual + delta."""
+        _need_cuda(residual, norm_weight)
+        if out is None:
+            out = torch.empty(1, self.n, dtype=torch.float32, device=residual.device)
+        _check(lib().syn_cuda_qmatmul_rmsnorm(
+            self.ctx.handle, self.handle, _ptr(residual), _ptr(delta), _ptr(norm_weight),
+            float(eps), _ptr(residual_out), 1 if parallel_sum else 0, _ptr(out),
+            _stream(residual)), "qmatmul_rmsnorm")
+        return out
+
     def matmul_pre_quantized(self, x_int8, scales_x, m, out=None):
         _need_cuda(x_int8, scales_x)
         if out is None:

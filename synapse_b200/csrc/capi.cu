@@ -118,6 +118,8 @@ syn_status_t grow(void** buf, size_t* cap, size_t bytes, cudaStream_t st) {
   return SYN_OK;
 }
 
+}  // namespace
+
 syn_status_t ensure_scratch(syn_cuda_ctx_s* ctx, const syn_cuda_weight_s* w, size_t m,
                             cudaStream_t st) {
   syn_status_t s = grow(reinterpret_cast<void**>(&ctx->part), &ctx->part_bytes,
@@ -126,6 +128,8 @@ syn_status_t ensure_scratch(syn_cuda_ctx_s* ctx, const syn_cuda_weight_s* w, siz
   return grow(reinterpret_cast<void**>(&ctx->cnt), &ctx->cnt_bytes, gemv_counter_bytes(m, w->n),
               st);
 }
+
+namespace {
 
 // Stream-ordered scratch for the context-free entry points: `extra` leading
 // bytes for the caller, then partials and zeroed counters; freed after the
@@ -445,6 +449,21 @@ syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t* ctx, const syn_cuda_
   if (s != SYN_OK) return s;
   return launch_qgemv(w, nullptr, w->k, x_i8, scales_x, m, y, w->n, m > 16 ? 1 : 0, ctx->part,
                       ctx->cnt, ctx->err, st);
+}
+
+syn_status_t syn_cuda_qmatmul_rmsnorm(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w,
+                                      const float* residual, const float* delta,
+                                      const float* norm_weight, float eps, float* residual_out,
+                                      int parallel_sum, float* y, void* stream) {
+  if (!ctx || !w || !residual || !norm_weight || !y) return SYN_ERR_NULL_PTR;
+  if (residual_out && residual_out == residual) return SYN_ERR_INVALID_ARG;
+  DeviceGuard g(w->device);
+  if (!g.ok) return SYN_ERR_CUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  syn_status_t s = ensure_scratch(ctx, w, 1, st);
+  if (s != SYN_OK) return s;
+  GemvNorm nm{residual, delta, norm_weight, eps, residual_out, parallel_sum ? 1 : 0};
+  return launch_qgemv_norm(w, nm, y, ctx->part, ctx->cnt, ctx->err, st);
 }
 
 }  // extern "C"

@@ -110,6 +110,15 @@ struct GemvParams {
   float* part;  // [m][nks or nchunks][groups*32]
   int* cnt;     // [m slices][groups]
   int* err;
+  // optional fused prologue (M = 1): x = RMSNorm(nres (+ ndelta)) with weight
+  // nw; the CTA at the grid origin stores nres + ndelta into nres_out
+  const float* nres;
+  const float* ndelta;
+  const float* nw;
+  float neps;
+  float* nres_out;
+  int nfast;  // 1: parallel sum of squares; 0: the reference's vecHsum order
+  int xs_off; // byte offset of the normalised row in dynamic shared memory
 };
 
 __device__ __forceinline__ void consumer_sync() {
@@ -435,6 +444,49 @@ __device__ void cta_prologue(const GemvParams& p, int m0, int cb0, int cb1, uint
   const int act_stride = p.kr * act_block_bytes(FMT);
   if constexpr (FMT == F_INT8) {
     for (int i = threadIdx.x; i < MT * ncc * 32; i += THREADS) csum[i] = 0;
+    constexpr int XR = 16;  // x values per thread held in registers
+    const int k0 = cb0 * 32, k1 = min(cb1 * 32, p.kp);
+    if (MT == 1 && !p.xq && m0 < p.m && k1 - k0 <= XR * THREADS) {
+      // one pass over x: the row max spans all of K (quantize.zig:12-47), so
+      // this CTA's elements are kept in registers while it is reduced
+      const float* xr = p.x + (long long)m0 * p.ldx;
+      float xv[XR];
+      float amax = 0.0f;
+#pragma unroll
+      for (int u = 0; u < XR; u++) {
+        const int kk = k0 + threadIdx.x + u * THREADS;
+        xv[u] = kk < k1 && kk < p.k ? xr[kk] : 0.0f;
+        amax = fmaxf(amax, fabsf(xv[u]));
+      }
+      const bool whole = k0 == 0 && k1 >= p.k;
+      if (!whole)  // the max also spans the elements outside this CTA's range
+        for (int i = threadIdx.x; i < p.k; i += THREADS)
+          if (i < k0 || i >= k1) amax = fmaxf(amax, fabsf(xr[i]));
+      amax = warp_max(amax);
+      if (lane == 0) sh.red[warp][0][0] = amax;
+      consumer_sync();
+      float a = sh.red[0][0][0];
+#pragma unroll
+      for (int i = 1; i < WARPS; i++) a = fmaxf(a, sh.red[i][0][0]);
+      if (threadIdx.x == 0) sh.srow[0] = (a == 0.0f) ? 1.0f : __fdiv_rn(a, 127.0f);
+      const float inv = (a == 0.0f) ? 0.0f : __fdiv_rn(127.0f, a);
+      int8_t* codes = reinterpret_cast<int8_t*>(act) - k0;
+#pragma unroll
+      for (int u = 0; u < XR; u++) {
+        const int kk = k0 + threadIdx.x + u * THREADS;
+        if (kk < k1) {
+          int8_t v = 0;
+          if (a != 0.0f && kk < p.k) {
+            float r = roundf(__fmul_rn(xv[u], inv));
+            r = fminf(127.0f, fmaxf(-127.0f, r));
+            v = (int8_t)(int)r;
+          }
+          codes[kk] = v;
+        }
+      }
+      consumer_sync();
+      return;
+    }
     for (int mm = 0; mm < MT; mm++) {
       const int m = m0 + mm;
       if (m >= p.m) continue;  // uniform across the CTA
@@ -480,7 +532,8 @@ __device__ void cta_prologue(const GemvParams& p, int m0, int cb0, int cb1, uint
 // final sum by the last CTA of the row group. Consumer threads only.
 template <int FMT, int MT>
 __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, int ncc,
-                           const int* csum, CtaShared<MT>& sh) {
+                           const int* csum, CtaShared<MT>& sh, float sb_pre = 0.0f,
+                           bool have_sb = false) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = g * 32 + lane;
   const bool split = p.nks > 1;
@@ -492,7 +545,7 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
       if constexpr (FMT == F_INT8) {
         if (!split) {
           if (row < p.n) {
-            const float sa = sh.srow[mm], sbv = p.sb[row];
+            const float sa = sh.srow[mm], sbv = have_sb ? sb_pre : p.sb[row];
             float out = 0.0f;
             if (p.chunked) {
               for (int c = 0; c < ncc; c++)
@@ -542,7 +595,7 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
       float out = 0.0f;
       if constexpr (FMT == F_INT8) {
         const float* src = p.part + (long long)m * p.nchunks * G32;
-        const float sa = sh.srow[mm], sbv = p.sb[row];
+        const float sa = sh.srow[mm], sbv = have_sb ? sb_pre : p.sb[row];
         if (p.chunked) {
           for (int c = 0; c < p.nchunks; c++) {
             const int cv = __float_as_int(__ldcg(src + c * G32 + row));
@@ -560,6 +613,84 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
       p.y[(long long)m * p.ldy + row] = out;
     }
   }
+}
+
+// Fused RMSNorm prologue (consumer threads): xs[0, k) = (v * w) * scale with
+// v = nres (+ ndelta) and scale = 1 / sqrt(sum(v*v)/k + eps), the sum in the
+// reference's vecHsum order (four lanes of stride 4, lanes in order, tail)
+// or, with nfast, in a parallel order. Same arithmetic as k_add_rmsnorm.
+constexpr int NW_PRE = 16;  // norm weights per thread held in registers (k <= 4096)
+
+template <int MT>
+__device__ void norm_prologue(const GemvParams& p, float* xs, CtaShared<MT>& sh,
+                              const float (&nwp)[NW_PRE]) {
+  const int tid = threadIdx.x, k = p.k;
+  const bool origin = blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+  for (int j0 = 0; j0 < k; j0 += THREADS * 4) {
+    float v[4], dl[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int j = j0 + tid + u * THREADS;
+      v[u] = j < k ? p.nres[j] : 0.0f;
+      dl[u] = (j < k && p.ndelta) ? p.ndelta[j] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int j = j0 + tid + u * THREADS;
+      if (j < k) {
+        const float x = p.ndelta ? __fadd_rn(v[u], dl[u]) : v[u];
+        xs[j] = x;
+        if (origin && p.nres_out) p.nres_out[j] = x;
+      }
+    }
+  }
+  consumer_sync();
+  float* lanes = &sh.red[0][0][0];
+  if (p.nfast) {
+    float a = 0.0f;
+    for (int j = tid; j < k; j += THREADS) a = fmaf(xs[j], xs[j], a);
+    a = warp_sum(a);
+    if ((tid & 31) == 0) lanes[8 + (tid >> 5)] = a;
+    consumer_sync();
+    if (tid == 0) {
+      float t = 0.0f;
+      for (int w = 0; w < WARPS; w++) t += lanes[8 + w];
+      lanes[16] = 1.0f / sqrtf(t / (float)k + p.neps);
+    }
+  } else {
+    if (tid < 4) {
+      const int n4 = k & ~3;
+      float acc = 0.0f;
+      int i = tid;
+      for (; i + 60 < n4; i += 64) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) v[u] = xs[i + 4 * u];
+#pragma unroll
+        for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, __fmul_rn(v[u], v[u]));
+      }
+      for (; i < n4; i += 4) acc = __fadd_rn(acc, __fmul_rn(xs[i], xs[i]));
+      lanes[tid] = acc;
+    }
+    consumer_sync();
+    if (tid == 0) {
+      float t = __fadd_rn(__fadd_rn(__fadd_rn(lanes[0], lanes[1]), lanes[2]), lanes[3]);
+      for (int i = k & ~3; i < k; i++) t = __fadd_rn(t, __fmul_rn(xs[i], xs[i]));
+      lanes[16] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), p.neps)));
+    }
+  }
+  consumer_sync();
+  const float scale = lanes[16];
+  if (k <= NW_PRE * THREADS) {
+#pragma unroll
+    for (int u = 0; u < NW_PRE; u++) {
+      const int j = tid + u * THREADS;
+      if (j < k) xs[j] = __fmul_rn(__fmul_rn(xs[j], nwp[u]), scale);
+    }
+  } else {
+    for (int j = tid; j < k; j += THREADS) xs[j] = __fmul_rn(__fmul_rn(xs[j], p.nw[j]), scale);
+  }
+  consumer_sync();
 }
 
 // ---------------------------------------------------------------------------
@@ -633,9 +764,35 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
   }
 
   // ---- consumers ----
+  // Constants of the weight (per-row INT8 scales, the fused norm's weights)
+  // are read before griddepcontrol.wait: they do not depend on the
+  // preceding kernel, so their latency overlaps it.
+  float sb_pre[RG];
+#pragma unroll
+  for (int r = 0; r < RG; r++) {
+    const int row = (g + r) * 32 + lane;
+    sb_pre[r] = (FMT == F_INT8 && r < ng && row < p.n) ? p.sb[row] : 0.0f;
+  }
+  float nwp[NW_PRE];
+  if (p.nw && p.k <= NW_PRE * THREADS) {
+#pragma unroll
+    for (int u = 0; u < NW_PRE; u++) {
+      const int j = threadIdx.x + u * THREADS;
+      nwp[u] = j < p.k ? p.nw[j] : 0.0f;
+    }
+  }
   griddep_wait();  // x may be written by the preceding kernel
   griddep_launch();
-  cta_prologue<FMT, MT>(p, m0, cb0, cb1, act, csum, ncc, sh);
+  if (p.nw) {  // fused RMSNorm (M = 1): the normalised row becomes x
+    float* xs = reinterpret_cast<float*>(sm + p.xs_off);
+    norm_prologue<MT>(p, xs, sh, nwp);
+    GemvParams q = p;
+    q.x = xs;
+    q.ldx = 0;
+    cta_prologue<FMT, MT>(q, m0, cb0, cb1, act, csum, ncc, sh);
+  } else {
+    cta_prologue<FMT, MT>(p, m0, cb0, cb1, act, csum, ncc, sh);
+  }
 
   float facc[MT][RG];
 #pragma unroll
@@ -689,7 +846,7 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
 #pragma unroll
       for (int mm = 0; mm < MT; mm++) sh.red[warp][mm][lane] = facc[mm][r];
     }
-    cta_finish<FMT, MT>(p, g + r, ks, m0, cc0, ncc, csum, sh);
+    cta_finish<FMT, MT>(p, g + r, ks, m0, cc0, ncc, csum, sh, sb_pre[r], FMT == F_INT8);
   }
 }
 
@@ -776,6 +933,7 @@ __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
 // ---------------------------------------------------------------------------
 struct Plan {
   int groups, nblk, kr, nks, nchunks, mt, rg;
+  size_t xs_bytes;  // fused-norm row in shared memory (0 = none)
   size_t act_smem;  // activations + INT8 chunk sums
 };
 
@@ -874,20 +1032,25 @@ syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
     allow_smem(k_qgemv<FMT, MT>);
     e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.act_smem, st, p);
   } else if constexpr (FMT != F_INT8 && MT == 1) {
+    GemvParams q = p;
+    const size_t ring = (size_t)Stage<FMT>::NS * pl.rg * Stage<FMT>::BYTES;
+    q.xs_off = (int)((ring + pl.act_smem + 15) & ~size_t(15));
+    const size_t smem = pl.xs_bytes ? q.xs_off + pl.xs_bytes : ring + pl.act_smem;
     if (pl.rg == 2) {
       allow_smem(k_qgemv_tma<FMT, 1, 2>);
       grid.x = (unsigned)((pl.groups + 1) / 2);
-      const size_t smem = (size_t)Stage<FMT>::NS * 2 * Stage<FMT>::BYTES + pl.act_smem;
-      e = launch_pdl(k_qgemv_tma<FMT, 1, 2>, grid, dim3(THREADS + 32), smem, st, p);
+      e = launch_pdl(k_qgemv_tma<FMT, 1, 2>, grid, dim3(THREADS + 32), smem, st, q);
     } else {
       allow_smem(k_qgemv_tma<FMT, 1, 1>);
-      const size_t smem = (size_t)Stage<FMT>::NS * Stage<FMT>::BYTES + pl.act_smem;
-      e = launch_pdl(k_qgemv_tma<FMT, 1, 1>, grid, dim3(THREADS + 32), smem, st, p);
+      e = launch_pdl(k_qgemv_tma<FMT, 1, 1>, grid, dim3(THREADS + 32), smem, st, q);
     }
   } else {
     allow_smem(k_qgemv_tma<FMT, MT, 1>);
-    const size_t smem = (size_t)Stage<FMT>::NS * Stage<FMT>::BYTES + pl.act_smem;
-    e = launch_pdl(k_qgemv_tma<FMT, MT, 1>, grid, dim3(THREADS + 32), smem, st, p);
+    const size_t ring = (size_t)Stage<FMT>::NS * Stage<FMT>::BYTES;
+    GemvParams q = p;
+    q.xs_off = (int)((ring + pl.act_smem + 15) & ~size_t(15));
+    const size_t smem = pl.xs_bytes ? q.xs_off + pl.xs_bytes : ring + pl.act_smem;
+    e = launch_pdl(k_qgemv_tma<FMT, MT, 1>, grid, dim3(THREADS + 32), smem, st, q);
   }
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_qgemv");
@@ -967,6 +1130,39 @@ syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx
   p.y = y;
   p.ldy = (long long)ldy;
   p.chunked = chunked;
+  fill_common(p, pl, part, cnt, err);
+  if (pl.nks > 1 && (!part || !cnt)) return SYN_ERR_INTERNAL;
+  return run_gemv(fk, p, pl, st);
+}
+
+syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, float* y,
+                               float* part, int* cnt, int* err, cudaStream_t st) {
+  if (w->n > 0x7FFFFFFFull || w->kp > 0x3FFFFFFFull) return SYN_ERR_UNSUPPORTED;
+  if (w->k > 16384) return SYN_ERR_UNSUPPORTED;  // the row is staged in shared memory
+  const int fk = w->fmt == SYN_QFMT_INT8_KN ? F_INT8 : w->fmt;
+  Plan pl = make_plan(fk, 1, w->n, w->kp);
+  pl.xs_bytes = w->k * sizeof(float);
+  GemvParams p{};
+  p.q = w->q;
+  p.d = w->d;
+  p.sb = w->sb;
+  p.hdr = w->hdr;
+  p.qh = w->qh;
+  p.sc = reinterpret_cast<const uint16_t*>(w->sc);
+  p.x = nullptr;  // replaced by the normalised row in shared memory
+  p.n = (int)w->n;
+  p.k = (int)w->k;
+  p.kp = (int)w->kp;
+  p.nsb = (int)(w->k / 256);
+  p.m = 1;
+  p.y = y;
+  p.ldy = (long long)w->n;
+  p.nres = nm.res;
+  p.ndelta = nm.delta;
+  p.nw = nm.w;
+  p.neps = nm.eps;
+  p.nres_out = nm.res_out;
+  p.nfast = nm.fast;
   fill_common(p, pl, part, cnt, err);
   if (pl.nks > 1 && (!part || !cnt)) return SYN_ERR_INTERNAL;
   return run_gemv(fk, p, pl, st);

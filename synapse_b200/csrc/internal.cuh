@@ -96,6 +96,24 @@ syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx
                           const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
                           int chunked, float* part, int* cnt, int* err, cudaStream_t st);
 
+// The GEMV for one activation row x = RMSNorm(res (+ delta)) * w, fused into
+// its prologue (same arithmetic as launch_add_rmsnorm; fast = parallel sum of
+// squares). The grid's first CTA stores res + delta into res_out, which must
+// not alias res. Scratch as launch_qgemv with m = 1.
+struct GemvNorm {
+  const float* res;
+  const float* delta;  // or nullptr
+  const float* w;
+  float eps;
+  float* res_out;      // or nullptr
+  int fast;
+};
+syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, float* y,
+                               float* part, int* cnt, int* err, cudaStream_t st);
+// Grows the context's GEMV scratch for m rows of w (refused during capture).
+syn_status_t ensure_scratch(syn_cuda_ctx_s* ctx, const syn_cuda_weight_s* w, size_t m,
+                            cudaStream_t st);
+
 // Tensor-core GEMM (gemm.cu) for m >= kGemmMinRows activation rows. abuf:
 // scratch of gemm_a_bytes(fmt, m, kp) bytes for the prepared activations.
 constexpr size_t kGemmMinRows = 8;

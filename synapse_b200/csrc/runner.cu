@@ -210,6 +210,8 @@ struct syn_cuda_model_s {
   int32_t* hist = nullptr;  // [max_batch][max_seq + 1] generated token per position
   void* am_scratch = nullptr;
   float* logits_l = nullptr;  // this rank's vocabulary slice of the logits (tp > 1)
+  float* resid2 = nullptr;     // second residual buffer (fused single-row steps)
+  bool no_fuse = false;        // SYN_RUNNER_FUSE=0 keeps the norms as separate kernels
   float *resid = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *o = nullptr,
         *gu = nullptr, *hid = nullptr, *dn = nullptr, *logits = nullptr;
   // pinned host staging
@@ -304,17 +306,31 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   // INT8 models keep the reference's reduction order (bit-exact tokens)
   a.flash = m->int8 ? 0 : 1;
   const bool tp = m->tp > 1;
+  // One row (decode at batch 1): each RMSNorm runs in the prologue of the
+  // matmul it feeds, with the residual stream ping-ponging between two
+  // buffers (a kernel never rewrites the residual it reads).
+  const bool fuse = rows == 1 && !m->no_fuse;
+  float* cur = m->resid;
+  auto other = [&](float* r) { return r == m->resid ? m->resid2 : m->resid; };
   for (size_t li = 0; li < m->L; li++) {
     LayerDev& ly = m->layers[li];
-    if (li == 0)
-      s = launch_add_rmsnorm(nullptr, 0, nullptr, 0, chained ? m->tok : m->ids, m->embed, m->V,
-                             m->resid, h,
-                             ly.attn_norm, rows, h, m->eps, m->x, h, st, a.flash);
-    else
-      s = launch_add_rmsnorm(m->resid, h, m->dn, h, nullptr, nullptr, 0, m->resid, h,
-                             ly.attn_norm, rows, h, m->eps, m->x, h, st, a.flash);
-    if (s) return s;
-    if ((s = mm(m, ly.qkv, m->x, rows, m->qkv))) return s;
+    if (fuse && li > 0) {
+      float* nxt = other(cur);
+      GemvNorm nm{cur, m->dn, ly.attn_norm, m->eps, nxt, a.flash};
+      if ((s = ensure_scratch(m->ctx, ly.qkv, 1, st))) return s;
+      s = launch_qgemv_norm(ly.qkv, nm, m->qkv, m->ctx->part, m->ctx->cnt, m->ctx->err, st);
+      if (s) return s;
+      cur = nxt;
+    } else {
+      if (li == 0)
+        s = launch_add_rmsnorm(nullptr, 0, nullptr, 0, chained ? m->tok : m->ids, m->embed, m->V,
+                               cur, h, ly.attn_norm, rows, h, m->eps, m->x, h, st, a.flash);
+      else
+        s = launch_add_rmsnorm(cur, h, m->dn, h, nullptr, nullptr, 0, cur, h, ly.attn_norm, rows,
+                               h, m->eps, m->x, h, st, a.flash);
+      if (s) return s;
+      if ((s = mm(m, ly.qkv, m->x, rows, m->qkv))) return s;
+    }
     a.q = m->qkv;
     a.k = m->qkv + m->qd_l;
     a.v = m->qkv + m->qd_l + m->kvd_l;
@@ -327,10 +343,19 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
     if (s) return s;
     if ((s = mm(m, ly.o, m->att, rows, m->o))) return s;
     if (tp && (s = tp_allreduce_sum(m->ctx, m->o, rows * h, st))) return s;  // row-parallel O
-    s = launch_add_rmsnorm(m->resid, h, m->o, h, nullptr, nullptr, 0, m->resid, h, ly.ffn_norm,
-                           rows, h, m->eps, m->x, h, st, a.flash);
-    if (s) return s;
-    if ((s = mm(m, ly.gu, m->x, rows, m->gu))) return s;
+    if (fuse) {
+      float* nxt = other(cur);
+      GemvNorm nm{cur, m->o, ly.ffn_norm, m->eps, nxt, a.flash};
+      if ((s = ensure_scratch(m->ctx, ly.gu, 1, st))) return s;
+      s = launch_qgemv_norm(ly.gu, nm, m->gu, m->ctx->part, m->ctx->cnt, m->ctx->err, st);
+      if (s) return s;
+      cur = nxt;
+    } else {
+      s = launch_add_rmsnorm(cur, h, m->o, h, nullptr, nullptr, 0, cur, h, ly.ffn_norm, rows, h,
+                             m->eps, m->x, h, st, a.flash);
+      if (s) return s;
+      if ((s = mm(m, ly.gu, m->x, rows, m->gu))) return s;
+    }
     s = launch_swiglu(m->gu, m->gu + m->ff_l, 2 * m->ff_l, rows, m->ff_l, variant, m->hid,
                       m->ff_l, st);
     if (s) return s;
@@ -339,17 +364,22 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   }
   // final norm and LM head: prefill keeps only the last token (int8.rs:619-627)
   const size_t r0 = prefill ? rows - 1 : 0, nr = prefill ? 1 : rows;
-  s = launch_add_rmsnorm(m->resid + r0 * h, h, m->dn + r0 * h, h, nullptr, nullptr, 0,
-                         m->resid + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st,
-                         a.flash);
-  if (s) return s;
+  float* logits_dst = tp ? m->logits_l : m->logits;
+  if (fuse) {
+    GemvNorm nm{cur, m->dn, m->final_norm, m->eps, nullptr, a.flash};
+    if ((s = ensure_scratch(m->ctx, m->lm_head, 1, st))) return s;
+    s = launch_qgemv_norm(m->lm_head, nm, logits_dst, m->ctx->part, m->ctx->cnt, m->ctx->err, st);
+    if (s) return s;
+  } else {
+    s = launch_add_rmsnorm(cur + r0 * h, h, m->dn + r0 * h, h, nullptr, nullptr, 0,
+                           cur + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st, a.flash);
+    if (s) return s;
+    if ((s = mm(m, m->lm_head, m->x, nr, logits_dst))) return s;
+  }
   if (tp) {  // vocab-parallel LM head: gather each row's logits in rank (= vocab) order
-    if ((s = mm(m, m->lm_head, m->x, nr, m->logits_l))) return s;
     for (size_t b = 0; b < nr; b++)
       if ((s = tp_allgather(m->ctx, m->logits_l + b * m->v_l, m->logits + b * m->V, m->v_l, st)))
         return s;
-  } else if ((s = mm(m, m->lm_head, m->x, nr, m->logits))) {
-    return s;
   }
   // the generated token of sequence b lands in tok[b] (prefill: tok[seq])
   s = launch_argmax(m->logits, m->V, nr, m->V, m->tok + (prefill ? seq : 0),
@@ -551,7 +581,12 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   if ((s = dev_alloc_t(m, &m->tok, m->max_batch))) return s;
   if ((s = dev_alloc_t(m, &m->hist, m->max_batch * (m->max_seq + 1)))) return s;
   if ((s = dev_alloc_t(m, &m->resid, R * h))) return s;
+  if ((s = dev_alloc_t(m, &m->resid2, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->x, R * h))) return s;
+  {
+    const char* e = getenv("SYN_RUNNER_FUSE");
+    m->no_fuse = e && e[0] == '0';
+  }
   if ((s = dev_alloc_t(m, &m->qkv, R * m->qkv_n))) return s;
   if ((s = dev_alloc_t(m, &m->att, R * m->qd_l))) return s;
   if ((s = dev_alloc_t(m, &m->o, R * h))) return s;

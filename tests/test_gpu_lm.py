@@ -312,3 +312,31 @@ def test_qwen3_0p6b_int8_greedy_64_tokens_identical(ctx):
     m.close()
     ref, margins = OracleLM(cfg, w, 128).generate_greedy(prompt, 64)
     assert got == ref, (got, ref, margins)
+
+
+@pytest.mark.parametrize("fmt", ["INT8_KN", "Q4_0", "Q6_K"])
+@pytest.mark.parametrize("fast", [False, True])
+def test_qmatmul_rmsnorm_fused_equals_separate(ctx, fmt, fast):
+    """The fused RMSNorm + GEMV gives the bits of rmsnorm then matmul (and the
+    residual sum); with fast=False the norm is the reference-order one."""
+    rng = np.random.default_rng(7)
+    n, k = 640, 1024
+    f = sb.QFormat[fmt]
+    data, scales = synth.gen_weight(f, n, k, rng)
+    w = sb.QuantizedWeight(ctx, f, data, n, k, scales)
+    r = cuda(rng.standard_normal((1, k)).astype(np.float32))
+    d = cuda(rng.standard_normal((1, k)).astype(np.float32))
+    nw = cuda((1 + 0.1 * rng.standard_normal(k)).astype(np.float32))
+    ro = torch.empty_like(r)
+    y = w.matmul_rmsnorm(r, nw, 1e-6, delta=d, residual_out=ro, parallel_sum=fast)
+    if not fast:
+        r2 = r.clone()
+        x = sb.add_rmsnorm(r2, d, nw, 1e-6)
+        assert exact(ro.cpu().numpy(), r2.cpu().numpy())
+        assert exact(y.cpu().numpy(), w.matmul(x).cpu().numpy())
+    else:
+        xs = (r + d).cpu().numpy()
+        x = xs / np.sqrt((xs.astype(np.float64) ** 2).mean() + 1e-6) * nw.cpu().numpy()
+        yr = w.matmul(torch.from_numpy(x.astype(np.float32)).cuda()).cpu().numpy()
+        assert np.allclose(y.cpu().numpy(), yr, rtol=1e-3, atol=1e-3 * np.abs(yr).max())
+    w.close()
