@@ -810,18 +810,33 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
   griddep_launch();
   if (!last) return;
   __threadfence();
+  // combine: split maxima and rescaled sums in parallel over the splits (the
+  // factors go to smem, reusing the V staging rows), then each output column
+  // sums its splits with the loads issued in batches
+  float* fac = vb;  // nsplit floats
+  float M = -INFINITY;
+  for (int c = tid; c < nsplit; c += FD_THREADS) M = fmaxf(M, __ldcg(base + c * (HD + 2)));
+  M = block_max(M, red);
+  float lsum = 0.0f;
+  for (int c = tid; c < nsplit; c += FD_THREADS) {
+    const float m = __ldcg(base + c * (HD + 2));
+    const float f = m == -INFINITY ? 0.0f : expf(m - M);
+    fac[c] = f;
+    lsum += f * __ldcg(base + c * (HD + 2) + 1);
+  }
+  lsum = block_sum(lsum, red);  // (its barriers also publish fac)
   if (tid < HD) {
-    float M = -INFINITY;
-    for (int c = 0; c < nsplit; c++) M = fmaxf(M, base[c * (HD + 2)]);
-    float l = 0.0f, o = 0.0f;
-    for (int c = 0; c < nsplit; c++) {
-      const float m = base[c * (HD + 2)];
-      if (m == -INFINITY) continue;
-      const float f = expf(m - M);
-      l += base[c * (HD + 2) + 1] * f;
-      o += base[c * (HD + 2) + 2 + tid] * f;
+    float o = 0.0f;
+    int c = 0;
+    for (; c + 8 <= nsplit; c += 8) {
+      float ov[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) ov[u] = __ldcg(base + (c + u) * (HD + 2) + 2 + tid);
+#pragma unroll
+      for (int u = 0; u < 8; u++) o = fmaf(ov[u], fac[c + u], o);
     }
-    p.out[(long long)b * p.ldo + (long long)h * HD + tid] = o / l;
+    for (; c < nsplit; c++) o = fmaf(__ldcg(base + c * (HD + 2) + 2 + tid), fac[c], o);
+    p.out[(long long)b * p.ldo + (long long)h * HD + tid] = o / lsum;
   }
   if (tid == 0) cnt[b * p.n_heads + h] = 0;  // ready for the next launch
 }
@@ -1201,6 +1216,7 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
                                  cudaStream_t st) {
   syn_cuda_kvcache_t* c = a.cache;
   const int nsplit = (int)((eff + FD_CH - 1) / FD_CH);
+  if (nsplit > 32 * (p.hd + 4)) return SYN_ERR_UNSUPPORTED;  // combine factors fit in smem
   const size_t pbytes = (batch * p.n_heads * (size_t)nsplit * (p.hd + 2) * sizeof(float) + 255) &
                         ~size_t(255);
   const size_t need = pbytes + batch * p.n_heads * sizeof(int);
