@@ -340,51 +340,62 @@ template <int FMT>
 __device__ void prep_blocks(const float* xr, bool live, int wb0, int wb1, uint8_t* act, int cb0) {
   const int lane = threadIdx.x & 31;
   const int j = lane & 7;  // elements 4j..4j+3 of the block
-  for (int b0 = wb0; b0 < wb1; b0 += 4) {
-    const int b = b0 + (lane >> 3);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (live && b < wb1) v = *reinterpret_cast<const float4*>(xr + (size_t)b * 32 + 4 * j);
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  constexpr int PF = 4;    // 4-block iterations whose loads are issued together
+  for (int base = wb0; base < wb1; base += 4 * PF) {
+    float4 vv[PF];
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
-    float scale = 0.0f;
-    if (amax > 0.0f) {
-      const float inv = 32767.0f / amax;
-      q0 = max(-32767, min(32767, __float2int_rn(v.x * inv)));
-      q1 = max(-32767, min(32767, __float2int_rn(v.y * inv)));
-      q2 = max(-32767, min(32767, __float2int_rn(v.z * inv)));
-      q3 = max(-32767, min(32767, __float2int_rn(v.w * inv)));
-      scale = amax / 32767.0f;
+    for (int u = 0; u < PF; u++) {
+      const int b = base + 4 * u + (lane >> 3);
+      vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (live && b < wb1) vv[u] = *reinterpret_cast<const float4*>(xr + (size_t)b * 32 + 4 * j);
     }
-    int ssum = q0 + q1 + q2 + q3;
-    ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
-    ssum += __shfl_xor_sync(0xffffffffu, ssum, 2);
-    if (b >= wb1) continue;
-    uint8_t* blk = act + (size_t)(b - cb0) * act_block_bytes(FMT);
-    // signed high bytes / unsigned low bytes
-    const uint32_t h0 = (q0 >> 8) & 0xFF, h1 = (q1 >> 8) & 0xFF, h2 = (q2 >> 8) & 0xFF,
-                   h3 = (q3 >> 8) & 0xFF;
-    const uint32_t l0 = q0 & 0xFF, l1 = q1 & 0xFF, l2 = q2 & 0xFF, l3 = q3 & 0xFF;
-    if constexpr (interleaved(FMT)) {
-      // elements 4j, 4j+2 are even -> even-plane slots 2j, 2j+1
-      uint16_t* P = reinterpret_cast<uint16_t*>(blk);
-      P[0 * 8 + j] = (uint16_t)(h0 | (h2 << 8));
-      P[1 * 8 + j] = (uint16_t)(h1 | (h3 << 8));
-      P[2 * 8 + j] = (uint16_t)(l0 | (l2 << 8));
-      P[3 * 8 + j] = (uint16_t)(l1 | (l3 << 8));
-    } else {
-      uint32_t* P = reinterpret_cast<uint32_t*>(blk);
-      const int half = j >> 2, o = j & 3;
-      P[half * 4 + o] = h0 | (h1 << 8) | (h2 << 16) | (h3 << 24);
-      P[(half + 2) * 4 + o] = l0 | (l1 << 8) | (l2 << 16) | (l3 << 24);
+#pragma unroll
+    for (int u = 0; u < PF; u++) {
+      if (base + 4 * u >= wb1) break;  // uniform across the warp
+      const int b = base + 4 * u + (lane >> 3);
+      const float4 v = vv[u];
+      float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
+      float scale = 0.0f;
+      if (amax > 0.0f) {
+        const float inv = 32767.0f / amax;
+        q0 = max(-32767, min(32767, __float2int_rn(v.x * inv)));
+        q1 = max(-32767, min(32767, __float2int_rn(v.y * inv)));
+        q2 = max(-32767, min(32767, __float2int_rn(v.z * inv)));
+        q3 = max(-32767, min(32767, __float2int_rn(v.w * inv)));
+        scale = amax / 32767.0f;
+      }
+      int ssum = q0 + q1 + q2 + q3;
+      ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
+      ssum += __shfl_xor_sync(0xffffffffu, ssum, 2);
+      if (b >= wb1) continue;
+      uint8_t* blk = act + (size_t)(b - cb0) * act_block_bytes(FMT);
+      // signed high bytes / unsigned low bytes
+      const uint32_t h0 = (q0 >> 8) & 0xFF, h1 = (q1 >> 8) & 0xFF, h2 = (q2 >> 8) & 0xFF,
+                     h3 = (q3 >> 8) & 0xFF;
+      const uint32_t l0 = q0 & 0xFF, l1 = q1 & 0xFF, l2 = q2 & 0xFF, l3 = q3 & 0xFF;
+      if constexpr (interleaved(FMT)) {
+        // elements 4j, 4j+2 are even -> even-plane slots 2j, 2j+1
+        uint16_t* P = reinterpret_cast<uint16_t*>(blk);
+        P[0 * 8 + j] = (uint16_t)(h0 | (h2 << 8));
+        P[1 * 8 + j] = (uint16_t)(h1 | (h3 << 8));
+        P[2 * 8 + j] = (uint16_t)(l0 | (l2 << 8));
+        P[3 * 8 + j] = (uint16_t)(l1 | (l3 << 8));
+      } else {
+        uint32_t* P = reinterpret_cast<uint32_t*>(blk);
+        const int half = j >> 2, o = j & 3;
+        P[half * 4 + o] = h0 | (h1 << 8) | (h2 << 16) | (h3 << 24);
+        P[(half + 2) * 4 + o] = l0 | (l1 << 8) | (l2 << 16) | (l3 << 24);
+      }
+      float* tail = reinterpret_cast<float*>(blk + 64);
+      if (j == 0) {
+        tail[0] = (float)ssum;
+        tail[2] = scale;
+      }
+      if (j == 4) tail[1] = (float)ssum;
     }
-    float* tail = reinterpret_cast<float*>(blk + 64);
-    if (j == 0) {
-      tail[0] = (float)ssum;
-      tail[2] = scale;
-    }
-    if (j == 4) tail[1] = (float)ssum;
   }
 }
 
