@@ -336,65 +336,82 @@ __device__ __forceinline__ float dot_block(const WB<FMT>& w, const AB& a, int b)
 // Activation conversion (per warp, over the warp's share [wb0, wb1) of the
 // CTA's blocks).
 // ---------------------------------------------------------------------------
+// Two lanes per block: lane half h = lane & 1 quantises elements
+// [16h, 16h + 16) of block b. The block max takes one shuffle; each half's
+// code sum is its own (sums[h]), so no other cross-lane step is needed.
 template <int FMT>
 __device__ void prep_blocks(const float* xr, bool live, int wb0, int wb1, uint8_t* act, int cb0) {
   const int lane = threadIdx.x & 31;
-  const int j = lane & 7;  // elements 4j..4j+3 of the block
-  constexpr int PF = 4;    // 4-block iterations whose loads are issued together
-  for (int base = wb0; base < wb1; base += 4 * PF) {
-    float4 vv[PF];
+  const int h = lane & 1;
+  constexpr int PF = 2;  // 16-block iterations whose loads are issued together
+  for (int base = wb0; base < wb1; base += 16 * PF) {
+    float4 vv[PF][4];
 #pragma unroll
     for (int u = 0; u < PF; u++) {
-      const int b = base + 4 * u + (lane >> 3);
-      vv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (live && b < wb1) vv[u] = *reinterpret_cast<const float4*>(xr + (size_t)b * 32 + 4 * j);
+      const int b = base + 16 * u + (lane >> 1);
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        vv[u][e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live && b < wb1)
+          vv[u][e] = *reinterpret_cast<const float4*>(xr + (size_t)b * 32 + 16 * h + 4 * e);
+      }
     }
 #pragma unroll
     for (int u = 0; u < PF; u++) {
-      if (base + 4 * u >= wb1) break;  // uniform across the warp
-      const int b = base + 4 * u + (lane >> 3);
-      const float4 v = vv[u];
-      float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+      if (base + 16 * u >= wb1) break;  // uniform across the warp
+      const int b = base + 16 * u + (lane >> 1);
+      float v[16];
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      int q0 = 0, q1 = 0, q2 = 0, q3 = 0;
-      float scale = 0.0f;
-      if (amax > 0.0f) {
-        const float inv = 32767.0f / amax;
-        q0 = max(-32767, min(32767, __float2int_rn(v.x * inv)));
-        q1 = max(-32767, min(32767, __float2int_rn(v.y * inv)));
-        q2 = max(-32767, min(32767, __float2int_rn(v.z * inv)));
-        q3 = max(-32767, min(32767, __float2int_rn(v.w * inv)));
-        scale = amax / 32767.0f;
+      for (int e = 0; e < 4; e++) {
+        v[4 * e] = vv[u][e].x;
+        v[4 * e + 1] = vv[u][e].y;
+        v[4 * e + 2] = vv[u][e].z;
+        v[4 * e + 3] = vv[u][e].w;
       }
-      int ssum = q0 + q1 + q2 + q3;
-      ssum += __shfl_xor_sync(0xffffffffu, ssum, 1);
-      ssum += __shfl_xor_sync(0xffffffffu, ssum, 2);
+      float amax = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 16; e++) amax = fmaxf(amax, fabsf(v[e]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      int q[16];
+      int ssum = 0;
+      const float inv = amax > 0.0f ? 32767.0f * __frcp_rn(amax) : 0.0f;
+#pragma unroll
+      for (int e = 0; e < 16; e++) {
+        q[e] = max(-32767, min(32767, __float2int_rn(v[e] * inv)));
+        ssum += q[e];
+      }
       if (b >= wb1) continue;
       uint8_t* blk = act + (size_t)(b - cb0) * act_block_bytes(FMT);
-      // signed high bytes / unsigned low bytes
-      const uint32_t h0 = (q0 >> 8) & 0xFF, h1 = (q1 >> 8) & 0xFF, h2 = (q2 >> 8) & 0xFF,
-                     h3 = (q3 >> 8) & 0xFF;
-      const uint32_t l0 = q0 & 0xFF, l1 = q1 & 0xFF, l2 = q2 & 0xFF, l3 = q3 & 0xFF;
+      // byte 1 (signed high byte) or byte 0 (unsigned low byte) of four codes
+      auto hi4 = [](int a, int b2, int c, int d) {
+        return __byte_perm(__byte_perm(a, b2, 0x0051), __byte_perm(c, d, 0x0051), 0x5410);
+      };
+      auto lo4 = [](int a, int b2, int c, int d) {
+        return __byte_perm(__byte_perm(a, b2, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+      };
       if constexpr (interleaved(FMT)) {
-        // elements 4j, 4j+2 are even -> even-plane slots 2j, 2j+1
-        uint16_t* P = reinterpret_cast<uint16_t*>(blk);
-        P[0 * 8 + j] = (uint16_t)(h0 | (h2 << 8));
-        P[1 * 8 + j] = (uint16_t)(h1 | (h3 << 8));
-        P[2 * 8 + j] = (uint16_t)(l0 | (l2 << 8));
-        P[3 * 8 + j] = (uint16_t)(l1 | (l3 << 8));
+        // element 16h + j sits in the even (j even) or odd plane at byte
+        // 8h + j/2: this lane fills words 2h, 2h + 1 of each plane
+        const uint2 he = make_uint2(hi4(q[0], q[2], q[4], q[6]), hi4(q[8], q[10], q[12], q[14]));
+        const uint2 ho = make_uint2(hi4(q[1], q[3], q[5], q[7]), hi4(q[9], q[11], q[13], q[15]));
+        const uint2 le = make_uint2(lo4(q[0], q[2], q[4], q[6]), lo4(q[8], q[10], q[12], q[14]));
+        const uint2 lo = make_uint2(lo4(q[1], q[3], q[5], q[7]), lo4(q[9], q[11], q[13], q[15]));
+        *reinterpret_cast<uint2*>(blk + 0 + 8 * h) = he;
+        *reinterpret_cast<uint2*>(blk + 16 + 8 * h) = ho;
+        *reinterpret_cast<uint2*>(blk + 32 + 8 * h) = le;
+        *reinterpret_cast<uint2*>(blk + 48 + 8 * h) = lo;
       } else {
-        uint32_t* P = reinterpret_cast<uint32_t*>(blk);
-        const int half = j >> 2, o = j & 3;
-        P[half * 4 + o] = h0 | (h1 << 8) | (h2 << 16) | (h3 << 24);
-        P[(half + 2) * 4 + o] = l0 | (l1 << 8) | (l2 << 16) | (l3 << 24);
+        // natural order: plane h (high bytes) and plane 2 + h (low bytes)
+        *reinterpret_cast<uint4*>(blk + 16 * h) =
+            make_uint4(hi4(q[0], q[1], q[2], q[3]), hi4(q[4], q[5], q[6], q[7]),
+                       hi4(q[8], q[9], q[10], q[11]), hi4(q[12], q[13], q[14], q[15]));
+        *reinterpret_cast<uint4*>(blk + 32 + 16 * h) =
+            make_uint4(lo4(q[0], q[1], q[2], q[3]), lo4(q[4], q[5], q[6], q[7]),
+                       lo4(q[8], q[9], q[10], q[11]), lo4(q[12], q[13], q[14], q[15]));
       }
       float* tail = reinterpret_cast<float*>(blk + 64);
-      if (j == 0) {
-        tail[0] = (float)ssum;
-        tail[2] = scale;
-      }
-      if (j == 4) tail[1] = (float)ssum;
+      tail[h] = (float)ssum;
+      if (h == 0) tail[2] = amax > 0.0f ? amax * (1.0f / 32767.0f) : 0.0f;
     }
   }
 }
