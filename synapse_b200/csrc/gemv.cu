@@ -119,6 +119,7 @@ struct GemvParams {
   float* nres_out;
   int nfast;  // 1: parallel sum of squares; 0: the reference's vecHsum order
   int xs_off; // byte offset of the normalised row in dynamic shared memory
+  int ns;     // k_qgemv_tma ring depth
 };
 
 __device__ __forceinline__ void consumer_sync() {
@@ -740,13 +741,14 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
   const int nst = (cb1 - cb0 + SB - 1) / SB;
   constexpr int SBYTES = RG * S::BYTES;  // one stage: RG sub-stages
   uint8_t* ring = sm;
-  uint8_t* act = sm + S::NS * SBYTES;
+  const int ns = p.ns;  // ring depth, <= S::NS (chosen by the plan for occupancy)
+  uint8_t* act = sm + ns * SBYTES;
   const int act_stride = p.kr * act_block_bytes(FMT);
   const int cc0 = cb0 >> 4, ncc = ((cb1 + 15) >> 4) - cc0;
   int* csum = reinterpret_cast<int*>(act + MT * act_stride);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S::NS; s++) {
+    for (int s = 0; s < ns; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], WARPS);
     }
@@ -758,9 +760,12 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
     // ---- producer: stream this CTA's weight bytes, stage by stage ----
     griddep_launch();
     if (lane == 0) {
-      for (int s = 0; s < nst; s++) {
-        const int slot = s % S::NS;
-        if (s >= S::NS && !mbar_wait_bounded(&empty[slot], ((s / S::NS) - 1) & 1)) {
+      for (int s = 0, slot = 0, round = 0; s < nst; s++) {
+        if (s > 0 && ++slot == ns) {
+          slot = 0;
+          round++;
+        }
+        if (round > 0 && !mbar_wait_bounded(&empty[slot], (round - 1) & 1)) {
           report(p, SYN_ERR_TIMEOUT);
           break;
         }
@@ -827,9 +832,12 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
   for (int mm = 0; mm < MT; mm++)
 #pragma unroll
     for (int r = 0; r < RG; r++) facc[mm][r] = 0.0f;
-  for (int s = 0; s < nst; s++) {
-    const int slot = s % S::NS;
-    const bool ok = mbar_wait_bounded(&full[slot], (s / S::NS) & 1);
+  for (int s = 0, slot = 0, round = 0; s < nst; s++) {
+    if (s > 0 && ++slot == ns) {
+      slot = 0;
+      round++;
+    }
+    const bool ok = mbar_wait_bounded(&full[slot], round & 1);
     if (!ok && lane == 0) report(p, SYN_ERR_TIMEOUT);
     const int b0 = cb0 + s * SB, nbs = min(SB, cb1 - b0);
     const uint8_t* st = ring + slot * SBYTES;
@@ -961,6 +969,7 @@ __global__ void __launch_bounds__(THREADS) k_qgemv(const GemvParams p) {
 // ---------------------------------------------------------------------------
 struct Plan {
   int groups, nblk, kr, nks, nchunks, mt, rg;
+  int ns;  // ring depth of k_qgemv_tma
   size_t xs_bytes;  // fused-norm row in shared memory (0 = none)
   size_t act_smem;  // activations + INT8 chunk sums
 };
@@ -981,7 +990,20 @@ int tune(const char* name, int dflt) {
   return r;
 }
 
-Plan make_plan(int fmt, size_t m, size_t n, size_t kp) {
+// Dynamic shared memory of k_qgemv_tma: the ring, the activations and, for
+// the fused norm, the normalised row.
+size_t stage_bytes(int fmt);
+size_t tma_smem(const Plan& pl, int fmt, int rg, int ns) {
+  const size_t ring = (size_t)ns * rg * stage_bytes(fmt);
+  const size_t base = ring + pl.act_smem;
+  return pl.xs_bytes ? ((base + 15) & ~size_t(15)) + pl.xs_bytes : base;
+}
+
+int tma_occupancy(int fmt, int mt, int rg, size_t smem);
+size_t stage_bytes(int fmt);
+int stage_depth(int fmt);
+
+Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
   Plan pl{};
   pl.groups = (int)((n + 31) / 32);
   pl.nblk = (int)(kp / 32);
@@ -1018,6 +1040,30 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp) {
   }
   const int ncc = kr / 16 + 1;
   pl.act_smem = (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
+  pl.xs_bytes = xs_bytes;
+  pl.ns = 0;
+  if (fmt != F_Q4_0RAW) {
+    // All CTAs resident at once: row pairs only while two CTAs still fit on
+    // an SM, and a shallower ring where one more CTA per SM would otherwise
+    // spill the grid into a second wave.
+    const int nsmax = stage_depth(fmt);
+    auto occ = [&](int rg, int ns) {
+      return tma_occupancy(fmt, pl.mt, rg, tma_smem(pl, fmt, rg, ns));
+    };
+    if (pl.rg == 2 && occ(2, nsmax) < 2) pl.rg = 1;
+    const long long ctas =
+        (long long)((pl.groups + pl.rg - 1) / pl.rg) * pl.nks * mslices;
+    int ns = nsmax;
+    if (ctas > (long long)sms * occ(pl.rg, ns)) {
+      for (int t = nsmax - 1; t >= 2; t--)
+        if (ctas <= (long long)sms * occ(pl.rg, t)) {
+          ns = t;
+          break;
+        }
+    }
+    const int forced = tune("SYN_GEMV_NS", 0);
+    pl.ns = forced >= 2 && forced <= nsmax ? forced : ns;
+  }
   return pl;
 }
 
@@ -1052,6 +1098,77 @@ void allow_smem(K kern) {
   done.insert(key);
 }
 
+size_t stage_bytes(int fmt) {
+  switch (fmt) {
+    case F_INT8: return Stage<F_INT8>::BYTES;
+    case F_Q4_0: return Stage<F_Q4_0>::BYTES;
+    case F_Q8_0: return Stage<F_Q8_0>::BYTES;
+    case F_Q4_K: return Stage<F_Q4_K>::BYTES;
+    case F_Q6_K: return Stage<F_Q6_K>::BYTES;
+  }
+  return 0;
+}
+
+int stage_depth(int fmt) {
+  switch (fmt) {
+    case F_INT8: return Stage<F_INT8>::NS;
+    case F_Q4_0: return Stage<F_Q4_0>::NS;
+    case F_Q8_0: return Stage<F_Q8_0>::NS;
+    case F_Q4_K: return Stage<F_Q4_K>::NS;
+    case F_Q6_K: return Stage<F_Q6_K>::NS;
+  }
+  return 2;
+}
+
+template <typename K>
+int occ_of(K kern, size_t smem) {
+  allow_smem(kern);
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, THREADS + 32, smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 1;
+  }
+  return occ;
+}
+
+template <int FMT>
+int tma_occ_f(int mt, int rg, size_t smem) {
+  if constexpr (FMT != F_INT8) {
+    if (mt == 1) return rg == 2 ? occ_of(k_qgemv_tma<FMT, 1, 2>, smem)
+                                : occ_of(k_qgemv_tma<FMT, 1, 1>, smem);
+  } else {
+    if (mt == 1) return occ_of(k_qgemv_tma<FMT, 1, 1>, smem);
+  }
+  return mt == 2 ? occ_of(k_qgemv_tma<FMT, 2, 1>, smem) : occ_of(k_qgemv_tma<FMT, 4, 1>, smem);
+}
+
+// CTAs of k_qgemv_tma resident per SM at `smem` bytes (cached per device).
+int tma_occupancy(int fmt, int mt, int rg, size_t smem) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::vector<long long>, int>> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const std::vector<long long> key{fmt, mt, rg, (long long)smem, dev};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (auto& kv : cache)
+      if (kv.first == key) return kv.second;
+  }
+  int occ = 1;
+  switch (fmt) {
+    case F_INT8: occ = tma_occ_f<F_INT8>(mt, rg, smem); break;
+    case F_Q4_0: occ = tma_occ_f<F_Q4_0>(mt, rg, smem); break;
+    case F_Q8_0: occ = tma_occ_f<F_Q8_0>(mt, rg, smem); break;
+    case F_Q4_K: occ = tma_occ_f<F_Q4_K>(mt, rg, smem); break;
+    case F_Q6_K: occ = tma_occ_f<F_Q6_K>(mt, rg, smem); break;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace_back(key, occ);
+  return occ;
+}
+
 template <int FMT, int MT>
 syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   dim3 grid((unsigned)pl.groups, (unsigned)pl.nks, (unsigned)((p.m + MT - 1) / MT));
@@ -1059,26 +1176,25 @@ syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   if constexpr (FMT == F_Q4_0RAW) {
     allow_smem(k_qgemv<FMT, MT>);
     e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.act_smem, st, p);
-  } else if constexpr (FMT != F_INT8 && MT == 1) {
-    GemvParams q = p;
-    const size_t ring = (size_t)Stage<FMT>::NS * pl.rg * Stage<FMT>::BYTES;
-    q.xs_off = (int)((ring + pl.act_smem + 15) & ~size_t(15));
-    const size_t smem = pl.xs_bytes ? q.xs_off + pl.xs_bytes : ring + pl.act_smem;
-    if (pl.rg == 2) {
-      allow_smem(k_qgemv_tma<FMT, 1, 2>);
-      grid.x = (unsigned)((pl.groups + 1) / 2);
-      e = launch_pdl(k_qgemv_tma<FMT, 1, 2>, grid, dim3(THREADS + 32), smem, st, q);
-    } else {
-      allow_smem(k_qgemv_tma<FMT, 1, 1>);
-      e = launch_pdl(k_qgemv_tma<FMT, 1, 1>, grid, dim3(THREADS + 32), smem, st, q);
-    }
   } else {
-    allow_smem(k_qgemv_tma<FMT, MT, 1>);
-    const size_t ring = (size_t)Stage<FMT>::NS * Stage<FMT>::BYTES;
     GemvParams q = p;
-    q.xs_off = (int)((ring + pl.act_smem + 15) & ~size_t(15));
-    const size_t smem = pl.xs_bytes ? q.xs_off + pl.xs_bytes : ring + pl.act_smem;
-    e = launch_pdl(k_qgemv_tma<FMT, MT, 1>, grid, dim3(THREADS + 32), smem, st, q);
+    const int rg = (FMT != F_INT8 && MT == 1) ? pl.rg : 1;
+    q.ns = pl.ns;
+    q.xs_off = (int)(((size_t)pl.ns * rg * Stage<FMT>::BYTES + pl.act_smem + 15) & ~size_t(15));
+    const size_t smem = tma_smem(pl, FMT, rg, pl.ns);
+    if constexpr (FMT != F_INT8 && MT == 1) {
+      if (rg == 2) {
+        allow_smem(k_qgemv_tma<FMT, 1, 2>);
+        grid.x = (unsigned)((pl.groups + 1) / 2);
+        e = launch_pdl(k_qgemv_tma<FMT, 1, 2>, grid, dim3(THREADS + 32), smem, st, q);
+      } else {
+        allow_smem(k_qgemv_tma<FMT, 1, 1>);
+        e = launch_pdl(k_qgemv_tma<FMT, 1, 1>, grid, dim3(THREADS + 32), smem, st, q);
+      }
+    } else {
+      allow_smem(k_qgemv_tma<FMT, MT, 1>);
+      e = launch_pdl(k_qgemv_tma<FMT, MT, 1>, grid, dim3(THREADS + 32), smem, st, q);
+    }
   }
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_qgemv");
@@ -1168,8 +1284,7 @@ syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, f
   if (w->n > 0x7FFFFFFFull || w->kp > 0x3FFFFFFFull) return SYN_ERR_UNSUPPORTED;
   if (w->k > 16384) return SYN_ERR_UNSUPPORTED;  // the row is staged in shared memory
   const int fk = w->fmt == SYN_QFMT_INT8_KN ? F_INT8 : w->fmt;
-  Plan pl = make_plan(fk, 1, w->n, w->kp);
-  pl.xs_bytes = w->k * sizeof(float);
+  const Plan pl = make_plan(fk, 1, w->n, w->kp, w->k * sizeof(float));
   GemvParams p{};
   p.q = w->q;
   p.d = w->d;
