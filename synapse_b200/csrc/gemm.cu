@@ -33,6 +33,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -48,7 +50,9 @@ enum : int { F_INT8 = SYN_QFMT_INT8_KN, F_Q4_0 = SYN_QFMT_Q4_0, F_Q8_0 = SYN_QFM
 constexpr int BM = 128;  // tokens per tile (MMA M)
 constexpr int BN = 128;  // weight rows per tile (4 row groups of 32) = MMA N
 constexpr int NG = BN / 32;
-constexpr int WORKERS = 8;                       // dequant / epilogue warps
+constexpr int WORKERS = 16;                      // dequant / epilogue warps
+constexpr int WSETS = WORKERS / 4;               // warps per tensor-memory lane quarter
+constexpr int CGW = 4 / WSETS;                   // 32-column groups per epilogue warp
 constexpr int GEMM_THREADS = 64 + WORKERS * 32;  // producer + MMA + workers
 
 // ---------------------------------------------------------------------------
@@ -73,6 +77,30 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t 
   d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
   d |= (uint64_t)1 << 46;  // descriptor version for sm_100
   return d;                // base offset 0, legacy LBO mode, layout SWIZZLE_NONE
+}
+
+// fp16 operands use the 128-byte-swizzled K-major layout: atoms of 8 rows x
+// 128 B (64 halves of K) at 1024-byte-aligned addresses, 8-row groups 1024 B
+// apart, and within a row the 16-byte chunk j stored at chunk j ^ (row & 7).
+// A tile of R rows and 128 K (one stage) is two atoms columns of R * 128 B.
+// Descriptor: SBO = 1024 B, LBO = 16 B, layout type 2 (SWIZZLE_128B); a K
+// step inside an atom advances the start address (the hardware applies the
+// XOR to the final address bits).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;          // LBO = 16 B
+  d |= (uint64_t)(1024 >> 4) << 32;  // SBO = 1024 B
+  d |= (uint64_t)1 << 46;          // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;          // SWIZZLE_128B
+  return d;
+}
+
+// Byte offset of 16-byte K column c (0..15 within a stage) of row r in a
+// swizzled stage tile of `rows` rows.
+__host__ __device__ __forceinline__ uint32_t sw128_off(int c, int r, int rows) {
+  return (uint32_t)((c >> 3) * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 +
+                    (((c & 7) ^ (r & 7)) << 4));
 }
 
 // Instruction descriptor: M = 128, N = 128, K-major A and B.
@@ -101,6 +129,16 @@ __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uin
             tmem_d),
         "l"(a), "l"(b), "r"(id), "r"(accumulate), "r"(0u));
   }
+}
+
+// kind::f16 MMA with a runtime instruction descriptor (SW: N = npad).
+__device__ __forceinline__ void mma_f16_id(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(
+          tmem_d),
+      "l"(a), "l"(b), "r"(id), "r"(accumulate), "r"(0u));
 }
 
 // Arrives on `bar` once every MMA issued so far by this thread is complete.
@@ -151,11 +189,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 // ---------------------------------------------------------------------------
 // Per-format stage geometry
 // ---------------------------------------------------------------------------
-template <int FMT>
+// SW (few tokens, block formats): the operands swap roles -- the 128
+// dequantised weight rows are the MMA's M and the tokens its N -- so a
+// stage's activation tile is small and the ring can be deeper. Each token
+// enters as two fp16 rows, x = hi + lo (hi = fp16(x), lo = fp16(x - hi)), so
+// only the weights are rounded: N = 2 npad <= 64 (npad = tokens padded to a
+// multiple of 16), and the epilogue adds the hi and lo columns.
+template <int FMT, bool SW = false>
 struct GS {
   static constexpr bool I8 = FMT == F_INT8;
   static constexpr int KB = I8 ? 8 : 4;                        // 32-element blocks per stage
-  static constexpr int A_BYTES = BM * KB * 32 * (I8 ? 1 : 2);  // 32 KB
+  static constexpr int A_BYTES =
+      SW ? KB * 4 * 64 * 16 : BM * KB * 32 * (I8 ? 1 : 2);     // 16 KB (SW) / 32 KB
   // INT8: B stage = [2*KB K columns][128 rows][16 B] (tensor-map gather)
   static constexpr int B8_BYTES = I8 ? BN * KB * 32 : 0;       // 32 KB
   // block formats: raw bytes per row group (q tiles + per-block aux)
@@ -173,11 +218,12 @@ struct GS {
   static constexpr int G_D6 = G_H + HT;
   static constexpr int G_BYTES = I8 ? 0 : (G_D6 + D6T + 127) / 128 * 128;  // per row group
   static constexpr int RAW_BYTES = I8 ? B8_BYTES : NG * G_BYTES;
-  static constexpr int STAGE_BYTES = A_BYTES + RAW_BYTES;
-  static constexpr int NS = 3;                                 // ring depth
+  static constexpr int STAGE_BYTES = (A_BYTES + RAW_BYTES + 1023) / 1024 * 1024;  // atom aligned
   // block formats: dequantised fp16 B = [block][4 K columns][128 rows][16 B]
   static constexpr int BH_BYTES = I8 ? 0 : BN * KB * 32 * 2;   // 32 KB
   static constexpr int NBH = I8 ? 0 : 2;
+  static constexpr int NS_FIT = (230400 - NBH * BH_BYTES) / STAGE_BYTES;
+  static constexpr int NS = SW ? (NS_FIT < 8 ? NS_FIT : 8) : 3;  // ring depth
   static constexpr int SMEM = NS * STAGE_BYTES + NBH * BH_BYTES;
   static constexpr uint32_t TMEM_COLS = I8 ? 512 : 128;
 };
@@ -198,6 +244,9 @@ struct GemmParams {
   long long ldy;
   int chunked;
   int* err;
+  int short_rows;  // m-tiles with at most this many valid rows copy only those
+  int npad;        // SW: tokens padded to a multiple of 16 (the MMA's N is 2 npad)
+  int astg;        // fp16 A: stages (16 K columns each) per m-tile in the prepared buffer
 };
 
 __device__ __forceinline__ void greport(const GemmParams& p) {
@@ -259,7 +308,7 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
     }
 #pragma unroll
     for (int c = 0; c < 4; c++)
-      reinterpret_cast<uint4*>(out + bl * 8192 + c * 2048)[row] =
+      *reinterpret_cast<uint4*>(out + sw128_off(bl * 4 + c, row, BN)) =
           make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
     return;
   }
@@ -337,14 +386,15 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
     o.y = *reinterpret_cast<const uint32_t*>(&h1);
     o.z = *reinterpret_cast<const uint32_t*>(&h2);
     o.w = *reinterpret_cast<const uint32_t*>(&h3);
-    reinterpret_cast<uint4*>(out + bl * 8192 + c * 2048)[row] = o;
+    *reinterpret_cast<uint4*>(out + sw128_off(bl * 4 + c, row, BN)) = o;
   }
 }
 
-template <int FMT>
+template <int FMT, bool SW = false>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_qgemm(const GemmParams p, const __grid_constant__ CUtensorMap tmb) {
-  using S = GS<FMT>;
+  using S = GS<FMT, SW>;
+  static_assert(!SW || FMT != F_INT8, "swapped operands: block formats");
   constexpr bool I8 = S::I8;
   extern __shared__ __align__(1024) uint8_t sm[];
   __shared__ __align__(8) uint64_t full[S::NS], empty[S::NS];
@@ -400,20 +450,36 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // A: a short m-tile (few tokens) copies only its valid rows of every
         // 16-byte K column (the rows beyond are never stored to y)
         const int rv = (min(BM, p.m - mt * BM) + 7) & ~7;
-        const bool short_a = rv <= 64;
-        const uint32_t a_bytes = short_a ? (uint32_t)(nbs * cpb * rv * 16) : nbs * cpb * 2048;
+        const bool short_a = !SW && rv <= p.short_rows;
+        // fp16 A: swizzled stage tiles [atom][rows][128 B], one atom per 2 blocks
+        const int arows = SW ? 2 * p.npad : BM, atoms = (nbs + 1) / 2;
+        uint32_t a_bytes;
+        if constexpr (I8)
+          a_bytes = short_a ? (uint32_t)(nbs * cpb * rv * 16) : nbs * cpb * 2048;
+        else
+          a_bytes = (uint32_t)(atoms * (short_a ? rv : arows) * 128);
         uint32_t bytes = a_bytes;
         if constexpr (I8)
           bytes += S::B8_BYTES;  // the full tensor-map box (out of range reads as zero)
         else
           bytes += ngr * (nbs * (S::QT + S::DT + S::QHT + S::SCT) + S::HT + S::D6T);
         mbar_expect_tx(&full[slot], bytes);
-        const uint8_t* asrc = p.a + ((size_t)mt * p.kcols + (size_t)b0 * cpb) * 2048;
-        if (short_a) {
-          for (int c = 0; c < nbs * cpb; c++)
-            bulk_g2s(st + c * 2048, asrc + (size_t)c * 2048, rv * 16, &full[slot]);
+        if constexpr (I8) {
+          const uint8_t* asrc = p.a + ((size_t)mt * p.kcols + (size_t)b0 * cpb) * 2048;
+          if (short_a) {
+            for (int c = 0; c < nbs * cpb; c++)
+              bulk_g2s(st + c * 2048, asrc + (size_t)c * 2048, rv * 16, &full[slot]);
+          } else {
+            bulk_g2s(st, asrc, a_bytes, &full[slot]);
+          }
         } else {
-          bulk_g2s(st, asrc, a_bytes, &full[slot]);
+          const uint8_t* asrc = p.a + ((size_t)mt * p.astg + s) * arows * 256;
+          if (short_a) {  // the valid rows' 8-row groups of each atom
+            for (int a = 0; a < atoms; a++)
+              bulk_g2s(st + a * BM * 128, asrc + (size_t)a * BM * 128, rv * 128, &full[slot]);
+          } else {
+            bulk_g2s(st, asrc, a_bytes, &full[slot]);
+          }
         }
         if constexpr (I8) {
           tma_load_4d(raw, &tmb, 0, 0, nt * NG, 2 * b0, &full[slot]);
@@ -472,12 +538,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const bool first = chunked ? ((b & 15) == 0) : (b == 0);
             mma<true>(dcol, sdesc(a_addr + bl * 2 * 2048, 2048, 128),
                       sdesc(b_addr + bl * 2 * 2048, 2048, 128), first ? 0u : 1u);
+          } else if constexpr (SW) {
+            // weights (128 rows) x token rows (2 npad): two 128 x 2npad x 16 MMAs
+            const int rows = 2 * p.npad;
+            const uint32_t id = (1u << 4) | ((uint32_t)(rows >> 3) << 17) |
+                                ((uint32_t)(BM >> 4) << 24);
+            for (int kh = 0; kh < 2; kh++) {
+              const uint32_t ko = (bl & 1) * 64 + kh * 32;  // K offset inside the atom
+              mma_f16_id(dcol, sdesc_sw128(b_addr + (bl >> 1) * BN * 128 + ko),
+                         sdesc_sw128(a_addr + (bl >> 1) * rows * 128 + ko), id,
+                         (b == 0 && kh == 0) ? 0u : 1u);
+            }
           } else {
             // one block = K of 32 halves = two 128 x 128 x 16 MMAs
-            for (int kh = 0; kh < 2; kh++)
-              mma<false>(dcol, sdesc(a_addr + (bl * 4 + kh * 2) * 2048, 2048, 128),
-                         sdesc(b_addr + bl * 8192 + kh * 4096, 2048, 128),
+            for (int kh = 0; kh < 2; kh++) {
+              const uint32_t ko = (bl & 1) * 64 + kh * 32;  // K offset inside the atom
+              mma<false>(dcol, sdesc_sw128(a_addr + (bl >> 1) * BM * 128 + ko),
+                         sdesc_sw128(b_addr + (bl >> 1) * BN * 128 + ko),
                          (b == 0 && kh == 0) ? 0u : 1u);
+            }
           }
         }
         mma_commit(&empty[slot]);
@@ -497,7 +576,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------- warps 2-9: dequantise B / epilogue ----------------
     const int ew = warp - 2;          // 0..7
     const int quarter = warp & 3;     // tensor memory lane quarter of this warp
-    const int chalf = ew >> 2;        // column half (64 columns) of the epilogue
+    const int chalf = ew >> 2;        // epilogue column share: CGW groups of 32 columns
     const int tok = mt * BM + quarter * 32 + lane;
     const uint32_t tq = tbase + ((uint32_t)(quarter * 32) << 16);
     if constexpr (!I8) {
@@ -511,7 +590,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const uint8_t* raw = sm + slot * S::STAGE_BYTES + S::A_BYTES + gi * S::G_BYTES;
         uint8_t* out = sm + S::NS * S::STAGE_BYTES + (s & 1) * S::BH_BYTES;
         if (ok1 && ok2 && gvalid)
-          for (int bl = bpar; bl < nbs; bl += 2) dequant_block<FMT>(raw, out, lane, row, bl, b0 + bl);
+          for (int bl = bpar; bl < nbs; bl += WSETS)
+            dequant_block<FMT>(raw, out, lane, row, bl, b0 + bl);
         fence_async_smem();  // generic-proxy smem writes -> visible to the MMA
         __syncwarp();
         if (lane == 0) {
@@ -522,8 +602,27 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // epilogue: fp32 accumulators -> y
       bwait(p, &accfull[0], 0);
       tc_fence_after();
-      for (int h = 0; h < 2; h++) {
-        const int cg = chalf * 2 + h;
+      if constexpr (SW) {
+        // lane = weight row; column t = token t's hi part, npad + t its lo
+        // part (npad is 16 or 32: columns [0, 32) and, for 32, [32, 64))
+        if (chalf == 0) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tq, r0);
+          if (p.npad == 32) tmem_ld32(tq + 32, r1);
+          const int n = nt * BN + quarter * 32 + lane;
+          if (n < p.n) {
+#pragma unroll
+            for (int t = 0; t < 32; t++) {
+              if (t >= p.npad) break;
+              const float hi = __uint_as_float(r0[t]);
+              const float lo = __uint_as_float(p.npad == 32 ? r1[t] : r0[16 + (t & 15)]);
+              if (t < p.m) p.y[(long long)t * p.ldy + n] = __fmul_rn(__fadd_rn(hi, lo), p.sa[t]);
+            }
+          }
+        }
+      }
+      for (int h = 0; h < (SW ? 0 : CGW); h++) {
+        const int cg = chalf * CGW + h;
         uint32_t r[32];
         tmem_ld32(tq + cg * 32, r);
         const int n0 = nt * BN + cg * 32;
@@ -541,8 +640,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // one int32 accumulator over all of K: float(acc) * sa * sb
         bwait(p, &accfull[0], 0);
         tc_fence_after();
-        for (int h = 0; h < 2; h++) {
-          const int cg = chalf * 2 + h;
+        for (int h = 0; h < CGW; h++) {
+          const int cg = chalf * CGW + h;
           uint32_t r[32];
           tmem_ld32(tq + cg * 32, r);
           const int n0 = nt * BN + cg * 32;
@@ -560,8 +659,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int c = 0; c < nchunks; c++) {
           bwait(p, &accfull[c & 1], (c >> 1) & 1);
           tc_fence_after();
-          for (int h = 0; h < 2; h++) {
-            const int cg = chalf * 2 + h;
+          for (int h = 0; h < CGW; h++) {
+            const int cg = chalf * CGW + h;
             const int n0 = nt * BN + cg * 32;
             uint32_t r[32], cr[32];
             tmem_ld32(tq + (c & 1) * BN + cg * 32, r);
@@ -580,8 +679,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (lane == 0) mbar_arrive(&accempty[c & 1]);
         }
         tc_fence_after();
-        for (int h = 0; h < 2; h++) {
-          const int cg = chalf * 2 + h;
+        for (int h = 0; h < CGW; h++) {
+          const int cg = chalf * CGW + h;
           uint32_t cr[32];
           tmem_ld32(tq + 2 * BN + cg * 32, cr);
           const int n0 = nt * BN + cg * 32;
@@ -663,19 +762,21 @@ __global__ void __launch_bounds__(256) k_prep_a_i8(const float* __restrict__ x,
   }
 }
 
-// Block formats: fp16(x * 2^-s) per row, with the power of two s chosen so
+// Block formats (rows_pad rows per tile: 128, or 2 npad for the swapped
+// small-M kernel, whose lo_off = npad rows further hold x - fp16(x)):
+// fp16(x * 2^-s) per row, with the power of two s chosen so
 // that the row's largest magnitude lands in [2^14, 2^15): no fp16 overflow
 // and full fp16 precision whatever the activations' range. The scaling is
 // exact; the epilogue multiplies the row's accumulators by 2^s (sa[row]).
 __global__ void __launch_bounds__(256) k_prep_a_f16(const float* __restrict__ x, long long ldx,
                                                     int m, int k, int kcols,
                                                     uint8_t* __restrict__ a,
-                                                    float* __restrict__ sa) {
+                                                    float* __restrict__ sa, int rows_pad, int lo_off) {
   __shared__ float red[8];
   griddep_wait();
   griddep_launch();
   const int row = blockIdx.x;
-  const int mt = row >> 7, rr = row & 127;
+  const int mt = row / rows_pad, rr = row - mt * rows_pad;
   float inv = 1.0f;
   if (row < m) {
     const float* xr = x + (long long)row * ldx;
@@ -695,17 +796,27 @@ __global__ void __launch_bounds__(256) k_prep_a_f16(const float* __restrict__ x,
     if (threadIdx.x == 0) sa[row] = ldexpf(1.0f, ex);
   }
   for (int c = threadIdx.x; c < kcols; c += 256) {
-    uint32_t wv[4] = {0, 0, 0, 0};
+    uint32_t wv[4] = {0, 0, 0, 0}, lv[4] = {0, 0, 0, 0};
     if (row < m) {
 #pragma unroll
       for (int e = 0; e < 8; e++) {
         const int kk = c * 8 + e;
         const float v = kk < k ? __fmul_rn(x[(long long)row * ldx + kk], inv) : 0.0f;
-        wv[e >> 1] |= (uint32_t)__half_as_ushort(__float2half_rn(v)) << (16 * (e & 1));
+        const __half h = __float2half_rn(v);
+        wv[e >> 1] |= (uint32_t)__half_as_ushort(h) << (16 * (e & 1));
+        if (lo_off) {
+          const __half l = __float2half_rn(__fsub_rn(v, __half2float(h)));
+          lv[e >> 1] |= (uint32_t)__half_as_ushort(l) << (16 * (e & 1));
+        }
       }
     }
-    reinterpret_cast<uint4*>(a + (((size_t)mt * kcols + c) * 128 + rr) * 16)[0] =
+    // swizzled stage tiles: [m-tile][stage of 16 columns][atom][rows_pad][128 B]
+    uint8_t* tile = a + ((size_t)mt * ((kcols + 15) >> 4) + (c >> 4)) * rows_pad * 256;
+    *reinterpret_cast<uint4*>(tile + sw128_off(c & 15, rr, rows_pad)) =
         make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    if (lo_off)
+      *reinterpret_cast<uint4*>(tile + sw128_off(c & 15, rr + lo_off, rows_pad)) =
+          make_uint4(lv[0], lv[1], lv[2], lv[3]);
   }
 }
 
@@ -758,8 +869,8 @@ bool make_int8_map(CUtensorMap* map, const syn_cuda_weight_s* w, int groups) {
          CUDA_SUCCESS;
 }
 
-template <int FMT>
-syn_status_t launch_gemm_t(const GemmParams& p, const CUtensorMap& map, int mtiles, int ntiles,
+template <int FMT, bool SW>
+syn_status_t launch_gemm_k(const GemmParams& p, const CUtensorMap& map, int mtiles, int ntiles,
                            cudaStream_t st) {
   static std::mutex mu;
   static std::set<int> done;
@@ -768,13 +879,13 @@ syn_status_t launch_gemm_t(const GemmParams& p, const CUtensorMap& map, int mtil
   {
     std::lock_guard<std::mutex> g(mu);
     if (!done.count(dev)) {
-      cudaFuncSetAttribute(k_qgemm<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GS<FMT>::SMEM);
+      cudaFuncSetAttribute(k_qgemm<FMT, SW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GS<FMT, SW>::SMEM);
       done.insert(dev);
     }
   }
-  cudaError_t e = launch_pdl2(k_qgemm<FMT>, dim3(mtiles, ntiles), dim3(GEMM_THREADS),
-                              (size_t)GS<FMT>::SMEM, st, p, map);
+  cudaError_t e = launch_pdl2(k_qgemm<FMT, SW>, dim3(mtiles, ntiles), dim3(GEMM_THREADS),
+                              (size_t)GS<FMT, SW>::SMEM, st, p, map);
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_qgemm");
     return SYN_ERR_CUDA;
@@ -782,12 +893,31 @@ syn_status_t launch_gemm_t(const GemmParams& p, const CUtensorMap& map, int mtil
   return SYN_OK;
 }
 
+template <int FMT>
+syn_status_t launch_gemm_t(const GemmParams& p, const CUtensorMap& map, int mtiles, int ntiles,
+                           cudaStream_t st) {
+  if constexpr (FMT != F_INT8)
+    if (p.npad) return launch_gemm_k<FMT, true>(p, map, 1, ntiles, st);
+  return launch_gemm_k<FMT, false>(p, map, mtiles, ntiles, st);
+}
+
 }  // namespace
 
 size_t gemm_a_bytes(int fmt, size_t m, size_t kp) {
   const size_t mtiles = (m + BM - 1) / BM;
-  const size_t kcols = (fmt == SYN_QFMT_INT8_KN) ? kp / 16 : kp / 8;
+  // fp16: whole stages of 16 columns (the swizzled tiles)
+  const size_t kcols = (fmt == SYN_QFMT_INT8_KN) ? kp / 16 : (kp / 8 + 15) / 16 * 16;
   return mtiles * BM * kcols * 16 + mtiles * BM * sizeof(float) + 256;
+}
+
+size_t gemm_min_rows(int fmt) {
+  static const size_t forced = [] {
+    const char* v = getenv("SYN_GEMM_MIN_ROWS");
+    return v ? (size_t)atoll(v) : (size_t)0;
+  }();
+  if (forced) return forced;
+  (void)fmt;
+  return 8;
 }
 
 syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx,
@@ -802,15 +932,24 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
   alignas(64) CUtensorMap map;
   memset(&map, 0, sizeof(map));
   if (i8 && !make_int8_map(&map, w, groups)) return SYN_ERR_UNSUPPORTED;
+  // few tokens (block formats): the swapped-operand kernel, tokens padded to
+  // a multiple of 16
+  static const int swap_max = [] {
+    const char* v = getenv("SYN_GEMM_SWAP_MAX");
+    return v ? atoi(v) : 32;
+  }();
+  const int npad =
+      (!i8 && (long long)m <= std::min(swap_max, 32)) ? (int)((m + 15) / 16 * 16) : 0;
   uint8_t* a = abuf;
-  float* sa = reinterpret_cast<float*>(abuf + (size_t)mtiles * BM * kcols * 16);
+  const int acols = i8 ? kcols : (kcols + 15) / 16 * 16;  // fp16: whole swizzled stages
+  float* sa = reinterpret_cast<float*>(abuf + (size_t)mtiles * BM * acols * 16);
   cudaError_t e;
   if (i8)
     e = launch_pdl2(k_prep_a_i8, dim3(mtiles * BM), dim3(256), 0, st, x, xq, sx, (long long)ldx,
                     (int)m, (int)w->k, kcols, a, sa);
   else
-    e = launch_pdl2(k_prep_a_f16, dim3(mtiles * BM), dim3(256), 0, st, x, (long long)ldx, (int)m,
-                    (int)w->k, kcols, a, sa);
+    e = launch_pdl2(k_prep_a_f16, dim3(npad ? npad : mtiles * BM), dim3(256), 0, st, x,
+                    (long long)ldx, (int)m, (int)w->k, kcols, a, sa, npad ? 2 * npad : BM, npad);
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_prep_a");
     return SYN_ERR_CUDA;
@@ -835,6 +974,13 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
   p.ldy = (long long)ldy;
   p.chunked = chunked;
   p.err = err;
+  static const int short_rows = [] {
+    const char* v = getenv("SYN_GEMM_SHORT_ROWS");
+    return v ? atoi(v) : 64;
+  }();
+  p.short_rows = short_rows;
+  p.npad = npad;
+  p.astg = (kcols + 15) / 16;
   switch (w->fmt) {
     case SYN_QFMT_INT8_KN: return launch_gemm_t<F_INT8>(p, map, mtiles, ntiles, st);
     case SYN_QFMT_Q4_0: return launch_gemm_t<F_Q4_0>(p, map, mtiles, ntiles, st);
