@@ -213,7 +213,9 @@ def run_decode(args, local_rank, dist, cpu_leg):
         "roofline": {"bound": "hbm", "achieved": round(bpt * n_dec / dec_s / 1e9, 1),
                      "peak": peak, "unit": "GB/s",
                      "frac": round(bpt * n_dec / dec_s / 1e9 / peak, 4), "peak_source": src},
-        "gpu_launches_per_token": 8 * cfg["architecture"]["num_layers"] + 3,
+        # per layer: QKV (norm fused), attention, O, gate/up (norm fused),
+        # SwiGLU, down; then embedding+norm, LM head (norm fused), argmax
+        "gpu_launches_per_token": 6 * cfg["architecture"]["num_layers"] + 3,
     }
     if cpu_leg:
         out["cpu_baseline"] = cpu_decode_sample(cfg, w, prompt)
@@ -362,6 +364,15 @@ def run_gemm_case(args):
     us = e0.elapsed_time(e1) * 1e3 / args.steps
     print(json.dumps({"gemm": args.gemm, "us": round(us, 2),
                       "tflops": round(2 * m * n * k / us / 1e6, 1)}), flush=True)
+
+
+def run_decode_only(args, local_rank):
+    """The config-1 decode leg alone (one process, no sweep, no CPU leg): the
+    command the decode-step launch list is taken from."""
+    import torch
+    torch.cuda.set_device(local_rank)
+    out = run_decode(args, local_rank, None, cpu_leg=False)
+    print(json.dumps({"decode": out}), flush=True)
 
 
 def run_synapse(args, rank, world, local_rank):
@@ -675,6 +686,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the model decode leg")
     ap.add_argument("--case", default=None, help="FMT:N:K -- time one GEMV only (profiling)")
     ap.add_argument("--gemm", default=None, help="FMT:M:N:K -- time one GEMM only (profiling)")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="run only the config-1 decode leg (profiling one decode step)")
     args = ap.parse_args()
     global CASE_FILTER
     CASE_FILTER = args.case
@@ -688,6 +701,8 @@ def main():
         args.warmup = 3
     if args.gemm:
         run_gemm_case(args)
+    elif args.decode_only:
+        run_decode_only(args, local_rank)
     elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
