@@ -531,31 +531,41 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t dcol = tbase + (chunked ? (uint32_t)(chunk & 1) * BN : 0u);
-        for (int bl = 0; bl < nbs; bl++) {
-          const int b = b0 + bl;
-          if constexpr (I8) {
+        // Descriptors are built once per stage and stepped by adding the
+        // operand offset (in 16-byte units) to their address field: the
+        // issuing thread shares its scheduler with busy dequant warps, so
+        // each MMA must cost it only a few instructions.
+        if constexpr (I8) {
+          const uint64_t da0 = sdesc(a_addr, 2048, 128), db0 = sdesc(b_addr, 2048, 128);
+#pragma unroll
+          for (int bl = 0; bl < S::KB; bl++) {
+            if (bl >= nbs) break;
             // one block = K of 32 int8 = one 128 x 128 x 32 MMA
+            const int b = b0 + bl;
             const bool first = chunked ? ((b & 15) == 0) : (b == 0);
-            mma<true>(dcol, sdesc(a_addr + bl * 2 * 2048, 2048, 128),
-                      sdesc(b_addr + bl * 2 * 2048, 2048, 128), first ? 0u : 1u);
-          } else if constexpr (SW) {
-            // weights (128 rows) x token rows (2 npad): two 128 x 2npad x 16 MMAs
-            const int rows = 2 * p.npad;
-            const uint32_t id = (1u << 4) | ((uint32_t)(rows >> 3) << 17) |
-                                ((uint32_t)(BM >> 4) << 24);
+            const uint64_t off = (uint64_t)(bl * 2 * 2048 / 16);
+            mma<true>(dcol, da0 + off, db0 + off, first ? 0u : 1u);
+          }
+        } else {
+          // weights (128 rows) x activations: 128 or 2 npad token rows (SW)
+          const int rows = SW ? 2 * p.npad : BM;
+          const uint32_t id = (1u << 4) | ((uint32_t)((SW ? rows : BN) >> 3) << 17) |
+                              ((uint32_t)(BM >> 4) << 24);
+          const uint64_t dw0 = sdesc_sw128(b_addr), dx0 = sdesc_sw128(a_addr);
+          const uint32_t w_atom = BN * 128 / 16, x_atom = (uint32_t)rows * 128 / 16;
+#pragma unroll
+          for (int bl = 0; bl < S::KB; bl++) {
+            if (bl >= nbs) break;
+#pragma unroll
             for (int kh = 0; kh < 2; kh++) {
-              const uint32_t ko = (bl & 1) * 64 + kh * 32;  // K offset inside the atom
-              mma_f16_id(dcol, sdesc_sw128(b_addr + (bl >> 1) * BN * 128 + ko),
-                         sdesc_sw128(a_addr + (bl >> 1) * rows * 128 + ko), id,
-                         (b == 0 && kh == 0) ? 0u : 1u);
-            }
-          } else {
-            // one block = K of 32 halves = two 128 x 128 x 16 MMAs
-            for (int kh = 0; kh < 2; kh++) {
-              const uint32_t ko = (bl & 1) * 64 + kh * 32;  // K offset inside the atom
-              mma<false>(dcol, sdesc_sw128(a_addr + (bl >> 1) * BM * 128 + ko),
-                         sdesc_sw128(b_addr + (bl >> 1) * BN * 128 + ko),
-                         (b == 0 && kh == 0) ? 0u : 1u);
+              const uint32_t ko = ((bl & 1) * 64 + kh * 32) / 16;  // K offset inside the atom
+              const uint64_t dw = dw0 + (uint64_t)((bl >> 1) * w_atom + ko);
+              const uint64_t dx = dx0 + (uint64_t)((bl >> 1) * x_atom + ko);
+              const uint32_t acc = (b0 + bl == 0 && kh == 0) ? 0u : 1u;
+              if constexpr (SW)
+                mma_f16_id(dcol, dw, dx, id, acc);  // A = weights, B = tokens
+              else
+                mma_f16_id(dcol, dx, dw, id, acc);  // A = tokens, B = weights
             }
           }
         }
