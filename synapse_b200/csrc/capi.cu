@@ -281,7 +281,7 @@ syn_status_t syn_cuda_qgemm_int8(size_t m, size_t n, size_t k, const int8_t* a, 
   w.k = k;
   w.kp = (k + 31) / 32 * 32;
   const size_t wbytes = align256((n + 31) / 32 * 32 * w.kp);
-  const bool gemm = m >= gemm_min_rows(w.fmt);
+  const bool gemm = m >= gemm_min_rows(w.fmt, n);
   const size_t abytes = gemm ? align256(gemm_a_bytes(w.fmt, m, w.kp)) : 0;
   CallScratch cs;
   syn_status_t s = cs.init(w.fmt, m, n, w.kp, wbytes + abytes, st);
@@ -416,7 +416,7 @@ syn_status_t syn_cuda_qmatmul(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w, c
   if (!g.ok) return SYN_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
   const int chunked = (w->fmt == SYN_QFMT_INT8_KN && m > 16) ? 1 : 0;
-  if (m >= gemm_min_rows(w->fmt)) {
+  if (m >= gemm_min_rows(w->fmt, w->n)) {
     syn_status_t s = grow(reinterpret_cast<void**>(&ctx->abuf), &ctx->abuf_bytes,
                           gemm_a_bytes(w->fmt, m, w->kp), st);
     if (s != SYN_OK) return s;
@@ -438,7 +438,7 @@ syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t* ctx, const syn_cuda_
   DeviceGuard g(w->device);
   if (!g.ok) return SYN_ERR_CUDA;
   cudaStream_t st = (cudaStream_t)stream;
-  if (m >= gemm_min_rows(w->fmt)) {
+  if (m >= gemm_min_rows(w->fmt, w->n)) {
     syn_status_t s = grow(reinterpret_cast<void**>(&ctx->abuf), &ctx->abuf_bytes,
                           gemm_a_bytes(w->fmt, m, w->kp), st);
     if (s != SYN_OK) return s;

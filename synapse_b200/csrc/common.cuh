@@ -3,6 +3,7 @@
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -83,6 +84,21 @@ __device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c) {
   int d;
   asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
+}
+
+// exp as the reference evaluates it for f32 (one double-precision exp,
+// rounded once); both the CPU oracle and these kernels use this definition.
+__device__ __forceinline__ float exp_f32(float x) { return (float)exp((double)x); }
+
+// One SwiGLU element i of a row whose first n4 = n - n % 4 elements are the
+// vector part: variant 0 = silu(g) * u with silu = g / (1 + exp(-g))
+// (quantization/lm/int8.rs:500-503, ops/activation.rs:30-32); variant 1 =
+// swigluFused (zig/src/ops/silu.zig:85-114): g * (1 / (1 + exp(-g))) * u on
+// the vector part, (g / (1 + exp(-g))) * u on the tail.
+__device__ __forceinline__ float swiglu_elem(float g, float u, int i, int n4, int variant) {
+  const float e = __fadd_rn(1.0f, exp_f32(-g));
+  if (variant == 1 && i < n4) return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, e)), u);
+  return __fmul_rn(__fdiv_rn(g, e), u);
 }
 
 // Streaming loads that bypass L1 allocation (weights are read once).

@@ -920,14 +920,21 @@ size_t gemm_a_bytes(int fmt, size_t m, size_t kp) {
   return mtiles * BM * kcols * 16 + mtiles * BM * sizeof(float) + 256;
 }
 
-size_t gemm_min_rows(int fmt) {
+size_t gemm_min_rows(int fmt, size_t n) {
   static const size_t forced = [] {
     const char* v = getenv("SYN_GEMM_MIN_ROWS");
     return v ? (size_t)atoll(v) : (size_t)0;
   }();
   if (forced) return forced;
   (void)fmt;
-  return 8;
+  // The GEMM runs one CTA per 128 weight rows over all of K, so with few
+  // row tiles it is latency-bound and the GEMV (all SMs, weights re-read
+  // from L2 per 4-row slice) is faster. Crossovers measured on B200: N =
+  // 2048 -> GEMV up to 32 rows; N = 4096 -> up to about 16; N = 14336 -> the
+  // GEMM from 8 rows.
+  if (n >= 8192) return 8;
+  if (n >= 4096) return 24;
+  return 40;
 }
 
 syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx,

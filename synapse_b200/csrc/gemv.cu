@@ -1003,6 +1003,7 @@ int tma_occupancy(int fmt, int mt, int rg, size_t smem);
 size_t stage_bytes(int fmt);
 int stage_depth(int fmt);
 
+// xs_bytes: the fused norm's row staged in shared memory (all of K).
 Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
   Plan pl{};
   pl.groups = (int)((n + 31) / 32);
@@ -1021,13 +1022,20 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
   // a split CTA would stream fewer than 64 blocks)
   const int min_split_blocks = tune("SYN_GEMV_MIN_SPLIT_BLOCKS", 64);
   while (nks > 1 && pl.nblk / nks < min_split_blocks) nks--;
-  int kr = (pl.nblk + nks - 1) / nks;
-  kr = (kr + SB - 1) / SB * SB;
-  // shared memory bound (activations of MT rows)
   const int abb = fmt == F_INT8 ? 32 : 80;
-  while ((size_t)pl.mt * kr * abb > 96 * 1024 && kr > SB) kr = ((kr + 1) / 2 + SB - 1) / SB * SB;
-  pl.kr = kr;
-  pl.nks = (pl.nblk + kr - 1) / kr;
+  auto set_split = [&](int splits) {
+    int kr = (pl.nblk + splits - 1) / splits;
+    kr = (kr + SB - 1) / SB * SB;
+    // shared memory bound (activations of MT rows)
+    while ((size_t)pl.mt * kr * abb > 96 * 1024 && kr > SB) kr = ((kr + 1) / 2 + SB - 1) / SB * SB;
+    pl.kr = kr;
+    pl.nks = (pl.nblk + kr - 1) / kr;
+    const int ncc = kr / 16 + 1;
+    pl.act_smem =
+        (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
+    pl.xs_bytes = xs_bytes;
+  };
+  set_split(nks);
   // Row-group pairs (block formats, M = 1, K not split): two groups share
   // each activation block, which saves about a third of the instructions per
   // weight; taken when the busiest SM's load goes down (per-SM CTA counts).
@@ -1038,9 +1046,6 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
     const double t2 = 2.0 * 0.7 * (double)(((pl.groups + 1) / 2 + sms - 1) / sms);
     if (t2 < t1) pl.rg = 2;
   }
-  const int ncc = kr / 16 + 1;
-  pl.act_smem = (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
-  pl.xs_bytes = xs_bytes;
   pl.ns = 0;
   if (fmt != F_Q4_0RAW) {
     // All CTAs resident at once: row pairs only while two CTAs still fit on
@@ -1051,16 +1056,22 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
       return tma_occupancy(fmt, pl.mt, rg, tma_smem(pl, fmt, rg, ns));
     };
     if (pl.rg == 2 && occ(2, nsmax) < 2) pl.rg = 1;
-    const long long ctas =
-        (long long)((pl.groups + pl.rg - 1) / pl.rg) * pl.nks * mslices;
-    int ns = nsmax;
-    if (ctas > (long long)sms * occ(pl.rg, ns)) {
-      for (int t = nsmax - 1; t >= 2; t--)
-        if (ctas <= (long long)sms * occ(pl.rg, t)) {
-          ns = t;
-          break;
-        }
+    // deepest ring that keeps the grid in one wave; failing that, fewer K
+    // splits (registers, not shared memory, may be what limits residency)
+    auto pick_ns = [&]() {
+      const long long ctas = (long long)((pl.groups + pl.rg - 1) / pl.rg) * pl.nks * mslices;
+      for (int t = nsmax; t >= 2; t--)
+        if (ctas <= (long long)sms * occ(pl.rg, t)) return t;
+      return 0;
+    };
+    int ns = pick_ns();
+    while (ns == 0 && pl.nks > 1) {
+      const int before = pl.nks;
+      set_split(before - 1);
+      if (pl.nks >= before) break;  // the shared-memory bound split it again
+      ns = pick_ns();
     }
+    if (ns == 0) ns = nsmax;
     const int forced = tune("SYN_GEMV_NS", 0);
     pl.ns = forced >= 2 && forced <= nsmax ? forced : ns;
   }

@@ -114,10 +114,10 @@ syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, f
 syn_status_t ensure_scratch(syn_cuda_ctx_s* ctx, const syn_cuda_weight_s* w, size_t m,
                             cudaStream_t st);
 
-// Tensor-core GEMM (gemm.cu) for m >= gemm_min_rows(fmt) activation rows
-// (fewer rows run the GEMV). abuf: scratch of gemm_a_bytes(fmt, m, kp) bytes
-// for the prepared activations.
-size_t gemm_min_rows(int fmt);
+// Tensor-core GEMM (gemm.cu) for m >= gemm_min_rows(fmt, n) activation rows
+// of an n-row weight (fewer rows run the GEMV). abuf: scratch of
+// gemm_a_bytes(fmt, m, kp) bytes for the prepared activations.
+size_t gemm_min_rows(int fmt, size_t n);
 size_t gemm_a_bytes(int fmt, size_t m, size_t kp);
 syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx,
                           const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,

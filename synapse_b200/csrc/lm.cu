@@ -33,7 +33,6 @@
 namespace syn {
 namespace {
 
-__device__ __forceinline__ float exp_f32(float x) { return (float)exp((double)x); }
 
 // one step of a sum-of-products chain: fused (@mulAdd) or two roundings
 __device__ __forceinline__ float chain(bool fused, float a, float b, float acc) {
@@ -987,14 +986,7 @@ __global__ void k_swiglu(const float* __restrict__ gate, const float* __restrict
   for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
        t += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(t / n), i = (int)(t - (long long)r * n);
-    const float g = gate[r * ld_in + i], u = up[r * ld_in + i];
-    const float e = __fadd_rn(1.0f, exp_f32(-g));
-    float y;
-    if (variant == 1 && i < n4)
-      y = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, e)), u);
-    else
-      y = __fmul_rn(__fdiv_rn(g, e), u);
-    out[r * ldo + i] = y;
+    out[r * ldo + i] = swiglu_elem(gate[r * ld_in + i], up[r * ld_in + i], i, n4, variant);
   }
 }
 

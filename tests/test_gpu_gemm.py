@@ -16,7 +16,10 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
 
+# Below 40 rows, weights of fewer than 4096 rows (24 rows: 8192) run the GEMV;
+# the n >= 8192 cases keep the tensor-core GEMM covered at small M.
 @pytest.mark.parametrize("m,n,k", [(8, 64, 64), (16, 3072, 1024), (17, 128, 1536), (33, 200, 520),
+                                   (8, 8192, 512), (17, 8192, 512), (33, 8224, 256),
                                    (128, 1024, 4096), (130, 96, 2048), (512, 512, 1024)])
 def test_gemm_int8_bit_exact(ctx, m, n, k):
     import synapse_b200 as sb
@@ -35,6 +38,7 @@ def test_gemm_int8_bit_exact(ctx, m, n, k):
 
 @pytest.mark.parametrize("fmt", ["Q4_0", "Q8_0", "Q4_K", "Q6_K"])
 @pytest.mark.parametrize("m,n,k", [(8, 256, 512), (9, 4096, 512), (16, 1024, 1024),
+                                   (9, 8192, 512), (24, 8320, 256), (48, 8192, 512),
                                    (48, 384, 1024), (64, 160, 2048), (65, 256, 512),
                                    (128, 3072, 2048), (300, 100, 1024), (512, 1024, 4096)])
 def test_gemm_block_formats_within_tol(ctx, fmt, m, n, k):
