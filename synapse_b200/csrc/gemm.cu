@@ -1,13 +1,17 @@
 // gemm.cu -- prefill / batched path: quantized matmul on the 5th-generation
 // tensor cores (tcgen05.mma, accumulators in tensor memory).
 //
-//   y[M, N] = x[M, K] * W[N, K]^T, for M >= 8 (tokens), all five formats.
+//   y[M, N] = x[M, K] * W[N, K]^T for batched rows (tokens), all five
+//   formats; gemm_min_rows() decides, per weight row count, from which M the
+//   GEMM runs instead of the GEMV.
 //
-// Operands (shared memory, K-major, no swizzle: core matrices of 8 rows x
-// 16 bytes; a [rows][16 B] column of 128 rows is 2 KB).
+// Operands in shared memory are K-major.
+//   INT8 uses the plain layout (core matrices of 8 rows x 16 bytes; a
+//   [rows][16 B] column of 128 rows is 2 KB). fp16 (block formats) uses the
+//   128-byte-swizzled layout: 1024-byte atoms of 8 rows x 128 B (64 halves of
+//   K), chunk j of row r stored at j ^ (r & 7), two atom columns per stage.
 //   A (activations) is prepared by k_prep_a_* into global memory already in
-//   that layout, [m-tile][16-byte K column][128 rows][16 B], so one stage of
-//   A is one contiguous run for a 1-D bulk copy.
+//   the stage layout, so one stage of A is one contiguous 1-D bulk copy.
 //     INT8 weights: A = int8 codes of the reference's per-row quantisation
 //       (quantize.zig:12-47), bit-exact; products are exact int32
 //       (kind::i8). M <= 16: one int32 accumulator over K, then
@@ -15,18 +19,21 @@
 //       reference's per-512-K-chunk epilogue C += float(chunk) * sa * sb in
 //       chunk order (qmatmul.zig:68-98), every op rounded -- bit-exact for
 //       every M.
-//     Block formats: A = fp16(x * 2^-s) with a power-of-two scale per row (no
-//       fp16 overflow; undone exactly in the epilogue); the weights are dequantised in shared
-//       memory with the reference's formulas (gguf.rs:255-487), rounded to
-//       fp16 and multiplied with kind::f16, fp32 accumulation.
+//     Block formats: A = fp16(x * 2^-s) with a power-of-two scale per row
+//       (no fp16 overflow; undone exactly in the epilogue); the weights are
+//       dequantised in shared memory with the reference's formulas
+//       (gguf.rs:255-487), rounded to fp16 and multiplied with kind::f16,
+//       fp32 accumulation.
 //   B (weights) comes from the row-interleaved repack (repack.cu). For INT8
 //   a 4-D tensor map (TMA) gathers the 4 row groups' tiles of a stage into
 //   [16-byte K column][128 rows][16 B]; block formats bring the raw tiles in
-//   with 1-D bulk copies and 8 warps write the dequantised fp16 tiles in the
-//   same 128-row layout. Each K step is then one 128 x 128 MMA.
+//   with 1-D bulk copies and the worker warps write the dequantised fp16
+//   tiles. Each K step is one 128 x 128 x 16 (fp16) or x 32 (int8) MMA.
+//   Up to 32 tokens (block formats) the roles swap (SW): the 128 weight rows
+//   are the MMA's M and the tokens, each as an fp16 hi and lo row, its N.
 //
-// CTA = 10 warps: warp 0 issues the copies into a smem ring; warp 1 owns
-// tensor memory and one of its threads issues the MMAs; warps 2-9
+// CTA = 18 warps: warp 0 issues the copies into a smem ring; warp 1 owns
+// tensor memory and one of its threads issues the MMAs; warps 2-17
 // dequantise B (block formats) and run the epilogue (tensor memory ->
 // registers -> y). Tile: 128 tokens x 128 weight rows. Every wait is bounded
 // and reports SYN_ERR_TIMEOUT instead of hanging.
@@ -583,7 +590,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int c = chunk; c < (chunked ? nchunks : 1); c++) mbar_arrive(&accfull[c & 1]);
     }
   } else {
-    // ---------------- warps 2-9: dequantise B / epilogue ----------------
+    // ---------------- warps 2-17: dequantise B / epilogue ---------------
     const int ew = warp - 2;          // 0..7
     const int quarter = warp & 3;     // tensor memory lane quarter of this warp
     const int chalf = ew >> 2;        // epilogue column share: CGW groups of 32 columns

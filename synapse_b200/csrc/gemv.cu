@@ -19,6 +19,11 @@
 // CTA to arrive for a row group (atomic counter, reset by that CTA) sums them
 // in K order. Results are deterministic.
 //
+// The plan keeps the whole grid resident in one wave: block formats at M = 1
+// pair two row groups per CTA (sharing each activation block) only while two
+// such CTAs fit on an SM, the ring depth (2-4 stages) is the deepest at which
+// every CTA fits, and failing that K is split fewer times.
+//
 // The raw-layout Q4_0 GEMV (syn_q4_0_gemv, 18-byte blocks, 2-byte aligned)
 // cannot be bulk-copied; k_qgemv streams it with direct loads instead.
 //
