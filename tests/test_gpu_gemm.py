@@ -64,6 +64,27 @@ def test_gemm_block_formats_within_tol(ctx, fmt, m, n, k):
     w.close()
 
 
+@pytest.mark.parametrize("fmt", ["Q4_0", "Q8_0"])
+@pytest.mark.parametrize("m,n,k", [(20, 8192, 544), (64, 256, 544), (130, 200, 96)])
+def test_gemm_odd_block_count(ctx, fmt, m, n, k):
+    """K with an odd number of 32-element blocks: the last stage fills half
+    of its 128-byte swizzle atom (swapped kernel, short and full 128-row
+    tiles)."""
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    rng = np.random.default_rng(m + 3 * n + k)
+    f = sb.QFormat[fmt]
+    blocks, _ = synth.gen_weight(f, n, k, rng)
+    x = synth.gen_activations(m, k, rng)
+    w = sb.QuantizedWeight(ctx, f, blocks, n, k)
+    y = w.matmul(torch.from_numpy(x).cuda()).cpu().numpy().reshape(m, n)
+    st, yo = oracle.block_matmul(fmt, m, n, k, x, blocks)
+    assert st == 0
+    yo = yo.reshape(m, n)
+    assert max(max_rel_err(y[i], yo[i]) for i in range(m)) <= TOL
+    w.close()
+
+
 def test_gemm_error_word_clear(ctx):
     import ctypes
     import synapse_b200 as sb
