@@ -1161,15 +1161,19 @@ int tma_occ_f(int mt, int rg, size_t smem) {
 
 // CTAs of k_qgemv_tma resident per SM at `smem` bytes (cached per device).
 int tma_occupancy(int fmt, int mt, int rg, size_t smem) {
+  struct Key {
+    int fmt, mt, rg, dev;
+    size_t smem;
+    int occ;
+  };
   static std::mutex mu;
-  static std::vector<std::pair<std::vector<long long>, int>> cache;
+  static std::vector<Key> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const std::vector<long long> key{fmt, mt, rg, (long long)smem, dev};
   {
     std::lock_guard<std::mutex> g(mu);
-    for (auto& kv : cache)
-      if (kv.first == key) return kv.second;
+    for (const Key& k : cache)
+      if (k.fmt == fmt && k.mt == mt && k.rg == rg && k.dev == dev && k.smem == smem) return k.occ;
   }
   int occ = 1;
   switch (fmt) {
@@ -1181,7 +1185,7 @@ int tma_occupancy(int fmt, int mt, int rg, size_t smem) {
   }
   std::lock_guard<std::mutex> g(mu);
   if (cache.size() > 4096) cache.clear();
-  cache.emplace_back(key, occ);
+  cache.push_back(Key{fmt, mt, rg, dev, smem, occ});
   return occ;
 }
 
