@@ -337,6 +337,87 @@ def cpu_decode_sample(cfg, w, prompt, budget_s=20.0):
                       f"{n} decode steps, 1 thread"}
 
 
+def _timed_generate(m, steps, batch):
+    """Device-chained greedy steps (syn_cuda_generate); the first call
+    captures the step graph and is not timed."""
+    import torch
+    m.generate(2, batch=batch)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    m.generate(steps, batch=batch)
+    torch.cuda.synchronize()
+    return time.perf_counter() - t0
+
+
+def run_configs(local_rank):
+    """Configs 3 and 5 of the baseline (random-init weights, seeded random
+    prompts), one GPU:
+    - 3: the LLaMA-3.2-1B shape with Q4_K weights; a 512-token prompt, then
+      256 greedy decode steps at batch 1 and at batch 8 (8 prompts);
+    - 5: the Qwen3-0.6B shape with Q8_0 weights serving 32 sequences, prompt
+      lengths uniform in [128, 2048], then 256 decode steps each."""
+    import torch
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    ctx = sb.Context(local_rank)
+    out = {}
+    for key, name, fmt in (("llama_3_2_1b_q4_k", "llama-3.2-1b", "Q4_K"),
+                           ("qwen3_0p6b_q8_0_serving", "qwen3-0.6b", "Q8_0")):
+        cfg = synth.lm_config(name)
+        a = cfg["architecture"]
+
+        def gpu_dequant(f, b, n, a=a):
+            w = sb.QuantizedWeight(ctx, f, b, a["vocab_size"], a["hidden_size"])
+            o = w.dequant()
+            w.close()
+            return o
+        w = synth.gen_lm_weights(cfg, fmt, seed=1234, dequant=gpu_dequant)
+        rng = np.random.default_rng(1234)
+        steps = 256
+        if key.startswith("llama"):
+            P, B = 512, 8
+            m = sb.Model(ctx, cfg, w, P + steps + 8, max_batch=B)
+            del w
+            prompts = [rng.integers(0, a["vocab_size"], P).tolist() for _ in range(B)]
+            m.forward_prefill(prompts[0], seq=0, want_logits=False)  # warm-up
+            m.reset()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            m.forward_prefill(prompts[0], seq=0, want_logits=False)
+            torch.cuda.synchronize()
+            pre = time.perf_counter() - t0
+            t1 = _timed_generate(m, steps - 3, 1)
+            m.reset()
+            for i in range(B):
+                m.forward_prefill(prompts[i], seq=i, want_logits=False)
+            t8 = _timed_generate(m, steps - 3, B)
+            out[key] = {"prompt_tokens": P, "prefill_tok_s": round(P / pre, 1),
+                        "decode_tok_s_batch1": round((steps - 3) / t1, 1),
+                        "decode_tok_s_batch8": round(B * (steps - 3) / t8, 1),
+                        "timed_steps": steps - 3}
+        else:
+            B = 32
+            m = sb.Model(ctx, cfg, w, 2048 + steps + 8, max_batch=B)
+            del w
+            lens = rng.integers(128, 2049, B)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for i in range(B):
+                m.forward_prefill(rng.integers(0, a["vocab_size"], int(lens[i])).tolist(), seq=i,
+                                  want_logits=False)
+            torch.cuda.synchronize()
+            pre = time.perf_counter() - t0
+            td = _timed_generate(m, steps - 3, B)
+            out[key] = {"sequences": B, "prompt_tokens_total": int(lens.sum()),
+                        "prefill_tok_s": round(float(lens.sum()) / pre, 1),
+                        "decode_tok_s": round(B * (steps - 3) / td, 1),
+                        "ms_per_step": round(td / (steps - 3) * 1e3, 3),
+                        "timed_steps": steps - 3}
+        m.close()
+    ctx.close()
+    return out
+
+
 def run_gemm_case(args):
     """--gemm FMT:M:N:K: times one prefill matmul (tcgen05 GEMM) on cuda:0 and
     prints its TFLOP/s (profiling aid; not the benchmark line)."""
@@ -520,6 +601,9 @@ def run_synapse(args, rank, world, local_rank):
         decode = run_decode(args, local_rank, dist,
                             cpu_leg=rank == 0 and world == 1 and not args.no_cpu_baseline)
         tp_decode = run_tp_decode(args, rank, world, local_rank, dist)
+    configs = None
+    if not args.no_decode and world == 1 and not args.no_configs:
+        configs = run_configs(local_rank)
 
     if rank == 0:
         line = {
@@ -547,6 +631,7 @@ def run_synapse(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "decode": decode,
             "tp_decode": tp_decode,
+            "configs_3_5": configs,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -686,6 +771,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the model decode leg")
     ap.add_argument("--case", default=None, help="FMT:N:K -- time one GEMV only (profiling)")
     ap.add_argument("--gemm", default=None, help="FMT:M:N:K -- time one GEMM only (profiling)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the config-3/5 decode legs (LLaMA Q4_K batch 1/8, Qwen3 Q8_0 serving)")
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the config-1 decode leg (profiling one decode step)")
     args = ap.parse_args()
