@@ -193,9 +193,48 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit columns; thread i writes lane (base + i).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// kind::f16 MMA with A from tensor memory (128 lanes = rows of A, K along the
+// columns, two halves per 32-bit column) and B from shared memory.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b,
+                                           uint32_t id, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(id), "r"(accumulate));
+}
+
 // ---------------------------------------------------------------------------
 // Per-format stage geometry
 // ---------------------------------------------------------------------------
+// Raw block-format bytes of one 32-row group for a stage of KBX blocks: the
+// q tiles, then per-block aux arrays, then one super-block tile (Q4_K
+// header, Q6_K scale; a stage never crosses a 256-element super-block).
+template <int FMT, int KBX>
+struct RawG {
+  static constexpr int QT = (FMT == F_Q8_0) ? 1024 : 512;
+  static constexpr int DT = (FMT == F_Q4_0 || FMT == F_Q8_0) ? 64 : 0;
+  static constexpr int QHT = (FMT == F_Q6_K) ? 256 : 0;
+  static constexpr int SCT = (FMT == F_Q6_K) ? 64 : 0;
+  static constexpr int HT = (FMT == F_Q4_K) ? 512 : 0;
+  static constexpr int D6T = (FMT == F_Q6_K) ? 64 : 0;
+  static constexpr int G_Q = 0;
+  static constexpr int G_D = G_Q + KBX * QT;
+  static constexpr int G_QH = G_D + KBX * DT;
+  static constexpr int G_SC = G_QH + KBX * QHT;
+  static constexpr int G_H = G_SC + KBX * SCT;
+  static constexpr int G_D6 = G_H + HT;
+  static constexpr int G_BYTES = (G_D6 + D6T + 127) / 128 * 128;
+};
 // SW (few tokens, block formats): the operands swap roles -- the 128
 // dequantised weight rows are the MMA's M and the tokens its N -- so a
 // stage's activation tile is small and the ring can be deeper. Each token
@@ -266,13 +305,13 @@ __device__ __forceinline__ bool bwait(const GemmParams& p, uint64_t* bar, uint32
   return false;
 }
 
-// Dequantises block bl of one row group's raw stage (thread = row l of the
-// group) into fp16: 4 K columns of 8 halves, written as rows of the 128-row
-// tile. Reference formulas: gguf.rs:255-487.
-template <int FMT>
-__device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, int l, int row,
-                                              int bl, int b) {
-  using S = GS<FMT>;
+// Dequantises block bl of one row group's raw stage of KBX blocks (thread =
+// row l of the group) into 32 fp16 values in K order, packed in pairs:
+// o[i] = (value 2i, value 2i+1). Reference formulas: gguf.rs:255-487.
+template <int FMT, int KBX>
+__device__ __forceinline__ void dequant_regs(const uint8_t* raw, int l, int bl, int b,
+                                             uint32_t (&o)[16]) {
+  using S = RawG<FMT, KBX>;
   if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0) {
     // fp16 arithmetic, same values: (q - 8) and q are exact in fp16, d is an
     // fp16 value, and the product of two fp16 values rounded once to fp16
@@ -284,7 +323,6 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
     const __half2 d2 = __half2half2(__ushort_as_half(dbits));
     const bool sub = (dbits & 0x7C00u) == 0;
     const __half2 half2_05 = __float2half2_rn(0.5f);
-    uint32_t o[16];
     if constexpr (FMT == F_Q4_0) {
       const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
       const uint32_t w[4] = {q.x, q.y, q.z, q.w};
@@ -313,32 +351,10 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
         o[i] = *reinterpret_cast<const uint32_t*>(&h);
       }
     }
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-      *reinterpret_cast<uint4*>(out + sw128_off(bl * 4 + c, row, BN)) =
-          make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
     return;
-  }
+  } else {
   float v[32];
-  if constexpr (FMT == F_Q4_0) {
-    const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
-    const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-      v[2 * i] = __fmul_rn(dd, i2f_small((int)(byte & 15) - 8));
-      v[2 * i + 1] = __fmul_rn(dd, i2f_small((int)(byte >> 4) - 8));
-    }
-  } else if constexpr (FMT == F_Q8_0) {
-    const uint4 q0 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024)[l];
-    const uint4 q1 = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 1024 + 512)[l];
-    const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D + bl * 64)[l]);
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-    for (int i = 0; i < 32; i++)
-      v[i] = __fmul_rn(dd, i2f_small((int)(int8_t)((w[i >> 2] >> (8 * (i & 3))) & 0xFF)));
-  } else if constexpr (FMT == F_Q4_K) {
+  if constexpr (FMT == F_Q4_K) {
     const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
     const uint4 h = reinterpret_cast<const uint4*>(raw + S::G_H)[l];
     const int s = b & 7;
@@ -383,18 +399,24 @@ __device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, 
     }
   }
 #pragma unroll
-  for (int c = 0; c < 4; c++) {  // paired f32 -> f16 conversions (round to nearest)
-    uint4 o;
-    const __half2 h0 = __floats2half2_rn(v[8 * c + 0], v[8 * c + 1]);
-    const __half2 h1 = __floats2half2_rn(v[8 * c + 2], v[8 * c + 3]);
-    const __half2 h2 = __floats2half2_rn(v[8 * c + 4], v[8 * c + 5]);
-    const __half2 h3 = __floats2half2_rn(v[8 * c + 6], v[8 * c + 7]);
-    o.x = *reinterpret_cast<const uint32_t*>(&h0);
-    o.y = *reinterpret_cast<const uint32_t*>(&h1);
-    o.z = *reinterpret_cast<const uint32_t*>(&h2);
-    o.w = *reinterpret_cast<const uint32_t*>(&h3);
-    *reinterpret_cast<uint4*>(out + sw128_off(bl * 4 + c, row, BN)) = o;
+  for (int i = 0; i < 16; i++) {  // paired f32 -> f16 conversions (round to nearest)
+    const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    o[i] = *reinterpret_cast<const uint32_t*>(&h);
   }
+  }
+}
+
+// dequant_regs into the swizzled 128-row fp16 tile in shared memory: the 4
+// K columns (8 halves each) of block bl, row `row`.
+template <int FMT>
+__device__ __forceinline__ void dequant_block(const uint8_t* raw, uint8_t* out, int l, int row,
+                                              int bl, int b) {
+  uint32_t o[16];
+  dequant_regs<FMT, GS<FMT>::KB>(raw, l, bl, b, o);
+#pragma unroll
+  for (int c = 0; c < 4; c++)
+    *reinterpret_cast<uint4*>(out + sw128_off(bl * 4 + c, row, BN)) =
+        make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
 }
 
 template <int FMT, bool SW = false>
@@ -723,6 +745,205 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// k_qgemm_tm: block formats, more than 32 tokens. The dequantised weights go
+// to tensor memory instead of shared memory: a dequant thread owns one weight
+// row, which is one tensor-memory lane, and writes its 32 fp16 values of a
+// block with tcgen05.st. The MMA reads them as its A operand (M = 128 weight
+// rows) and the token tile (N = up to 256 tokens, swizzled K-major) from
+// shared memory as B. Shared memory then carries only the TMA traffic and the
+// token-operand reads, instead of also the dequantised tile's writes and
+// reads.
+//   stage: KB = 2 blocks (64 K) = one 128-byte swizzle atom column of tokens
+//   tensor memory: accumulator columns [0, 256) (lane = weight row, column =
+//   token); NA weight buffers of 32 columns (64 halves) from column 256.
+// ---------------------------------------------------------------------------
+template <int FMT>
+struct TM {
+  static constexpr int KB = 2;
+  using R = RawG<FMT, KB>;
+  static constexpr int X_BYTES = 256 * 128;  // up to 256 token rows x 128 B
+  static constexpr int RAW_BYTES = NG * R::G_BYTES;
+  static constexpr int STAGE_BYTES = (X_BYTES + RAW_BYTES + 1023) / 1024 * 1024;
+  static constexpr int NS_FIT = 230400 / STAGE_BYTES;
+  static constexpr int NS = NS_FIT < 6 ? NS_FIT : 6;
+  static constexpr int SMEM = NS * STAGE_BYTES;
+  static constexpr int NA = 4;               // weight buffers in tensor memory
+  static constexpr uint32_t A_COL0 = 256;    // first weight-buffer column
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int TN = 256;             // tokens per tile (MMA N, at most)
+};
+
+template <int FMT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_qgemm_tm(const GemmParams p) {
+  using S = TM<FMT>;
+  using R = typename S::R;
+  static_assert(FMT != F_INT8, "block formats");
+  extern __shared__ __align__(1024) uint8_t sm[];
+  __shared__ __align__(8) uint64_t full[S::NS], empty[S::NS];
+  __shared__ __align__(8) uint64_t afull[S::NA], aempty[S::NA], accfull;
+  __shared__ uint32_t tmem_base_sh;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x, nt = blockIdx.y;
+  const int ntok = p.npad;  // token rows of a tile: min(256, tokens rounded up to 16)
+  const int nst = (p.nblk + S::KB - 1) / S::KB;
+  constexpr int DQ = 8;     // dequant warps (2 per tensor-memory lane quarter)
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::NS; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + DQ);  // MMA commit + dequant warps
+    }
+    for (int i = 0; i < S::NA; i++) {
+      mbar_init(&afull[i], DQ);
+      mbar_init(&aempty[i], 1);
+    }
+    mbar_init(&accfull, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tmem_base_sh)),
+                 "r"(S::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base_sh;
+  griddep_wait();  // the token tile and sa come from the kernel before
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int ngr = 0;
+      for (int gi = 0; gi < NG; gi++)
+        if (nt * NG + gi < p.groups) ngr++;
+      for (int s = 0; s < nst; s++) {
+        const int slot = s % S::NS;
+        if (s >= S::NS && !bwait(p, &empty[slot], ((s / S::NS) - 1) & 1)) break;
+        const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
+        uint8_t* st = sm + slot * S::STAGE_BYTES;
+        uint8_t* raw = st + S::X_BYTES;
+        const uint32_t x_bytes = (uint32_t)ntok * 128;
+        mbar_expect_tx(&full[slot],
+                       x_bytes + ngr * (nbs * (R::QT + R::DT + R::QHT + R::SCT) + R::HT + R::D6T));
+        // tokens: [m-tile][stage][ntok rows][128 B], one copy
+        bulk_g2s(st, p.a + ((size_t)mt * p.astg + s) * x_bytes, x_bytes, &full[slot]);
+        for (int gi = 0; gi < ngr; gi++) {
+          const size_t g = (size_t)nt * NG + gi;
+          uint8_t* gr = raw + gi * R::G_BYTES;
+          const size_t t0 = g * p.nblk + b0;
+          bulk_g2s(gr + R::G_Q, p.q + t0 * R::QT, nbs * R::QT, &full[slot]);
+          if constexpr (R::DT)
+            bulk_g2s(gr + R::G_D, reinterpret_cast<const uint8_t*>(p.d) + t0 * 64, nbs * 64,
+                     &full[slot]);
+          if constexpr (R::QHT) {
+            bulk_g2s(gr + R::G_QH, p.qh + t0 * 256, nbs * 256, &full[slot]);
+            bulk_g2s(gr + R::G_SC, reinterpret_cast<const uint8_t*>(p.sc) + t0 * 64, nbs * 64,
+                     &full[slot]);
+          }
+          if constexpr (R::HT)
+            bulk_g2s(gr + R::G_H, p.hdr + (g * p.nsb + b0 / 8) * 512, 512, &full[slot]);
+          if constexpr (R::D6T)
+            bulk_g2s(gr + R::G_D6,
+                     reinterpret_cast<const uint8_t*>(p.d) + (g * p.nsb + b0 / 8) * 64, 64,
+                     &full[slot]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t id = (1u << 4) | ((uint32_t)(ntok >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      for (int s = 0; s < nst; s++) {
+        const int slot = s % S::NS, buf = s % S::NA;
+        if (!bwait(p, &full[slot], (s / S::NS) & 1)) break;
+        if (!bwait(p, &afull[buf], (s / S::NA) & 1)) break;
+        tc_fence_after();
+        const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
+        const uint64_t dx0 = sdesc_sw128(smem_u32(sm + slot * S::STAGE_BYTES));
+        const uint32_t ta = tbase + S::A_COL0 + (uint32_t)buf * 32;
+#pragma unroll
+        for (int bl = 0; bl < S::KB; bl++) {
+          if (bl >= nbs) break;
+#pragma unroll
+          for (int kh = 0; kh < 2; kh++) {
+            // K offset kh*16 + bl*32 halves: 8 columns of A, 32 bytes of the atom
+            mma_f16_ts(tbase, ta + (uint32_t)(bl * 16 + kh * 8),
+                       dx0 + (uint64_t)((bl * 64 + kh * 32) / 16), id,
+                       (b0 + bl == 0 && kh == 0) ? 0u : 1u);
+          }
+        }
+        mma_commit(&empty[slot]);
+        mma_commit(&aempty[buf]);
+      }
+      mma_commit(&accfull);
+    }
+  } else {
+    // ---------------- warps 2-17: dequantise into tensor memory / epilogue ----------------
+    const int ew = warp - 2;         // 0..15
+    const int quarter = warp & 3;    // tensor-memory lane quarter = row group of the tile
+    const uint32_t tq = tbase + ((uint32_t)(quarter * 32) << 16);
+    if (ew < DQ) {
+      const int bl = ew >> 2;        // block of the stage this warp dequantises
+      const bool gvalid = nt * NG + quarter < p.groups;
+      for (int s = 0; s < nst; s++) {
+        const int slot = s % S::NS, buf = s % S::NA;
+        const bool ok1 = bwait(p, &full[slot], (s / S::NS) & 1);
+        const bool ok2 = s < S::NA || bwait(p, &aempty[buf], ((s / S::NA) - 1) & 1);
+        const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
+        // tcgen05.st is warp-wide: the whole warp decides together
+        if (__all_sync(0xffffffffu, ok1 && ok2) && gvalid && bl < nbs) {
+          const uint8_t* raw = sm + slot * S::STAGE_BYTES + S::X_BYTES + quarter * R::G_BYTES;
+          uint32_t o[16];
+          dequant_regs<FMT, S::KB>(raw, lane, bl, b0 + bl, o);
+          tmem_st16(tq + S::A_COL0 + (uint32_t)buf * 32 + (uint32_t)bl * 16, o);
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&afull[buf]);
+          mbar_arrive(&empty[slot]);
+        }
+      }
+    }
+    // epilogue: lane = weight row, column = token; warp column share
+    // [64 cs, 64 cs + 64)
+    bwait(p, &accfull, 0);
+    tc_fence_after();
+    const int cs = ew >> 2;
+    const int n = nt * BN + quarter * 32 + lane;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int c0 = cs * 64 + h * 32;
+      if (c0 >= ntok) break;  // uniform across the warp
+      uint32_t r[32];
+      tmem_ld32(tq + (uint32_t)c0, r);
+      if (n < p.n) {
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+          const int t = mt * S::TN + c0 + j;
+          if (c0 + j < ntok && t < p.m)
+            p.y[(long long)t * p.ldy + n] = __fmul_rn(__uint_as_float(r[j]), p.sa[t]);
+        }
+      }
+    }
+  }
+  griddep_launch();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase),
+                 "r"(S::TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // A preparation: canonical K-major tiles [m-tile][16-byte column][128][16 B]
 // ---------------------------------------------------------------------------
 // INT8: per-row quantisation (quantize.zig:12-47) or copy of given codes.
@@ -779,8 +1000,10 @@ __global__ void __launch_bounds__(256) k_prep_a_i8(const float* __restrict__ x,
   }
 }
 
-// Block formats (rows_pad rows per tile: 128, or 2 npad for the swapped
-// small-M kernel, whose lo_off = npad rows further hold x - fp16(x)):
+// Block formats (rows_pad rows per tile: 128; 2 npad for the swapped
+// small-M kernel, whose lo_off = npad rows further hold x - fp16(x); the
+// tile's token count for k_qgemm_tm; cps = 16-byte columns per stage: 16,
+// or 8 for k_qgemm_tm):
 // fp16(x * 2^-s) per row, with the power of two s chosen so
 // that the row's largest magnitude lands in [2^14, 2^15): no fp16 overflow
 // and full fp16 precision whatever the activations' range. The scaling is
@@ -788,7 +1011,8 @@ __global__ void __launch_bounds__(256) k_prep_a_i8(const float* __restrict__ x,
 __global__ void __launch_bounds__(256) k_prep_a_f16(const float* __restrict__ x, long long ldx,
                                                     int m, int k, int kcols,
                                                     uint8_t* __restrict__ a,
-                                                    float* __restrict__ sa, int rows_pad, int lo_off) {
+                                                    float* __restrict__ sa, int rows_pad, int lo_off,
+                                                    int cps) {
   __shared__ float red[8];
   griddep_wait();
   griddep_launch();
@@ -827,12 +1051,13 @@ __global__ void __launch_bounds__(256) k_prep_a_f16(const float* __restrict__ x,
         }
       }
     }
-    // swizzled stage tiles: [m-tile][stage of 16 columns][atom][rows_pad][128 B]
-    uint8_t* tile = a + ((size_t)mt * ((kcols + 15) >> 4) + (c >> 4)) * rows_pad * 256;
-    *reinterpret_cast<uint4*>(tile + sw128_off(c & 15, rr, rows_pad)) =
+    // swizzled stage tiles: [m-tile][stage of cps columns][atom][rows_pad][128 B]
+    const int nstg = (kcols + cps - 1) / cps, sc = c / cps, cc = c - sc * cps;
+    uint8_t* tile = a + ((size_t)mt * nstg + sc) * rows_pad * cps * 16;
+    *reinterpret_cast<uint4*>(tile + sw128_off(cc, rr, rows_pad)) =
         make_uint4(wv[0], wv[1], wv[2], wv[3]);
     if (lo_off)
-      *reinterpret_cast<uint4*>(tile + sw128_off(c & 15, rr + lo_off, rows_pad)) =
+      *reinterpret_cast<uint4*>(tile + sw128_off(cc, rr + lo_off, rows_pad)) =
           make_uint4(lv[0], lv[1], lv[2], lv[3]);
   }
 }
@@ -918,13 +1143,38 @@ syn_status_t launch_gemm_t(const GemmParams& p, const CUtensorMap& map, int mtil
   return launch_gemm_k<FMT, false>(p, map, mtiles, ntiles, st);
 }
 
+template <int FMT>
+syn_status_t launch_tm(const GemmParams& p, int mtiles, int ntiles, cudaStream_t st) {
+  static std::mutex mu;
+  static std::set<int> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (!done.count(dev)) {
+      cudaFuncSetAttribute(k_qgemm_tm<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           TM<FMT>::SMEM);
+      done.insert(dev);
+    }
+  }
+  cudaError_t e = launch_pdl2(k_qgemm_tm<FMT>, dim3(mtiles, ntiles), dim3(GEMM_THREADS),
+                              (size_t)TM<FMT>::SMEM, st, p);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e, "k_qgemm_tm");
+    return SYN_ERR_CUDA;
+  }
+  return SYN_OK;
+}
+
 }  // namespace
 
 size_t gemm_a_bytes(int fmt, size_t m, size_t kp) {
-  const size_t mtiles = (m + BM - 1) / BM;
-  // fp16: whole stages of 16 columns (the swizzled tiles)
-  const size_t kcols = (fmt == SYN_QFMT_INT8_KN) ? kp / 16 : (kp / 8 + 15) / 16 * 16;
-  return mtiles * BM * kcols * 16 + mtiles * BM * sizeof(float) + 256;
+  // fp16: whole stages of 16 columns (the swizzled tiles), rows for 256-token
+  // tiles (k_qgemm_tm) or 128-token tiles, whichever is more
+  const bool i8 = fmt == SYN_QFMT_INT8_KN;
+  const size_t rows = i8 ? (m + BM - 1) / BM * BM : (m + 255) / 256 * 256;
+  const size_t kcols = i8 ? kp / 16 : (kp / 8 + 15) / 16 * 16;
+  return rows * kcols * 16 + rows * sizeof(float) + 256;
 }
 
 size_t gemm_min_rows(int fmt, size_t n) {
@@ -964,16 +1214,29 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
   }();
   const int npad =
       (!i8 && (long long)m <= std::min(swap_max, 32)) ? (int)((m + 15) / 16 * 16) : 0;
+  // more than 128 tokens (block formats): weights in tensor memory, tiles of
+  // up to 256 tokens (k_qgemm_tm). Measured on B200 (Q4_0 14336x4096): 64
+  // tokens 53 us vs 44 us on the 128-token tiles, 512 tokens 109 vs 177 us,
+  // 2048 tokens 347 vs 611 us.
+  static const int tm_min = [] {
+    const char* v = getenv("SYN_GEMM_TM_MIN_ROWS");
+    return v ? atoi(v) : 129;
+  }();
+  const bool tm = !i8 && !npad && tm_min > 0 && (long long)m >= tm_min;
+  const int tm_tiles = (int)((m + 255) / 256);
+  const int tm_ntok = m >= 256 ? 256 : (int)((m + 15) / 16 * 16);
   uint8_t* a = abuf;
   const int acols = i8 ? kcols : (kcols + 15) / 16 * 16;  // fp16: whole swizzled stages
-  float* sa = reinterpret_cast<float*>(abuf + (size_t)mtiles * BM * acols * 16);
+  const size_t a_rows = i8 ? (size_t)mtiles * BM : (m + 255) / 256 * 256;
+  float* sa = reinterpret_cast<float*>(abuf + a_rows * acols * 16);
   cudaError_t e;
   if (i8)
     e = launch_pdl2(k_prep_a_i8, dim3(mtiles * BM), dim3(256), 0, st, x, xq, sx, (long long)ldx,
                     (int)m, (int)w->k, kcols, a, sa);
   else
-    e = launch_pdl2(k_prep_a_f16, dim3(npad ? npad : mtiles * BM), dim3(256), 0, st, x,
-                    (long long)ldx, (int)m, (int)w->k, kcols, a, sa, npad ? 2 * npad : BM, npad);
+    e = launch_pdl2(k_prep_a_f16, dim3(tm ? tm_tiles * tm_ntok : npad ? npad : mtiles * BM),
+                    dim3(256), 0, st, x, (long long)ldx, (int)m, (int)w->k, kcols, a, sa,
+                    tm ? tm_ntok : npad ? 2 * npad : BM, tm ? 0 : npad, tm ? 8 : 16);
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_prep_a");
     return SYN_ERR_CUDA;
@@ -1003,8 +1266,17 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
     return v ? atoi(v) : 64;
   }();
   p.short_rows = short_rows;
-  p.npad = npad;
-  p.astg = (kcols + 15) / 16;
+  p.npad = tm ? tm_ntok : npad;
+  p.astg = tm ? (kcols + 7) / 8 : (kcols + 15) / 16;
+  if (tm) {
+    switch (w->fmt) {
+      case SYN_QFMT_Q4_0: return launch_tm<F_Q4_0>(p, tm_tiles, ntiles, st);
+      case SYN_QFMT_Q8_0: return launch_tm<F_Q8_0>(p, tm_tiles, ntiles, st);
+      case SYN_QFMT_Q4_K: return launch_tm<F_Q4_K>(p, tm_tiles, ntiles, st);
+      case SYN_QFMT_Q6_K: return launch_tm<F_Q6_K>(p, tm_tiles, ntiles, st);
+    }
+    return SYN_ERR_INVALID_ARG;
+  }
   switch (w->fmt) {
     case SYN_QFMT_INT8_KN: return launch_gemm_t<F_INT8>(p, map, mtiles, ntiles, st);
     case SYN_QFMT_Q4_0: return launch_gemm_t<F_Q4_0>(p, map, mtiles, ntiles, st);
