@@ -31,6 +31,9 @@
 //   tiles. Each K step is one 128 x 128 x 16 (fp16) or x 32 (int8) MMA.
 //   Up to 32 tokens (block formats) the roles swap (SW): the 128 weight rows
 //   are the MMA's M and the tokens, each as an fp16 hi and lo row, its N.
+//   From 129 tokens (block formats) k_qgemm_tm keeps the dequantised weights
+//   in tensor memory as the MMA's A operand, with tiles of up to 256 tokens
+//   as B.
 //
 // CTA = 18 warps: warp 0 issues the copies into a smem ring; warp 1 owns
 // tensor memory and one of its threads issues the MMAs; warps 2-17
@@ -353,56 +356,56 @@ __device__ __forceinline__ void dequant_regs(const uint8_t* raw, int l, int bl, 
     }
     return;
   } else {
-  float v[32];
-  if constexpr (FMT == F_Q4_K) {
-    const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
-    const uint4 h = reinterpret_cast<const uint4*>(raw + S::G_H)[l];
-    const int s = b & 7;
-    const float dd = f16_loader((uint16_t)(h.x & 0xFFFF));
-    const float dmin = f16_loader((uint16_t)(h.x >> 16));
-    uint32_t scv, mnv;
-    if (s < 4) {
-      const int sh = 8 * s;
-      scv = (h.y >> sh) & 0x3F;
-      mnv = (((h.z >> sh) & 0xFF) >> 4) | (((h.w >> sh) & 0x0F) << 4);
-    } else {
-      const int sh = 8 * (s - 4);
-      const uint32_t ys = (h.y >> sh) & 0xFF;
-      scv = ((h.z >> sh) & 0x0F) | ((ys >> 6) << 4);
-      mnv = (((h.w >> sh) & 0xFF) >> 4) | (((ys >> 4) & 0x0C) << 4);
-    }
-    const float scl = __fmul_rn(dd, (float)scv), mv = __fmul_rn(dmin, (float)mnv);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    float v[32];
+    if constexpr (FMT == F_Q4_K) {
+      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+      const uint4 h = reinterpret_cast<const uint4*>(raw + S::G_H)[l];
+      const int s = b & 7;
+      const float dd = f16_loader((uint16_t)(h.x & 0xFFFF));
+      const float dmin = f16_loader((uint16_t)(h.x >> 16));
+      uint32_t scv, mnv;
+      if (s < 4) {
+        const int sh = 8 * s;
+        scv = (h.y >> sh) & 0x3F;
+        mnv = (((h.z >> sh) & 0xFF) >> 4) | (((h.w >> sh) & 0x0F) << 4);
+      } else {
+        const int sh = 8 * (s - 4);
+        const uint32_t ys = (h.y >> sh) & 0xFF;
+        scv = ((h.z >> sh) & 0x0F) | ((ys >> 6) << 4);
+        mnv = (((h.w >> sh) & 0xFF) >> 4) | (((ys >> 4) & 0x0C) << 4);
+      }
+      const float scl = __fmul_rn(dd, (float)scv), mv = __fmul_rn(dmin, (float)mnv);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
-      v[2 * i] = __fsub_rn(__fmul_rn(i2f_small((int)(byte & 15)), scl), mv);
-      v[2 * i + 1] = __fsub_rn(__fmul_rn(i2f_small((int)(byte >> 4)), scl), mv);
-    }
-  } else {  // F_Q6_K
-    const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
-    const uint2 hq = reinterpret_cast<const uint2*>(raw + S::G_QH + bl * 256)[l];
-    const uint32_t scp = reinterpret_cast<const uint16_t*>(raw + S::G_SC + bl * 64)[l];
-    const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D6)[l]);
-    const float s0 = __fmul_rn((float)(int8_t)(scp & 0xFF), dd);
-    const float s1 = __fmul_rn((float)(int8_t)(scp >> 8), dd);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      for (int i = 0; i < 16; i++) {
+        const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+        v[2 * i] = __fsub_rn(__fmul_rn(i2f_small((int)(byte & 15)), scl), mv);
+        v[2 * i + 1] = __fsub_rn(__fmul_rn(i2f_small((int)(byte >> 4)), scl), mv);
+      }
+    } else {  // F_Q6_K
+      const uint4 q = reinterpret_cast<const uint4*>(raw + S::G_Q + bl * 512)[l];
+      const uint2 hq = reinterpret_cast<const uint2*>(raw + S::G_QH + bl * 256)[l];
+      const uint32_t scp = reinterpret_cast<const uint16_t*>(raw + S::G_SC + bl * 64)[l];
+      const float dd = f16_loader(reinterpret_cast<const uint16_t*>(raw + S::G_D6)[l]);
+      const float s0 = __fmul_rn((float)(int8_t)(scp & 0xFF), dd);
+      const float s1 = __fmul_rn((float)(int8_t)(scp >> 8), dd);
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int e = 0; e < 32; e++) {
-      const uint32_t byte = (w[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
-      const uint32_t lo = (e & 1) ? (byte >> 4) : (byte & 15);
-      // invert the high-bit re-arrangement of repack.cu (k_repack_q6_k)
-      const int half = e >> 4, r = e & 15, f = 2 * (r >> 3) + (r & 1), tt = (r & 7) >> 1;
-      const uint32_t H = half ? hq.y : hq.x;
-      const uint32_t hi = (H >> (8 * tt + 2 * f)) & 3u;
-      v[e] = __fmul_rn(i2f_small((int)(lo | (hi << 4)) - 32), half ? s1 : s0);
+      for (int e = 0; e < 32; e++) {
+        const uint32_t byte = (w[e >> 3] >> (8 * ((e >> 1) & 3))) & 0xFF;
+        const uint32_t lo = (e & 1) ? (byte >> 4) : (byte & 15);
+        // invert the high-bit re-arrangement of repack.cu (k_repack_q6_k)
+        const int half = e >> 4, r = e & 15, f = 2 * (r >> 3) + (r & 1), tt = (r & 7) >> 1;
+        const uint32_t H = half ? hq.y : hq.x;
+        const uint32_t hi = (H >> (8 * tt + 2 * f)) & 3u;
+        v[e] = __fmul_rn(i2f_small((int)(lo | (hi << 4)) - 32), half ? s1 : s0);
+      }
     }
-  }
 #pragma unroll
-  for (int i = 0; i < 16; i++) {  // paired f32 -> f16 conversions (round to nearest)
-    const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-    o[i] = *reinterpret_cast<const uint32_t*>(&h);
-  }
+    for (int i = 0; i < 16; i++) {  // paired f32 -> f16 conversions (round to nearest)
+      const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+      o[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
   }
 }
 
