@@ -54,8 +54,9 @@ def test_gemm_block_formats_within_tol(ctx, fmt, m, n, k):
     assert st == 0
     yo = yo.reshape(m, n)
     errs = [max_rel_err(y[i], yo[i]) for i in range(m)]
-    # More than 32 rows run the large-tile kernel on fp16 activations and fp16
-    # weights: Q4_K's min offset (d*sc*q - dmin*m) cancels in the sums, and the
+    # More than 32 rows run on fp16 activations and fp16 weights (128-token
+    # tiles, or weights in tensor memory from 129 rows): Q4_K's min offset
+    # (d*sc*q - dmin*m) cancels in the sums, and the
     # per-row error reaches 1.07e-3 on a 256-column row (a CPU model of the
     # same roundings gives the same figure). Up to 32 rows the activations
     # enter as hi + lo fp16 parts and the bound is 1e-3.
