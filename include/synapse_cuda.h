@@ -170,7 +170,15 @@ syn_status_t syn_cuda_weight_dequant(const syn_cuda_weight_t *w,
  * W8A8 product bit-exactly like QuantizedLinear::forward
  * (int8_linear.rs:87-117). Block formats follow the reference's route
  * "dequantise to f32, then matmul_t" (gguf.rs + ops/matmul.rs:55-79)
- * within 1e-3 relative error. */
+ * within 1e-3 relative error (normwise per output row: max|y - ref| /
+ * max|ref|); Q4_K and Q6_K above 32 rows to about 1e-7.
+ * Scratch: the context's buffers grow the first time a call needs more
+ * (a larger m or weight). That growth calls cudaDeviceSynchronize, then
+ * cudaFree / cudaMalloc, and is refused (SYN_ERR_UNSUPPORTED) while the
+ * stream is being captured; warm a context up with its largest shapes
+ * before capturing or timing. Calls at sizes already seen never
+ * synchronise. The same holds for syn_cuda_qmatmul_int8_prequant and
+ * syn_cuda_qmatmul_rmsnorm. */
 syn_status_t syn_cuda_qmatmul(syn_cuda_ctx_t *ctx, const syn_cuda_weight_t *w,
                               const float *x, size_t m, float *y,
                               void *stream);
@@ -200,8 +208,11 @@ syn_status_t syn_cuda_qmatmul_rmsnorm(syn_cuda_ctx_t *ctx, const syn_cuda_weight
  * reference: it is for callers that must not allocate device memory while
  * they run (latency-critical decode loops, processes whose device memory is
  * owned by an external pool or budget, hosts that forbid the CUDA
- * allocator). Same inputs, outputs and results as syn_cuda_qmatmul; no
- * context is needed, and the weight's device must be current.
+ * allocator). Same inputs and outputs as syn_cuda_qmatmul, and results
+ * within the same tolerances: it always runs the GEMV, so INT8 is bit-exact
+ * either way, while block formats from the tensor-core GEMM's row threshold
+ * on differ from syn_cuda_qmatmul's values within 1e-3. No context is
+ * needed, and the weight's device must be current.
  * Its scratch (split-K partial sums and arrival counters) is a fixed device
  * array of SYN_CUDA_NOALLOC_SCRATCH_BYTES that every GPU loading the library
  * keeps until exit. A call needing more returns SYN_ERR_OUT_OF_MEMORY without

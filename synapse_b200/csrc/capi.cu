@@ -123,7 +123,7 @@ syn_status_t grow(void** buf, size_t* cap, size_t bytes, cudaStream_t st) {
 syn_status_t ensure_scratch(syn_cuda_ctx_s* ctx, const syn_cuda_weight_s* w, size_t m,
                             cudaStream_t st) {
   syn_status_t s = grow(reinterpret_cast<void**>(&ctx->part), &ctx->part_bytes,
-                        gemv_partial_bytes(w->fmt, m, w->n, w->kp), st);
+                        gemv_partial_bytes(w->fmt, m, w->n, w->kp, w->k), st);
   if (s != SYN_OK) return s;
   return grow(reinterpret_cast<void**>(&ctx->cnt), &ctx->cnt_bytes, gemv_counter_bytes(m, w->n),
               st);
@@ -137,9 +137,11 @@ namespace {
 struct CallScratch {
   void* mem = nullptr;
   float* part = nullptr;
+  size_t part_cap = 0;
   int* cnt = nullptr;
   syn_status_t init(int fmt, size_t m, size_t n, size_t kp, size_t extra, cudaStream_t st) {
     const size_t pb = align256(gemv_partial_bytes(fmt, m, n, kp));
+    part_cap = pb;
     const size_t cb = align256(gemv_counter_bytes(m, n));
     SYN_CUDA_TRY(cudaMallocAsync(&mem, extra + pb + cb + 256, st));
     part = reinterpret_cast<float*>(static_cast<uint8_t*>(mem) + extra);
@@ -295,8 +297,8 @@ syn_status_t syn_cuda_qgemm_int8(size_t m, size_t n, size_t k, const int8_t* a, 
     s = launch_qgemm(&w, nullptr, lda, a, scales_a, m, c, ldc, m > 16 ? 1 : 0,
                      static_cast<uint8_t*>(cs.mem) + wbytes, nullptr, st);
   else if (s == SYN_OK)
-    s = launch_qgemv(&w, nullptr, lda, a, scales_a, m, c, ldc, m > 16 ? 1 : 0, cs.part, cs.cnt,
-                     nullptr, st);
+    s = launch_qgemv(&w, nullptr, lda, a, scales_a, m, c, ldc, m > 16 ? 1 : 0, cs.part, cs.part_cap,
+                     cs.cnt, nullptr, st);
   return cs.release(s, st);
 }
 
@@ -308,7 +310,7 @@ syn_status_t syn_cuda_q4_0_gemv(size_t n, size_t k, const float* a, const uint8_
   cudaStream_t st = (cudaStream_t)stream;
   CallScratch cs;
   syn_status_t s = cs.init(SYN_QFMT_Q4_0, 1, n, k, 0, st);
-  if (s == SYN_OK) s = launch_q4_0_raw(n, k, a, b_q4, c, cs.part, cs.cnt, nullptr, st);
+  if (s == SYN_OK) s = launch_q4_0_raw(n, k, a, b_q4, c, cs.part, cs.part_cap, cs.cnt, nullptr, st);
   return cs.release(s, st);
 }
 
@@ -425,8 +427,8 @@ syn_status_t syn_cuda_qmatmul(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w, c
   }
   syn_status_t s = ensure_scratch(ctx, w, m, st);
   if (s != SYN_OK) return s;
-  return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, chunked, ctx->part, ctx->cnt,
-                      ctx->err, st);
+  return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, chunked, ctx->part,
+                      ctx->part_bytes, ctx->cnt, ctx->err, st);
 }
 
 syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w,
@@ -448,7 +450,7 @@ syn_status_t syn_cuda_qmatmul_int8_prequant(syn_cuda_ctx_t* ctx, const syn_cuda_
   syn_status_t s = ensure_scratch(ctx, w, m, st);
   if (s != SYN_OK) return s;
   return launch_qgemv(w, nullptr, w->k, x_i8, scales_x, m, y, w->n, m > 16 ? 1 : 0, ctx->part,
-                      ctx->cnt, ctx->err, st);
+                      ctx->part_bytes, ctx->cnt, ctx->err, st);
 }
 
 syn_status_t syn_cuda_qmatmul_rmsnorm(syn_cuda_ctx_t* ctx, const syn_cuda_weight_t* w,
@@ -463,7 +465,7 @@ syn_status_t syn_cuda_qmatmul_rmsnorm(syn_cuda_ctx_t* ctx, const syn_cuda_weight
   syn_status_t s = ensure_scratch(ctx, w, 1, st);
   if (s != SYN_OK) return s;
   GemvNorm nm{residual, delta, norm_weight, eps, residual_out, parallel_sum ? 1 : 0};
-  return launch_qgemv_norm(w, nm, y, ctx->part, ctx->cnt, ctx->err, st);
+  return launch_qgemv_norm(w, nm, y, ctx->part, ctx->part_bytes, ctx->cnt, ctx->err, st);
 }
 
 }  // extern "C"

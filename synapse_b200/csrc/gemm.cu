@@ -311,9 +311,12 @@ __device__ __forceinline__ bool bwait(const GemmParams& p, uint64_t* bar, uint32
 // Dequantises block bl of one row group's raw stage of KBX blocks (thread =
 // row l of the group) into 32 fp16 values in K order, packed in pairs:
 // o[i] = (value 2i, value 2i+1). Reference formulas: gguf.rs:255-487.
-template <int FMT, int KBX>
+// With LO (Q4_K, Q6_K in k_qgemm_tm), lo[i] receives the fp16 remainders
+// v - fp16(v) of the same pairs, so that hi + lo carries about 22 bits of
+// the reference's f32 value.
+template <int FMT, int KBX, bool LO = false>
 __device__ __forceinline__ void dequant_regs(const uint8_t* raw, int l, int bl, int b,
-                                             uint32_t (&o)[16]) {
+                                             uint32_t (&o)[16], uint32_t* lo = nullptr) {
   using S = RawG<FMT, KBX>;
   if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0) {
     // fp16 arithmetic, same values: (q - 8) and q are exact in fp16, d is an
@@ -405,6 +408,12 @@ __device__ __forceinline__ void dequant_regs(const uint8_t* raw, int l, int bl, 
     for (int i = 0; i < 16; i++) {  // paired f32 -> f16 conversions (round to nearest)
       const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
       o[i] = *reinterpret_cast<const uint32_t*>(&h);
+      if constexpr (LO) {
+        // v - fp16(v) is exact in f32
+        const __half2 r = __floats2half2_rn(__fsub_rn(v[2 * i], __low2float(h)),
+                                            __fsub_rn(v[2 * i + 1], __high2float(h)));
+        lo[i] = *reinterpret_cast<const uint32_t*>(&r);
+      }
     }
   }
 }
@@ -641,13 +650,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           mbar_arrive(&empty[slot]);
         }
       }
-      // epilogue: fp32 accumulators -> y
-      bwait(p, &accfull[0], 0);
+      // epilogue: fp32 accumulators -> y (nothing on a timed-out wait)
+      const bool accok = __all_sync(0xffffffffu, bwait(p, &accfull[0], 0));
       tc_fence_after();
       if constexpr (SW) {
         // lane = weight row; column t = token t's hi part, npad + t its lo
         // part (npad is 16 or 32: columns [0, 32) and, for 32, [32, 64))
-        if (chalf == 0) {
+        if (chalf == 0 && accok) {
           uint32_t r0[32], r1[32];
           tmem_ld32(tq, r0);
           if (p.npad == 32) tmem_ld32(tq + 32, r1);
@@ -663,7 +672,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       }
-      for (int h = 0; h < (SW ? 0 : CGW); h++) {
+      for (int h = 0; h < (SW || !accok ? 0 : CGW); h++) {
         const int cg = chalf * CGW + h;
         uint32_t r[32];
         tmem_ld32(tq + cg * 32, r);
@@ -680,9 +689,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const float sa = tok < p.m ? p.sa[tok] : 0.0f;
       if (!chunked) {
         // one int32 accumulator over all of K: float(acc) * sa * sb
-        bwait(p, &accfull[0], 0);
+        const bool accok = __all_sync(0xffffffffu, bwait(p, &accfull[0], 0));
         tc_fence_after();
-        for (int h = 0; h < CGW; h++) {
+        for (int h = 0; h < (accok ? CGW : 0); h++) {
           const int cg = chalf * CGW + h;
           uint32_t r[32];
           tmem_ld32(tq + cg * 32, r);
@@ -698,8 +707,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       } else {
         // C = 0; per chunk C += float(acc) * sa * sb (running C in tensor
         // memory columns 256..383)
+        bool cok = true;  // every chunk arrived (a timeout writes no output)
         for (int c = 0; c < nchunks; c++) {
-          bwait(p, &accfull[c & 1], (c >> 1) & 1);
+          cok = __all_sync(0xffffffffu, bwait(p, &accfull[c & 1], (c >> 1) & 1)) && cok;
           tc_fence_after();
           for (int h = 0; h < CGW; h++) {
             const int cg = chalf * CGW + h;
@@ -721,7 +731,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (lane == 0) mbar_arrive(&accempty[c & 1]);
         }
         tc_fence_after();
-        for (int h = 0; h < CGW; h++) {
+        for (int h = 0; h < (cok ? CGW : 0); h++) {
           const int cg = chalf * CGW + h;
           uint32_t cr[32];
           tmem_ld32(tq + 2 * BN + cg * 32, cr);
@@ -758,22 +768,33 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // reads.
 //   stage: KB = 2 blocks (64 K) = one 128-byte swizzle atom column of tokens
 //   tensor memory: accumulator columns [0, 256) (lane = weight row, column =
-//   token); NA weight buffers of 32 columns (64 halves) from column 256.
+//   token); NA weight buffers of AW columns from column 256.
+// Split operands (Q4_K, Q6_K): both operands enter as fp16 pairs, weights
+// w = wh + wl (dequant_regs<LO>) and tokens x = xh + xl (k_prep_a_f16's lo
+// rows), and three MMAs per K step accumulate wh*xh + wh*xl + wl*xh into
+// the same fp32 accumulator. The dropped wl*xl term is below 2^-22 of the
+// products, so the result is within f32 summation error of the reference's
+// f32 dequantise + sgemm (gguf.rs:375-487, matmul.zig:125-347). Without the
+// split, a single fp16 rounding of each operand gives 3-6e-4 normwise per
+// row, and for Q4_K's and Q6_K's sums up to about 1.1e-3 on narrow rows.
 // ---------------------------------------------------------------------------
 template <int FMT>
 struct TM {
+  static constexpr bool SPLIT = FMT == F_Q4_K || FMT == F_Q6_K;
   static constexpr int KB = 2;
   using R = RawG<FMT, KB>;
-  static constexpr int X_BYTES = 256 * 128;  // up to 256 token rows x 128 B
+  static constexpr int X_BYTES = (SPLIT ? 2 : 1) * 256 * 128;  // up to 256 token rows x 128 B (x2)
   static constexpr int RAW_BYTES = NG * R::G_BYTES;
   static constexpr int STAGE_BYTES = (X_BYTES + RAW_BYTES + 1023) / 1024 * 1024;
   static constexpr int NS_FIT = 230400 / STAGE_BYTES;
   static constexpr int NS = NS_FIT < 6 ? NS_FIT : 6;
   static constexpr int SMEM = NS * STAGE_BYTES;
   static constexpr int NA = 4;               // weight buffers in tensor memory
+  static constexpr uint32_t AW = SPLIT ? 64 : 32;  // columns per buffer (hi, then lo)
   static constexpr uint32_t A_COL0 = 256;    // first weight-buffer column
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int TN = 256;             // tokens per tile (MMA N, at most)
+  static_assert(A_COL0 + NA * AW <= TMEM_COLS, "tensor memory columns");
 };
 
 template <int FMT>
@@ -790,7 +811,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int mt = blockIdx.x, nt = blockIdx.y;
   const int ntok = p.npad;  // token rows of a tile: min(256, tokens rounded up to 16)
   const int nst = (p.nblk + S::KB - 1) / S::KB;
-  constexpr int DQ = 8;     // dequant warps (2 per tensor-memory lane quarter)
+  constexpr int DQ = 8;     // dequant warps per stage (2 per tensor-memory lane quarter)
+  static_assert(WORKERS == 2 * DQ && S::NA % 2 == 0, "two alternating dequant sets");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::NS; s++) {
@@ -829,10 +851,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
         uint8_t* st = sm + slot * S::STAGE_BYTES;
         uint8_t* raw = st + S::X_BYTES;
-        const uint32_t x_bytes = (uint32_t)ntok * 128;
+        const uint32_t x_bytes = (uint32_t)ntok * 128 * (S::SPLIT ? 2 : 1);
         mbar_expect_tx(&full[slot],
                        x_bytes + ngr * (nbs * (R::QT + R::DT + R::QHT + R::SCT) + R::HT + R::D6T));
-        // tokens: [m-tile][stage][ntok rows][128 B], one copy
+        // tokens: [m-tile][stage][ntok rows (hi, then ntok lo rows)][128 B], one copy
         bulk_g2s(st, p.a + ((size_t)mt * p.astg + s) * x_bytes, x_bytes, &full[slot]);
         for (int gi = 0; gi < ngr; gi++) {
           const size_t g = (size_t)nt * NG + gi;
@@ -867,16 +889,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tc_fence_after();
         const int b0 = s * S::KB, nbs = min(S::KB, p.nblk - b0);
         const uint64_t dx0 = sdesc_sw128(smem_u32(sm + slot * S::STAGE_BYTES));
-        const uint32_t ta = tbase + S::A_COL0 + (uint32_t)buf * 32;
+        const uint64_t dxl = dx0 + (uint64_t)(ntok * 128 / 16);  // lo token rows (split)
+        const uint32_t ta = tbase + S::A_COL0 + (uint32_t)buf * S::AW;
 #pragma unroll
         for (int bl = 0; bl < S::KB; bl++) {
           if (bl >= nbs) break;
 #pragma unroll
           for (int kh = 0; kh < 2; kh++) {
             // K offset kh*16 + bl*32 halves: 8 columns of A, 32 bytes of the atom
-            mma_f16_ts(tbase, ta + (uint32_t)(bl * 16 + kh * 8),
-                       dx0 + (uint64_t)((bl * 64 + kh * 32) / 16), id,
-                       (b0 + bl == 0 && kh == 0) ? 0u : 1u);
+            const uint32_t tak = ta + (uint32_t)(bl * 16 + kh * 8);
+            const uint64_t ko = (uint64_t)((bl * 64 + kh * 32) / 16);
+            mma_f16_ts(tbase, tak, dx0 + ko, id, (b0 + bl == 0 && kh == 0) ? 0u : 1u);
+            if constexpr (S::SPLIT) {
+              mma_f16_ts(tbase, tak, dxl + ko, id, 1u);       // wh * xl
+              mma_f16_ts(tbase, tak + 32, dx0 + ko, id, 1u);  // wl * xh
+            }
           }
         }
         mma_commit(&empty[slot]);
@@ -889,10 +916,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int ew = warp - 2;         // 0..15
     const int quarter = warp & 3;    // tensor-memory lane quarter = row group of the tile
     const uint32_t tq = tbase + ((uint32_t)(quarter * 32) << 16);
-    if (ew < DQ) {
-      const int bl = ew >> 2;        // block of the stage this warp dequantises
+    {
+      // two sets of DQ warps take alternate stages, so one set's dequant
+      // latency overlaps the other's
+      const int bl = (ew >> 2) & 1;  // block of the stage this warp dequantises
       const bool gvalid = nt * NG + quarter < p.groups;
-      for (int s = 0; s < nst; s++) {
+      for (int s = ew / DQ; s < nst; s += WORKERS / DQ) {
         const int slot = s % S::NS, buf = s % S::NA;
         const bool ok1 = bwait(p, &full[slot], (s / S::NS) & 1);
         const bool ok2 = s < S::NA || bwait(p, &aempty[buf], ((s / S::NA) - 1) & 1);
@@ -900,9 +929,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // tcgen05.st is warp-wide: the whole warp decides together
         if (__all_sync(0xffffffffu, ok1 && ok2) && gvalid && bl < nbs) {
           const uint8_t* raw = sm + slot * S::STAGE_BYTES + S::X_BYTES + quarter * R::G_BYTES;
-          uint32_t o[16];
-          dequant_regs<FMT, S::KB>(raw, lane, bl, b0 + bl, o);
-          tmem_st16(tq + S::A_COL0 + (uint32_t)buf * 32 + (uint32_t)bl * 16, o);
+          uint32_t o[16], ol[16];
+          dequant_regs<FMT, S::KB, S::SPLIT>(raw, lane, bl, b0 + bl, o, ol);
+          const uint32_t ta = tq + S::A_COL0 + (uint32_t)buf * S::AW + (uint32_t)bl * 16;
+          tmem_st16(ta, o);
+          if constexpr (S::SPLIT) tmem_st16(ta + 32, ol);
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
         tc_fence_before();
@@ -914,15 +945,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
     // epilogue: lane = weight row, column = token; warp column share
-    // [64 cs, 64 cs + 64)
-    bwait(p, &accfull, 0);
+    // [64 cs, 64 cs + 64). A timed-out wait (reported in p.err) writes no
+    // output.
+    const bool accok = __all_sync(0xffffffffu, bwait(p, &accfull, 0));
     tc_fence_after();
     const int cs = ew >> 2;
     const int n = nt * BN + quarter * 32 + lane;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
       const int c0 = cs * 64 + h * 32;
-      if (c0 >= ntok) break;  // uniform across the warp
+      if (c0 >= ntok || !accok) break;  // uniform across the warp
       uint32_t r[32];
       tmem_ld32(tq + (uint32_t)c0, r);
       if (n < p.n) {
@@ -1003,10 +1035,11 @@ __global__ void __launch_bounds__(256) k_prep_a_i8(const float* __restrict__ x,
   }
 }
 
-// Block formats (rows_pad rows per tile: 128; 2 npad for the swapped
-// small-M kernel, whose lo_off = npad rows further hold x - fp16(x); the
-// tile's token count for k_qgemm_tm; cps = 16-byte columns per stage: 16,
-// or 8 for k_qgemm_tm):
+// Block formats (tile_rows tokens per tile, rows_pad rows per tile in the
+// buffer: 128; 2 npad for the swapped small-M kernel, whose lo_off = npad
+// rows further hold x - fp16(x); the tile's token count for k_qgemm_tm,
+// twice that for its split formats, lo rows again at lo_off = the token
+// count; cps = 16-byte columns per stage: 16, or 8 for k_qgemm_tm):
 // fp16(x * 2^-s) per row, with the power of two s chosen so
 // that the row's largest magnitude lands in [2^14, 2^15): no fp16 overflow
 // and full fp16 precision whatever the activations' range. The scaling is
@@ -1015,12 +1048,12 @@ __global__ void __launch_bounds__(256) k_prep_a_f16(const float* __restrict__ x,
                                                     int m, int k, int kcols,
                                                     uint8_t* __restrict__ a,
                                                     float* __restrict__ sa, int rows_pad, int lo_off,
-                                                    int cps) {
+                                                    int cps, int tile_rows) {
   __shared__ float red[8];
   griddep_wait();
   griddep_launch();
   const int row = blockIdx.x;
-  const int mt = row / rows_pad, rr = row - mt * rows_pad;
+  const int mt = row / tile_rows, rr = row - mt * tile_rows;
   float inv = 1.0f;
   if (row < m) {
     const float* xr = x + (long long)row * ldx;
@@ -1171,11 +1204,17 @@ syn_status_t launch_tm(const GemmParams& p, int mtiles, int ntiles, cudaStream_t
 
 }  // namespace
 
+// Split-operand formats of k_qgemm_tm (hi and lo fp16 parts of both
+// operands); they take k_qgemm_tm from 33 rows, above the swapped kernel.
+bool tm_split_fmt(int fmt) { return fmt == SYN_QFMT_Q4_K || fmt == SYN_QFMT_Q6_K; }
+
 size_t gemm_a_bytes(int fmt, size_t m, size_t kp) {
   // fp16: whole stages of 16 columns (the swizzled tiles), rows for 256-token
-  // tiles (k_qgemm_tm) or 128-token tiles, whichever is more
+  // tiles (k_qgemm_tm, twice for the split formats' lo rows) or 128-token
+  // tiles, whichever is more
   const bool i8 = fmt == SYN_QFMT_INT8_KN;
-  const size_t rows = i8 ? (m + BM - 1) / BM * BM : (m + 255) / 256 * 256;
+  const size_t rows = i8 ? (m + BM - 1) / BM * BM
+                         : (m + 255) / 256 * 256 * (tm_split_fmt(fmt) ? 2 : 1);
   const size_t kcols = i8 ? kp / 16 : (kp / 8 + 15) / 16 * 16;
   return rows * kcols * 16 + rows * sizeof(float) + 256;
 }
@@ -1221,16 +1260,19 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
   // up to 256 tokens (k_qgemm_tm). Measured on B200 (Q4_0 14336x4096): 64
   // tokens 53 us vs 44 us on the 128-token tiles, 512 tokens 109 vs 177 us,
   // 2048 tokens 347 vs 611 us.
-  static const int tm_min = [] {
+  // Q4_K and Q6_K (split operands, the f32-grade path) take it from 33 rows.
+  static const int tm_min_env = [] {
     const char* v = getenv("SYN_GEMM_TM_MIN_ROWS");
-    return v ? atoi(v) : 129;
+    return v ? atoi(v) : -1;
   }();
+  const bool split = tm_split_fmt(w->fmt);
+  const int tm_min = tm_min_env >= 0 ? tm_min_env : split ? 33 : 129;
   const bool tm = !i8 && !npad && tm_min > 0 && (long long)m >= tm_min;
   const int tm_tiles = (int)((m + 255) / 256);
   const int tm_ntok = m >= 256 ? 256 : (int)((m + 15) / 16 * 16);
   uint8_t* a = abuf;
   const int acols = i8 ? kcols : (kcols + 15) / 16 * 16;  // fp16: whole swizzled stages
-  const size_t a_rows = i8 ? (size_t)mtiles * BM : (m + 255) / 256 * 256;
+  const size_t a_rows = i8 ? (size_t)mtiles * BM : (m + 255) / 256 * 256 * (split ? 2 : 1);
   float* sa = reinterpret_cast<float*>(abuf + a_rows * acols * 16);
   cudaError_t e;
   if (i8)
@@ -1239,7 +1281,9 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
   else
     e = launch_pdl2(k_prep_a_f16, dim3(tm ? tm_tiles * tm_ntok : npad ? npad : mtiles * BM),
                     dim3(256), 0, st, x, (long long)ldx, (int)m, (int)w->k, kcols, a, sa,
-                    tm ? tm_ntok : npad ? 2 * npad : BM, tm ? 0 : npad, tm ? 8 : 16);
+                    tm ? tm_ntok * (split ? 2 : 1) : npad ? 2 * npad : BM,
+                    tm ? (split ? tm_ntok : 0) : npad, tm ? 8 : 16,
+                    tm ? tm_ntok : npad ? 2 * npad : BM);
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "k_prep_a");
     return SYN_ERR_CUDA;

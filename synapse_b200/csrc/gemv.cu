@@ -1242,6 +1242,13 @@ syn_status_t run_gemv(int fmt, const GemvParams& p, const Plan& pl, cudaStream_t
   return SYN_ERR_INVALID_ARG;
 }
 
+// Bytes of split-K partial sums a launch of plan `pl` writes (0 unsplit).
+size_t plan_part_bytes(int fk, const Plan& pl, size_t m) {
+  if (pl.nks <= 1) return 0;
+  const size_t per = fk == F_INT8 ? (size_t)pl.nchunks : (size_t)pl.nks;
+  return m * per * (size_t)pl.groups * 32 * sizeof(float);
+}
+
 void fill_common(GemvParams& p, const Plan& pl, float* part, int* cnt, int* err) {
   p.groups = pl.groups;
   p.nblk = pl.nblk;
@@ -1255,11 +1262,14 @@ void fill_common(GemvParams& p, const Plan& pl, float* part, int* cnt, int* err)
 
 }  // namespace
 
-size_t gemv_partial_bytes(int fmt, size_t m, size_t n, size_t kp) {
-  const Plan pl = make_plan(fmt == SYN_QFMT_INT8_KN ? F_INT8 : F_Q4_0, m, n, kp);
-  if (pl.nks <= 1) return 0;
-  const size_t per = fmt == SYN_QFMT_INT8_KN ? (size_t)pl.nchunks : (size_t)pl.nks;
-  return m * per * (size_t)pl.groups * 32 * sizeof(float);
+size_t gemv_partial_bytes(int fmt, size_t m, size_t n, size_t kp, size_t k) {
+  // the weight's own plan, as the launches make it (the K split depends on
+  // each format's occupancy); for one row also the fused-RMSNorm plan
+  const int fk = fmt == SYN_QFMT_INT8_KN ? F_INT8 : fmt;
+  size_t b = plan_part_bytes(fk, make_plan(fk, m, n, kp), m);
+  if (m == 1 && k > 0 && k <= 16384)
+    b = std::max(b, plan_part_bytes(fk, make_plan(fk, 1, n, kp, k * sizeof(float)), 1));
+  return b;
 }
 
 size_t gemv_counter_bytes(size_t m, size_t n) {
@@ -1268,7 +1278,8 @@ size_t gemv_counter_bytes(size_t m, size_t n) {
 
 syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx,
                           const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
-                          int chunked, float* part, int* cnt, int* err, cudaStream_t st) {
+                          int chunked, float* part, size_t part_cap, int* cnt, int* err,
+                          cudaStream_t st) {
   if (w->n > 0x7FFFFFFFull || w->kp > 0x3FFFFFFFull || m > 0xFFFFull) return SYN_ERR_UNSUPPORTED;
   // the float4 activation loads of the block formats need 16-byte aligned rows
   if (w->fmt != SYN_QFMT_INT8_KN && ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 3)))
@@ -1295,12 +1306,14 @@ syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx
   p.ldy = (long long)ldy;
   p.chunked = chunked;
   fill_common(p, pl, part, cnt, err);
-  if (pl.nks > 1 && (!part || !cnt)) return SYN_ERR_INTERNAL;
+  if (pl.nks > 1 && (!part || !cnt || plan_part_bytes(fk, pl, m) > part_cap))
+    return SYN_ERR_INTERNAL;
   return run_gemv(fk, p, pl, st);
 }
 
 syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, float* y,
-                               float* part, int* cnt, int* err, cudaStream_t st) {
+                               float* part, size_t part_cap, int* cnt, int* err,
+                               cudaStream_t st) {
   if (w->n > 0x7FFFFFFFull || w->kp > 0x3FFFFFFFull) return SYN_ERR_UNSUPPORTED;
   if (w->k > 16384) return SYN_ERR_UNSUPPORTED;  // the row is staged in shared memory
   const int fk = w->fmt == SYN_QFMT_INT8_KN ? F_INT8 : w->fmt;
@@ -1327,12 +1340,14 @@ syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, f
   p.nres_out = nm.res_out;
   p.nfast = nm.fast;
   fill_common(p, pl, part, cnt, err);
-  if (pl.nks > 1 && (!part || !cnt)) return SYN_ERR_INTERNAL;
+  if (pl.nks > 1 && (!part || !cnt || plan_part_bytes(fk, pl, 1) > part_cap))
+    return SYN_ERR_INTERNAL;
   return run_gemv(fk, p, pl, st);
 }
 
 syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* b, float* c,
-                             float* part, int* cnt, int* err, cudaStream_t st) {
+                             float* part, size_t part_cap, int* cnt, int* err,
+                             cudaStream_t st) {
   if (n > 0x7FFFFFFFull || k > 0x3FFFFFFFull) return SYN_ERR_UNSUPPORTED;
   if (reinterpret_cast<uintptr_t>(a) & 15) return SYN_ERR_NOT_CONTIGUOUS;
   const Plan pl = make_plan(F_Q4_0, 1, n, k);
@@ -1347,7 +1362,8 @@ syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* 
   p.y = c;
   p.ldy = (long long)n;
   fill_common(p, pl, part, cnt, err);
-  if (pl.nks > 1 && (!part || !cnt)) return SYN_ERR_INTERNAL;
+  if (pl.nks > 1 && (!part || !cnt || plan_part_bytes(F_Q4_0, pl, 1) > part_cap))
+    return SYN_ERR_INTERNAL;
   return run_gemv(F_Q4_0RAW, p, pl, st);
 }
 

@@ -81,9 +81,12 @@ struct DeviceGuard {
 
 
 // Scratch of a GEMV over m activation rows: partial sums (0 when K is not
-// split across CTAs) and per-row-group arrival counters (zero before the
-// first launch; the kernel leaves them zero).
-size_t gemv_partial_bytes(int fmt, size_t m, size_t n, size_t kp);
+// split across CTAs; planned with the weight's own format, and for m = 1
+// with k > 0 also covering the fused-RMSNorm launch) and per-row-group
+// arrival counters (zero before the first launch; the kernel leaves them
+// zero). Every launch takes the capacity of its partial-sum buffer and
+// returns SYN_ERR_INTERNAL, launching nothing, if its plan needs more.
+size_t gemv_partial_bytes(int fmt, size_t m, size_t n, size_t kp, size_t k = 0);
 size_t gemv_counter_bytes(size_t m, size_t n);
 
 // Launches the fused GEMV for rows [0, m) of x (programmatic dependent
@@ -94,7 +97,8 @@ size_t gemv_counter_bytes(size_t m, size_t n);
 // or nullptr.
 syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx,
                           const int8_t* xq, const float* sx, size_t m, float* y, size_t ldy,
-                          int chunked, float* part, int* cnt, int* err, cudaStream_t st);
+                          int chunked, float* part, size_t part_cap, int* cnt, int* err,
+                          cudaStream_t st);
 
 // The GEMV for one activation row x = RMSNorm(res (+ delta)) * w, fused into
 // its prologue (same arithmetic as launch_add_rmsnorm; fast = parallel sum of
@@ -109,7 +113,8 @@ struct GemvNorm {
   int fast;
 };
 syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, float* y,
-                               float* part, int* cnt, int* err, cudaStream_t st);
+                               float* part, size_t part_cap, int* cnt, int* err,
+                               cudaStream_t st);
 // Grows the context's GEMV scratch for m rows of w (refused during capture).
 syn_status_t ensure_scratch(syn_cuda_ctx_s* ctx, const syn_cuda_weight_s* w, size_t m,
                             cudaStream_t st);
@@ -125,7 +130,8 @@ syn_status_t launch_qgemm(const syn_cuda_weight_s* w, const float* x, size_t ldx
 
 // Raw-layout Q4_0 GEMV over the reference's 18-byte blocks (M = 1).
 syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* b, float* c,
-                             float* part, int* cnt, int* err, cudaStream_t st);
+                             float* part, size_t part_cap, int* cnt, int* err,
+                             cudaStream_t st);
 
 // Per-row INT8 quantisation (quantize.zig:12-47).
 syn_status_t launch_quantize_rows(const float* x, size_t rows, size_t cols, int8_t* out,

@@ -74,5 +74,6 @@ extern "C" syn_status_t syn_cuda_qmatmul_noalloc(const syn_cuda_weight_t* w, con
   // at zero.
   SYN_CUDA_TRY(cudaMemsetAsync(cnt, 0, cnt_bytes, st));
   const int chunked = (w->fmt == SYN_QFMT_INT8_KN && m > 16) ? 1 : 0;
-  return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, chunked, part, cnt, nullptr, st);
+  return launch_qgemv(w, x, w->k, nullptr, nullptr, m, y, w->n, chunked, part, part_bytes, cnt, nullptr,
+                      st);
 }

@@ -318,7 +318,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
       float* nxt = other(cur);
       GemvNorm nm{cur, m->dn, ly.attn_norm, m->eps, nxt, a.flash};
       if ((s = ensure_scratch(m->ctx, ly.qkv, 1, st))) return s;
-      s = launch_qgemv_norm(ly.qkv, nm, m->qkv, m->ctx->part, m->ctx->cnt, m->ctx->err, st);
+      s = launch_qgemv_norm(ly.qkv, nm, m->qkv, m->ctx->part, m->ctx->part_bytes,
+                            m->ctx->cnt, m->ctx->err, st);
       if (s) return s;
       cur = nxt;
     } else {
@@ -347,7 +348,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
       float* nxt = other(cur);
       GemvNorm nm{cur, m->o, ly.ffn_norm, m->eps, nxt, a.flash};
       if ((s = ensure_scratch(m->ctx, ly.gu, 1, st))) return s;
-      s = launch_qgemv_norm(ly.gu, nm, m->gu, m->ctx->part, m->ctx->cnt, m->ctx->err, st);
+      s = launch_qgemv_norm(ly.gu, nm, m->gu, m->ctx->part, m->ctx->part_bytes,
+                            m->ctx->cnt, m->ctx->err, st);
       if (s) return s;
       cur = nxt;
     } else {
@@ -368,7 +370,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   if (fuse) {
     GemvNorm nm{cur, m->dn, m->final_norm, m->eps, nullptr, a.flash};
     if ((s = ensure_scratch(m->ctx, m->lm_head, 1, st))) return s;
-    s = launch_qgemv_norm(m->lm_head, nm, logits_dst, m->ctx->part, m->ctx->cnt, m->ctx->err, st);
+    s = launch_qgemv_norm(m->lm_head, nm, logits_dst, m->ctx->part, m->ctx->part_bytes,
+                            m->ctx->cnt, m->ctx->err, st);
     if (s) return s;
   } else {
     s = launch_add_rmsnorm(cur + r0 * h, h, m->dn + r0 * h, h, nullptr, nullptr, 0,

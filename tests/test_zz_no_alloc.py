@@ -84,3 +84,34 @@ def test_noalloc_rejects_oversized_scratch():
     assert bool(torch.all(y == 7.0))
     w.close()
     ctx.close()
+
+
+@pytest.mark.parametrize("fmt", ["Q6_K", "Q8_0"])
+def test_noalloc_near_the_limit(fmt):
+    """Rows 1..16 of a 14336 x 4096 weight: the split-K partials grow with
+    the rows until the fixed array no longer holds them. Accepted calls
+    match syn_cuda_qmatmul; refused ones touch nothing."""
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    ctx = sb.Context(0)
+    rng = np.random.default_rng(99)
+    n, k = 14336, 4096
+    f = sb.QFormat[fmt]
+    data, _ = synth.gen_weight(f, n, k, rng)
+    w = sb.QuantizedWeight(ctx, f, data, n, k)
+    accepted = []
+    for m in range(1, 17):
+        x = torch.from_numpy(synth.gen_activations(m, k, rng)).cuda()
+        y = torch.full((m, n), 7.0, device="cuda")
+        st = _noalloc(sb, w, x, m, y)
+        if st == 3:
+            torch.cuda.synchronize()
+            assert bool(torch.all(y == 7.0)), m
+            continue
+        assert st == 0, (m, st, sb.lib.syn_cuda_last_error())
+        ref = w.matmul(x).cpu().numpy()
+        assert _rel(y.cpu().numpy(), ref) <= TOL, m
+        accepted.append(m)
+    assert accepted and accepted[0] == 1, accepted
+    w.close()
+    ctx.close()
