@@ -45,7 +45,7 @@ CASE_FILTER = None  # "FMT:N:K" restricts the sweep to one GEMV (profiling runs)
 
 def sweep_cases():
     from synapse_b200 import synth
-    from synapse_b200.api import QFormat
+    from synapse_b200.formats import QFormat
     cases = [(fmt, n, k) for fmt in synth.FORMATS for n in synth.SWEEP_N for k in synth.SWEEP_K]
     if CASE_FILTER:
         f, n, k = CASE_FILTER.split(":")
@@ -310,10 +310,105 @@ def run_tp_decode(args, rank, world, local_rank, dist):
         "roofline": {"bound": "hbm", "achieved": round(per_gpu * n_dec / dec_s / 1e9, 1),
                      "peak": peak, "unit": "GB/s",
                      "frac": round(per_gpu * n_dec / dec_s / 1e9 / peak, 4), "peak_source": src},
+        "prefill_roofline": roof_tensor(lm_prefill_flops(cfg, TP_PROMPT) / pre_s / world),
     }
     m.close()
     ctx.close()
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_lm_sample(cfg, TP_FMT)
     return out
+
+
+def lm_linear_shapes(cfg):
+    """(n, k) of every linear of one decoder layer (reference naming order)."""
+    a, at = cfg["architecture"], cfg["attention"]
+    h, hd = a["hidden_size"], at["head_dim"]
+    qd, kvd = at["num_heads"] * hd, at["num_kv_heads"] * hd
+    ff = cfg["ffn"]["intermediate_size"]
+    return [(qd, h), (kvd, h), (kvd, h), (h, qd), (ff, h), (ff, h), (h, ff)]
+
+
+def lm_weight_bytes(cfg, fmt):
+    """Bytes of every linear weight plus the LM head in the reference format."""
+    from synapse_b200 import synth
+    from synapse_b200.formats import QFormat
+    f = QFormat[fmt]
+    a = cfg["architecture"]
+    per_layer = sum(synth.format_bytes(f, n, k) for n, k in lm_linear_shapes(cfg))
+    return a["num_layers"] * per_layer + synth.format_bytes(f, a["vocab_size"], a["hidden_size"])
+
+
+def lm_kv_bytes(cfg, positions):
+    """f32 K and V of `positions` cached positions over all layers."""
+    at = cfg["attention"]
+    return cfg["architecture"]["num_layers"] * 2 * at["num_kv_heads"] * at["head_dim"] * 4 * \
+        positions
+
+
+def lm_prefill_flops(cfg, tokens):
+    """2 x linear parameters per token, causal attention (QK^T and PV over
+    the visible positions), and the LM head for the last token only."""
+    a, at = cfg["architecture"], cfg["attention"]
+    params = sum(n * k for n, k in lm_linear_shapes(cfg))
+    L = a["num_layers"]
+    att = L * at["num_heads"] * at["head_dim"] * 2 * 2 * tokens * (tokens + 1) / 2
+    return 2.0 * L * params * tokens + att + 2.0 * a["vocab_size"] * a["hidden_size"]
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def cpu_lm_sample(cfg, fmt, prompt_len=8, decode_steps=3):
+    """The oracle restatement of the reference's f32 LM route on 1 core, for
+    shapes whose full run takes hours there: one decoder layer plus the
+    embedding, final norm and LM head are run on a prompt_len-token prompt
+    and decode_steps steps; the LM head is timed alone; the per-layer time is
+    scaled to the model's layer count. Prefill is extrapolated linearly in
+    tokens (the quadratic attention term is left out, which favours the
+    CPU), decode at a prompt_len-token context."""
+    import copy
+    from oracle import oracle as O
+    from oracle.lm import OracleLM
+    from synapse_b200 import synth
+    L = cfg["architecture"]["num_layers"]
+    one = copy.deepcopy(cfg)
+    one["architecture"]["num_layers"] = 1
+    dq = (lambda f, b, n: O.dequant(f.name, b, n)[1]) if fmt != "INT8_KN" else None
+    w = synth.gen_lm_weights(one, fmt, seed=1234, dequant=dq)
+    lm = OracleLM(one, w, prompt_len + decode_steps + 4)
+    V = cfg["architecture"]["vocab_size"]
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, V, prompt_len).tolist()
+    lm.forward_prefill(prompt)  # first touch of the weights
+    lm.reset()
+    t0 = time.perf_counter()
+    logits = lm.forward_prefill(prompt)
+    t_pre = time.perf_counter() - t0
+    tok = int(np.argmax(logits))
+    t0 = time.perf_counter()
+    for _ in range(decode_steps):
+        tok = int(np.argmax(lm.forward_one(tok)))
+    t_dec = (time.perf_counter() - t0) / decode_steps
+    head = lm.lm_head
+    x = np.ones(cfg["architecture"]["hidden_size"], np.float32)
+    t0 = time.perf_counter()
+    for _ in range(decode_steps):
+        head.forward(x, 1)
+    t_head = (time.perf_counter() - t0) / decode_steps
+    dec_full = t_head + L * max(t_dec - t_head, 0.0)
+    pre_full = t_head + L * max(t_pre - t_head, 0.0)
+    del w, lm, head
+    return {"decode_tok_s": round(1.0 / dec_full, 4),
+            "prefill_tok_s": round(prompt_len / pre_full, 4),
+            "cores": 1, "kind": "port",
+            "sample": f"oracle f32 route, 1 of {L} layers + LM head, {prompt_len}-token prompt "
+                      f"and {decode_steps} decode steps on 1 thread; extrapolated to {L} layers "
+                      "(prefill linear in tokens, decode at a short context)"}
 
 
 def cpu_decode_sample(cfg, w, prompt, budget_s=20.0):
@@ -349,7 +444,21 @@ def _timed_generate(m, steps, batch):
     return time.perf_counter() - t0
 
 
-def run_configs(local_rank):
+def roof_hbm(bytes_per_s, bytes_per_step):
+    peak, src = peaks()
+    return {"bound": "hbm", "achieved": round(bytes_per_s / 1e9, 1), "peak": peak,
+            "unit": "GB/s", "frac": round(bytes_per_s / 1e9 / peak, 4), "peak_source": src,
+            "bytes_per_step": int(bytes_per_step)}
+
+
+def roof_tensor(flops_per_s):
+    peak, src = tensor_peak()
+    return {"bound": "tensor", "achieved": round(flops_per_s / 1e12, 1), "peak": peak,
+            "unit": "TFLOP/s", "frac": round(flops_per_s / 1e12 / peak, 4),
+            "peak_source": src + " bf16 dense (the block formats multiply fp16 operands)"}
+
+
+def run_configs(local_rank, cpu_leg=False):
     """Configs 3 and 5 of the baseline (random-init weights, seeded random
     prompts), one GPU:
     - 3: the LLaMA-3.2-1B shape with Q4_K weights; a 512-token prompt, then
@@ -391,10 +500,20 @@ def run_configs(local_rank):
             for i in range(B):
                 m.forward_prefill(prompts[i], seq=i, want_logits=False)
             t8 = _timed_generate(m, steps - 3, B)
+            n = steps - 3
+            wb = lm_weight_bytes(cfg, fmt)
+            kv = lm_kv_bytes(cfg, P + 2 + n / 2.0)
+            b1, b8 = wb + kv, wb + B * kv
             out[key] = {"prompt_tokens": P, "prefill_tok_s": round(P / pre, 1),
-                        "decode_tok_s_batch1": round((steps - 3) / t1, 1),
-                        "decode_tok_s_batch8": round(B * (steps - 3) / t8, 1),
-                        "timed_steps": steps - 3}
+                        "decode_tok_s_batch1": round(n / t1, 1),
+                        "decode_tok_s_batch8": round(B * n / t8, 1),
+                        "timed_steps": n,
+                        "roofline": {
+                            "decode_batch1": roof_hbm(b1 * n / t1, b1),
+                            "decode_batch8": roof_hbm(b8 * n / t8, b8),
+                            "prefill": roof_tensor(lm_prefill_flops(cfg, P) / pre)}}
+            if cpu_leg:
+                out[key]["cpu_baseline"] = cpu_lm_sample(cfg, fmt)
         else:
             B = 32
             m = sb.Model(ctx, cfg, w, 2048 + steps + 8, max_batch=B)
@@ -408,11 +527,17 @@ def run_configs(local_rank):
             torch.cuda.synchronize()
             pre = time.perf_counter() - t0
             td = _timed_generate(m, steps - 3, B)
+            n = steps - 3
+            # KV positions read per step: each sequence's prompt, the two
+            # warm-up tokens and on average half of the timed steps
+            bstep = lm_weight_bytes(cfg, fmt) + lm_kv_bytes(cfg, float(lens.sum()) +
+                                                           B * (2 + n / 2.0))
             out[key] = {"sequences": B, "prompt_tokens_total": int(lens.sum()),
                         "prefill_tok_s": round(float(lens.sum()) / pre, 1),
-                        "decode_tok_s": round(B * (steps - 3) / td, 1),
-                        "ms_per_step": round(td / (steps - 3) * 1e3, 3),
-                        "timed_steps": steps - 3}
+                        "decode_tok_s": round(B * n / td, 1),
+                        "ms_per_step": round(td / n * 1e3, 3),
+                        "timed_steps": n,
+                        "roofline": {"decode": roof_hbm(bstep * n / td, bstep)}}
         m.close()
     ctx.close()
     return out
@@ -603,15 +728,19 @@ def run_synapse(args, rank, world, local_rank):
         tp_decode = run_tp_decode(args, rank, world, local_rank, dist)
     configs = None
     if not args.no_decode and world == 1 and not args.no_configs:
-        configs = run_configs(local_rank)
+        configs = run_configs(local_rank, cpu_leg=not args.no_cpu_baseline)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "mixed",
-            "dtype_detail": "int8 x int8 -> int32 (INT8 W8A8); packed 4/6/8-bit weights x "
-                            "16-bit-split f32 activations -> exact int32 blocks, f32 accumulate",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 W8A8 (INT8); int16-split activations x 4/6/8-bit codes (block formats)",
+            "dtype_detail": "INT8: int8 x int8 -> int32 as the reference. Block formats: each f32 "
+                            "activation block is rounded to a 16-bit integer (per-block scale, "
+                            "split into two byte planes) and dotted with the packed codes as "
+                            "exact int32 block sums, then f32 accumulation; normwise error "
+                            "<= 1e-3 against the reference's f32 route",
             "data": "synthetic (seeded PCG64; codes uniform, f16 scales |N(0,0.01)|, x N(0,1))",
             "config": {"workload": WORKLOAD, "m": 1, "formats": 5, "shapes": 15,
                        "weight_bytes_per_step": int(sum(c["w"].format_bytes for c in cases)),
@@ -650,7 +779,7 @@ class RefRoute:
 
     def __init__(self, fmt, n, k, rng):
         from synapse_b200 import synth
-        from synapse_b200.api import QFormat
+        from synapse_b200.formats import QFormat
         from oracle import oracle
         self.o = oracle
         self.fmt, self.n, self.k = QFormat(fmt), n, k
@@ -666,7 +795,7 @@ class RefRoute:
         """Rows [r0, r1) of the output (threads split rows), on raw pointers
         so that no copy lands inside the timed region."""
         import ctypes
-        from synapse_b200.api import QFormat
+        from synapse_b200.formats import QFormat
         lib = self.o._load(fast=True)
         n, k, rows = self.n, self.k, r1 - r0
         P = lambda a, off=0: ctypes.c_void_p(a.ctypes.data + off)  # noqa: E731
@@ -711,52 +840,67 @@ def sample_routes(rng, per_format_shapes):
 SAMPLE_SHAPES = [(1024, 1024), (3072, 2048), (4096, 4096), (11008, 4096), (14336, 1024)]
 
 
-def cpu_baseline_sample():
-    """1-core timing of the oracle on a bounded sample of the sweep."""
-    rng = np.random.default_rng(77)
-    routes = sample_routes(rng, SAMPLE_SHAPES)
+def cpu_baseline_sample(budget_s=10.0):
+    """1-core timing of the oracle restatement of the reference's route on
+    the whole M=1 sweep (the GPU arm's step), repeated for about budget_s."""
+    rng = np.random.default_rng(1234)
+    routes = [RefRoute(fmt, n, k, rng) for fmt, n, k in sweep_cases()]
     run_ref_step(routes, 1)
-    total_b, t = 0, 0.0
     reps = 0
     t0 = time.perf_counter()
-    while time.perf_counter() - t0 < 10.0 or reps < 1:
+    while time.perf_counter() - t0 < budget_s or reps < 1:
         run_ref_step(routes, 1)
         reps += 1
     t = time.perf_counter() - t0
     total_b = reps * sum(r.bytes for r in routes)
     return {"value": round(total_b / t / 1e9, 3), "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{reps} pass(es) of 5 formats x {len(SAMPLE_SHAPES)} (N,K) shapes of the "
-                      "M=1 sweep, oracle -O3 build, 1 thread"}
+            "sample": f"{reps} pass(es) of the whole step ({len(routes)} GEMVs), oracle -O3 "
+                      "build, 1 thread"}
 
 
 def run_reference(args, rank, world):
+    """The reference's CPU route for the same workload as the GPU arm: all 75
+    GEMVs of the M=1 sweep per step, same shapes, formats and value
+    distributions. The reference's implementation is single-threaded
+    (synapse-core's wrappers are !Sync; the Zig kernels run on the calling
+    thread), so it runs on one thread pinned to one core. Neither torch nor
+    the CUDA library is loaded in this process: the inputs come from
+    synapse_b200.synth (numpy only) and the arithmetic from the oracle's
+    -O3 build."""
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(77)
-    routes = sample_routes(rng, SAMPLE_SHAPES)
+    try:
+        cpu = sorted(os.sched_getaffinity(0))[0]
+        os.sched_setaffinity(0, {cpu})
+    except (AttributeError, OSError):
+        cpu = None
+    rng = np.random.default_rng(1234)
+    routes = [RefRoute(fmt, n, k, rng) for fmt, n, k in sweep_cases()]
     for _ in range(args.warmup):
-        run_ref_step(routes, threads)
+        run_ref_step(routes, 1)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        run_ref_step(routes, threads)
+        run_ref_step(routes, 1)
     t = time.perf_counter() - t0
     step_bytes = sum(r.bytes for r in routes)
     value = step_bytes * args.steps / t / 1e9
-    sample = (f"5 formats x {len(SAMPLE_SHAPES)} (N,K) shapes of the M=1 sweep per step, "
-              f"rows split over {threads} threads")
+    sample = (f"the whole step: {len(routes)} GEMVs of the M=1 sweep (5 formats x 15 (N,K)), "
+              f"oracle -O3 build, 1 thread pinned to cpu {cpu} of {os.cpu_count()}")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(t / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "mixed",
-        "data": "synthetic (seeded PCG64)",
-        "config": {"workload": WORKLOAD, "m": 1, "sample": sample},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (block formats), int8 (W8A8)",
+        "data": "synthetic (seeded PCG64; codes uniform, f16 scales |N(0,0.01)|, x N(0,1))",
+        "config": {"workload": WORKLOAD, "m": 1, "formats": 5, "shapes": 15,
+                   "same_config": True, "sample": sample},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": 1,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": "reference is Zig+Rust (no toolchain here): CPU restatement of its route",
+        "note": "the reference is Zig + Rust with no toolchain here or on the GPU box: this is "
+                "the C restatement of its route (quantize + qgemm_int8, q4_0_gemv, "
+                "dequantise-at-load + f32 GEMV), single-threaded as the reference is",
     }
     print(json.dumps(line), flush=True)
 

@@ -44,8 +44,9 @@ def layer_names(i):
 
 
 class _Linear:
-    def __init__(self, spec, n, k):
+    def __init__(self, spec, n, k, threads=1):
         self.n, self.k = n, k
+        self.threads = threads
         self.int8 = spec[0] == "INT8_KN"
         if self.int8:
             self.q = np.ascontiguousarray(spec[1], dtype=np.int8)
@@ -61,8 +62,39 @@ class _Linear:
             st, xq, sx = O.quantize_per_channel_int8(x, m, self.k)
             assert st == 0
             return self.forward_pre_quantized(xq, sx, m)
+        if self.threads > 1 and self.n >= 128:
+            return self._forward_threaded(x, m)
         st, y = O.sgemm_nt(m, self.n, self.k, x, self.w, fast=True)
         assert st == 0
+        return y
+
+    def _forward_threaded(self, x, m):
+        """The same sgemm split over output columns in slices of whole
+        64-column blocks: every output keeps its micro-kernel and its
+        summation order (the column blocks of matmul.zig:125-347 start at
+        multiples of 8 and 64), so the result is bit-identical to one call.
+        The C calls release the GIL."""
+        import ctypes
+        import threading
+        lib = O._load(fast=True)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(m * self.n, np.float32)
+        per = (self.n + self.threads - 1) // self.threads
+        per = (per + 63) // 64 * 64
+        vp = ctypes.c_void_p
+        res = []
+
+        def run(r0, r1):
+            res.append(lib.orc_sgemm_nt(m, r1 - r0, self.k, vp(x.ctypes.data), self.k,
+                                        vp(self.w.ctypes.data + 4 * r0 * self.k), self.k,
+                                        vp(y.ctypes.data + 4 * r0), self.n))
+        ts = [threading.Thread(target=run, args=(r0, min(self.n, r0 + per)))
+              for r0 in range(0, self.n, per)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        assert all(r == 0 for r in res), res
         return y
 
     def forward_pre_quantized(self, xq, sx, m):
@@ -72,7 +104,7 @@ class _Linear:
 
 
 class OracleLM:
-    def __init__(self, cfg, weights, max_seq):
+    def __init__(self, cfg, weights, max_seq, threads=1):
         a, at = cfg["architecture"], cfg["attention"]
         self.h = a["hidden_size"]
         self.L = a["num_layers"]
@@ -94,16 +126,16 @@ class OracleLM:
                 "ffn_norm": weights[nm["ffn_norm"]],
                 "q_norm": weights.get(nm["q_norm"], np.zeros(0, np.float32)),
                 "k_norm": weights.get(nm["k_norm"], np.zeros(0, np.float32)),
-                "wq": _Linear(weights[nm["wq"]], qd, self.h),
-                "wk": _Linear(weights[nm["wk"]], kvd, self.h),
-                "wv": _Linear(weights[nm["wv"]], kvd, self.h),
-                "wo": _Linear(weights[nm["wo"]], self.h, qd),
-                "gate": _Linear(weights[nm["gate"]], self.ff, self.h),
-                "up": _Linear(weights[nm["up"]], self.ff, self.h),
-                "down": _Linear(weights[nm["down"]], self.h, self.ff),
+                "wq": _Linear(weights[nm["wq"]], qd, self.h, threads),
+                "wk": _Linear(weights[nm["wk"]], kvd, self.h, threads),
+                "wv": _Linear(weights[nm["wv"]], kvd, self.h, threads),
+                "wo": _Linear(weights[nm["wo"]], self.h, qd, threads),
+                "gate": _Linear(weights[nm["gate"]], self.ff, self.h, threads),
+                "up": _Linear(weights[nm["up"]], self.ff, self.h, threads),
+                "down": _Linear(weights[nm["down"]], self.h, self.ff, threads),
             }
             self.layers.append(ly)
-        self.lm_head = _Linear(weights["lm_head.weight"], self.V, self.h)
+        self.lm_head = _Linear(weights["lm_head.weight"], self.V, self.h, threads)
         self.int8 = self.lm_head.int8
         self.kc = np.zeros((self.L, max_seq, kvd), np.float32)
         self.vc = np.zeros((self.L, max_seq, kvd), np.float32)
@@ -111,6 +143,16 @@ class OracleLM:
 
     def reset(self):
         self.pos = 0
+
+    def fork(self):
+        """Another sequence over the same (read-only) weights: its own empty
+        KV cache, so a batch of sequences costs one copy of the f32 weights."""
+        import copy
+        other = copy.copy(self)
+        other.kc = np.zeros_like(self.kc)
+        other.vc = np.zeros_like(self.vc)
+        other.pos = 0
+        return other
 
     # -- pieces --------------------------------------------------------------
     def _embed(self, ids):

@@ -7,11 +7,12 @@ operate on CUDA tensors through the C ABI in include/synapse_cuda.h. torch
 is used only for device memory and the current stream.
 """
 import ctypes
-import enum
 
 import torch
 
 from . import _lib
+from . import formats as _formats
+from .formats import QFormat
 
 
 class SynapseError(RuntimeError):
@@ -46,27 +47,12 @@ def _check(status, where):
         raise SynapseError(status, where)
 
 
-class QFormat(enum.IntEnum):
-    INT8_KN = 0
-    Q4_0 = 1
-    Q8_0 = 2
-    Q4_K = 3
-    Q6_K = 4
-
-
-_BLOCK = {QFormat.Q4_0: (32, 18), QFormat.Q8_0: (32, 34), QFormat.Q4_K: (256, 144),
-          QFormat.Q6_K: (256, 210)}
-
-
 def row_bytes(fmt, k):
     """Bytes of one K-element row in the reference's storage format."""
-    fmt = QFormat(fmt)
-    if fmt == QFormat.INT8_KN:
-        return k
-    elems, nbytes = _BLOCK[fmt]
-    if k % elems:
-        raise SynapseError(4, "row_bytes")
-    return k // elems * nbytes
+    try:
+        return _formats.row_bytes(fmt, k)
+    except ValueError:
+        raise SynapseError(4, "row_bytes") from None
 
 
 def _ptr(t):

@@ -7,7 +7,7 @@ as f32; activations N(0, 1). All draws use numpy PCG64.
 """
 import numpy as np
 
-from .api import QFormat, row_bytes
+from .formats import QFormat, row_bytes
 
 SWEEP_N = (1024, 3072, 4096, 11008, 14336)
 SWEEP_K = (1024, 2048, 4096)

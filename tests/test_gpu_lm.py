@@ -282,21 +282,19 @@ def test_block_model_logits_within_tolerance(ctx, fmt, name):
     tok, lg = m.forward_prefill(prompt)
     err = np.linalg.norm(lg - lref) / np.linalg.norm(lref)
     assert err < 5e-3, err
-    agree = 0
     for i in range(16):
         srt = np.sort(lref)
         if O.argmax(lref) != tok:
-            # a disagreement is only allowed where the oracle's margin is tiny
-            assert srt[-1] - srt[-2] < 20 * np.abs(lg - lref).max() + 1e-6
+            # a disagreement is only allowed where the oracle's top-2 margin
+            # is below the observed logit error; nothing is compared after it
+            assert srt[-1] - srt[-2] <= np.abs(lg - lref).max(), (i, srt[-1] - srt[-2])
             break
-        agree += 1
         lref = ref.forward_one(tok)
         nxt, lgs = m.forward_one([tok])
         lg = lgs[0]
         err = np.linalg.norm(lg - lref) / np.linalg.norm(lref)
         assert err < 5e-3, (i, err)
         tok = int(nxt[0])
-    assert agree >= 4
     m.close()
 
 

@@ -1,7 +1,8 @@
 """Tensor parallelism on 2 GPUs (one process per GPU, NCCL through the
 library's own communicator): a block-format model split over 2 ranks gives
-the logits of the unsharded oracle within tolerance and the same greedy
-tokens wherever the oracle's top-2 margin exceeds the observed error.
+the logits of the unsharded oracle within tolerance and the same 64 greedy
+tokens, unless the oracle's top-2 margin at the first divergence is below
+the observed logit error.
 Skipped on boxes with fewer than 2 GPUs."""
 import os
 import socket
@@ -13,7 +14,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-STEPS = 12
+STEPS = 64
 PROMPT = [7, 8, 9, 100, 200, 11, 12, 13]
 
 
@@ -102,7 +103,8 @@ def test_tp2_model_matches_oracle(fmt, name):
         assert err < 5e-3, (i, err)
         if O.argmax(lref) != toks[i]:
             srt = np.sort(lref)
-            assert srt[-1] - srt[-2] < 20 * np.abs(logits[i] - lref).max() + 1e-6
+            # only where the oracle's top-2 margin is below the observed error
+            assert srt[-1] - srt[-2] <= np.abs(logits[i] - lref).max(), i
             break
         if i < STEPS:
             lref = ref.forward_one(toks[i])

@@ -99,3 +99,19 @@ def test_oracle_greedy_generation_is_deterministic():
     t2, _ = OracleLM(cfg, w, 64).generate_greedy([1, 2, 3, 4], 12)
     assert t1 == t2 and len(t1) == 12 and all(0 <= t < 512 for t in t1)
     assert all(m >= 0 for m in m1)
+
+
+@pytest.mark.parametrize("fmt", ["Q4_0", "Q4_K"])
+def test_threaded_oracle_bit_identical(fmt):
+    """The oracle's column-sliced threaded matmul (used to make full-size
+    parity runs affordable) gives the bits of the single-call one, for
+    prefill (M > 16, tiled) and decode (M = 1) alike."""
+    cfg = synth.lm_config("tiny-hd64")
+    w = synth.gen_lm_weights(cfg, fmt, seed=5, dequant=lambda f, b, n: O.dequant(f.name, b, n)[1])
+    prompt = list(range(3, 23))
+    a = OracleLM(cfg, w, 48)
+    b = OracleLM(cfg, w, 48, threads=3)
+    la, lb = a.forward_prefill(prompt), b.forward_prefill(prompt)
+    assert np.array_equal(la, lb)
+    for t in (5, 77, 300):
+        assert np.array_equal(a.forward_one(t), b.forward_one(t))
