@@ -71,6 +71,16 @@ typedef enum syn_qformat_t {
     SYN_QFMT_Q6_K = 4     /* GGUF super-blocks, 210 B / 256 (gguf.rs:440-487) */
 } syn_qformat_t;
 
+/* Element types of safetensors tensors (weight_loading/safetensors.rs:233-290). */
+typedef enum syn_dtype_t {
+    SYN_DTYPE_F32 = 0,
+    SYN_DTYPE_F16 = 1,  /* IEEE half; converted like converter.rs:12-40 */
+    SYN_DTYPE_BF16 = 2, /* upper 16 bits of an f32 (converter.rs:43-48) */
+    SYN_DTYPE_I64 = 3,
+    SYN_DTYPE_I32 = 4,
+    SYN_DTYPE_U8 = 5
+} syn_dtype_t;
+
 typedef struct syn_cuda_ctx_s syn_cuda_ctx_t;
 typedef struct syn_cuda_weight_s syn_cuda_weight_t;
 
@@ -417,6 +427,94 @@ syn_status_t syn_cuda_tp_shard_linear(syn_qformat_t fmt, const void *host, size_
                                       size_t k, const float *scales, int axis, int rank,
                                       int world, void *out, float *out_scales,
                                       size_t *n_out, size_t *k_out);
+
+/* ------------------------------------------------------------------ */
+/* Weight files (host side; the parsers need no GPU).                  */
+/* ------------------------------------------------------------------ */
+typedef struct syn_gguf_s syn_gguf_t;
+typedef struct syn_safetensors_s syn_safetensors_t;
+
+/* GGUF v2/v3 (weight_loading/gguf.rs:71-152 and :156-248): the file is
+ * memory-mapped; the header, metadata and tensor infos are parsed as the
+ * reference parses them (data section at the 32-byte default alignment, or
+ * general.alignment when present). Bad magic, an unsupported version, a
+ * truncated header or tensor data beyond the file -> SYN_ERR_INVALID_ARG. */
+syn_status_t syn_gguf_open(const char *path, syn_gguf_t **out);
+syn_status_t syn_gguf_close(syn_gguf_t *g);
+syn_status_t syn_gguf_tensor_count(const syn_gguf_t *g, size_t *count);
+/* Tensor i: name, GGML type (0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 8 Q8_0, 12 Q4_K,
+ * 14 Q6_K; others report nbytes 0), dims (ne0 = the contiguous one first;
+ * unused dims are 1), a pointer to its bytes inside the mapping and their
+ * size. Pointers live until syn_gguf_close. */
+syn_status_t syn_gguf_tensor_info(const syn_gguf_t *g, size_t i, const char **name,
+                                  uint32_t *ggml_type, size_t *n_dims, uint64_t *dims4,
+                                  const void **data, size_t *nbytes);
+/* Scalar metadata (numbers and bools as double; strings). */
+syn_status_t syn_gguf_meta_num(const syn_gguf_t *g, const char *key, double *value);
+syn_status_t syn_gguf_meta_str(const syn_gguf_t *g, const char *key, const char **value);
+/* llama.cpp tensor names onto the runner's (Hugging Face) names:
+ * token_embd / output_norm / output and blk.N.{attn_norm, attn_q, attn_k,
+ * attn_v, attn_output, attn_q_norm, attn_k_norm, ffn_norm, ffn_gate,
+ * ffn_up, ffn_down}.weight. Other names -> SYN_ERR_INVALID_ARG. The
+ * reference's weight map has no such table (weight_map.rs:37-135). */
+syn_status_t syn_gguf_runner_name(const char *gguf_name, char *out, size_t cap);
+/* The model config (the reference's config-JSON schema, as read by
+ * syn_cuda_model_create) from <arch>.* metadata and token_embd's shape.
+ * *needed = bytes including the terminator; out may be NULL to query. */
+syn_status_t syn_gguf_config_json(const syn_gguf_t *g, char *out, size_t cap, size_t *needed);
+
+/* safetensors (weight_loading/safetensors.rs:176-290): F32, F16, BF16, I64,
+ * I32 and U8 tensors; "__metadata__" skipped; another dtype ->
+ * SYN_ERR_UNSUPPORTED; a bad header or data beyond the file ->
+ * SYN_ERR_INVALID_ARG. */
+syn_status_t syn_safetensors_open(const char *path, syn_safetensors_t **out);
+syn_status_t syn_safetensors_close(syn_safetensors_t *f);
+syn_status_t syn_safetensors_tensor_count(const syn_safetensors_t *f, size_t *count);
+syn_status_t syn_safetensors_tensor_info(const syn_safetensors_t *f, size_t i, const char **name,
+                                         syn_dtype_t *dtype, size_t *n_dims, uint64_t *dims4,
+                                         const void **data, size_t *nbytes);
+/* Element conversion of the safetensors loader (converter.rs:12-48; f16
+ * subnormals come out at half their value, as there). */
+syn_status_t syn_convert_to_f32(syn_dtype_t dtype, const void *src, size_t count, float *dst);
+
+/* Load-time INT8 quantisation from f16 / bf16 weights on the device
+ * (syn_cuda_quantize_weights_int8 after the loader's conversion:
+ * safetensors.rs + converter.rs, then int8.rs:78-152). w: device bits
+ * [n,k]; out_kn: int8 [k,n]; scales: f32 [n]. Bit-exact. */
+syn_status_t syn_cuda_quantize_weights_int8_half(const uint16_t *w, syn_dtype_t dtype,
+                                                 size_t n, size_t k, int8_t *out_kn,
+                                                 float *scales, void *stream);
+/* The same from HOST f32 / f16 / bf16 [n,k] into host int8 [k,n] + scales,
+ * computed on the context's device. Synchronous. */
+syn_status_t syn_cuda_quantize_weights_int8_host(syn_cuda_ctx_t *ctx, syn_dtype_t dtype,
+                                                 const void *w, size_t n, size_t k,
+                                                 int8_t *out_kn, float *scales);
+
+/* syn_cuda_weight_upload with an on-disk cache of the repacked device
+ * bytes: the file <cache_dir>/<hash>.synw is named by a 64-bit hash of the
+ * source bytes (and scales, format and shape). When it exists and its
+ * header matches, the weight is read from it (*hit = 1); otherwise the
+ * weight is uploaded and repacked, and the file written (atomically). */
+syn_status_t syn_cuda_weight_upload_cached(syn_cuda_ctx_t *ctx, syn_qformat_t fmt,
+                                           const void *host, size_t n, size_t k,
+                                           const float *scales_or_null, const char *cache_dir,
+                                           syn_cuda_weight_t **out, int *hit);
+
+/* Model weights from files, into a model before syn_cuda_model_finalize.
+ * GGUF: quantised linears keep their raw blocks (no f32 copy); norms and
+ * F32/F16 embeddings become f32; a quantised token_embd is dequantised
+ * with the reference's formulas; no output.weight = tied LM head. For
+ * general.architecture "llama" the attn_q / attn_k rows are put back from
+ * the GGUF converter's pairwise-RoPE order into rotate-half order.
+ * safetensors: the reference's --quantize load (int8.rs:78-152): 2-D
+ * *_proj.weight and lm_head.weight are quantised to INT8 on the device,
+ * other float tensors become f32, a missing lm_head is tied. */
+syn_status_t syn_cuda_model_load_gguf(syn_cuda_model_t *m, const syn_gguf_t *g);
+syn_status_t syn_cuda_model_load_safetensors(syn_cuda_model_t *m, const syn_safetensors_t *f);
+/* Repacked-weight cache for the model's finalize (NULL or "" = none), and
+ * how many of its weights finalize read from the cache. */
+syn_status_t syn_cuda_model_set_cache_dir(syn_cuda_model_t *m, const char *dir);
+syn_status_t syn_cuda_model_cache_hits(const syn_cuda_model_t *m, int *hits);
 
 #ifdef __cplusplus
 }

@@ -15,7 +15,8 @@ _API = ("QFormat", "SynapseError", "Context", "QuantizedWeight", "QuantizedLinea
         "capability_summary", "quantize_per_channel_int8", "quantize_weights_int8",
         "qgemm_int8", "q4_0_gemv", "row_bytes", "rope_tables", "rmsnorm", "add_rmsnorm",
         "swiglu", "argmax", "KVCache", "attention_decode", "attention_prefill", "Model",
-        "tp_unique_id", "tp_shard_linear")
+        "tp_unique_id", "tp_shard_linear", "GGUFFile", "SafetensorsFile", "gguf_runner_name",
+        "quantize_weights_int8_half")
 
 __all__ = ["lib"] + list(_API)
 

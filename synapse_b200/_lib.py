@@ -87,6 +87,36 @@ SIGNATURES = {
     "syn_cuda_tp_unique_id": (c_st, [c_vp]),
     "syn_cuda_tp_init": (c_st, [c_vp, ctypes.c_int, ctypes.c_int, c_vp]),
     "syn_cuda_tp_allreduce_sum": (c_st, [c_vp, c_vp, c_size, c_vp]),
+    "syn_gguf_open": (c_st, [ctypes.c_char_p, ctypes.POINTER(c_vp)]),
+    "syn_gguf_close": (c_st, [c_vp]),
+    "syn_gguf_tensor_count": (c_st, [c_vp, ctypes.POINTER(c_size)]),
+    "syn_gguf_tensor_info": (c_st, [c_vp, c_size, ctypes.POINTER(ctypes.c_char_p),
+                                    ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(c_size),
+                                    ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(c_vp),
+                                    ctypes.POINTER(c_size)]),
+    "syn_gguf_meta_num": (c_st, [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+    "syn_gguf_meta_str": (c_st, [c_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_char_p)]),
+    "syn_gguf_runner_name": (c_st, [ctypes.c_char_p, ctypes.c_char_p, c_size]),
+    "syn_gguf_config_json": (c_st, [c_vp, ctypes.c_char_p, c_size, ctypes.POINTER(c_size)]),
+    "syn_safetensors_open": (c_st, [ctypes.c_char_p, ctypes.POINTER(c_vp)]),
+    "syn_safetensors_close": (c_st, [c_vp]),
+    "syn_safetensors_tensor_count": (c_st, [c_vp, ctypes.POINTER(c_size)]),
+    "syn_safetensors_tensor_info": (c_st, [c_vp, c_size, ctypes.POINTER(ctypes.c_char_p),
+                                           ctypes.POINTER(ctypes.c_int), ctypes.POINTER(c_size),
+                                           ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(c_vp),
+                                           ctypes.POINTER(c_size)]),
+    "syn_convert_to_f32": (c_st, [ctypes.c_int, c_vp, c_size, c_vp]),
+    "syn_cuda_quantize_weights_int8_half": (c_st, [c_vp, ctypes.c_int, c_size, c_size, c_vp, c_vp,
+                                                   c_vp]),
+    "syn_cuda_quantize_weights_int8_host": (c_st, [c_vp, ctypes.c_int, c_vp, c_size, c_size, c_vp,
+                                                   c_vp]),
+    "syn_cuda_weight_upload_cached": (c_st, [c_vp, ctypes.c_int, c_vp, c_size, c_size, c_vp,
+                                             ctypes.c_char_p, ctypes.POINTER(c_vp),
+                                             ctypes.POINTER(ctypes.c_int)]),
+    "syn_cuda_model_load_gguf": (c_st, [c_vp, c_vp]),
+    "syn_cuda_model_load_safetensors": (c_st, [c_vp, c_vp]),
+    "syn_cuda_model_set_cache_dir": (c_st, [c_vp, ctypes.c_char_p]),
+    "syn_cuda_model_cache_hits": (c_st, [c_vp, ctypes.POINTER(ctypes.c_int)]),
     "syn_cuda_tp_shard_linear": (c_st, [ctypes.c_int, c_vp, c_size, c_size, c_vp, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, c_vp, c_vp,
                                         ctypes.POINTER(c_size), ctypes.POINTER(c_size)]),

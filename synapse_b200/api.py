@@ -506,7 +506,7 @@ class Model:
     ("INT8_KN", q_kn int8 [K*N], scales [N]) / (fmt_name, block bytes).
     """
 
-    def __init__(self, ctx, config, weights, max_seq, max_batch=1):
+    def __init__(self, ctx, config, weights, max_seq, max_batch=1, cache_dir=None, _stage=None):
         import json
         import numpy as np
         cfg = json.loads(config) if isinstance(config, str) else config
@@ -519,6 +519,12 @@ class Model:
         _check(lib().syn_cuda_model_create(ctx.handle, json.dumps(cfg).encode(), max_seq,
                                            max_batch, ctypes.byref(h)), "model_create")
         self.handle = h
+        if cache_dir:
+            _check(lib().syn_cuda_model_set_cache_dir(h, str(cache_dir).encode()),
+                   "model_set_cache_dir")
+        if _stage is not None:
+            _stage(h)
+            weights = {}
         hd = at["head_dim"]
         qd, kvd = at["num_heads"] * hd, at["num_kv_heads"] * hd
         hid, ff = a["hidden_size"], cfg["ffn"]["intermediate_size"]
@@ -546,6 +552,38 @@ class Model:
                                                        arr.ctypes.data_as(ctypes.c_void_p),
                                                        arr.size), "model_set_tensor " + name)
         _check(lib().syn_cuda_model_finalize(self.handle), "model_finalize")
+
+    @classmethod
+    def from_gguf(cls, ctx, path, max_seq, max_batch=1, cache_dir=None, config=None):
+        """A model from a GGUF file (syn_cuda_model_load_gguf): config from
+        its metadata unless given; quantised blocks go to the repacker as
+        they are; cache_dir keeps the repacked weights between loads."""
+        g = GGUFFile(path)
+        try:
+            cfg = config if config is not None else g.config()
+            return cls(ctx, cfg, None, max_seq, max_batch, cache_dir=cache_dir,
+                       _stage=lambda h: _check(lib().syn_cuda_model_load_gguf(h, g.handle),
+                                               "model_load_gguf"))
+        finally:
+            g.close()
+
+    @classmethod
+    def from_safetensors(cls, ctx, path, config, max_seq, max_batch=1, cache_dir=None):
+        """The reference's --quantize load of a safetensors checkpoint
+        (syn_cuda_model_load_safetensors): linears quantised to INT8 on the
+        device from f32 / f16 / bf16."""
+        f = SafetensorsFile(path)
+        try:
+            return cls(ctx, config, None, max_seq, max_batch, cache_dir=cache_dir,
+                       _stage=lambda h: _check(lib().syn_cuda_model_load_safetensors(h, f.handle),
+                                               "model_load_safetensors"))
+        finally:
+            f.close()
+
+    def cache_hits(self):
+        v = ctypes.c_int()
+        _check(lib().syn_cuda_model_cache_hits(self.handle, ctypes.byref(v)), "model_cache_hits")
+        return v.value
 
     def forward_prefill(self, token_ids, seq=0, want_logits=True):
         """Prefill of an empty sequence; returns (greedy next token, logits or None)."""
@@ -612,3 +650,124 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+class GGUFFile:
+    """A memory-mapped GGUF v2/v3 file (syn_gguf_*): tensor infos with the
+    raw bytes, scalar metadata, and the model config built from them."""
+
+    def __init__(self, path):
+        h = ctypes.c_void_p()
+        _check(lib().syn_gguf_open(str(path).encode(), ctypes.byref(h)), "gguf_open")
+        self.handle = h
+
+    def tensors(self):
+        """[(name, ggml_type, dims (ne0 first), bytes)] -- bytes copied out."""
+        n = ctypes.c_size_t()
+        _check(lib().syn_gguf_tensor_count(self.handle, ctypes.byref(n)), "gguf_tensor_count")
+        out = []
+        for i in range(n.value):
+            name, typ, nd = ctypes.c_char_p(), ctypes.c_uint32(), ctypes.c_size_t()
+            dims = (ctypes.c_uint64 * 4)()
+            data, nb = ctypes.c_void_p(), ctypes.c_size_t()
+            _check(lib().syn_gguf_tensor_info(self.handle, i, ctypes.byref(name), ctypes.byref(typ),
+                                              ctypes.byref(nd), dims, ctypes.byref(data),
+                                              ctypes.byref(nb)), "gguf_tensor_info")
+            raw = ctypes.string_at(data.value, nb.value) if nb.value else b""
+            out.append((name.value.decode(), typ.value, list(dims[:nd.value]), raw))
+        return out
+
+    def meta_num(self, key):
+        v = ctypes.c_double()
+        _check(lib().syn_gguf_meta_num(self.handle, key.encode(), ctypes.byref(v)), "gguf_meta_num")
+        return v.value
+
+    def meta_str(self, key):
+        v = ctypes.c_char_p()
+        _check(lib().syn_gguf_meta_str(self.handle, key.encode(), ctypes.byref(v)), "gguf_meta_str")
+        return v.value.decode()
+
+    def config(self):
+        import json
+        need = ctypes.c_size_t()
+        _check(lib().syn_gguf_config_json(self.handle, None, 0, ctypes.byref(need)), "gguf_config")
+        buf = ctypes.create_string_buffer(need.value)
+        _check(lib().syn_gguf_config_json(self.handle, buf, need.value, ctypes.byref(need)),
+               "gguf_config")
+        return json.loads(buf.value.decode())
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().syn_gguf_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def gguf_runner_name(name):
+    """llama.cpp tensor name -> the runner's name (None if unmapped)."""
+    buf = ctypes.create_string_buffer(512)
+    st = lib().syn_gguf_runner_name(name.encode(), buf, 512)
+    return buf.value.decode() if st == 0 else None
+
+
+class SafetensorsFile:
+    """A memory-mapped safetensors file (syn_safetensors_*)."""
+
+    DTYPES = {0: "F32", 1: "F16", 2: "BF16", 3: "I64", 4: "I32", 5: "U8"}
+
+    def __init__(self, path):
+        h = ctypes.c_void_p()
+        _check(lib().syn_safetensors_open(str(path).encode(), ctypes.byref(h)), "safetensors_open")
+        self.handle = h
+
+    def tensors(self):
+        """{name: (dtype name, shape, f32 numpy array as the loader converts it)}"""
+        import numpy as np
+        n = ctypes.c_size_t()
+        _check(lib().syn_safetensors_tensor_count(self.handle, ctypes.byref(n)), "st_count")
+        out = {}
+        for i in range(n.value):
+            name, dt, nd = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_size_t()
+            dims = (ctypes.c_uint64 * 4)()
+            data, nb = ctypes.c_void_p(), ctypes.c_size_t()
+            _check(lib().syn_safetensors_tensor_info(self.handle, i, ctypes.byref(name),
+                                                     ctypes.byref(dt), ctypes.byref(nd), dims,
+                                                     ctypes.byref(data), ctypes.byref(nb)),
+                   "st_info")
+            shape = list(dims[:nd.value])
+            cnt = int(np.prod(shape)) if shape else 1
+            arr = np.empty(cnt, np.float32)
+            _check(lib().syn_convert_to_f32(dt.value, data, cnt, arr.ctypes.data_as(ctypes.c_void_p)),
+                   "convert_to_f32")
+            out[name.value.decode()] = (self.DTYPES[dt.value], shape, arr.reshape(shape))
+        return out
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().syn_safetensors_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def quantize_weights_int8_half(bits, dtype, out_features, in_features):
+    """f16 / bf16 weight bits (device uint16/int16 tensor [N, K]) -> (int8
+    [K, N], f32 scales [N]) on the device (syn_cuda_quantize_weights_int8_half),
+    bit-exact with the reference's load-and-quantize route."""
+    _need_cuda(bits)
+    dt = {"F16": 1, "BF16": 2}[dtype]
+    q = torch.empty(in_features * out_features, dtype=torch.int8, device=bits.device)
+    s = torch.empty(out_features, dtype=torch.float32, device=bits.device)
+    _check(lib().syn_cuda_quantize_weights_int8_half(_ptr(bits), dt, out_features, in_features,
+                                                     _ptr(q), _ptr(s), _stream(bits)),
+           "quantize_weights_int8_half")
+    return q, s

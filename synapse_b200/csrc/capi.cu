@@ -161,6 +161,10 @@ struct CallScratch {
 };
 
 }  // namespace
+
+size_t weight_layout(syn_cuda_weight_s* w, uint8_t* base) { return layout(w, base); }
+size_t weight_src_row_bytes(int fmt, size_t k) { return src_row_bytes(fmt, k); }
+
 }  // namespace syn
 
 using namespace syn;

@@ -141,6 +141,19 @@ syn_status_t launch_quantize_rows(const float* x, size_t rows, size_t cols, int8
 syn_status_t launch_quantize_weights(const float* w, size_t n, size_t k, int8_t* out_kn,
                                      float* scales, cudaStream_t st);
 
+// The same from f16 / bf16 bit patterns (dtype SYN_DTYPE_F16 / _BF16),
+// converted to f32 as weight_loading/converter.rs does.
+syn_status_t launch_quantize_weights_half(const uint16_t* w, int dtype, size_t n, size_t k,
+                                          int8_t* out_kn, float* scales, cudaStream_t st);
+
+// The context a model was created on (runner.cu).
+syn_cuda_ctx_s* model_context(const syn_cuda_model_s* m);
+
+// Byte layout of a repacked weight (capi.cu): sets the array views of `w`
+// inside `base` (nullptr: sizes only) and returns the allocation's bytes.
+size_t weight_layout(syn_cuda_weight_s* w, uint8_t* base);
+size_t weight_src_row_bytes(int fmt, size_t k);
+
 // Repack kernels (repack.cu). ld_src: row stride of an INT8_KN source
 // (0 = n); ignored by block formats. w->buf / w->bytes are zero-filled first.
 syn_status_t repack_weight(syn_cuda_weight_s* w, const uint8_t* d_src, size_t ld_src,

@@ -13,6 +13,8 @@
 // quantization/primitives/int8_linear.rs:21-70): per output row
 // s = max|w| / 127 (1.0 for a zero row), q = clamp(round(w * (1/s)), -128, 127),
 // written in the reference's GEMM layout [K, N].
+// k_quantize_weights_half: the same from f16 / bf16 weights (safetensors
+// --quantize loads), converted as the reference's loader converts them.
 #include "internal.cuh"
 
 namespace syn {
@@ -70,7 +72,61 @@ __global__ void __launch_bounds__(QT) k_quantize_weights(const float* __restrict
   if (threadIdx.x == 0) scales[ch] = s;
 }
 
+// f16 / bf16 bits -> f32 as the safetensors loader converts them
+// (weight_loading/converter.rs:12-48; f16 subnormals come out at half their
+// value there, which f16_loader reproduces).
+template <int DT>
+__device__ __forceinline__ float half_bits_to_f32(uint16_t b) {
+  if constexpr (DT == SYN_DTYPE_BF16) return __uint_as_float((uint32_t)b << 16);
+  return f16_loader(b);
+}
+
+// k_quantize_weights on f16 / bf16 input: the row is converted to f32 by the
+// loader's rule first, so the result equals quantize_model on the f32
+// tensors the reference would have loaded (int8.rs:78-152).
+template <int DT>
+__global__ void __launch_bounds__(QT) k_quantize_weights_half(const uint16_t* __restrict__ w,
+                                                              long long n, long long k,
+                                                              int8_t* __restrict__ out_kn,
+                                                              float* __restrict__ scales) {
+  __shared__ float red[QT / 32];
+  const long long ch = blockIdx.x;
+  const uint16_t* row = w + ch * k;
+  float amax = 0.0f;
+  for (long long i = threadIdx.x; i < k; i += QT)
+    amax = fmaxf(amax, fabsf(half_bits_to_f32<DT>(row[i])));
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < QT / 32; i++) amax = fmaxf(amax, red[i]);
+  const float s = (amax == 0.0f) ? 1.0f : __fdiv_rn(amax, 127.0f);
+  const float inv_s = __fdiv_rn(1.0f, s);
+  for (long long j = threadIdx.x; j < k; j += QT) {
+    float r = roundf(__fmul_rn(half_bits_to_f32<DT>(row[j]), inv_s));
+    r = fminf(127.0f, fmaxf(-128.0f, r));
+    out_kn[j * n + ch] = (int8_t)(int)r;
+  }
+  if (threadIdx.x == 0) scales[ch] = s;
+}
+
 }  // namespace
+
+syn_status_t launch_quantize_weights_half(const uint16_t* w, int dtype, size_t n, size_t k,
+                                          int8_t* out_kn, float* scales, cudaStream_t st) {
+  if (n > 0x7FFFFFFFull) return SYN_ERR_INVALID_ARG;
+  if (dtype == SYN_DTYPE_F16)
+    k_quantize_weights_half<SYN_DTYPE_F16><<<(unsigned)n, QT, 0, st>>>(w, (long long)n,
+                                                                       (long long)k, out_kn, scales);
+  else if (dtype == SYN_DTYPE_BF16)
+    k_quantize_weights_half<SYN_DTYPE_BF16><<<(unsigned)n, QT, 0, st>>>(w, (long long)n,
+                                                                        (long long)k, out_kn, scales);
+  else
+    return SYN_ERR_INVALID_ARG;
+  SYN_LAUNCH_CHECK("k_quantize_weights_half");
+  return SYN_OK;
+}
 
 syn_status_t launch_quantize_rows(const float* x, size_t rows, size_t cols, int8_t* out,
                                   float* scales, cudaStream_t st) {

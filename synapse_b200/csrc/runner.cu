@@ -195,6 +195,8 @@ struct syn_cuda_model_s {
   size_t max_seq = 0, max_batch = 0, max_rows = 0;
   bool int8 = false;
   bool finalized = false;
+  std::string cache_dir;  // repacked-weight cache (empty: none)
+  int cache_hits = 0;     // weights read from the cache by finalize
   // staged host weights
   std::map<std::string, HostLinear> lin;
   std::map<std::string, std::vector<float>> ten;
@@ -239,6 +241,14 @@ syn_status_t dev_alloc(syn_cuda_model_s* m, void** p, size_t bytes) {
   return SYN_OK;
 }
 
+}  // namespace
+
+namespace syn {
+syn_cuda_ctx_s* model_context(const syn_cuda_model_s* m) { return m->ctx; }
+}  // namespace syn
+
+namespace {
+
 template <typename T>
 syn_status_t dev_alloc_t(syn_cuda_model_s* m, T** p, size_t count) {
   return dev_alloc(m, reinterpret_cast<void**>(p), count * sizeof(T));
@@ -263,8 +273,16 @@ syn_status_t upload_tensor(syn_cuda_model_s* m, const std::string& name, size_t 
 }
 
 syn_status_t upload_linear(syn_cuda_model_s* m, const HostLinear& hl, syn_cuda_weight_t** out) {
-  return syn_cuda_weight_upload(m->ctx, (syn_qformat_t)hl.fmt, hl.data.data(), hl.n, hl.k,
-                                hl.fmt == SYN_QFMT_INT8_KN ? hl.scales.data() : nullptr, out);
+  const float* sc = hl.fmt == SYN_QFMT_INT8_KN ? hl.scales.data() : nullptr;
+  if (!m->cache_dir.empty()) {
+    int hit = 0;
+    syn_status_t s = syn_cuda_weight_upload_cached(m->ctx, (syn_qformat_t)hl.fmt, hl.data.data(),
+                                                   hl.n, hl.k, sc, m->cache_dir.c_str(), out, &hit);
+    m->cache_hits += hit;
+    return s;
+  }
+  return syn_cuda_weight_upload(m->ctx, (syn_qformat_t)hl.fmt, hl.data.data(), hl.n, hl.k, sc,
+                                out);
 }
 
 const HostLinear* find_lin(syn_cuda_model_s* m, const std::string& name, size_t n, size_t k) {
@@ -466,6 +484,19 @@ syn_status_t syn_cuda_model_create(syn_cuda_ctx_t* ctx, const char* config_json,
   m->max_batch = max_batch;
   m->max_rows = std::max(max_seq, max_batch);
   *out = m;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_set_cache_dir(syn_cuda_model_t* m, const char* dir) {
+  if (!m) return SYN_ERR_NULL_PTR;
+  if (m->finalized) return SYN_ERR_INVALID_ARG;
+  m->cache_dir = dir ? dir : "";
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_cache_hits(const syn_cuda_model_t* m, int* hits) {
+  if (!m || !hits) return SYN_ERR_NULL_PTR;
+  *hits = m->cache_hits;
   return SYN_OK;
 }
 

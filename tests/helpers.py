@@ -57,3 +57,67 @@ def max_rel_err(y, ref):
     ref = np.asarray(ref, np.float64)
     den = np.max(np.abs(ref))
     return float(np.max(np.abs(y - ref)) / den) if den > 0 else float(np.max(np.abs(y)))
+
+
+# ---------------------------------------------------------------------------
+# Weight-file writers (the layouts the reference's loaders read)
+# ---------------------------------------------------------------------------
+GGUF_TYPES = {"F32": 0, "F16": 1, "Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q6_K": 14}
+
+
+def _gguf_str(s):
+    b = s.encode()
+    return len(b).to_bytes(8, "little") + b
+
+
+def gguf_bytes(tensors, meta=(), version=3, alignment=32):
+    """A GGUF file as make_gguf_raw (weight_loading/gguf.rs:768-789) builds
+    one, generalised: tensors = [(name, ggml_type, dims ne0-first, raw
+    bytes)], meta = [(key, value)] with int -> u32, float -> f32, str ->
+    string, list of str -> array of strings. Tensor data is aligned to
+    `alignment` inside the data section."""
+    import struct
+    out = bytearray()
+    out += struct.pack("<IIQQ", 0x46554747, version, len(tensors), len(meta))
+    for k, v in meta:
+        out += _gguf_str(k)
+        if isinstance(v, bool):
+            out += struct.pack("<IB", 7, int(v))
+        elif isinstance(v, int):
+            out += struct.pack("<II", 4, v)
+        elif isinstance(v, float):
+            out += struct.pack("<If", 6, v)
+        elif isinstance(v, str):
+            out += struct.pack("<I", 8) + _gguf_str(v)
+        else:
+            out += struct.pack("<IIQ", 9, 8, len(v)) + b"".join(_gguf_str(x) for x in v)
+    offs, off = [], 0
+    for name, typ, dims, raw in tensors:
+        offs.append(off)
+        off = (off + len(raw) + alignment - 1) // alignment * alignment
+    for (name, typ, dims, raw), o in zip(tensors, offs):
+        out += _gguf_str(name) + struct.pack("<I", len(dims))
+        out += b"".join(struct.pack("<Q", d) for d in dims)
+        out += struct.pack("<IQ", typ, o)
+    out += b"\0" * ((-len(out)) % alignment)
+    data = bytearray()
+    for (name, typ, dims, raw), o in zip(tensors, offs):
+        data += b"\0" * (o - len(data))
+        data += raw
+    return bytes(out + data)
+
+
+def safetensors_bytes(tensors, metadata=None):
+    """tensors = [(name, dtype, shape, raw bytes)] -> safetensors file bytes
+    (make_safetensors, weight_loading/safetensors.rs:310-342)."""
+    import json
+    import struct
+    header, data = {}, bytearray()
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    for name, dtype, shape, raw in tensors:
+        header[name] = {"dtype": dtype, "shape": list(shape),
+                        "data_offsets": [len(data), len(data) + len(raw)]}
+        data += raw
+    h = json.dumps(header).encode()
+    return struct.pack("<Q", len(h)) + h + bytes(data)
