@@ -396,6 +396,25 @@ syn_status_t syn_cuda_decode_step(syn_cuda_model_t *m, size_t batch,
  * synchronisation at the end. out_tokens: host [batch][n_steps]. */
 syn_status_t syn_cuda_generate(syn_cuda_model_t *m, size_t batch, size_t n_steps,
                                int32_t *out_tokens);
+/* Speculative decoding support. syn_cuda_decode_span runs n (<= 16)
+ * tokens of sequence seq at positions len .. len+n-1 (each attending to the
+ * cache up to itself, RoPE at its position) through the first n_layers
+ * layers (0 = all), and returns every row's greedy token (and optionally
+ * its logits [n, vocab]); the cache length is NOT advanced, so the caller
+ * commits or rolls back with syn_cuda_model_truncate. Not for TP models. */
+syn_status_t syn_cuda_decode_span(syn_cuda_model_t *m, size_t seq, const int32_t *tokens,
+                                  size_t n, size_t n_layers, int32_t *out_tokens,
+                                  float *logits_host);
+/* Self-speculative greedy generation of n_steps tokens after last_token
+ * for sequence seq (generation/pipeline.rs:281-396): k (<= 15) draft tokens
+ * from the first draft_layers layers, KV rollback on the device, one
+ * full-model span step to verify them. Every draft token is checked (the
+ * reference accepts all), so the tokens are the plain greedy ones; drafted /
+ * accepted (optional) count the draft tokens made and kept. */
+syn_status_t syn_cuda_generate_speculative(syn_cuda_model_t *m, size_t seq, int32_t last_token,
+                                           size_t n_steps, size_t k, size_t draft_layers,
+                                           int32_t *out_tokens, size_t *drafted,
+                                           size_t *accepted);
 syn_status_t syn_cuda_model_seq_len(const syn_cuda_model_t *m, size_t seq, size_t *len);
 syn_status_t syn_cuda_model_reset(syn_cuda_model_t *m, size_t seq);
 syn_status_t syn_cuda_model_truncate(syn_cuda_model_t *m, size_t seq, size_t new_len);

@@ -629,6 +629,37 @@ class Model:
                                        out.ctypes.data_as(ctypes.c_void_p)), "generate")
         return out
 
+    def decode_span(self, tokens, seq=0, n_layers=0, want_logits=False):
+        """Tokens at the next positions of `seq` (syn_cuda_decode_span):
+        (greedy token per row, logits [n, vocab] or None); the cache length
+        is not advanced."""
+        import numpy as np
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        out = np.empty(ids.size, dtype=np.int32)
+        logits = np.empty((ids.size, self.vocab), dtype=np.float32) if want_logits else None
+        _check(lib().syn_cuda_decode_span(self.handle, seq, ids.ctypes.data_as(ctypes.c_void_p),
+                                          ids.size, n_layers, out.ctypes.data_as(ctypes.c_void_p),
+                                          logits.ctypes.data_as(ctypes.c_void_p)
+                                          if want_logits else None), "decode_span")
+        return out, logits
+
+    def generate_speculative(self, prompt, steps, k=4, draft_layers=None, seq=0):
+        """Greedy generation with self-speculative decoding
+        (syn_cuda_generate_speculative): returns (tokens, drafted, accepted);
+        tokens[0] comes from the prefill, as in generate_greedy."""
+        import numpy as np
+        if draft_layers is None:
+            draft_layers = max(1, self.cfg["architecture"]["num_layers"] // 4)
+        tok, _ = self.forward_prefill(prompt, seq, want_logits=False)
+        out = np.empty(max(0, steps - 1), dtype=np.int32)
+        nd, na = ctypes.c_size_t(), ctypes.c_size_t()
+        if steps > 1:
+            _check(lib().syn_cuda_generate_speculative(
+                self.handle, seq, tok, steps - 1, k, draft_layers,
+                out.ctypes.data_as(ctypes.c_void_p), ctypes.byref(nd), ctypes.byref(na)),
+                "generate_speculative")
+        return [tok] + out.tolist(), nd.value, na.value
+
     def seq_len(self, seq=0):
         v = ctypes.c_size_t()
         _check(lib().syn_cuda_model_seq_len(self.handle, seq, ctypes.byref(v)), "model_seq_len")

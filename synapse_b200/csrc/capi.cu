@@ -313,7 +313,7 @@ syn_status_t syn_cuda_q4_0_gemv(size_t n, size_t k, const float* a, const uint8_
   if (k % 32 != 0) return SYN_ERR_SHAPE_MISMATCH;
   cudaStream_t st = (cudaStream_t)stream;
   CallScratch cs;
-  syn_status_t s = cs.init(SYN_QFMT_Q4_0, 1, n, k, 0, st);
+  syn_status_t s = cs.init(GEMV_FMT_Q4_0_RAW, 1, n, k, 0, st);
   if (s == SYN_OK) s = launch_q4_0_raw(n, k, a, b_q4, c, cs.part, cs.part_cap, cs.cnt, nullptr, st);
   return cs.release(s, st);
 }

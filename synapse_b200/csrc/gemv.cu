@@ -125,6 +125,11 @@ struct GemvParams {
   int nfast;  // 1: parallel sum of squares; 0: the reference's vecHsum order
   int xs_off; // byte offset of the normalised row in dynamic shared memory
   int ns;     // k_qgemv_tma ring depth
+  // K split reduced through the thread-block cluster (1) instead of global
+  // scratch (0): the nks CTAs of a row group form one cluster along y, and
+  // rank 0 sums the others' partials from its shared memory (recv_off).
+  int cluster;
+  int recv_off;
 };
 
 __device__ __forceinline__ void consumer_sync() {
@@ -464,6 +469,7 @@ struct CtaShared {
   float srow[MT];  // INT8: per-row activation scale sa
   float sinv[MT];  // INT8: 127 / max (0 for an all-zero row)
   int slast;
+  uint64_t rbar;   // cluster K split: the peers' partials have arrived (rank 0)
 };
 
 // Converts the CTA's activation blocks [cb0, cb1) of MT rows into `act`
@@ -564,6 +570,80 @@ __device__ void cta_prologue(const GemvParams& p, int m0, int cb0, int cb1, uint
 // Reduces the CTA's warp partials (block formats: sh.red; INT8: csum) and
 // writes y or, with K split across CTAs, the CTA partials plus the ordered
 // final sum by the last CTA of the row group. Consumer threads only.
+// Cluster K split (p.cluster): every CTA of the row group's cluster (rank =
+// ks) stores its partials into rank 0's shared memory -- block formats
+// recv[ks][mm][lane] (f32); INT8 the exact int32 sum of its chunks
+// recv[ks][mm][lane], or with the chunked epilogue every chunk's sum
+// recv[mm][chunk][lane] -- and arrives on rank 0's mbarrier; rank 0 waits
+// (bounded) and sums them in K order, as the global-scratch path does: the
+// same bits, without the scratch round trips through L2.
+template <int FMT, int MT>
+__device__ void cluster_finish(const GemvParams& p, int g, int ks, int m0, int cc0, int ncc,
+                               const int* csum, CtaShared<MT>& sh, float sb_pre, bool have_sb) {
+  extern __shared__ __align__(128) uint8_t dsm[];
+  uint8_t* recv = dsm + p.recv_off;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = g * 32 + lane;
+  cluster_wait();  // every peer has initialised its barrier and buffers
+  if (warp < MT && m0 + warp < p.m) {
+    const int mm = warp;
+    if constexpr (FMT == F_INT8) {
+      if (MT > 1 && p.chunked) {
+        uint32_t* dst = reinterpret_cast<uint32_t*>(recv) + ((size_t)mm * p.nchunks + cc0) * 32 + lane;
+        for (int c = 0; c < ncc; c++) {
+          const uint32_t v = (uint32_t)csum[(mm * ncc + c) * 32 + lane];
+          if (ks == 0) dst[c * 32] = v;
+          else st_cluster_u32(cluster_map(dst + c * 32, 0), v);
+        }
+      } else {
+        int t = 0;
+        for (int c = 0; c < ncc; c++) t += csum[(mm * ncc + c) * 32 + lane];
+        uint32_t* dst = reinterpret_cast<uint32_t*>(recv) + ((size_t)ks * MT + mm) * 32 + lane;
+        if (ks == 0) *dst = (uint32_t)t;
+        else st_cluster_u32(cluster_map(dst, 0), (uint32_t)t);
+      }
+    } else {
+      float v = 0.0f;
+#pragma unroll
+      for (int i = 0; i < WARPS; i++) v += sh.red[i][mm][lane];
+      float* dst = reinterpret_cast<float*>(recv) + ((size_t)ks * MT + mm) * 32 + lane;
+      if (ks == 0) *dst = v;
+      else st_cluster_u32(cluster_map(dst, 0), __float_as_uint(v));
+    }
+  }
+  if (ks != 0) {
+    fence_acq_rel_cluster();
+    consumer_sync();
+    if (threadIdx.x == 0) mbar_arrive_remote(cluster_map(&sh.rbar, 0));
+    return;
+  }
+  if (threadIdx.x == 0 && !mbar_wait_cluster_bounded(&sh.rbar, 0)) report(p, SYN_ERR_TIMEOUT);
+  consumer_sync();
+  if (warp < MT) {
+    const int mm = warp, m = m0 + mm;
+    if (m < p.m && row < p.n) {
+      float out = 0.0f;
+      if constexpr (FMT == F_INT8) {
+        const float sa = sh.srow[mm], sbv = have_sb ? sb_pre : p.sb[row];
+        if (MT > 1 && p.chunked) {
+          const int* src = reinterpret_cast<const int*>(recv) + (size_t)mm * p.nchunks * 32 + lane;
+          for (int c = 0; c < p.nchunks; c++)
+            out = __fadd_rn(out, __fmul_rn(__fmul_rn((float)src[c * 32], sa), sbv));
+        } else {
+          const int* src = reinterpret_cast<const int*>(recv) + (size_t)mm * 32 + lane;
+          int tot = 0;
+          for (int s = 0; s < p.nks; s++) tot += src[(size_t)s * MT * 32];
+          out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
+        }
+      } else {
+        const float* src = reinterpret_cast<const float*>(recv) + (size_t)mm * 32 + lane;
+        for (int s = 0; s < p.nks; s++) out += src[(size_t)s * MT * 32];
+      }
+      p.y[(long long)m * p.ldy + row] = out;
+    }
+  }
+}
+
 template <int FMT, int MT>
 __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, int ncc,
                            const int* csum, CtaShared<MT>& sh, float sb_pre = 0.0f,
@@ -573,6 +653,10 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
   const bool split = p.nks > 1;
   const long long G32 = (long long)p.groups * 32;
   consumer_sync();
+  if (split && p.cluster) {
+    cluster_finish<FMT, MT>(p, g, ks, m0, cc0, ncc, csum, sh, sb_pre, have_sb);
+    return;
+  }
   if (warp < MT) {
     const int mm = warp, m = m0 + mm;
     if (m < p.m) {
@@ -732,7 +816,9 @@ __device__ void norm_prologue(const GemvParams& p, float* xs, CtaShared<MT>& sh,
 // Threads 0-255 consume, warp 8 (threads 256-287) produces.
 // ---------------------------------------------------------------------------
 template <int FMT, int MT, int RG>
-__global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) {
+// (The INT8 one-row kernel is held to 56 registers, four CTAs per SM.)
+__global__ void __launch_bounds__(THREADS + 32, (FMT == F_INT8 && MT == 1) ? 4 : 1)
+    k_qgemv_tma(const GemvParams p) {
   using S = Stage<FMT>;
   static_assert(RG == 1 || (FMT != F_INT8 && MT == 1), "row-group pairs: block formats, M=1");
   extern __shared__ __align__(128) uint8_t sm[];
@@ -757,9 +843,11 @@ __global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) 
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], WARPS);
     }
+    if (p.cluster) mbar_init(&sh.rbar, p.nks - 1);
     mbar_fence_init();
   }
   __syncthreads();
+  if (p.cluster) cluster_arrive_relaxed();  // all threads, before the producer leaves
 
   if (warp == WARPS) {
     // ---- producer: stream this CTA's weight bytes, stage by stage ----
@@ -977,6 +1065,8 @@ struct Plan {
   int ns;  // ring depth of k_qgemv_tma
   size_t xs_bytes;  // fused-norm row in shared memory (0 = none)
   size_t act_smem;  // activations + INT8 chunk sums
+  int cluster;      // K split reduced through the cluster (nks CTAs along y)
+  size_t recv_bytes;  // cluster rank 0's receive buffer for the peers' partials
 };
 
 int mt_for(size_t m) { return m == 1 ? 1 : (m == 2 ? 2 : 4); }
@@ -998,10 +1088,14 @@ int tune(const char* name, int dflt) {
 // Dynamic shared memory of k_qgemv_tma: the ring, the activations and, for
 // the fused norm, the normalised row.
 size_t stage_bytes(int fmt);
-size_t tma_smem(const Plan& pl, int fmt, int rg, int ns) {
+size_t tma_smem_no_recv(const Plan& pl, int fmt, int rg, int ns) {
   const size_t ring = (size_t)ns * rg * stage_bytes(fmt);
   const size_t base = ring + pl.act_smem;
   return pl.xs_bytes ? ((base + 15) & ~size_t(15)) + pl.xs_bytes : base;
+}
+size_t tma_smem(const Plan& pl, int fmt, int rg, int ns) {
+  const size_t b = tma_smem_no_recv(pl, fmt, rg, ns);
+  return pl.recv_bytes ? ((b + 15) & ~size_t(15)) + pl.recv_bytes : b;
 }
 
 int tma_occupancy(int fmt, int mt, int rg, size_t smem);
@@ -1027,6 +1121,9 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
   // a split CTA would stream fewer than 64 blocks)
   const int min_split_blocks = tune("SYN_GEMV_MIN_SPLIT_BLOCKS", 64);
   while (nks > 1 && pl.nblk / nks < min_split_blocks) nks--;
+  // Cluster K splits: at most 8 CTAs per cluster (the portable size).
+  const bool use_cluster = fmt != F_Q4_0RAW && tune("SYN_GEMV_CLUSTER", 1) != 0;
+  if (use_cluster) nks = std::min(nks, 8);
   const int abb = fmt == F_INT8 ? 32 : 80;
   auto set_split = [&](int splits) {
     int kr = (pl.nblk + splits - 1) / splits;
@@ -1039,6 +1136,10 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
     pl.act_smem =
         (size_t)pl.mt * kr * abb + (fmt == F_INT8 ? (size_t)pl.mt * ncc * 32 * 4 : 0);
     pl.xs_bytes = xs_bytes;
+    pl.cluster = use_cluster && pl.nks > 1 && pl.nks <= 8;
+    pl.recv_bytes = !pl.cluster ? 0
+                    : std::max((size_t)pl.nks, fmt == F_INT8 ? (size_t)pl.nchunks : (size_t)0) *
+                          pl.mt * 32 * 4;
   };
   set_split(nks);
   // Row-group pairs (block formats, M = 1, K not split): two groups share
@@ -1085,17 +1186,24 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                       cudaStream_t st, Args&&... args) {
+                       cudaStream_t st, int cluster_y, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = tune("SYN_GEMV_PDL", 1) ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cluster_y > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = (unsigned)cluster_y;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
@@ -1195,25 +1303,28 @@ syn_status_t launch_t(const GemvParams& p, const Plan& pl, cudaStream_t st) {
   cudaError_t e;
   if constexpr (FMT == F_Q4_0RAW) {
     allow_smem(k_qgemv<FMT, MT>);
-    e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.act_smem, st, p);
+    e = launch_pdl(k_qgemv<FMT, MT>, grid, dim3(THREADS), pl.act_smem, st, 1, p);
   } else {
     GemvParams q = p;
     const int rg = (FMT != F_INT8 && MT == 1) ? pl.rg : 1;
     q.ns = pl.ns;
     q.xs_off = (int)(((size_t)pl.ns * rg * Stage<FMT>::BYTES + pl.act_smem + 15) & ~size_t(15));
+    q.cluster = pl.cluster;
+    q.recv_off = (int)((tma_smem_no_recv(pl, FMT, rg, pl.ns) + 15) & ~size_t(15));
     const size_t smem = tma_smem(pl, FMT, rg, pl.ns);
+    const int cy = pl.cluster ? pl.nks : 1;
     if constexpr (FMT != F_INT8 && MT == 1) {
       if (rg == 2) {
         allow_smem(k_qgemv_tma<FMT, 1, 2>);
         grid.x = (unsigned)((pl.groups + 1) / 2);
-        e = launch_pdl(k_qgemv_tma<FMT, 1, 2>, grid, dim3(THREADS + 32), smem, st, q);
+        e = launch_pdl(k_qgemv_tma<FMT, 1, 2>, grid, dim3(THREADS + 32), smem, st, cy, q);
       } else {
         allow_smem(k_qgemv_tma<FMT, 1, 1>);
-        e = launch_pdl(k_qgemv_tma<FMT, 1, 1>, grid, dim3(THREADS + 32), smem, st, q);
+        e = launch_pdl(k_qgemv_tma<FMT, 1, 1>, grid, dim3(THREADS + 32), smem, st, cy, q);
       }
     } else {
       allow_smem(k_qgemv_tma<FMT, MT, 1>);
-      e = launch_pdl(k_qgemv_tma<FMT, MT, 1>, grid, dim3(THREADS + 32), smem, st, q);
+      e = launch_pdl(k_qgemv_tma<FMT, MT, 1>, grid, dim3(THREADS + 32), smem, st, cy, q);
     }
   }
   if (e != cudaSuccess) {
@@ -1244,7 +1355,7 @@ syn_status_t run_gemv(int fmt, const GemvParams& p, const Plan& pl, cudaStream_t
 
 // Bytes of split-K partial sums a launch of plan `pl` writes (0 unsplit).
 size_t plan_part_bytes(int fk, const Plan& pl, size_t m) {
-  if (pl.nks <= 1) return 0;
+  if (pl.nks <= 1 || pl.cluster) return 0;
   const size_t per = fk == F_INT8 ? (size_t)pl.nchunks : (size_t)pl.nks;
   return m * per * (size_t)pl.groups * 32 * sizeof(float);
 }
@@ -1306,7 +1417,7 @@ syn_status_t launch_qgemv(const syn_cuda_weight_s* w, const float* x, size_t ldx
   p.ldy = (long long)ldy;
   p.chunked = chunked;
   fill_common(p, pl, part, cnt, err);
-  if (pl.nks > 1 && (!part || !cnt || plan_part_bytes(fk, pl, m) > part_cap))
+  if (pl.nks > 1 && !pl.cluster && (!part || !cnt || plan_part_bytes(fk, pl, m) > part_cap))
     return SYN_ERR_INTERNAL;
   return run_gemv(fk, p, pl, st);
 }
@@ -1340,7 +1451,7 @@ syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, f
   p.nres_out = nm.res_out;
   p.nfast = nm.fast;
   fill_common(p, pl, part, cnt, err);
-  if (pl.nks > 1 && (!part || !cnt || plan_part_bytes(fk, pl, 1) > part_cap))
+  if (pl.nks > 1 && !pl.cluster && (!part || !cnt || plan_part_bytes(fk, pl, 1) > part_cap))
     return SYN_ERR_INTERNAL;
   return run_gemv(fk, p, pl, st);
 }
@@ -1350,7 +1461,7 @@ syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* 
                              cudaStream_t st) {
   if (n > 0x7FFFFFFFull || k > 0x3FFFFFFFull) return SYN_ERR_UNSUPPORTED;
   if (reinterpret_cast<uintptr_t>(a) & 15) return SYN_ERR_NOT_CONTIGUOUS;
-  const Plan pl = make_plan(F_Q4_0, 1, n, k);
+  const Plan pl = make_plan(F_Q4_0RAW, 1, n, k);
   GemvParams p{};
   p.q = b;
   p.x = a;
@@ -1362,7 +1473,7 @@ syn_status_t launch_q4_0_raw(size_t n, size_t k, const float* a, const uint8_t* 
   p.y = c;
   p.ldy = (long long)n;
   fill_common(p, pl, part, cnt, err);
-  if (pl.nks > 1 && (!part || !cnt || plan_part_bytes(F_Q4_0, pl, 1) > part_cap))
+  if (pl.nks > 1 && (!part || !cnt || plan_part_bytes(F_Q4_0RAW, pl, 1) > part_cap))
     return SYN_ERR_INTERNAL;
   return run_gemv(F_Q4_0RAW, p, pl, st);
 }

@@ -18,6 +18,7 @@ struct syn_cuda_ctx_s {
   int* err;          // device-side error word (e.g. SYN_ERR_TIMEOUT)
   void* nccl;        // tensor-parallel communicator (ncclComm_t) or nullptr
   int tp_rank, tp_world;
+  void* tp_peer;     // peer-memory all-reduce state (tp.cu) or nullptr
 };
 
 // Repacked weight in HBM. One allocation; the views below point into it.
@@ -87,6 +88,8 @@ struct DeviceGuard {
 // zero). Every launch takes the capacity of its partial-sum buffer and
 // returns SYN_ERR_INTERNAL, launching nothing, if its plan needs more.
 size_t gemv_partial_bytes(int fmt, size_t m, size_t n, size_t kp, size_t k = 0);
+// fmt value of the raw-layout Q4_0 GEMV (syn_cuda_q4_0_gemv) for the above
+constexpr int GEMV_FMT_Q4_0_RAW = 100;
 size_t gemv_counter_bytes(size_t m, size_t n);
 
 // Launches the fused GEMV for rows [0, m) of x (programmatic dependent
@@ -198,6 +201,11 @@ syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, 
 // length; RoPE at offsets 0..ntok-1 as the reference's prefill).
 syn_status_t launch_attn_prefill_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
                                       cudaStream_t st);
+// ntok new positions of sequence `seq` from its current length, each
+// attending to the cache up to itself (speculative verification; RoPE at
+// the cache slots). The cache length is not advanced.
+syn_status_t launch_attn_span_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                   cudaStream_t st);
 // The two halves of the prefill: norm/RoPE/append, then attention.
 syn_status_t launch_norm_rope_append_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
                                           cudaStream_t st);

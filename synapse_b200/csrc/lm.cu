@@ -204,6 +204,13 @@ struct AttnParams {
   const int* len;      // [batch] positions already committed
   int seq0;            // prefill: the sequence; decode: row b is sequence b
   int n_tokens;        // prefill tokens
+  // Decode kernels, span mode: row b is position len[seq0] + b of sequence
+  // seq0 (a multi-token verification step); q is already normalised and
+  // rotated and K/V already appended (k_norm_rope_append with rope_at_slot).
+  int span;
+  // k_norm_rope_append: RoPE at the cache slot (len + t) instead of the
+  // reference prefill's offset t (attention.rs:171-190)
+  int rope_at_slot;
   float* out;          // [rows][n_heads*hd]
   long long ldo;
   float scale;
@@ -305,15 +312,20 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   // Before griddepcontrol.wait only data written two or more kernels back is
   // read: the committed length (argmax of the previous step), the cached
   // rows below it (previous steps' attention) and the RoPE tables. Their
-  // loads overlap the tail of the Q/K/V matmul.
-  const int pos = p.len[b];
+  // loads overlap the tail of the Q/K/V matmul. Span mode: rows from len0 on
+  // were appended by the kernel before, so only rows below len0 are read
+  // early.
+  const int sq = p.span ? p.seq0 : b;  // this row's sequence
+  const int len0 = p.len[sq];
+  const int pos = p.span ? len0 + b : len0;
+  const int early = p.span ? len0 : pos;  // rows [0, early) may be read before the wait
   if (pos >= p.max_seq) {  // cache full: nothing is written (the host reports it)
     griddep_wait();
     if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
     return;
   }
-  float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
-  float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
+  float* kcb = p.kc + (size_t)sq * p.max_seq * kvd + kvh * HD;
+  float* vcb = p.vc + (size_t)sq * p.max_seq * kvd + kvh * HD;
   const int L = pos + 1;
   const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
   const int eff = L - off;
@@ -322,7 +334,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
     cs[HD / 2 + i] = p.sin_t[(size_t)pos * (HD / 2) + i];
   }
   float4 kv[Q4];  // K row of position `tid` (first pass of the score loop)
-  const bool kpre = tid < eff && off + tid != pos;
+  const bool kpre = tid < eff && off + tid < early;
   if (kpre) {
 #pragma unroll
     for (int c = 0; c < Q4; c++)
@@ -334,33 +346,44 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
 #pragma unroll
     for (int u = 0; u < PER; u++) {
       const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < cn0 && off + r != pos)
+      if (r < cn0 && off + r < early)
         tmp[u] = reinterpret_cast<const float4*>(vcb + (size_t)(off + r) * kvd)[c4];
     }
 #pragma unroll
     for (int u = 0; u < PER; u++) {
       const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < cn0 && off + r != pos) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
+      if (r < cn0 && off + r < early) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
     }
   }
   griddep_wait();
   const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
   const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
   const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
-  for (int i = tid; i < HD; i += DEC_THREADS) {
-    xs[i] = qrow[i];
-    xs[HD + i] = krow[i];
-    xs[2 * HD + i] = vrow[i];
-  }
-  __syncthreads();
-  norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, cs, cs + HD / 2, 0, lanes, scl, DEC_THREADS);
-  if (h % G == 0)
-    for (int i = tid; i < HD; i += DEC_THREADS) {
-      kcb[(size_t)pos * kvd + i] = xs[HD + i];
-      vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
+  if (p.span) {  // q is ready; this step's K/V rows are in the cache
+    for (int i = tid; i < HD; i += DEC_THREADS) xs[i] = qrow[i];
+    for (int t = tid; t < cn0 * Q4; t += DEC_THREADS) {
+      const int r = t / Q4, c4 = t - r * Q4;
+      if (off + r >= early)
+        reinterpret_cast<float4*>(vb + r * VS)[c4] =
+            reinterpret_cast<const float4*>(vcb + (size_t)(off + r) * kvd)[c4];
     }
-  if (pos - off < cn0)  // the new V row in the first chunk
-    for (int i = tid; i < HD; i += DEC_THREADS) vb[(pos - off) * VS + i] = xs[2 * HD + i];
+    __syncthreads();
+  } else {
+    for (int i = tid; i < HD; i += DEC_THREADS) {
+      xs[i] = qrow[i];
+      xs[HD + i] = krow[i];
+      xs[2 * HD + i] = vrow[i];
+    }
+    __syncthreads();
+    norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, cs, cs + HD / 2, 0, lanes, scl, DEC_THREADS);
+    if (h % G == 0)
+      for (int i = tid; i < HD; i += DEC_THREADS) {
+        kcb[(size_t)pos * kvd + i] = xs[HD + i];
+        vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
+      }
+    if (pos - off < cn0)  // the new V row in the first chunk
+      for (int i = tid; i < HD; i += DEC_THREADS) vb[(pos - off) * VS + i] = xs[2 * HD + i];
+  }
 
   // scores: below 64 positions the reference's scalar loop (sum += a*b);
   // from 64 on matmul_t (@mulAdd except the last eff%8 columns). Each thread
@@ -369,7 +392,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   for (int s = tid; s < eff; s += DEC_THREADS) {
     const int row = off + s;
     if (!(s == tid && kpre)) {
-      const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
+      const float* kr = row == pos && !p.span ? xs + HD : kcb + (size_t)row * kvd;
 #pragma unroll
       for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
     }
@@ -413,8 +436,9 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
         const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
         if (r < cn) {
           const int row = off + c0 + r;
-          tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
-                              : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+          tmp[u] = row == pos && !p.span
+                       ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
+                       : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
         }
       }
 #pragma unroll
@@ -469,8 +493,8 @@ __global__ void __launch_bounds__(512) k_norm_rope_append(const AttnParams p) {
                     : const_cast<float*>(p.k) + (long long)t * p.ld + (long long)(hh - p.n_heads) * hd;
   for (int i = threadIdx.x; i < hd; i += blockDim.x) xs[i] = src[i];
   __syncthreads();
-  norm_rope(xs, 1, hd, is_q ? p.qn : p.kn, nullptr, 1, p.eps, p.cos_t, p.sin_t, t, lanes, scl,
-            blockDim.x);
+  norm_rope(xs, 1, hd, is_q ? p.qn : p.kn, nullptr, 1, p.eps, p.cos_t, p.sin_t,
+            p.rope_at_slot ? slot : t, lanes, scl, blockDim.x);
   griddep_launch();
   if (is_q) {
     for (int i = threadIdx.x; i < hd; i += blockDim.x) src[i] = xs[i];
@@ -716,7 +740,8 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
   float* base = part + ((size_t)b * p.n_heads + h) * nsplit * (HD + 2);
   float* dst = base + (size_t)sp * (HD + 2);
   griddep_wait();
-  const int pos = p.len[b];
+  const int sq = p.span ? p.seq0 : b;  // this row's sequence (span: row b = position len + b)
+  const int pos = p.span ? p.len[sq] + b : p.len[b];
   if (pos >= p.max_seq) {
     if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
     return;
@@ -724,22 +749,23 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
   const int L = pos + 1;
   const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
   const int eff = L - off, c0 = sp * FD_CH;
-  const bool owner = sp == 0 && h % G == 0;
+  const bool owner = sp == 0 && h % G == 0 && !p.span;
   const int cn = min(FD_CH, eff - c0);
   float mx = -INFINITY, ls = 0.0f, acc = 0.0f;
   if (cn > 0 || owner) {
     const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
     const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
     const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
-    float* kcb = p.kc + (size_t)b * p.max_seq * kvd + kvh * HD;
-    float* vcb = p.vc + (size_t)b * p.max_seq * kvd + kvh * HD;
+    float* kcb = p.kc + (size_t)sq * p.max_seq * kvd + kvh * HD;
+    float* vcb = p.vc + (size_t)sq * p.max_seq * kvd + kvh * HD;
     for (int i = tid; i < HD; i += FD_THREADS) {
       xs[i] = qrow[i];
       xs[HD + i] = krow[i];
       xs[2 * HD + i] = vrow[i];
     }
     __syncthreads();
-    norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, FD_THREADS);
+    if (!p.span)  // span mode: q ready, K/V already in the cache
+      norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, FD_THREADS);
     if (owner)
       for (int i = tid; i < HD; i += FD_THREADS) {
         kcb[(size_t)pos * kvd + i] = xs[HD + i];
@@ -748,7 +774,7 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
     if (cn > 0) {
       for (int t = tid; t < cn; t += FD_THREADS) {
         const int row = off + c0 + t;
-        const float* kr = row == pos ? xs + HD : kcb + (size_t)row * kvd;
+        const float* kr = row == pos && !p.span ? xs + HD : kcb + (size_t)row * kvd;
         float4 kv[Q4];
 #pragma unroll
         for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
@@ -782,8 +808,9 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
           const int t = tid + u * FD_THREADS, r = t / Q4, c4 = t - r * Q4;
           if (r < vn) {
             const int row = off + c0 + v0 + r;
-            tmp[u] = row == pos ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
-                                : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+            tmp[u] = row == pos && !p.span
+                         ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
+                         : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
           }
         }
 #pragma unroll
@@ -1199,6 +1226,8 @@ syn_status_t make_params(const AttnArgs& a, AttnParams& p, int seq0, int ntok) {
   p.ldo = (long long)a.ldo;
   p.scale = 1.0f / sqrtf((float)c->hd);  // host: 1 / sqrt(hd) in f32
   p.err = nullptr;
+  p.span = 0;
+  p.rope_at_slot = 0;
   return SYN_OK;
 }
 
@@ -1240,6 +1269,8 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
                      "k_attn_decode_split");
 }
 
+syn_status_t launch_decode_p(const AttnArgs& a, AttnParams& p, size_t batch, cudaStream_t st);
+
 syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, cudaStream_t st) {
   AttnParams p;
   syn_status_t s = make_params(a, p, 0, 1);
@@ -1248,6 +1279,34 @@ syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, 
   if (batch > a.cache->batch) return SYN_ERR_INVALID_ARG;
   for (size_t b = 0; b < batch; b++)
     if (a.cache->len[b] >= a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  return launch_decode_p(a, p, batch, st);
+}
+
+// ntok new positions of sequence `seq` from its current length (a
+// speculative-decoding verification): norm / RoPE at the cache slots and
+// append, then each row attends to the cache up to its own position with
+// the decode kernels (the same reductions as a one-token decode step).
+syn_status_t launch_attn_span_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
+                                   cudaStream_t st) {
+  AttnParams p;
+  syn_status_t s = make_params(a, p, (int)seq, (int)ntok);
+  if (s) return s;
+  p.err = err;
+  if (seq >= a.cache->batch || ntok == 0) return SYN_ERR_INVALID_ARG;
+  if (a.cache->len[seq] + ntok > a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  p.rope_at_slot = 1;
+  const int thr = std::max(32, p.hd / 2);
+  s = cuda_status(launch_pdl(k_norm_rope_append, dim3((unsigned)ntok, (unsigned)(p.n_heads + p.n_kv)),
+                             dim3(thr), (p.hd + 8) * sizeof(float), st, p),
+                  "k_norm_rope_append");
+  if (s) return s;
+  p.rope_at_slot = 0;
+  p.span = 1;
+  return launch_decode_p(a, p, ntok, st);
+}
+
+syn_status_t launch_decode_p(const AttnArgs& a, AttnParams& p, size_t batch, cudaStream_t st) {
+  syn_status_t s;
   // A captured graph replays at growing positions: size for the window.
   size_t eff = a.cache->max_seq;
   if (a.window && a.window < eff) eff = a.window;

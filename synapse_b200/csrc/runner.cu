@@ -17,6 +17,7 @@
 // weights along N is exact: every output column is computed independently.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <new>
@@ -197,6 +198,10 @@ struct syn_cuda_model_s {
   bool finalized = false;
   std::string cache_dir;  // repacked-weight cache (empty: none)
   int cache_hits = 0;     // weights read from the cache by finalize
+  // speculative decoding: logits and tokens of up to 16 span rows
+  float* span_logits = nullptr;
+  int32_t* span_tok = nullptr;
+  int32_t* span_tok_h = nullptr;
   // staged host weights
   std::map<std::string, HostLinear> lin;
   std::map<std::string, std::vector<float>> ten;
@@ -305,8 +310,13 @@ syn_status_t mm(syn_cuda_model_s* m, const syn_cuda_weight_t* w, const float* x,
 // Decode: rows sequences [0, rows), one token each.
 // chained: the step's input tokens are the previous step's outputs (m->tok),
 // and nothing is copied to the host.
+// span: rows are consecutive new positions of sequence `seq` (speculative
+// drafting and verification): attention through launch_attn_span_args,
+// logits and greedy tokens for every row into the span buffers, no cache
+// length advanced. nlayers < L runs only the first nlayers layers (the
+// reference's layer-skipping draft, pipeline.rs:281-330).
 syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq, bool want_logits,
-                     bool chained = false) {
+                     bool chained = false, size_t nlayers = 0, bool span = false) {
   cudaStream_t st = m->st;
   syn_status_t s;
   const size_t h = m->h;
@@ -330,7 +340,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   const bool fuse = rows == 1 && !m->no_fuse;
   float* cur = m->resid;
   auto other = [&](float* r) { return r == m->resid ? m->resid2 : m->resid; };
-  for (size_t li = 0; li < m->L; li++) {
+  const size_t L = nlayers ? std::min(nlayers, m->L) : m->L;
+  for (size_t li = 0; li < L; li++) {
     LayerDev& ly = m->layers[li];
     if (fuse && li > 0) {
       float* nxt = other(cur);
@@ -357,8 +368,9 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
     a.kn = ly.k_norm;
     a.layer = li;
     a.out = m->att;
-    s = prefill ? launch_attn_prefill_args(a, seq, rows, m->ctx->err, st)
-                : launch_attn_decode_args(a, rows, m->ctx->err, st);
+    s = span      ? launch_attn_span_args(a, seq, rows, m->ctx->err, st)
+        : prefill ? launch_attn_prefill_args(a, seq, rows, m->ctx->err, st)
+                  : launch_attn_decode_args(a, rows, m->ctx->err, st);
     if (s) return s;
     if ((s = mm(m, ly.o, m->att, rows, m->o))) return s;
     if (tp && (s = tp_allreduce_sum(m->ctx, m->o, rows * h, st))) return s;  // row-parallel O
@@ -384,7 +396,7 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   }
   // final norm and LM head: prefill keeps only the last token (int8.rs:619-627)
   const size_t r0 = prefill ? rows - 1 : 0, nr = prefill ? 1 : rows;
-  float* logits_dst = tp ? m->logits_l : m->logits;
+  float* logits_dst = span ? m->span_logits : tp ? m->logits_l : m->logits;
   if (fuse) {
     GemvNorm nm{cur, m->dn, m->final_norm, m->eps, nullptr, a.flash};
     if ((s = ensure_scratch(m->ctx, m->lm_head, 1, st))) return s;
@@ -396,6 +408,18 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
                            cur + r0 * h, h, m->final_norm, nr, h, m->eps, m->x, h, st, a.flash);
     if (s) return s;
     if ((s = mm(m, m->lm_head, m->x, nr, logits_dst))) return s;
+  }
+  if (span) {  // every row's greedy token; lengths untouched
+    s = launch_argmax(m->span_logits, m->V, nr, m->V, m->span_tok, nullptr, 0, (int)m->max_seq,
+                      nullptr, 0, m->am_scratch, st);
+    if (s) return s;
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->span_tok_h, m->span_tok, nr * sizeof(int32_t),
+                                 cudaMemcpyDeviceToHost, st));
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->err_h, m->ctx->err, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    if (want_logits)
+      SYN_CUDA_TRY(cudaMemcpyAsync(m->logits_h, m->span_logits, nr * m->V * sizeof(float),
+                                   cudaMemcpyDeviceToHost, st));
+    return SYN_OK;
   }
   if (tp) {  // vocab-parallel LM head: gather each row's logits in rank (= vocab) order
     for (size_t b = 0; b < nr; b++)
@@ -629,14 +653,17 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   if (m->tp > 1 && (s = dev_alloc_t(m, &m->logits_l, m->max_batch * m->v_l))) return s;
   if ((s = dev_alloc_t(m, &m->dn, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->logits, m->max_batch * m->V))) return s;
+  if ((s = dev_alloc_t(m, &m->span_logits, 16 * m->V))) return s;
+  if ((s = dev_alloc_t(m, &m->span_tok, 16))) return s;
   {
-    const size_t ab = argmax_scratch_bytes(m->max_batch, m->V);
+    const size_t ab = argmax_scratch_bytes(std::max<size_t>(m->max_batch, 16), m->V);
     if ((s = dev_alloc(m, &m->am_scratch, ab))) return s;
     SYN_CUDA_TRY(cudaMemset(m->am_scratch, 0, ab));
   }
   SYN_CUDA_TRY(cudaMallocHost(&m->ids_h, R * sizeof(int32_t)));
   SYN_CUDA_TRY(cudaMallocHost(&m->tok_h, m->max_batch * sizeof(int32_t)));
-  SYN_CUDA_TRY(cudaMallocHost(&m->logits_h, m->max_batch * m->V * sizeof(float)));
+  SYN_CUDA_TRY(cudaMallocHost(&m->logits_h, std::max<size_t>(m->max_batch, 16) * m->V * sizeof(float)));
+  SYN_CUDA_TRY(cudaMallocHost(&m->span_tok_h, 16 * sizeof(int32_t)));
   SYN_CUDA_TRY(cudaMallocHost(&m->err_h, sizeof(int32_t)));
   *m->err_h = 0;
   SYN_CUDA_TRY(cudaDeviceSynchronize());
@@ -774,6 +801,93 @@ syn_status_t syn_cuda_generate(syn_cuda_model_t* m, size_t batch, size_t n_steps
   return SYN_OK;
 }
 
+syn_status_t syn_cuda_decode_span(syn_cuda_model_t* m, size_t seq, const int32_t* tokens,
+                                  size_t n, size_t n_layers, int32_t* out_tokens,
+                                  float* logits_host) {
+  if (!m || !tokens || !out_tokens) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  if (seq >= m->max_batch || n == 0 || n > 16 || n > m->max_rows) return SYN_ERR_INVALID_ARG;
+  if (m->tp > 1) return SYN_ERR_UNSUPPORTED;
+  if (m->cache->len[seq] == 0 || m->cache->len[seq] + n > m->max_seq)
+    return SYN_ERR_INVALID_ARG;  // not started, or CacheFull
+  DeviceGuard g(m->device);
+  memcpy(m->ids_h, tokens, n * sizeof(int32_t));
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->ids, m->ids_h, n * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+  syn_status_t s = forward(m, n, false, seq, logits_host != nullptr, false, n_layers, true);
+  if (s) return s;
+  SYN_CUDA_TRY(cudaStreamSynchronize(m->st));
+  if (*m->err_h != SYN_OK) {
+    const syn_status_t e = *m->err_h;
+    int32_t zero = 0;
+    cudaMemcpy(m->ctx->err, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    *m->err_h = 0;
+    return e;
+  }
+  memcpy(out_tokens, m->span_tok_h, n * sizeof(int32_t));
+  if (logits_host) memcpy(logits_host, m->logits_h, n * m->V * sizeof(float));
+  return SYN_OK;
+}
+
+// Self-speculative greedy decoding with KV rollback on the device
+// (generation/pipeline.rs:281-396): k draft tokens from the first
+// draft_layers layers (each one span step, its K/V kept for those layers
+// only), the cache rolled back, then one span step of the full model over
+// [last, d_0 .. d_{k-1}]. Unlike the reference, which accepts every draft
+// token, each d_i is checked against the full model's greedy token g_i at
+// its position: the accepted prefix, then g at the first mismatch (or the
+// bonus g_k) are emitted, and the cache is truncated to the accepted
+// positions. The output is therefore the plain greedy sequence.
+syn_status_t syn_cuda_generate_speculative(syn_cuda_model_t* m, size_t seq, int32_t last_token,
+                                           size_t n_steps, size_t k, size_t draft_layers,
+                                           int32_t* out_tokens, size_t* drafted,
+                                           size_t* accepted) {
+  if (!m || !out_tokens) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  if (k == 0 || k > 15 || draft_layers == 0 || draft_layers > m->L || seq >= m->max_batch)
+    return SYN_ERR_INVALID_ARG;
+  DeviceGuard g(m->device);
+  size_t done = 0, nd = 0, na = 0;
+  int32_t last = last_token;
+  syn_status_t s = SYN_OK;
+  auto set_len = [&](size_t len) -> syn_status_t {
+    m->cache->len[seq] = len;
+    return launch_kv_set(m->cache, seq, (int)len, 0, m->st);
+  };
+  while (done < n_steps) {
+    const size_t L0 = m->cache->len[seq];
+    const size_t kk = std::min(k, m->max_seq - std::min(m->max_seq, L0 + 1));
+    if (kk == 0) return SYN_ERR_INVALID_ARG;  // CacheFull
+    int32_t draft[16], verify[16], greedy[16];
+    int32_t t = last;
+    for (size_t j = 0; j < kk; j++) {
+      if ((s = syn_cuda_decode_span(m, seq, &t, 1, draft_layers, &draft[j], nullptr))) return s;
+      if ((s = set_len(L0 + j + 1))) return s;
+      t = draft[j];
+    }
+    if ((s = set_len(L0))) return s;
+    verify[0] = last;
+    for (size_t j = 0; j < kk; j++) verify[j + 1] = draft[j];
+    if ((s = syn_cuda_decode_span(m, seq, verify, kk + 1, 0, greedy, nullptr))) return s;
+    size_t a = 0;
+    while (a < kk && draft[a] == greedy[a]) a++;
+    nd += kk;
+    na += a;
+    // emitted this round: d_0 .. d_{a-1}, then greedy[a] (within n_steps);
+    // the cache keeps `last` and every emitted token but the final one
+    size_t e = 0;
+    for (; e < a && done < n_steps; e++) out_tokens[done++] = last = draft[e];
+    if (done < n_steps) {
+      out_tokens[done++] = last = greedy[a];
+      e++;
+    }
+    if ((s = set_len(L0 + e))) return s;
+  }
+  SYN_CUDA_TRY(cudaStreamSynchronize(m->st));
+  if (drafted) *drafted = nd;
+  if (accepted) *accepted = na;
+  return SYN_OK;
+}
+
 syn_status_t syn_cuda_model_seq_len(const syn_cuda_model_t* m, size_t seq, size_t* len) {
   if (!m || !len) return SYN_ERR_NULL_PTR;
   if (!m->finalized) return SYN_ERR_INVALID_ARG;
@@ -817,6 +931,7 @@ syn_status_t syn_cuda_model_destroy(syn_cuda_model_t* m) {
   for (void* p : m->allocs) cudaFree(p);
   if (m->ids_h) cudaFreeHost(m->ids_h);
   if (m->tok_h) cudaFreeHost(m->tok_h);
+  if (m->span_tok_h) cudaFreeHost(m->span_tok_h);
   if (m->logits_h) cudaFreeHost(m->logits_h);
   if (m->err_h) cudaFreeHost(m->err_h);
   if (m->st) cudaStreamDestroy(m->st);

@@ -11,9 +11,12 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <new>
 
 #include "internal.cuh"
 
@@ -78,9 +81,197 @@ size_t blk_bytes(int fmt) {
   return 1;
 }
 
+// ---------------------------------------------------------------------------
+// One-shot all-reduce over peer memory (NVLink P2P stores and loads, no
+// multicast). Every rank holds one buffer, mapped into every other rank with
+// CUDA IPC: two data slots of [world][PEER_CAP] floats (double-buffered by
+// call parity) and [world][PEER_CTAS] arrival flags. A call with epoch e:
+//   1. each CTA stores its chunk of the local partial into slot e&1, row
+//      `rank`, of every rank's buffer (its own included), fences at system
+//      scope, and raises flag [rank][cta] = e+1 on every rank;
+//   2. waits (bounded) until its flags from all ranks reach e+1;
+//   3. sums the world rows of its chunk in rank order -- the same order, so
+//      the same bits, on every rank -- into the caller's buffer.
+// The last CTA advances the device epoch, so CUDA-graph replays stay in
+// step. A rank can only reuse slot e&1 at epoch e+2, after every rank has
+// raised its e+1 flags, i.e. finished reading epoch e.
+// ---------------------------------------------------------------------------
+constexpr size_t PEER_CAP = 1u << 18;  // floats per rank row (1 MiB); larger -> NCCL
+constexpr int PEER_CTAS = 32;
+constexpr int PEER_THREADS = 256;
+constexpr int PEER_MAX_WORLD = 8;
+
+struct PeerState {
+  int world = 0, rank = 0;
+  uint8_t* local = nullptr;                  // this rank's buffer (cudaMalloc)
+  void* mapped[PEER_MAX_WORLD] = {nullptr};  // opened peer buffers (nullptr for self)
+  float** d_bufs = nullptr;                  // device array: every rank's buffer base
+  int* d_sync = nullptr;                     // device: epoch, done counter
+};
+
+size_t peer_buf_bytes(int world) {
+  return 2 * (size_t)world * PEER_CAP * sizeof(float) + (size_t)world * PEER_CTAS * sizeof(int);
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(PEER_THREADS) k_peer_allreduce(float* x, int n4, int world,
+                                                                 int rank, float* const* bufs,
+                                                                 int* sync, int* err) {
+  griddep_wait();  // x comes from the kernel before; the epoch from the call before
+  const int cta = blockIdx.x, nct = gridDim.x, tid = threadIdx.x;
+  const int e = *reinterpret_cast<volatile int*>(sync);
+  const int slot = e & 1;
+  const int per = (n4 + nct - 1) / nct, c0 = cta * per, c1 = min(n4, c0 + per);
+  const size_t row4 = PEER_CAP / 4;
+  const size_t flag_off = 2 * (size_t)world * PEER_CAP * sizeof(float);
+  float4* xv = reinterpret_cast<float4*>(x);
+  // 1. push this rank's chunk to every rank
+  for (int i = c0 + tid; i < c1; i += PEER_THREADS) {
+    const float4 v = xv[i];
+    for (int r = 0; r < world; r++)
+      reinterpret_cast<float4*>(bufs[r])[((size_t)slot * world + rank) * row4 + i] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid < world) {
+    int* f = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bufs[tid]) + flag_off);
+    st_release_sys(f + rank * PEER_CTAS + cta, e + 1);
+  }
+  // 2. wait (bounded) for every rank's chunk
+  __shared__ int ok;
+  if (tid == 0) ok = 1;
+  __syncthreads();
+  if (tid < world) {
+    const int* f = reinterpret_cast<const int*>(reinterpret_cast<uint8_t*>(bufs[rank]) + flag_off);
+    bool got = false;
+    for (int it = 0; it < (1 << 24) && !got; it++) {
+      got = ld_acquire_sys(f + tid * PEER_CTAS + cta) >= e + 1;
+      if (!got && it > 64) __nanosleep(64);
+    }
+    if (!got) {
+      ok = 0;
+      if (err) atomicExch(err, SYN_ERR_TIMEOUT);
+    }
+  }
+  __syncthreads();
+  // 3. sum in rank order
+  if (ok) {
+    const float4* mine = reinterpret_cast<const float4*>(bufs[rank]) + (size_t)slot * world * row4;
+    for (int i = c0 + tid; i < c1; i += PEER_THREADS) {
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < world; r++) {
+        const float4 v = __ldcv(mine + (size_t)r * row4 + i);
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+      xv[i] = s;
+    }
+  }
+  griddep_launch();
+  // the last CTA advances the epoch for the next call
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(sync + 1, 1) == nct - 1) {
+      sync[1] = 0;
+      __threadfence();
+      atomicAdd(sync, 1);
+    }
+  }
+}
+
+void peer_release(syn_cuda_ctx_s* ctx) {
+  auto* ps = static_cast<PeerState*>(ctx->tp_peer);
+  if (!ps) return;
+  for (int r = 0; r < ps->world; r++)
+    if (ps->mapped[r]) cudaIpcCloseMemHandle(ps->mapped[r]);
+  if (ps->local) cudaFree(ps->local);
+  if (ps->d_bufs) cudaFree(ps->d_bufs);
+  if (ps->d_sync) cudaFree(ps->d_sync);
+  delete ps;
+  ctx->tp_peer = nullptr;
+}
+
+// Sets up the peer buffers (collective over the communicator). Failure
+// leaves ctx->tp_peer null and the NCCL path in use.
+syn_status_t peer_init(syn_cuda_ctx_s* ctx) {
+  if (ctx->tp_world < 2 || ctx->tp_world > PEER_MAX_WORLD) return SYN_OK;
+  const char* env = getenv("SYN_TP_PEER_ALLREDUCE");
+  if (env && env[0] == '0') return SYN_OK;
+  auto* ps = new (std::nothrow) PeerState();
+  if (!ps) return SYN_ERR_OUT_OF_MEMORY;
+  ps->world = ctx->tp_world;
+  ps->rank = ctx->tp_rank;
+  ctx->tp_peer = ps;
+  const int W = ps->world;
+  cudaStream_t st = ctx->upload_stream;
+  cudaIpcMemHandle_t* all = nullptr;
+  void* d_h = nullptr;
+  syn_status_t s = SYN_OK;
+  auto fail = [&](cudaError_t e, const char* where) {
+    set_last_cuda_error(e, where);
+    s = SYN_ERR_CUDA;
+  };
+  do {
+    cudaError_t e = cudaMalloc(&ps->local, peer_buf_bytes(W));
+    if (e != cudaSuccess) { fail(e, "peer buffer"); break; }
+    if ((e = cudaMemset(ps->local, 0, peer_buf_bytes(W))) != cudaSuccess) { fail(e, "peer buffer"); break; }
+    if ((e = cudaMalloc(&ps->d_sync, 2 * sizeof(int))) != cudaSuccess) { fail(e, "peer sync"); break; }
+    if ((e = cudaMemset(ps->d_sync, 0, 2 * sizeof(int))) != cudaSuccess) { fail(e, "peer sync"); break; }
+    cudaIpcMemHandle_t mine;
+    if ((e = cudaIpcGetMemHandle(&mine, ps->local)) != cudaSuccess) { fail(e, "cudaIpcGetMemHandle"); break; }
+    if ((e = cudaMalloc(&d_h, (size_t)W * sizeof(mine))) != cudaSuccess) { fail(e, "ipc exchange"); break; }
+    uint8_t* dh = static_cast<uint8_t*>(d_h);
+    if ((e = cudaMemcpy(dh + (size_t)ps->rank * sizeof(mine), &mine, sizeof(mine),
+                        cudaMemcpyHostToDevice)) != cudaSuccess) { fail(e, "ipc exchange"); break; }
+    s = nccl_status(nccl().all_gather(dh + (size_t)ps->rank * sizeof(mine), dh, sizeof(mine),
+                                      ncclUint8, static_cast<ncclComm_t>(ctx->nccl), st),
+                    "ncclAllGather(ipc handles)");
+    if (s) break;
+    all = new cudaIpcMemHandle_t[W];
+    if ((e = cudaMemcpyAsync(all, dh, (size_t)W * sizeof(mine), cudaMemcpyDeviceToHost, st)) !=
+            cudaSuccess ||
+        (e = cudaStreamSynchronize(st)) != cudaSuccess) { fail(e, "ipc exchange"); break; }
+    float* bases[PEER_MAX_WORLD];
+    for (int r = 0; r < W && s == SYN_OK; r++) {
+      if (r == ps->rank) {
+        bases[r] = reinterpret_cast<float*>(ps->local);
+        continue;
+      }
+      void* p = nullptr;
+      if ((e = cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) {
+        fail(e, "cudaIpcOpenMemHandle");
+        break;
+      }
+      ps->mapped[r] = p;
+      bases[r] = static_cast<float*>(p);
+    }
+    if (s) break;
+    if ((e = cudaMalloc(&ps->d_bufs, W * sizeof(float*))) != cudaSuccess ||
+        (e = cudaMemcpy(ps->d_bufs, bases, W * sizeof(float*), cudaMemcpyHostToDevice)) !=
+            cudaSuccess) { fail(e, "peer table"); break; }
+  } while (0);
+  delete[] all;
+  if (d_h) cudaFree(d_h);
+  if (s != SYN_OK) peer_release(ctx);  // fall back to NCCL
+  cudaGetLastError();
+  return SYN_OK;
+}
+
 }  // namespace
 
 void tp_release(syn_cuda_ctx_s* ctx) {
+  peer_release(ctx);
   if (ctx->nccl && nccl().ok) nccl().comm_destroy(static_cast<ncclComm_t>(ctx->nccl));
   ctx->nccl = nullptr;
   ctx->tp_rank = 0;
@@ -89,6 +280,27 @@ void tp_release(syn_cuda_ctx_s* ctx) {
 
 syn_status_t tp_allreduce_sum(syn_cuda_ctx_s* ctx, float* buf, size_t count, cudaStream_t st) {
   if (!ctx->nccl) return SYN_ERR_INVALID_ARG;
+  auto* ps = static_cast<PeerState*>(ctx->tp_peer);
+  if (ps && count <= PEER_CAP && count % 4 == 0 && (reinterpret_cast<uintptr_t>(buf) & 15) == 0) {
+    const int n4 = (int)(count / 4);
+    const int ctas = std::max(1, std::min(PEER_CTAS, (n4 + PEER_THREADS - 1) / PEER_THREADS));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(PEER_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_peer_allreduce, buf, n4, ps->world, ps->rank,
+                                       (float* const*)ps->d_bufs, ps->d_sync, ctx->err);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e, "k_peer_allreduce");
+      return SYN_ERR_CUDA;
+    }
+    return SYN_OK;
+  }
   return nccl_status(nccl().all_reduce(buf, buf, count, ncclFloat32, ncclSum,
                                        static_cast<ncclComm_t>(ctx->nccl), st),
                      "ncclAllReduce");
@@ -137,7 +349,7 @@ syn_status_t syn_cuda_tp_init(syn_cuda_ctx_t* ctx, int rank, int world, const ui
   ctx->nccl = comm;
   ctx->tp_rank = rank;
   ctx->tp_world = world;
-  return SYN_OK;
+  return peer_init(ctx);
 }
 
 syn_status_t syn_cuda_tp_allreduce_sum(syn_cuda_ctx_t* ctx, float* buf, size_t count,

@@ -108,3 +108,57 @@ def test_tp2_model_matches_oracle(fmt, name):
             break
         if i < STEPS:
             lref = ref.forward_one(toks[i])
+
+
+def _ar_rank(rank, world, port, q):
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import synapse_b200 as sb
+        torch.cuda.set_device(rank)
+        ctx = sb.Context(rank)
+        obj = [sb.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.tp_init(rank, world, obj[0])
+        res = []
+        for n in (4096, 1000 * 4, 3 << 18, 4096):  # peer path, peer, NCCL (large), peer again
+            rng = np.random.default_rng(100 * n + rank)
+            x = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda()
+            for _ in range(3):  # repeated calls walk the double-buffered slots
+                y = x.clone()
+                ctx.tp_allreduce_sum(y)
+            torch.cuda.synchronize()
+            res.append(y.cpu().numpy())
+        q.put((rank, res))
+        ctx.close()
+    except Exception as e:
+        q.put(("error", rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_allreduce_sums_in_rank_order():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ar_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert all(g[0] != "error" for g in got), got
+    by = {g[0]: g[1] for g in got}
+    for i, n in enumerate((4096, 4000, 3 << 18, 4096)):
+        xs = [np.random.default_rng(100 * n + r).standard_normal(n).astype(np.float32)
+              for r in range(2)]
+        want = (np.float32(0) + xs[0]) + xs[1]
+        assert np.array_equal(by[0][i], by[1][i]), n  # the same bits on every rank
+        assert np.allclose(by[0][i], want, rtol=1e-6, atol=1e-6), n
