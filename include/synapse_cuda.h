@@ -273,6 +273,18 @@ syn_status_t syn_cuda_kvcache_create(syn_cuda_ctx_t *ctx, size_t max_seq,
                                      size_t n_kv_heads, size_t head_dim,
                                      size_t num_layers, size_t batch,
                                      syn_cuda_kvcache_t **out);
+/* Paged variant (no counterpart in the reference, whose cache is one
+ * contiguous buffer per layer, kv_cache/cache.rs:26-340): every layer holds
+ * a pool of n_pages pages of `page` positions; a sequence takes pages as it
+ * grows (append, advance and the attention entry points) and returns them
+ * on truncate / reset. No free page -> SYN_ERR_OUT_OF_MEMORY. page = 0 is
+ * the contiguous cache. _view is unsupported on a paged cache. */
+syn_status_t syn_cuda_kvcache_create_paged(syn_cuda_ctx_t *ctx, size_t max_seq,
+                                           size_t n_kv_heads, size_t head_dim,
+                                           size_t num_layers, size_t batch, size_t page,
+                                           size_t n_pages, syn_cuda_kvcache_t **out);
+/* Free pages of a paged cache (0 for a contiguous one). */
+syn_status_t syn_cuda_kvcache_pages_free(const syn_cuda_kvcache_t *cache, size_t *n);
 syn_status_t syn_cuda_kvcache_destroy(syn_cuda_kvcache_t *cache);
 syn_status_t syn_cuda_kvcache_len(const syn_cuda_kvcache_t *cache, size_t seq,
                                   size_t *len);
@@ -396,6 +408,22 @@ syn_status_t syn_cuda_decode_step(syn_cuda_model_t *m, size_t batch,
  * synchronisation at the end. out_tokens: host [batch][n_steps]. */
 syn_status_t syn_cuda_generate(syn_cuda_model_t *m, size_t batch, size_t n_steps,
                                int32_t *out_tokens);
+/* Continuous batching (the reference decodes one sequence at a time,
+ * generation/pipeline.rs:197-280). syn_cuda_model_set_kv_paging, before
+ * finalize, gives the model a paged KV cache of n_pages pages of `page`
+ * positions shared by all its max_batch sequence slots, so memory follows
+ * the live contexts rather than max_batch * max_seq.
+ * syn_cuda_decode_step_slots runs one decode step for an arbitrary set of
+ * started sequences (slots[i], distinct) -- sequences join with
+ * syn_cuda_prefill into a free slot and leave with syn_cuda_model_reset,
+ * between steps -- and returns each row's greedy token (and optionally its
+ * logits [n, vocab]); each sequence advances by one position. */
+syn_status_t syn_cuda_model_set_kv_paging(syn_cuda_model_t *m, size_t page, size_t n_pages);
+syn_status_t syn_cuda_model_kv_pages_free(const syn_cuda_model_t *m, size_t *n);
+syn_status_t syn_cuda_decode_step_slots(syn_cuda_model_t *m, size_t n, const int32_t *slots,
+                                        const int32_t *last_tokens, int32_t *out_tokens,
+                                        float *logits_host);
+
 /* Speculative decoding support. syn_cuda_decode_span runs n (<= 16)
  * tokens of sequence seq at positions len .. len+n-1 (each attending to the
  * cache up to itself, RoPE at its position) through the first n_layers

@@ -80,6 +80,12 @@ SIGNATURES = {
     "syn_cuda_prefill": (c_st, [c_vp, c_size, c_vp, c_size, c_vp, c_vp]),
     "syn_cuda_decode_step": (c_st, [c_vp, c_size, c_vp, c_vp, c_vp]),
     "syn_cuda_generate": (c_st, [c_vp, c_size, c_size, c_vp]),
+    "syn_cuda_kvcache_create_paged": (c_st, [c_vp, c_size, c_size, c_size, c_size, c_size, c_size,
+                                             c_size, ctypes.POINTER(c_vp)]),
+    "syn_cuda_kvcache_pages_free": (c_st, [c_vp, ctypes.POINTER(c_size)]),
+    "syn_cuda_model_set_kv_paging": (c_st, [c_vp, c_size, c_size]),
+    "syn_cuda_model_kv_pages_free": (c_st, [c_vp, ctypes.POINTER(c_size)]),
+    "syn_cuda_decode_step_slots": (c_st, [c_vp, c_size, c_vp, c_vp, c_vp, c_vp]),
     "syn_cuda_decode_span": (c_st, [c_vp, c_size, c_vp, c_size, c_size, c_vp, c_vp]),
     "syn_cuda_generate_speculative": (c_st, [c_vp, c_size, ctypes.c_int32, c_size, c_size, c_size,
                                              c_vp, ctypes.POINTER(c_size), ctypes.POINTER(c_size)]),

@@ -388,14 +388,21 @@ def argmax(logits):
 class KVCache:
     """KV cache in HBM (syn_cuda_kvcache_*; kvcache.zig:13-170)."""
 
-    def __init__(self, ctx, max_seq, n_kv_heads, head_dim, num_layers, batch=1):
+    def __init__(self, ctx, max_seq, n_kv_heads, head_dim, num_layers, batch=1, page=0,
+                 n_pages=0):
         self.max_seq, self.n_kv, self.hd = max_seq, n_kv_heads, head_dim
         self.layers, self.batch = num_layers, batch
         h = ctypes.c_void_p()
-        _check(lib().syn_cuda_kvcache_create(ctx.handle, max_seq, n_kv_heads, head_dim,
-                                             num_layers, batch, ctypes.byref(h)),
+        _check(lib().syn_cuda_kvcache_create_paged(ctx.handle, max_seq, n_kv_heads, head_dim,
+                                                   num_layers, batch, page, n_pages,
+                                                   ctypes.byref(h)),
                "kvcache_create")
         self.handle = h
+
+    def pages_free(self):
+        v = ctypes.c_size_t()
+        _check(lib().syn_cuda_kvcache_pages_free(self.handle, ctypes.byref(v)), "pages_free")
+        return v.value
 
     def length(self, seq=0):
         v = ctypes.c_size_t()
@@ -506,7 +513,8 @@ class Model:
     ("INT8_KN", q_kn int8 [K*N], scales [N]) / (fmt_name, block bytes).
     """
 
-    def __init__(self, ctx, config, weights, max_seq, max_batch=1, cache_dir=None, _stage=None):
+    def __init__(self, ctx, config, weights, max_seq, max_batch=1, cache_dir=None, _stage=None,
+                 kv_page=0, kv_pages=0):
         import json
         import numpy as np
         cfg = json.loads(config) if isinstance(config, str) else config
@@ -519,6 +527,8 @@ class Model:
         _check(lib().syn_cuda_model_create(ctx.handle, json.dumps(cfg).encode(), max_seq,
                                            max_batch, ctypes.byref(h)), "model_create")
         self.handle = h
+        if kv_page:
+            _check(lib().syn_cuda_model_set_kv_paging(h, kv_page, kv_pages), "set_kv_paging")
         if cache_dir:
             _check(lib().syn_cuda_model_set_cache_dir(h, str(cache_dir).encode()),
                    "model_set_cache_dir")
@@ -628,6 +638,26 @@ class Model:
         _check(lib().syn_cuda_generate(self.handle, batch, n_steps,
                                        out.ctypes.data_as(ctypes.c_void_p)), "generate")
         return out
+
+    def decode_slots(self, slots, tokens, want_logits=False):
+        """One decode step of the started sequences `slots` (any subset, in
+        any order; syn_cuda_decode_step_slots): (greedy tokens, logits
+        [n, vocab] or None)."""
+        import numpy as np
+        sl = np.ascontiguousarray(np.asarray(slots, dtype=np.int32))
+        ids = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        out = np.empty(sl.size, dtype=np.int32)
+        logits = np.empty((sl.size, self.vocab), dtype=np.float32) if want_logits else None
+        _check(lib().syn_cuda_decode_step_slots(
+            self.handle, sl.size, sl.ctypes.data_as(ctypes.c_void_p),
+            ids.ctypes.data_as(ctypes.c_void_p), out.ctypes.data_as(ctypes.c_void_p),
+            logits.ctypes.data_as(ctypes.c_void_p) if want_logits else None), "decode_step_slots")
+        return out, logits
+
+    def kv_pages_free(self):
+        v = ctypes.c_size_t()
+        _check(lib().syn_cuda_model_kv_pages_free(self.handle, ctypes.byref(v)), "kv_pages_free")
+        return v.value
 
     def decode_span(self, tokens, seq=0, n_layers=0, want_logits=False):
         """Tokens at the next positions of `seq` (syn_cuda_decode_span):

@@ -130,7 +130,31 @@ struct GemvParams {
   // rank 0 sums the others' partials from its shared memory (recv_off).
   int cluster;
   int recv_off;
+  // SwiGLU epilogue (gate/up weights interleaved by 16 rows: group g holds
+  // gate rows 16g.. in lanes 0-15 and the matching up rows in lanes 16-31):
+  // lanes 0-15 write swiglu(gate, up) to sw_out[m * sw_ld + 16g + lane]
+  // instead of y (ops/activation.rs:30-32 / silu.zig:85-110, variant as
+  // launch_swiglu; sw_n = the FFN width).
+  float* sw_out;
+  long long sw_ld;
+  int sw_n, sw_variant;
 };
+
+// Final store of output `row` of activation row m; called by all 32 lanes of
+// a warp (valid = this lane's row exists).
+__device__ __forceinline__ void store_y(const GemvParams& p, int m, int row, float out,
+                                        bool valid) {
+  if (!p.sw_out) {
+    if (valid) p.y[(long long)m * p.ldy + row] = out;
+    return;
+  }
+  const float up = __shfl_down_sync(0xffffffffu, out, 16);
+  const int lane = threadIdx.x & 31;
+  if (valid && lane < 16) {
+    const int j = (row >> 5) * 16 + lane;
+    p.sw_out[(long long)m * p.sw_ld + j] = swiglu_elem(out, up, j, p.sw_n & ~3, p.sw_variant);
+  }
+}
 
 __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -621,9 +645,10 @@ __device__ void cluster_finish(const GemvParams& p, int g, int ks, int m0, int c
   consumer_sync();
   if (warp < MT) {
     const int mm = warp, m = m0 + mm;
-    if (m < p.m && row < p.n) {
+    if (m < p.m) {
       float out = 0.0f;
-      if constexpr (FMT == F_INT8) {
+      if (row >= p.n) {
+      } else if constexpr (FMT == F_INT8) {
         const float sa = sh.srow[mm], sbv = have_sb ? sb_pre : p.sb[row];
         if (MT > 1 && p.chunked) {
           const int* src = reinterpret_cast<const int*>(recv) + (size_t)mm * p.nchunks * 32 + lane;
@@ -639,12 +664,14 @@ __device__ void cluster_finish(const GemvParams& p, int g, int ks, int m0, int c
         const float* src = reinterpret_cast<const float*>(recv) + (size_t)mm * 32 + lane;
         for (int s = 0; s < p.nks; s++) out += src[(size_t)s * MT * 32];
       }
-      p.y[(long long)m * p.ldy + row] = out;
+      store_y(p, m, row, out, row < p.n);
     }
   }
 }
 
-template <int FMT, int MT>
+// CL: the kernel may be launched as clusters (k_qgemv_tma with one row group
+// per CTA; row-group pairs only run unsplit).
+template <int FMT, int MT, bool CL = false>
 __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, int ncc,
                            const int* csum, CtaShared<MT>& sh, float sb_pre = 0.0f,
                            bool have_sb = false) {
@@ -653,18 +680,22 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
   const bool split = p.nks > 1;
   const long long G32 = (long long)p.groups * 32;
   consumer_sync();
-  if (split && p.cluster) {
-    cluster_finish<FMT, MT>(p, g, ks, m0, cc0, ncc, csum, sh, sb_pre, have_sb);
-    return;
+  // (not compiled for the one-row INT8 kernel: it would cost that kernel
+  // 16 registers and a CTA per SM; its K splits reduce through scratch)
+  if constexpr (CL && !(FMT == F_INT8 && MT == 1)) {
+    if (split && p.cluster) {
+      cluster_finish<FMT, MT>(p, g, ks, m0, cc0, ncc, csum, sh, sb_pre, have_sb);
+      return;
+    }
   }
   if (warp < MT) {
     const int mm = warp, m = m0 + mm;
     if (m < p.m) {
       if constexpr (FMT == F_INT8) {
         if (!split) {
+          float out = 0.0f;
           if (row < p.n) {
             const float sa = sh.srow[mm], sbv = have_sb ? sb_pre : p.sb[row];
-            float out = 0.0f;
             if (p.chunked) {
               for (int c = 0; c < ncc; c++)
                 out = __fadd_rn(
@@ -674,8 +705,8 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
               for (int c = 0; c < ncc; c++) tot += csum[(mm * ncc + c) * 32 + lane];
               out = __fmul_rn(__fmul_rn((float)tot, sa), sbv);
             }
-            p.y[(long long)m * p.ldy + row] = out;
           }
+          store_y(p, m, row, out, row < p.n);
         } else {
           float* dst = p.part + (long long)m * p.nchunks * G32;
           for (int c = 0; c < ncc; c++)
@@ -686,7 +717,7 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
 #pragma unroll
         for (int i = 0; i < WARPS; i++) v += sh.red[i][mm][lane];
         if (!split) {
-          if (row < p.n) p.y[(long long)m * p.ldy + row] = v;
+          store_y(p, m, row, v, row < p.n);
         } else {
           p.part[((long long)m * p.nks + ks) * G32 + row] = v;
         }
@@ -709,9 +740,10 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
   __threadfence();
   if (warp < MT) {
     const int mm = warp, m = m0 + mm;
-    if (m < p.m && row < p.n) {
+    if (m < p.m) {
       float out = 0.0f;
-      if constexpr (FMT == F_INT8) {
+      if (row >= p.n) {
+      } else if constexpr (FMT == F_INT8) {
         const float* src = p.part + (long long)m * p.nchunks * G32;
         const float sa = sh.srow[mm], sbv = have_sb ? sb_pre : p.sb[row];
         if (p.chunked) {
@@ -728,7 +760,7 @@ __device__ void cta_finish(const GemvParams& p, int g, int ks, int m0, int cc0, 
         const float* src = p.part + (long long)m * p.nks * G32;
         for (int s = 0; s < p.nks; s++) out += __ldcg(src + s * G32 + row);
       }
-      p.y[(long long)m * p.ldy + row] = out;
+      store_y(p, m, row, out, row < p.n);
     }
   }
 }
@@ -816,9 +848,7 @@ __device__ void norm_prologue(const GemvParams& p, float* xs, CtaShared<MT>& sh,
 // Threads 0-255 consume, warp 8 (threads 256-287) produces.
 // ---------------------------------------------------------------------------
 template <int FMT, int MT, int RG>
-// (The INT8 one-row kernel is held to 56 registers, four CTAs per SM.)
-__global__ void __launch_bounds__(THREADS + 32, (FMT == F_INT8 && MT == 1) ? 4 : 1)
-    k_qgemv_tma(const GemvParams p) {
+__global__ void __launch_bounds__(THREADS + 32) k_qgemv_tma(const GemvParams p) {
   using S = Stage<FMT>;
   static_assert(RG == 1 || (FMT != F_INT8 && MT == 1), "row-group pairs: block formats, M=1");
   extern __shared__ __align__(128) uint8_t sm[];
@@ -975,7 +1005,7 @@ __global__ void __launch_bounds__(THREADS + 32, (FMT == F_INT8 && MT == 1) ? 4 :
 #pragma unroll
       for (int mm = 0; mm < MT; mm++) sh.red[warp][mm][lane] = facc[mm][r];
     }
-    cta_finish<FMT, MT>(p, g + r, ks, m0, cc0, ncc, csum, sh, sb_pre[r], FMT == F_INT8);
+    cta_finish<FMT, MT, RG == 1>(p, g + r, ks, m0, cc0, ncc, csum, sh, sb_pre[r], FMT == F_INT8);
   }
 }
 
@@ -1122,7 +1152,8 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
   const int min_split_blocks = tune("SYN_GEMV_MIN_SPLIT_BLOCKS", 64);
   while (nks > 1 && pl.nblk / nks < min_split_blocks) nks--;
   // Cluster K splits: at most 8 CTAs per cluster (the portable size).
-  const bool use_cluster = fmt != F_Q4_0RAW && tune("SYN_GEMV_CLUSTER", 1) != 0;
+  const bool use_cluster = fmt != F_Q4_0RAW && !(fmt == F_INT8 && pl.mt == 1) &&
+                           tune("SYN_GEMV_CLUSTER", 1) != 0;
   if (use_cluster) nks = std::min(nks, 8);
   const int abb = fmt == F_INT8 ? 32 : 80;
   auto set_split = [&](int splits) {
@@ -1450,6 +1481,11 @@ syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, f
   p.neps = nm.eps;
   p.nres_out = nm.res_out;
   p.nfast = nm.fast;
+  p.sw_out = nm.sw_out;
+  p.sw_ld = nm.sw_n;
+  p.sw_n = nm.sw_n;
+  p.sw_variant = nm.sw_variant;
+  if (nm.sw_out && (w->n != 2 * (size_t)nm.sw_n || nm.sw_n % 16)) return SYN_ERR_SHAPE_MISMATCH;
   fill_common(p, pl, part, cnt, err);
   if (pl.nks > 1 && !pl.cluster && (!part || !cnt || plan_part_bytes(fk, pl, 1) > part_cap))
     return SYN_ERR_INTERNAL;

@@ -59,6 +59,15 @@ struct syn_cuda_kvcache_s {
   size_t* len;  // [batch], host mirror
   float* part;  // split-attention partials (grown on demand)
   size_t part_bytes;
+  // Paged layout (page > 0): each layer's K and V are pools of n_pages pages
+  // of `page` positions, and position p of sequence s lives in page
+  // ptab[s * maxp + p / page]. Pages are taken from a free list as a
+  // sequence grows and returned when it is truncated or reset.
+  size_t page, n_pages, maxp;
+  int* ptab_h;       // pinned host table [batch][maxp], -1 = none
+  int* d_ptab;       // device copy
+  int* free_pages;   // stack of free page ids (host)
+  size_t n_free;
 };
 
 namespace syn {
@@ -114,6 +123,12 @@ struct GemvNorm {
   float eps;
   float* res_out;      // or nullptr
   int fast;
+  // optional SwiGLU epilogue: the weight's rows are gate/up interleaved by
+  // 16 (2 * sw_n rows); sw_out[0, sw_n) receives swiglu(gate, up) instead
+  // of y (variant as launch_swiglu)
+  float* sw_out;
+  int sw_n;
+  int sw_variant;
 };
 syn_status_t launch_qgemv_norm(const syn_cuda_weight_s* w, const GemvNorm& nm, float* y,
                                float* part, size_t part_cap, int* cnt, int* err,
@@ -193,7 +208,14 @@ struct AttnArgs {
   float* out;
   size_t ldo;
   int flash;        // 1: parallel reduction order (block-format models)
+  const int* slots; // decode: device map row -> sequence (nullptr: row b = sequence b)
 };
+// Paged cache: maps pages for positions [0, new_len) of sequence seq (host
+// table, copied to the device on `st`); SYN_ERR_OUT_OF_MEMORY when the pool
+// is exhausted. No-op for a contiguous cache.
+syn_status_t kv_reserve(syn_cuda_kvcache_t* c, size_t seq, size_t new_len, cudaStream_t st);
+// Frees the pages of seq beyond position keep_len (drains `st` first).
+syn_status_t kv_release(syn_cuda_kvcache_t* c, size_t seq, size_t keep_len, cudaStream_t st);
 // Decode step of sequences [0, batch): norm/RoPE/append of the new token,
 // attention over positions [0, len] (the cache lengths are not advanced).
 syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, cudaStream_t st);
@@ -212,7 +234,9 @@ syn_status_t launch_norm_rope_append_args(const AttnArgs& a, size_t seq, size_t 
 syn_status_t launch_prefill_attention_args(const AttnArgs& a, size_t seq, size_t ntok, int* err,
                                            cudaStream_t st);
 syn_status_t launch_swiglu(const float* gate, const float* up, size_t ld_in, size_t rows, size_t n,
-                           int variant, float* out, size_t ldo, cudaStream_t st);
+                           int variant, float* out, size_t ldo, cudaStream_t st, int il16 = 0);
+// il16 = 1: gate and up interleaved by 16 columns in one buffer (gate at
+// gu[r*ld_in + (i/16)*32 + i%16], up 16 further): pass gate = gu, up = gu + 16.
 // Greedy argmax per row; when len_adv != nullptr, len_adv[row] += adv after
 // and (hist != nullptr) the token is recorded at hist[row*hist_ld + new len].
 // scratch: argmax_scratch_bytes(rows, n) bytes, zero before the first launch
@@ -221,6 +245,9 @@ size_t argmax_scratch_bytes(size_t rows, size_t n);
 syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
                            int* len_adv, int adv, int max_len, int32_t* hist, int hist_ld,
                            void* scratch, cudaStream_t st);
+// Device lengths of the sequences slots[0, n) (device array) advanced by one.
+syn_status_t launch_kv_advance_slots(syn_cuda_kvcache_t* c, const int* slots, size_t n,
+                                     cudaStream_t st);
 // Device length of sequence seq: set to value (add=0) or advanced by it.
 syn_status_t launch_kv_set(syn_cuda_kvcache_t* c, size_t seq, int value, int add, cudaStream_t st);
 

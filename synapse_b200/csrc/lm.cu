@@ -208,6 +208,13 @@ struct AttnParams {
   // seq0 (a multi-token verification step); q is already normalised and
   // rotated and K/V already appended (k_norm_rope_append with rope_at_slot).
   int span;
+  // Paged cache: position `pos` of sequence `sq` lives in slot
+  // ptab[sq * maxp + pos / page] * page + pos % page of the layer's pool;
+  // ptab == nullptr: contiguous, slot sq * max_seq + pos.
+  const int* ptab;
+  int page, maxp;
+  // Decode kernels: row b's sequence is slots[b] (nullptr: b).
+  const int* slots;
   // k_norm_rope_append: RoPE at the cache slot (len + t) instead of the
   // reference prefill's offset t (attention.rs:171-190)
   int rope_at_slot;
@@ -216,6 +223,12 @@ struct AttnParams {
   float scale;
   int* err;
 };
+
+// Cache slot (row index of the layer's K/V pool) of position pos of sequence sq.
+__device__ __forceinline__ size_t kv_slot(const AttnParams& p, int sq, int pos) {
+  if (!p.ptab) return (size_t)sq * p.max_seq + pos;
+  return (size_t)p.ptab[(size_t)sq * p.maxp + pos / p.page] * p.page + pos % p.page;
+}
 
 // Headwise RMSNorm of `nv` vectors of length hd in smem (x, in place), with
 // weight w (nullptr = identity), then RotateHalf RoPE at position pos
@@ -315,7 +328,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   // loads overlap the tail of the Q/K/V matmul. Span mode: rows from len0 on
   // were appended by the kernel before, so only rows below len0 are read
   // early.
-  const int sq = p.span ? p.seq0 : b;  // this row's sequence
+  const int sq = p.span ? p.seq0 : p.slots ? p.slots[b] : b;  // this row's sequence
   const int len0 = p.len[sq];
   const int pos = p.span ? len0 + b : len0;
   const int early = p.span ? len0 : pos;  // rows [0, early) may be read before the wait
@@ -324,8 +337,8 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
     if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
     return;
   }
-  float* kcb = p.kc + (size_t)sq * p.max_seq * kvd + kvh * HD;
-  float* vcb = p.vc + (size_t)sq * p.max_seq * kvd + kvh * HD;
+  float* kcb = p.kc + kvh * HD;  // row r of the sequence: + kv_slot(p, sq, r) * kvd
+  float* vcb = p.vc + kvh * HD;
   const int L = pos + 1;
   const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
   const int eff = L - off;
@@ -338,7 +351,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   if (kpre) {
 #pragma unroll
     for (int c = 0; c < Q4; c++)
-      kv[c] = reinterpret_cast<const float4*>(kcb + (size_t)(off + tid) * kvd)[c];
+      kv[c] = reinterpret_cast<const float4*>(kcb + kv_slot(p, sq, off + tid) * kvd)[c];
   }
   const int cn0 = min(DEC_CH, eff);
   {  // first V chunk (the new position is filled in after its RoPE/append)
@@ -347,7 +360,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
     for (int u = 0; u < PER; u++) {
       const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
       if (r < cn0 && off + r < early)
-        tmp[u] = reinterpret_cast<const float4*>(vcb + (size_t)(off + r) * kvd)[c4];
+        tmp[u] = reinterpret_cast<const float4*>(vcb + kv_slot(p, sq, off + r) * kvd)[c4];
     }
 #pragma unroll
     for (int u = 0; u < PER; u++) {
@@ -365,7 +378,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
       const int r = t / Q4, c4 = t - r * Q4;
       if (off + r >= early)
         reinterpret_cast<float4*>(vb + r * VS)[c4] =
-            reinterpret_cast<const float4*>(vcb + (size_t)(off + r) * kvd)[c4];
+            reinterpret_cast<const float4*>(vcb + kv_slot(p, sq, off + r) * kvd)[c4];
     }
     __syncthreads();
   } else {
@@ -378,8 +391,8 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
     norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, cs, cs + HD / 2, 0, lanes, scl, DEC_THREADS);
     if (h % G == 0)
       for (int i = tid; i < HD; i += DEC_THREADS) {
-        kcb[(size_t)pos * kvd + i] = xs[HD + i];
-        vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
+        kcb[kv_slot(p, sq, pos) * kvd + i] = xs[HD + i];
+        vcb[kv_slot(p, sq, pos) * kvd + i] = xs[2 * HD + i];
       }
     if (pos - off < cn0)  // the new V row in the first chunk
       for (int i = tid; i < HD; i += DEC_THREADS) vb[(pos - off) * VS + i] = xs[2 * HD + i];
@@ -392,7 +405,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   for (int s = tid; s < eff; s += DEC_THREADS) {
     const int row = off + s;
     if (!(s == tid && kpre)) {
-      const float* kr = row == pos && !p.span ? xs + HD : kcb + (size_t)row * kvd;
+      const float* kr = row == pos && !p.span ? xs + HD : kcb + kv_slot(p, sq, row) * kvd;
 #pragma unroll
       for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
     }
@@ -438,7 +451,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
           const int row = off + c0 + r;
           tmp[u] = row == pos && !p.span
                        ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
-                       : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+                       : reinterpret_cast<const float4*>(vcb + kv_slot(p, sq, row) * kvd)[c4];
         }
       }
 #pragma unroll
@@ -500,8 +513,8 @@ __global__ void __launch_bounds__(512) k_norm_rope_append(const AttnParams p) {
     for (int i = threadIdx.x; i < hd; i += blockDim.x) src[i] = xs[i];
   } else {
     const int kh = hh - p.n_heads;
-    float* kd = p.kc + ((size_t)p.seq0 * p.max_seq + slot) * kvd + kh * hd;
-    float* vd = p.vc + ((size_t)p.seq0 * p.max_seq + slot) * kvd + kh * hd;
+    float* kd = p.kc + kv_slot(p, p.seq0, slot) * kvd + kh * hd;
+    float* vd = p.vc + kv_slot(p, p.seq0, slot) * kvd + kh * hd;
     const float* vs = p.v + (long long)t * p.ld + (long long)kh * hd;
     for (int i = threadIdx.x; i < hd; i += blockDim.x) {
       kd[i] = xs[i];
@@ -521,9 +534,11 @@ __global__ void __launch_bounds__(512) k_norm_rope_append(const AttnParams p) {
 constexpr int PF_THREADS = 256;
 constexpr int PF_CH = 32;  // keys staged per chunk
 
-// Copies rows [0, cn) of hd floats (global row stride gs) into smem rows of
-// stride ss, all loads of a thread issued before its stores.
-__device__ __forceinline__ void stage_rows_pf(float* dst, int ss, const float* src, size_t gs,
+// Copies cache rows row0 .. row0+cn-1 of sequence sq (hd floats each from
+// `cache`, which points at the head's columns) into smem rows of stride ss,
+// all loads of a thread issued before its stores.
+__device__ __forceinline__ void stage_rows_pf(float* dst, int ss, const float* cache,
+                                              const AttnParams& p, int sq, int row0, int kvd,
                                               int cn, int hd, int tid) {
   const int q = hd >> 2, tot = cn * q;
   constexpr int U = 8;
@@ -534,7 +549,7 @@ __device__ __forceinline__ void stage_rows_pf(float* dst, int ss, const float* s
       const int t = t0 + tid + u * PF_THREADS;
       if (t < tot) {
         const int r = t / q, c4 = t - r * q;
-        v[u] = *reinterpret_cast<const float4*>(src + (size_t)r * gs + 4 * c4);
+        v[u] = *reinterpret_cast<const float4*>(cache + kv_slot(p, sq, row0 + r) * kvd + 4 * c4);
       }
     }
 #pragma unroll
@@ -581,8 +596,8 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
   griddep_wait();
   // the prompt's own K/V: cache slots from the sequence's first free one on
   const int base = p.len[p.seq0];
-  const float* kcb = p.kc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * hd;
-  const float* vcb = p.vc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * hd;
+  const float* kcb = p.kc + kvh * hd;  // rows base + j of sequence seq0
+  const float* vcb = p.vc + kvh * hd;
   for (int t = tid; t < rows * hd; t += PF_THREADS) {
     const int i = t / hd, d = t - i * hd;
     qs[t] = p.q[(long long)(r0 + i) * p.ld + (long long)hh * hd + d];
@@ -592,7 +607,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
   for (int j0 = 0; j0 < jn; j0 += PF_CH) {
     const int cn = min(PF_CH, jn - j0);
     __syncthreads();
-    stage_rows_pf(kb, ks, kcb + (size_t)j0 * kvd, kvd, cn, hd, tid);
+    stage_rows_pf(kb, ks, kcb, p, p.seq0, base + j0, kvd, cn, hd, tid);
     __syncthreads();
     for (int t = tid; t < rows * cn; t += PF_THREADS) {
       const int i = t / cn, jj = t - i * cn, j = j0 + jj, q = r0 + i;
@@ -681,7 +696,7 @@ __global__ void __launch_bounds__(PF_THREADS) k_attn_prefill(const AttnParams p,
   for (int j0 = 0; j0 < jn; j0 += PF_CH) {
     const int cn = min(PF_CH, jn - j0);
     __syncthreads();
-    stage_rows_pf(kb, ks, vcb + (size_t)j0 * kvd, kvd, cn, hd, tid);
+    stage_rows_pf(kb, ks, vcb, p, p.seq0, base + j0, kvd, cn, hd, tid);
     __syncthreads();
     for (int jj = 0; jj < cn; jj++) {
       const float* vr = kb + jj * ks;
@@ -740,8 +755,9 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
   float* base = part + ((size_t)b * p.n_heads + h) * nsplit * (HD + 2);
   float* dst = base + (size_t)sp * (HD + 2);
   griddep_wait();
-  const int sq = p.span ? p.seq0 : b;  // this row's sequence (span: row b = position len + b)
-  const int pos = p.span ? p.len[sq] + b : p.len[b];
+  // this row's sequence (span: row b = position len + b)
+  const int sq = p.span ? p.seq0 : p.slots ? p.slots[b] : b;
+  const int pos = p.span ? p.len[sq] + b : p.len[sq];
   if (pos >= p.max_seq) {
     if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
     return;
@@ -756,8 +772,8 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
     const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
     const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
     const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
-    float* kcb = p.kc + (size_t)sq * p.max_seq * kvd + kvh * HD;
-    float* vcb = p.vc + (size_t)sq * p.max_seq * kvd + kvh * HD;
+    float* kcb = p.kc + kvh * HD;  // row r: + kv_slot(p, sq, r) * kvd
+    float* vcb = p.vc + kvh * HD;
     for (int i = tid; i < HD; i += FD_THREADS) {
       xs[i] = qrow[i];
       xs[HD + i] = krow[i];
@@ -768,13 +784,13 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
       norm_rope(xs, 2, HD, p.qn, p.kn, 1, p.eps, p.cos_t, p.sin_t, pos, lanes, scl, FD_THREADS);
     if (owner)
       for (int i = tid; i < HD; i += FD_THREADS) {
-        kcb[(size_t)pos * kvd + i] = xs[HD + i];
-        vcb[(size_t)pos * kvd + i] = xs[2 * HD + i];
+        kcb[kv_slot(p, sq, pos) * kvd + i] = xs[HD + i];
+        vcb[kv_slot(p, sq, pos) * kvd + i] = xs[2 * HD + i];
       }
     if (cn > 0) {
       for (int t = tid; t < cn; t += FD_THREADS) {
         const int row = off + c0 + t;
-        const float* kr = row == pos && !p.span ? xs + HD : kcb + (size_t)row * kvd;
+        const float* kr = row == pos && !p.span ? xs + HD : kcb + kv_slot(p, sq, row) * kvd;
         float4 kv[Q4];
 #pragma unroll
         for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
@@ -810,7 +826,7 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
             const int row = off + c0 + v0 + r;
             tmp[u] = row == pos && !p.span
                          ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
-                         : reinterpret_cast<const float4*>(vcb + (size_t)row * kvd)[c4];
+                         : reinterpret_cast<const float4*>(vcb + kv_slot(p, sq, row) * kvd)[c4];
           }
         }
 #pragma unroll
@@ -889,8 +905,8 @@ __global__ void __launch_bounds__(FP_THREADS) k_attn_prefill_flash(const AttnPar
   const int G = p.n_heads / p.n_kv, kvh = hh / G, kvd = p.n_kv * HD, S = p.n_tokens;
   griddep_wait();
   const int base = p.len[p.seq0];
-  const float* kcb = p.kc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * HD;
-  const float* vcb = p.vc + ((size_t)p.seq0 * p.max_seq + base) * kvd + kvh * HD;
+  const float* kcb = p.kc + kvh * HD;  // rows base + j of sequence seq0
+  const float* vcb = p.vc + kvh * HD;
   for (int t = tid; t < FP_B * (HD / 4); t += FP_THREADS) {
     const int r = t / (HD / 4), c4 = t - r * (HD / 4);
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -913,8 +929,9 @@ __global__ void __launch_bounds__(FP_THREADS) k_attn_prefill_flash(const AttnPar
       const int r = t / (HD / 4), c4 = t - r * (HD / 4);
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
       if (k0 + r < S) {
-        kv = reinterpret_cast<const float4*>(kcb + (size_t)(k0 + r) * kvd)[c4];
-        vv = reinterpret_cast<const float4*>(vcb + (size_t)(k0 + r) * kvd)[c4];
+        const size_t sl = kv_slot(p, p.seq0, base + k0 + r) * kvd;
+        kv = reinterpret_cast<const float4*>(kcb + sl)[c4];
+        vv = reinterpret_cast<const float4*>(vcb + sl)[c4];
       }
       reinterpret_cast<float4*>(ks + r * S4)[c4] = kv;
       reinterpret_cast<float4*>(vs + r * S4)[c4] = vv;
@@ -1005,7 +1022,7 @@ size_t flash_prefill_smem(int hd) {
 // ---------------------------------------------------------------------------
 __global__ void k_swiglu(const float* __restrict__ gate, const float* __restrict__ up,
                          long long ld_in, int rows, int n, int variant, float* __restrict__ out,
-                         long long ldo) {
+                         long long ldo, int il16) {
   griddep_wait();
   griddep_launch();
   const long long total = (long long)rows * n;
@@ -1013,7 +1030,8 @@ __global__ void k_swiglu(const float* __restrict__ gate, const float* __restrict
   for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
        t += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(t / n), i = (int)(t - (long long)r * n);
-    out[r * ldo + i] = swiglu_elem(gate[r * ld_in + i], up[r * ld_in + i], i, n4, variant);
+    const int c = il16 ? ((i >> 4) << 5) + (i & 15) : i;
+    out[r * ldo + i] = swiglu_elem(gate[r * ld_in + c], up[r * ld_in + c], i, n4, variant);
   }
 }
 
@@ -1145,12 +1163,13 @@ syn_status_t launch_add_rmsnorm(const float* x, size_t ldx, const float* delta, 
 }
 
 syn_status_t launch_swiglu(const float* gate, const float* up, size_t ld_in, size_t rows, size_t n,
-                           int variant, float* out, size_t ldo, cudaStream_t st) {
+                           int variant, float* out, size_t ldo, cudaStream_t st, int il16) {
   if (!rows || !n) return SYN_OK;
   const long long total = (long long)rows * n;
   const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
   return cuda_status(launch_pdl(k_swiglu, dim3(blocks), dim3(256), 0, st, gate, up,
-                                (long long)ld_in, (int)rows, (int)n, variant, out, (long long)ldo),
+                                (long long)ld_in, (int)rows, (int)n, variant, out, (long long)ldo,
+                                il16),
                      "k_swiglu");
 }
 
@@ -1216,8 +1235,13 @@ syn_status_t make_params(const AttnArgs& a, AttnParams& p, int seq0, int ntok) {
   p.sin_t = a.sin_t;
   p.window = (int)a.window;
   const size_t kvd = c->n_kv * c->hd;
-  p.kc = c->k + a.layer * c->batch * c->max_seq * kvd;
-  p.vc = c->v + a.layer * c->batch * c->max_seq * kvd;
+  const size_t rows_per_layer = c->page ? c->n_pages * c->page : c->batch * c->max_seq;
+  p.kc = c->k + a.layer * rows_per_layer * kvd;
+  p.vc = c->v + a.layer * rows_per_layer * kvd;
+  p.ptab = c->page ? c->d_ptab : nullptr;
+  p.page = (int)c->page;
+  p.maxp = (int)c->maxp;
+  p.slots = a.slots;
   p.max_seq = (int)c->max_seq;
   p.len = c->d_len;
   p.seq0 = seq0;
@@ -1277,8 +1301,11 @@ syn_status_t launch_attn_decode_args(const AttnArgs& a, size_t batch, int* err, 
   if (s) return s;
   p.err = err;
   if (batch > a.cache->batch) return SYN_ERR_INVALID_ARG;
-  for (size_t b = 0; b < batch; b++)
-    if (a.cache->len[b] >= a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  if (!a.slots)  // (with a slot map the caller checks and maps the sequences)
+    for (size_t b = 0; b < batch; b++) {
+      if (a.cache->len[b] >= a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+      if ((s = kv_reserve(a.cache, b, a.cache->len[b] + 1, st))) return s;
+    }
   return launch_decode_p(a, p, batch, st);
 }
 
@@ -1294,6 +1321,7 @@ syn_status_t launch_attn_span_args(const AttnArgs& a, size_t seq, size_t ntok, i
   p.err = err;
   if (seq >= a.cache->batch || ntok == 0) return SYN_ERR_INVALID_ARG;
   if (a.cache->len[seq] + ntok > a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
+  if ((s = kv_reserve(a.cache, seq, a.cache->len[seq] + ntok, st))) return s;
   p.rope_at_slot = 1;
   const int thr = std::max(32, p.hd / 2);
   s = cuda_status(launch_pdl(k_norm_rope_append, dim3((unsigned)ntok, (unsigned)(p.n_heads + p.n_kv)),
@@ -1336,6 +1364,7 @@ syn_status_t launch_norm_rope_append_args(const AttnArgs& a, size_t seq, size_t 
   if (seq >= a.cache->batch) return SYN_ERR_INVALID_ARG;
   if (a.cache->len[seq] + ntok > a.cache->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
   if (ntok == 0) return SYN_OK;
+  if ((s = kv_reserve(a.cache, seq, a.cache->len[seq] + ntok, st))) return s;
   const int thr = std::max(32, p.hd / 2);
   const size_t smem = (p.hd + 8) * sizeof(float);
   return cuda_status(
@@ -1377,6 +1406,60 @@ syn_status_t launch_attn_prefill_args(const AttnArgs& a, size_t seq, size_t ntok
   syn_status_t s = launch_norm_rope_append_args(a, seq, ntok, err, st);
   if (s) return s;
   return launch_prefill_attention_args(a, seq, ntok, err, st);
+}
+
+syn_status_t kv_reserve(syn_cuda_kvcache_t* c, size_t seq, size_t new_len, cudaStream_t st) {
+  if (!c->page) return SYN_OK;
+  if (seq >= c->batch || new_len > c->max_seq) return SYN_ERR_INVALID_ARG;
+  int* row = c->ptab_h + seq * c->maxp;
+  const size_t need = (new_len + c->page - 1) / c->page;
+  size_t first = need;
+  for (size_t i = 0; i < need; i++) {
+    if (row[i] >= 0) continue;
+    if (!c->n_free) {
+      set_last_cuda_error(cudaErrorMemoryAllocation, "paged KV cache: no free page");
+      return SYN_ERR_OUT_OF_MEMORY;
+    }
+    row[i] = c->free_pages[--c->n_free];
+    first = std::min(first, i);
+  }
+  if (first < need)
+    SYN_CUDA_TRY(cudaMemcpyAsync(c->d_ptab + seq * c->maxp + first, row + first,
+                                 (need - first) * sizeof(int), cudaMemcpyHostToDevice, st));
+  return SYN_OK;
+}
+
+// Returns the pages of sequence seq beyond position keep_len to the free
+// list. The stream is drained first: queued work may still read the table.
+syn_status_t kv_release(syn_cuda_kvcache_t* c, size_t seq, size_t keep_len, cudaStream_t st) {
+  if (!c->page) return SYN_OK;
+  SYN_CUDA_TRY(cudaStreamSynchronize(st));
+  int* row = c->ptab_h + seq * c->maxp;
+  const size_t keep = (keep_len + c->page - 1) / c->page;
+  bool changed = false;
+  for (size_t i = keep; i < c->maxp; i++)
+    if (row[i] >= 0) {
+      c->free_pages[c->n_free++] = row[i];
+      row[i] = -1;
+      changed = true;
+    }
+  if (changed)
+    SYN_CUDA_TRY(cudaMemcpy(c->d_ptab + seq * c->maxp, row, c->maxp * sizeof(int),
+                            cudaMemcpyHostToDevice));
+  return SYN_OK;
+}
+
+__global__ void k_kv_advance_slots(int* len, const int* slots, int n) {
+  griddep_wait();
+  griddep_launch();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) len[slots[i]] += 1;
+}
+
+syn_status_t launch_kv_advance_slots(syn_cuda_kvcache_t* c, const int* slots, size_t n,
+                                     cudaStream_t st) {
+  return cuda_status(launch_pdl(k_kv_advance_slots, dim3(1), dim3(128), 0, st, c->d_len, slots,
+                                (int)n),
+                     "k_kv_advance_slots");
 }
 
 syn_status_t launch_kv_set(syn_cuda_kvcache_t* c, size_t seq, int value, int add, cudaStream_t st) {
@@ -1432,14 +1515,16 @@ syn_status_t syn_cuda_embed_rmsnorm(const float* table, size_t vocab, const int3
                             hidden, eps, out, hidden, (cudaStream_t)stream);
 }
 
-syn_status_t syn_cuda_kvcache_create(syn_cuda_ctx_t* ctx, size_t max_seq, size_t n_kv_heads,
-                                     size_t head_dim, size_t num_layers, size_t batch,
-                                     syn_cuda_kvcache_t** out) {
+syn_status_t syn_cuda_kvcache_create_paged(syn_cuda_ctx_t* ctx, size_t max_seq,
+                                           size_t n_kv_heads, size_t head_dim, size_t num_layers,
+                                           size_t batch, size_t page, size_t n_pages,
+                                           syn_cuda_kvcache_t** out) {
   if (!ctx || !out) return SYN_ERR_NULL_PTR;
   *out = nullptr;
   if (!max_seq || !n_kv_heads || !head_dim || !num_layers || !batch)
     return SYN_ERR_INVALID_DIMENSIONS;  // kvcache.zig:31-34
   if (max_seq > 0x7FFFFFF || head_dim % 4) return SYN_ERR_UNSUPPORTED;
+  if (page && (!n_pages || n_pages > 0x7FFFFFF || page > max_seq)) return SYN_ERR_INVALID_ARG;
   DeviceGuard g(ctx->device);
   if (!g.ok) return SYN_ERR_CUDA;
   auto* c = new (std::nothrow) syn_cuda_kvcache_s();
@@ -1450,7 +1535,11 @@ syn_status_t syn_cuda_kvcache_create(syn_cuda_ctx_t* ctx, size_t max_seq, size_t
   c->hd = head_dim;
   c->layers = num_layers;
   c->batch = batch;
-  const size_t elems = num_layers * batch * max_seq * n_kv_heads * head_dim;
+  c->page = page;
+  c->n_pages = page ? n_pages : 0;
+  c->maxp = page ? (max_seq + page - 1) / page : 0;
+  const size_t rows = page ? n_pages * page : batch * max_seq;
+  const size_t elems = num_layers * rows * n_kv_heads * head_dim;
   c->len = new (std::nothrow) size_t[batch]();
   cudaError_t e = c->len ? cudaMalloc(&c->k, elems * sizeof(float)) : cudaErrorMemoryAllocation;
   if (e == cudaSuccess) e = cudaMalloc(&c->v, elems * sizeof(float));
@@ -1458,17 +1547,45 @@ syn_status_t syn_cuda_kvcache_create(syn_cuda_ctx_t* ctx, size_t max_seq, size_t
   if (e == cudaSuccess) e = cudaMemset(c->k, 0, elems * sizeof(float));
   if (e == cudaSuccess) e = cudaMemset(c->v, 0, elems * sizeof(float));
   if (e == cudaSuccess) e = cudaMemset(c->d_len, 0, batch * sizeof(int));
+  if (e == cudaSuccess && page) {
+    e = cudaMallocHost(&c->ptab_h, batch * c->maxp * sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_ptab, batch * c->maxp * sizeof(int));
+    c->free_pages = e == cudaSuccess ? new (std::nothrow) int[n_pages] : nullptr;
+    if (e == cudaSuccess && !c->free_pages) e = cudaErrorMemoryAllocation;
+    if (e == cudaSuccess) {
+      for (size_t i = 0; i < batch * c->maxp; i++) c->ptab_h[i] = -1;
+      for (size_t i = 0; i < n_pages; i++) c->free_pages[i] = (int)(n_pages - 1 - i);
+      c->n_free = n_pages;
+      e = cudaMemcpy(c->d_ptab, c->ptab_h, batch * c->maxp * sizeof(int), cudaMemcpyHostToDevice);
+    }
+  }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "syn_cuda_kvcache_create");
     cudaFree(c->k);
     cudaFree(c->v);
     cudaFree(c->d_len);
+    cudaFree(c->d_ptab);
+    if (c->ptab_h) cudaFreeHost(c->ptab_h);
+    delete[] c->free_pages;
     delete[] c->len;
     delete c;
     return SYN_ERR_OUT_OF_MEMORY;
   }
   *out = c;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_kvcache_create(syn_cuda_ctx_t* ctx, size_t max_seq, size_t n_kv_heads,
+                                     size_t head_dim, size_t num_layers, size_t batch,
+                                     syn_cuda_kvcache_t** out) {
+  return syn_cuda_kvcache_create_paged(ctx, max_seq, n_kv_heads, head_dim, num_layers, batch, 0,
+                                       0, out);
+}
+
+syn_status_t syn_cuda_kvcache_pages_free(const syn_cuda_kvcache_t* c, size_t* n) {
+  if (!c || !n) return SYN_ERR_NULL_PTR;
+  *n = c->page ? c->n_free : 0;
   return SYN_OK;
 }
 
@@ -1480,6 +1597,9 @@ syn_status_t syn_cuda_kvcache_destroy(syn_cuda_kvcache_t* c) {
   cudaFree(c->v);
   cudaFree(c->d_len);
   cudaFree(c->part);
+  cudaFree(c->d_ptab);
+  if (c->ptab_h) cudaFreeHost(c->ptab_h);
+  delete[] c->free_pages;
   delete[] c->len;
   delete c;
   return SYN_OK;
@@ -1496,6 +1616,7 @@ syn_status_t syn_cuda_kvcache_view(const syn_cuda_kvcache_t* c, size_t layer, si
                                    float** k, float** v) {
   if (!c) return SYN_ERR_NULL_PTR;
   if (layer >= c->layers || seq >= c->batch) return SYN_ERR_INVALID_ARG;
+  if (c->page) return SYN_ERR_UNSUPPORTED;  // a paged sequence is not one contiguous range
   const size_t off = (layer * c->batch + seq) * c->max_seq * c->n_kv * c->hd;
   if (k) *k = c->k + off;
   if (v) *v = c->v + off;
@@ -1510,10 +1631,27 @@ syn_status_t syn_cuda_kvcache_append(syn_cuda_kvcache_t* c, size_t layer, size_t
   if (c->len[seq] + n_tokens > c->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
   if (!n_tokens) return SYN_OK;
   DeviceGuard g(c->device);
+  const size_t row = c->n_kv * c->hd;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (c->page) {  // page by page
+    syn_status_t s = kv_reserve(c, seq, c->len[seq] + n_tokens, st);
+    if (s) return s;
+    const size_t base = layer * c->n_pages * c->page;
+    for (size_t t = 0; t < n_tokens;) {
+      const size_t pos = c->len[seq] + t, in = pos % c->page;
+      const size_t run = std::min(n_tokens - t, c->page - in);
+      const size_t slot = base + (size_t)c->ptab_h[seq * c->maxp + pos / c->page] * c->page + in;
+      SYN_CUDA_TRY(cudaMemcpyAsync(c->k + slot * row, k + t * row, run * row * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+      SYN_CUDA_TRY(cudaMemcpyAsync(c->v + slot * row, v + t * row, run * row * 4,
+                                   cudaMemcpyDeviceToDevice, st));
+      t += run;
+    }
+    return SYN_OK;
+  }
   float *kd, *vd;
   syn_cuda_kvcache_view(c, layer, seq, &kd, &vd);
-  const size_t row = c->n_kv * c->hd, off = c->len[seq] * row, bytes = n_tokens * row * 4;
-  cudaStream_t st = (cudaStream_t)stream;
+  const size_t off = c->len[seq] * row, bytes = n_tokens * row * 4;
   SYN_CUDA_TRY(cudaMemcpyAsync(kd + off, k, bytes, cudaMemcpyDeviceToDevice, st));
   SYN_CUDA_TRY(cudaMemcpyAsync(vd + off, v, bytes, cudaMemcpyDeviceToDevice, st));
   return SYN_OK;
@@ -1524,7 +1662,9 @@ syn_status_t syn_cuda_kvcache_advance(syn_cuda_kvcache_t* c, size_t seq, size_t 
   if (seq >= c->batch) return SYN_ERR_INVALID_ARG;
   if (c->len[seq] + n > c->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
   DeviceGuard g(c->device);
-  syn_status_t s = launch_kv_set(c, seq, (int)n, 1, (cudaStream_t)stream);
+  syn_status_t s = kv_reserve(c, seq, c->len[seq] + n, (cudaStream_t)stream);
+  if (s) return s;
+  s = launch_kv_set(c, seq, (int)n, 1, (cudaStream_t)stream);
   if (s == SYN_OK) c->len[seq] += n;
   return s;
 }
@@ -1537,6 +1677,7 @@ syn_status_t syn_cuda_kvcache_truncate(syn_cuda_kvcache_t* c, size_t seq, size_t
   DeviceGuard g(c->device);
   syn_status_t s = launch_kv_set(c, seq, (int)new_len, 0, (cudaStream_t)stream);
   if (s == SYN_OK) c->len[seq] = new_len;
+  if (s == SYN_OK) s = kv_release(c, seq, new_len, (cudaStream_t)stream);
   return s;
 }
 
@@ -1546,6 +1687,7 @@ syn_status_t syn_cuda_kvcache_reset(syn_cuda_kvcache_t* c, size_t seq, void* str
   DeviceGuard g(c->device);
   syn_status_t s = launch_kv_set(c, seq, 0, 0, (cudaStream_t)stream);
   if (s == SYN_OK) c->len[seq] = 0;
+  if (s == SYN_OK) s = kv_release(c, seq, 0, (cudaStream_t)stream);
   return s;
 }
 

@@ -175,6 +175,37 @@ bool concat(const std::vector<const HostLinear*>& parts, HostLinear& out) {
   return true;
 }
 
+// Gate and up (same format, k and n) interleaved by blocks of 16 output rows:
+// rows 32j..32j+15 = gate rows 16j.., rows 32j+16.. = up rows 16j.., so a
+// 32-row group of the GEMV holds 16 matching (gate, up) pairs and its
+// epilogue can apply SwiGLU.
+bool concat_il16(const HostLinear& g, const HostLinear& u, HostLinear& out) {
+  if (g.fmt != u.fmt || g.k != u.k || g.n != u.n || g.n % 16) return false;
+  out = HostLinear();
+  out.fmt = g.fmt;
+  out.k = g.k;
+  out.n = 2 * g.n;
+  out.data.resize(weight_bytes(out.fmt, out.n, out.k));
+  if (out.fmt == SYN_QFMT_INT8_KN) {  // [K, N] columns, and per-column scales
+    for (size_t kk = 0; kk < out.k; kk++)
+      for (size_t j = 0; j < g.n; j += 16) {
+        memcpy(out.data.data() + kk * out.n + 2 * j, g.data.data() + kk * g.n + j, 16);
+        memcpy(out.data.data() + kk * out.n + 2 * j + 16, u.data.data() + kk * u.n + j, 16);
+      }
+    for (size_t j = 0; j < g.n; j += 16) {
+      out.scales.insert(out.scales.end(), g.scales.begin() + j, g.scales.begin() + j + 16);
+      out.scales.insert(out.scales.end(), u.scales.begin() + j, u.scales.begin() + j + 16);
+    }
+  } else {  // whole rows
+    const size_t rb = row_bytes(out.fmt, out.k);
+    for (size_t j = 0; j < g.n; j += 16) {
+      memcpy(out.data.data() + 2 * j * rb, g.data.data() + j * rb, 16 * rb);
+      memcpy(out.data.data() + (2 * j + 16) * rb, u.data.data() + j * rb, 16 * rb);
+    }
+  }
+  return true;
+}
+
 struct LayerDev {
   float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   syn_cuda_weight_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
@@ -202,6 +233,11 @@ struct syn_cuda_model_s {
   float* span_logits = nullptr;
   int32_t* span_tok = nullptr;
   int32_t* span_tok_h = nullptr;
+  // continuous batching: paged KV (kv_page = 0: contiguous) and the row ->
+  // sequence map of slot-indexed decode steps
+  size_t kv_page = 0, kv_pages = 0;
+  int* slots_d = nullptr;
+  int* slots_h = nullptr;
   // staged host weights
   std::map<std::string, HostLinear> lin;
   std::map<std::string, std::vector<float>> ten;
@@ -316,7 +352,8 @@ syn_status_t mm(syn_cuda_model_s* m, const syn_cuda_weight_t* w, const float* x,
 // length advanced. nlayers < L runs only the first nlayers layers (the
 // reference's layer-skipping draft, pipeline.rs:281-330).
 syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq, bool want_logits,
-                     bool chained = false, size_t nlayers = 0, bool span = false) {
+                     bool chained = false, size_t nlayers = 0, bool span = false,
+                     const int* slots = nullptr) {
   cudaStream_t st = m->st;
   syn_status_t s;
   const size_t h = m->h;
@@ -333,6 +370,7 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
   // block-format models carry a 1e-3 tolerance: parallel-order attention;
   // INT8 models keep the reference's reduction order (bit-exact tokens)
   a.flash = m->int8 ? 0 : 1;
+  a.slots = slots;  // decode rows -> sequences (continuous batching)
   const bool tp = m->tp > 1;
   // One row (decode at batch 1): each RMSNorm runs in the prologue of the
   // matmul it feeds, with the residual stream ping-ponging between two
@@ -376,7 +414,8 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
     if (tp && (s = tp_allreduce_sum(m->ctx, m->o, rows * h, st))) return s;  // row-parallel O
     if (fuse) {
       float* nxt = other(cur);
-      GemvNorm nm{cur, m->o, ly.ffn_norm, m->eps, nxt, a.flash};
+      // SwiGLU in the GEMV's epilogue: hid comes out directly
+      GemvNorm nm{cur, m->o, ly.ffn_norm, m->eps, nxt, a.flash, m->hid, (int)m->ff_l, variant};
       if ((s = ensure_scratch(m->ctx, ly.gu, 1, st))) return s;
       s = launch_qgemv_norm(ly.gu, nm, m->gu, m->ctx->part, m->ctx->part_bytes,
                             m->ctx->cnt, m->ctx->err, st);
@@ -387,10 +426,11 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
                              m->eps, m->x, h, st, a.flash);
       if (s) return s;
       if ((s = mm(m, ly.gu, m->x, rows, m->gu))) return s;
+      // gate/up rows are interleaved by 16 (see concat_il16)
+      s = launch_swiglu(m->gu, m->gu + 16, 2 * m->ff_l, rows, m->ff_l, variant, m->hid, m->ff_l,
+                        st, 1);
+      if (s) return s;
     }
-    s = launch_swiglu(m->gu, m->gu + m->ff_l, 2 * m->ff_l, rows, m->ff_l, variant, m->hid,
-                      m->ff_l, st);
-    if (s) return s;
     if ((s = mm(m, ly.down, m->hid, rows, m->dn))) return s;
     if (tp && (s = tp_allreduce_sum(m->ctx, m->dn, rows * h, st))) return s;  // row-parallel down
   }
@@ -425,6 +465,18 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
     for (size_t b = 0; b < nr; b++)
       if ((s = tp_allgather(m->ctx, m->logits_l + b * m->v_l, m->logits + b * m->V, m->v_l, st)))
         return s;
+  }
+  if (slots) {  // row b's token into tok[b]; each mapped sequence advances by one
+    s = launch_argmax(m->logits, m->V, nr, m->V, m->tok, nullptr, 0, (int)m->max_seq, nullptr, 0,
+                      m->am_scratch, st);
+    if (s) return s;
+    if ((s = launch_kv_advance_slots(m->cache, slots, nr, st))) return s;
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->tok_h, m->tok, nr * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->err_h, m->ctx->err, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    if (want_logits)
+      SYN_CUDA_TRY(cudaMemcpyAsync(m->logits_h, m->logits, nr * m->V * sizeof(float),
+                                   cudaMemcpyDeviceToHost, st));
+    return SYN_OK;
   }
   // the generated token of sequence b lands in tok[b] (prefill: tok[seq])
   s = launch_argmax(m->logits, m->V, nr, m->V, m->tok + (prefill ? seq : 0),
@@ -610,7 +662,7 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
       return s;
     if (!concat({&qs, &ks, &vs}, cat)) return SYN_ERR_INVALID_ARG;
     if ((s = upload_linear(m, cat, &ly.qkv))) return s;
-    if (!concat({&gs, &us}, cat)) return SYN_ERR_INVALID_ARG;
+    if (!concat_il16(gs, us, cat)) return SYN_ERR_INVALID_ARG;
     if ((s = upload_linear(m, cat, &ly.gu))) return s;
     if ((s = upload_linear(m, os, &ly.o))) return s;
     if ((s = upload_linear(m, ds, &ly.down))) return s;
@@ -631,9 +683,11 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   if ((s = dev_alloc_t(m, &m->sin_t, c.size()))) return s;
   SYN_CUDA_TRY(cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
   SYN_CUDA_TRY(cudaMemcpy(m->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
-  if ((s = syn_cuda_kvcache_create(m->ctx, m->max_seq, m->hkv_l, m->hd, m->L, m->max_batch,
-                                   &m->cache)))
+  if ((s = syn_cuda_kvcache_create_paged(m->ctx, m->max_seq, m->hkv_l, m->hd, m->L, m->max_batch,
+                                         m->kv_page, m->kv_pages, &m->cache)))
     return s;
+  if ((s = dev_alloc_t(m, &m->slots_d, m->max_batch))) return s;
+  SYN_CUDA_TRY(cudaMallocHost(&m->slots_h, m->max_batch * sizeof(int)));
   const size_t R = m->max_rows;
   if ((s = dev_alloc_t(m, &m->ids, R))) return s;
   if ((s = dev_alloc_t(m, &m->tok, m->max_batch))) return s;
@@ -696,6 +750,9 @@ syn_status_t syn_cuda_decode_step(syn_cuda_model_t* m, size_t batch, const int32
   for (size_t b = 0; b < batch; b++)
     if (m->cache->len[b] + 1 > m->max_seq) return SYN_ERR_INVALID_ARG;  // CacheFull
   DeviceGuard g(m->device);
+  syn_status_t rs;
+  for (size_t b = 0; b < batch; b++)  // pages for the new positions, outside any graph
+    if ((rs = kv_reserve(m->cache, b, m->cache->len[b] + 1, m->st))) return rs;
   memcpy(m->ids_h, last_tokens, batch * sizeof(int32_t));
   const auto key = std::make_pair(batch, logits_host ? 1 : 0);
   syn_status_t s = SYN_OK;
@@ -750,6 +807,10 @@ syn_status_t syn_cuda_generate(syn_cuda_model_t* m, size_t batch, size_t n_steps
     if (m->cache->len[b] == 0 || m->cache->len[b] + n_steps > m->max_seq)
       return SYN_ERR_INVALID_ARG;  // not started, or CacheFull
   DeviceGuard g(m->device);
+  for (size_t b = 0; b < batch; b++) {  // pages for every position the steps will write
+    syn_status_t rs = kv_reserve(m->cache, b, m->cache->len[b] + n_steps, m->st);
+    if (rs) return rs;
+  }
   std::vector<size_t> len0(m->cache->len, m->cache->len + batch);
   syn_status_t s = SYN_OK;
   size_t done = 0;
@@ -799,6 +860,50 @@ syn_status_t syn_cuda_generate(syn_cuda_model_t* m, size_t batch, size_t n_steps
     m->cache->len[b] += n_steps;
   }
   return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_set_kv_paging(syn_cuda_model_t* m, size_t page, size_t n_pages) {
+  if (!m) return SYN_ERR_NULL_PTR;
+  if (m->finalized || (page && !n_pages)) return SYN_ERR_INVALID_ARG;
+  m->kv_page = page;
+  m->kv_pages = page ? n_pages : 0;
+  return SYN_OK;
+}
+
+syn_status_t syn_cuda_model_kv_pages_free(const syn_cuda_model_t* m, size_t* n) {
+  if (!m || !n) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  return syn_cuda_kvcache_pages_free(m->cache, n);
+}
+
+syn_status_t syn_cuda_decode_step_slots(syn_cuda_model_t* m, size_t n, const int32_t* slots,
+                                        const int32_t* last_tokens, int32_t* out_tokens,
+                                        float* logits_host) {
+  if (!m || !slots || !last_tokens || !out_tokens) return SYN_ERR_NULL_PTR;
+  if (!m->finalized) return SYN_ERR_INVALID_ARG;
+  if (n == 0 || n > m->max_batch) return SYN_ERR_INVALID_ARG;
+  for (size_t i = 0; i < n; i++) {
+    if (slots[i] < 0 || (size_t)slots[i] >= m->max_batch) return SYN_ERR_INVALID_ARG;
+    for (size_t j = 0; j < i; j++)
+      if (slots[j] == slots[i]) return SYN_ERR_INVALID_ARG;  // one row per sequence
+    const size_t len = m->cache->len[slots[i]];
+    if (len == 0 || len + 1 > m->max_seq) return SYN_ERR_INVALID_ARG;  // not started / full
+  }
+  DeviceGuard g(m->device);
+  syn_status_t s;
+  for (size_t i = 0; i < n; i++)
+    if ((s = kv_reserve(m->cache, slots[i], m->cache->len[slots[i]] + 1, m->st))) return s;
+  memcpy(m->ids_h, last_tokens, n * sizeof(int32_t));
+  memcpy(m->slots_h, slots, n * sizeof(int32_t));
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->ids, m->ids_h, n * sizeof(int32_t), cudaMemcpyHostToDevice, m->st));
+  SYN_CUDA_TRY(cudaMemcpyAsync(m->slots_d, m->slots_h, n * sizeof(int32_t), cudaMemcpyHostToDevice,
+                               m->st));
+  s = forward(m, n, false, 0, logits_host != nullptr, false, 0, false, m->slots_d);
+  if (s) return s;
+  s = finish(m, n, out_tokens, logits_host);
+  if (s == SYN_OK)
+    for (size_t i = 0; i < n; i++) m->cache->len[slots[i]] += 1;
+  return s;
 }
 
 syn_status_t syn_cuda_decode_span(syn_cuda_model_t* m, size_t seq, const int32_t* tokens,
@@ -932,6 +1037,7 @@ syn_status_t syn_cuda_model_destroy(syn_cuda_model_t* m) {
   if (m->ids_h) cudaFreeHost(m->ids_h);
   if (m->tok_h) cudaFreeHost(m->tok_h);
   if (m->span_tok_h) cudaFreeHost(m->span_tok_h);
+  if (m->slots_h) cudaFreeHost(m->slots_h);
   if (m->logits_h) cudaFreeHost(m->logits_h);
   if (m->err_h) cudaFreeHost(m->err_h);
   if (m->st) cudaStreamDestroy(m->st);

@@ -79,6 +79,8 @@ def _gguf_model_file(cfg, w, fmt, path):
 
 
 def _same_run(m1, m2, prompt, steps=6):
+    m1.reset()
+    m2.reset()
     t1, l1 = m1.forward_prefill(prompt)
     t2, l2 = m2.forward_prefill(prompt)
     assert np.array_equal(l1.view(np.uint32), l2.view(np.uint32))
