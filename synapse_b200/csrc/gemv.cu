@@ -1202,7 +1202,9 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
       return 0;
     };
     int ns = pick_ns();
-    while (ns == 0 && pl.nks > 1) {
+    // SYN_GEMV_ONE_WAVE=0 keeps the K splits even when the grid runs in
+    // several waves (the deepest ring is used then)
+    while (ns == 0 && pl.nks > 1 && tune("SYN_GEMV_ONE_WAVE", 1)) {
       const int before = pl.nks;
       set_split(before - 1);
       if (pl.nks >= before) break;  // the shared-memory bound split it again

@@ -28,6 +28,8 @@
 #include <new>
 #include <set>
 
+#include <cuda_bf16.h>
+
 #include "internal.cuh"
 
 namespace syn {
@@ -1015,6 +1017,286 @@ size_t flash_prefill_smem(int hd) {
 }
 
 // ---------------------------------------------------------------------------
+// Prefill attention on the tensor cores (block-format models): CTA = (head,
+// 128 queries), 128 threads, thread t owns query row t (tensor-memory lane
+// t). Per key tile of 64:
+//   S = Q K^T with tcgen05.mma kind::f16 (bf16 operands, fp32 accumulation
+//   in tensor memory), each f32 operand entering as bf16 hi + lo parts
+//   (x = hi + lo, lo = bf16(x - hi)) and the four products hi*hi + hi*lo +
+//   lo*hi + lo*lo summed, so a score carries about 2^-24 relative error:
+//   the f32 products of the CUDA-core kernel, in another summation order;
+//   online softmax (row max, rescale, exp) in registers, one row per thread;
+//   O_tile = P V the same way (P and V split likewise), added to the
+//   thread's f32 output row with the rescaling.
+// Operands live in shared memory in the 128-byte-swizzled K-major layout
+// (atoms of 8 rows x 128 B): Q [128][HD], K [64][HD], V^T [HD][64] (staged
+// transposed, so both MMAs read K-major operands), P [128][64]. Waits are
+// bounded (SYN_ERR_TIMEOUT). Reference: syn_fused_attention
+// (zig/src/ffi/exports.zig:1364-1478), causal, no window.
+// ---------------------------------------------------------------------------
+constexpr int TCA_Q = 128, TCA_K = 64, TCA_THREADS = 128;
+
+__device__ __forceinline__ uint32_t tca_sw(int c, int r, int rows) {  // 16-byte column c of row r
+  return (uint32_t)((c >> 3) * rows * 128 + (r >> 3) * 1024 + (r & 7) * 128 +
+                    (((c & 7) ^ (r & 7)) << 4));
+}
+__device__ __forceinline__ uint64_t tca_desc(uint32_t addr) {  // K-major, 128B swizzle
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;             // LBO 16 B
+  d |= (uint64_t)(1024 >> 4) << 32;   // SBO 1024 B
+  d |= (uint64_t)1 << 46;             // sm_100 descriptor version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+__device__ __forceinline__ void tca_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc), "r"(0u));
+}
+__device__ __forceinline__ void tca_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tca_ld32(uint32_t taddr, float (&r)[32]) {
+  uint32_t u[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]),
+        "=r"(u[7]), "=r"(u[8]), "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]),
+        "=r"(u[14]), "=r"(u[15]), "=r"(u[16]), "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]),
+        "=r"(u[21]), "=r"(u[22]), "=r"(u[23]), "=r"(u[24]), "=r"(u[25]), "=r"(u[26]), "=r"(u[27]),
+        "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) r[i] = __uint_as_float(u[i]);
+}
+// 8 f32 -> bf16 hi (16 B) and lo (16 B)
+__device__ __forceinline__ void tca_split8(const float (&v)[8], uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    const float2 bf = __bfloat1622float2(b);
+    const __nv_bfloat162 r = __floats2bfloat162_rn(v[2 * i] - bf.x, v[2 * i + 1] - bf.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&b);
+    l[i] = *reinterpret_cast<const uint32_t*>(&r);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+template <int HD>
+struct TcaSmem {
+  static constexpr int Q = TCA_Q * HD * 2;    // one bf16 part of Q
+  static constexpr int K = TCA_K * HD * 2;    // of K
+  static constexpr int V = HD * TCA_K * 2;    // of V^T
+  static constexpr int P = TCA_Q * TCA_K * 2; // of P
+  static constexpr int OQ = 0, OK = 2 * Q, OV = OK + 2 * K, OP = OV + 2 * V;
+  static constexpr int BYTES = OP + 2 * P + 1024;  // + alignment slack
+};
+
+template <int HD>
+__global__ void __launch_bounds__(TCA_THREADS, 1) k_attn_prefill_tc(const AttnParams p) {
+  using L = TcaSmem<HD>;
+  extern __shared__ uint8_t tca_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tca_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bar_s, bar_o;
+  __shared__ uint32_t tbase_sh;
+  __shared__ int fail;
+  const int hh = blockIdx.x, q0 = blockIdx.y * TCA_Q, t = threadIdx.x, warp = t >> 5;
+  const int G = p.n_heads / p.n_kv, kvh = hh / G, kvd = p.n_kv * HD, S = p.n_tokens;
+  constexpr uint32_t TMEM_COLS = 256, S_COL = 0, O_COL = 64;
+  if (t == 0) {
+    mbar_init(&bar_s, 1);
+    mbar_init(&bar_o, 1);
+    fail = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&tbase_sh)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tb = tbase_sh;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  griddep_wait();
+  const int base = p.len[p.seq0];  // the prompt's first cache position
+  // Q: row t (zero beyond the prompt)
+  {
+    const float* qr = p.q + (long long)(q0 + t) * p.ld + (long long)hh * HD;
+    for (int c = 0; c < HD / 8; c++) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) v[e] = q0 + t < S ? qr[c * 8 + e] : 0.0f;
+      uint4 hi, lo;
+      tca_split8(v, hi, lo);
+      *reinterpret_cast<uint4*>(sm + L::OQ + tca_sw(c, t, TCA_Q)) = hi;
+      *reinterpret_cast<uint4*>(sm + L::OQ + L::Q + tca_sw(c, t, TCA_Q)) = lo;
+    }
+  }
+  float o[HD];
+#pragma unroll
+  for (int d = 0; d < HD; d++) o[d] = 0.0f;
+  float m = -INFINITY, l = 0.0f;
+  const int qi = q0 + t;
+  const int kend = min(S, q0 + TCA_Q);  // causal: keys < kend
+  const uint32_t id_s = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TCA_K >> 3) << 17) |
+                        ((uint32_t)(TCA_Q >> 4) << 24);
+  const uint32_t id_o = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(HD >> 3) << 17) |
+                        ((uint32_t)(TCA_Q >> 4) << 24);
+  const uint32_t sq = smem_u32(sm + L::OQ), sk = smem_u32(sm + L::OK), sv = smem_u32(sm + L::OV),
+                 sp = smem_u32(sm + L::OP);
+  int tile = 0;
+  for (int k0 = 0; k0 < kend; k0 += TCA_K, tile++) {
+    // stage K [64 keys][HD] and V^T [HD][64 keys] as bf16 hi / lo
+    for (int w = t; w < TCA_K * (HD / 8); w += TCA_THREADS) {
+      const int r = w / (HD / 8), c = w - r * (HD / 8);
+      float v[8];
+      if (k0 + r < S) {
+        const float* kr = p.kc + kvh * HD + kv_slot(p, p.seq0, base + k0 + r) * kvd + c * 8;
+        const float4 a = reinterpret_cast<const float4*>(kr)[0], b = reinterpret_cast<const float4*>(kr)[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = 0.0f;
+      }
+      uint4 hi, lo;
+      tca_split8(v, hi, lo);
+      *reinterpret_cast<uint4*>(sm + L::OK + tca_sw(c, r, TCA_K)) = hi;
+      *reinterpret_cast<uint4*>(sm + L::OK + L::K + tca_sw(c, r, TCA_K)) = lo;
+    }
+    for (int w = t; w < HD * (TCA_K / 8); w += TCA_THREADS) {
+      const int d = w % HD, c = w / HD;  // V^T row d, keys 8c .. 8c+7
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int kk = k0 + c * 8 + e;
+        v[e] = kk < S ? p.vc[kvh * HD + kv_slot(p, p.seq0, base + kk) * kvd + d] : 0.0f;
+      }
+      uint4 hi, lo;
+      tca_split8(v, hi, lo);
+      *reinterpret_cast<uint4*>(sm + L::OV + tca_sw(c, d, HD)) = hi;
+      *reinterpret_cast<uint4*>(sm + L::OV + L::V + tca_sw(c, d, HD)) = lo;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    // S = Q K^T: 4 products per 16-wide K step
+    if (t == 0 && !fail) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int ks = 0; ks < HD / 16; ks++) {
+        const uint32_t qa = (uint32_t)((ks >> 2) * TCA_Q * 128 + (ks & 3) * 32);
+        const uint32_t ka = (uint32_t)((ks >> 2) * TCA_K * 128 + (ks & 3) * 32);
+#pragma unroll
+        for (int term = 0; term < 4; term++) {
+          const uint64_t da = tca_desc(sq + qa + ((term >> 1) ? L::Q : 0));
+          const uint64_t db = tca_desc(sk + ka + ((term & 1) ? L::K : 0));
+          tca_mma(tb + S_COL, da, db, id_s, (ks | term) ? 1u : 0u);
+        }
+      }
+      tca_commit(&bar_s);
+    }
+    if (!mbar_wait_bounded(&bar_s, tile & 1)) fail = 1;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    // softmax on row t
+    float sc[TCA_K];
+    {
+      float a[32];
+      tca_ld32(tb + lane_off + S_COL, a);
+#pragma unroll
+      for (int j = 0; j < 32; j++) sc[j] = a[j];
+      tca_ld32(tb + lane_off + S_COL + 32, a);
+#pragma unroll
+      for (int j = 0; j < 32; j++) sc[32 + j] = a[j];
+    }
+    float mt = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < TCA_K; j++) {
+      const int kk = k0 + j;
+      sc[j] = (kk <= qi && kk < S) ? sc[j] * p.scale : -INFINITY;
+      mt = fmaxf(mt, sc[j]);
+    }
+    const float mn = fmaxf(m, mt);
+    const float corr = mn == -INFINITY ? 1.0f : expf(m - mn);
+    float rs = 0.0f;
+#pragma unroll
+    for (int c = 0; c < TCA_K / 8; c++) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const float x = sc[c * 8 + e];
+        v[e] = mn == -INFINITY ? 0.0f : expf(x - mn);
+        rs += v[e];
+      }
+      uint4 hi, lo;
+      tca_split8(v, hi, lo);
+      *reinterpret_cast<uint4*>(sm + L::OP + tca_sw(c, t, TCA_Q)) = hi;
+      *reinterpret_cast<uint4*>(sm + L::OP + L::P + tca_sw(c, t, TCA_Q)) = lo;
+    }
+    l = l * corr + rs;
+    m = mn;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    // O_tile = P V
+    if (t == 0 && !fail) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+      for (int ks = 0; ks < TCA_K / 16; ks++) {
+        const uint32_t off = (uint32_t)(ks * 32);
+#pragma unroll
+        for (int term = 0; term < 4; term++) {
+          const uint64_t da = tca_desc(sp + off + ((term >> 1) ? L::P : 0));
+          const uint64_t db = tca_desc(sv + off + ((term & 1) ? L::V : 0));
+          tca_mma(tb + O_COL, da, db, id_o, (ks | term) ? 1u : 0u);
+        }
+      }
+      tca_commit(&bar_o);
+    }
+    if (!mbar_wait_bounded(&bar_o, tile & 1)) fail = 1;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+    for (int d0 = 0; d0 < HD; d0 += 32) {
+      float a[32];
+      tca_ld32(tb + lane_off + O_COL + d0, a);
+#pragma unroll
+      for (int j = 0; j < 32; j++) o[d0 + j] = fmaf(o[d0 + j], corr, a[j]);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+  }
+  griddep_launch();
+  if (fail) {
+    if (t == 0 && p.err) atomicExch(p.err, SYN_ERR_TIMEOUT);
+  } else if (qi < S) {
+    float* orow = p.out + (long long)qi * p.ldo + (long long)hh * HD;
+#pragma unroll
+    for (int d = 0; d < HD; d += 4)
+      *reinterpret_cast<float4*>(orow + d) =
+          make_float4(o[d] / l, o[d + 1] / l, o[d + 2] / l, o[d + 3] / l);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tb), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // SwiGLU: variant 0 = the INT8 model's silu(g) * u with silu = g/(1+exp(-g))
 // (quantization/lm/int8.rs:500-503, ops/activation.rs:30-32); variant 1 =
 // swigluFused (zig/src/ops/silu.zig:85-114): g * (1/(1+exp(-g))) * u for the
@@ -1382,6 +1664,18 @@ syn_status_t launch_prefill_attention_args(const AttnArgs& a, size_t seq, size_t
   if (seq >= a.cache->batch) return SYN_ERR_INVALID_ARG;
   if (a.cache->len[seq] + ntok > a.cache->max_seq) return SYN_ERR_INVALID_ARG;
   if (ntok == 0) return SYN_OK;
+  static const int use_tc = [] {
+    const char* v = getenv("SYN_ATTN_TC");
+    return v ? atoi(v) : 1;
+  }();
+  if (a.flash && use_tc && (p.hd == 64 || p.hd == 128)) {
+    void (*kern)(const AttnParams) = p.hd == 64 ? k_attn_prefill_tc<64> : k_attn_prefill_tc<128>;
+    const size_t fs = p.hd == 64 ? TcaSmem<64>::BYTES : TcaSmem<128>::BYTES;
+    if ((s = allow_smem((const void*)kern, fs))) return s;
+    return cuda_status(launch_pdl(kern, dim3((unsigned)p.n_heads, (unsigned)((ntok + TCA_Q - 1) / TCA_Q)),
+                                  dim3(TCA_THREADS), fs, st, p),
+                       "k_attn_prefill_tc");
+  }
   if (a.flash && (p.hd == 64 || p.hd == 128)) {
     void (*kern)(const AttnParams) = p.hd == 64 ? k_attn_prefill_flash<64> : k_attn_prefill_flash<128>;
     const size_t fs = flash_prefill_smem(p.hd);

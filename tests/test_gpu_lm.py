@@ -170,6 +170,34 @@ def test_attention_prefill_bit_exact(ctx, S, hq, hkv, hd, flash):
     cache.close()
 
 
+@pytest.mark.parametrize("S", [200, 511, 700])
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attention_prefill_tensor_core_long(ctx, S, hd):
+    """The block-format prefill attention (tcgen05, split bf16 operands) on
+    prompts of several 128-query tiles and 64-key tiles, against
+    syn_fused_attention's restatement: within f32 reassociation."""
+    rng = np.random.default_rng(S + hd)
+    hq, hkv = 4, 2
+    qd, kvd = hq * hd, hkv * hd
+    eps = 1e-6
+    cache = sb.KVCache(ctx, 768, hkv, hd, 1, batch=1)
+    cos, sin = sb.rope_tables(1e6, 768, hd)
+    oc, os_ = O.rope_tables(1e6, 768, hd)
+    qkv = (3 * rng.standard_normal((S, qd + 2 * kvd))).astype(np.float32)
+    out = sb.attention_prefill(cache, 0, cuda(qkv), hq, None, None, eps, cuda(cos),
+                               cuda(sin), seq=0, flash=True).cpu().numpy()
+    q = qkv[:, :qd].copy()
+    k = qkv[:, qd:qd + kvd].copy()
+    O.rope_inplace(q, oc, os_, S, hq, hd, 0)
+    O.rope_inplace(k, oc, os_, S, hkv, hd, 0)
+    q3, k3 = q.reshape(S, hq, hd), k.reshape(S, hkv, hd)
+    v3 = qkv[:, qd + kvd:].reshape(S, hkv, hd)
+    for h in range(hq):
+        st, o = O.fused_attention(S, S, hd, q3[:, h], k3[:, h // 2], v3[:, h // 2])
+        assert close(out[:, h * hd:(h + 1) * hd], o.reshape(S, hd), True), h
+    cache.close()
+
+
 def test_kvcache_lengths_and_full(ctx):
     c = sb.KVCache(ctx, 4, 1, 8, 2, batch=2)
     z = torch.zeros(3, 8, device="cuda")
