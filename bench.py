@@ -761,6 +761,10 @@ def run_synapse(args, rank, world, local_rank):
             "decode": decode,
             "tp_decode": tp_decode,
             "configs_3_5": configs,
+            # the multi-GPU work of this path: config-4 tensor-parallel decode
+            # over all N ranks (TP1 at N=1); `value` stays the sharded sweep
+            "tp_decode_tok_s": tp_decode["tok_s"] if tp_decode else None,
+            "tp_decode_roofline_frac": tp_decode["roofline"]["frac"] if tp_decode else None,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:

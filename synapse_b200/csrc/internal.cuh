@@ -57,8 +57,9 @@ struct syn_cuda_kvcache_s {
   float* v;
   int* d_len;   // [batch]
   size_t* len;  // [batch], host mirror
-  float* part;  // split-attention partials (grown on demand)
+  float* part;  // split-attention counters + partials (grown on demand)
   size_t part_bytes;
+  int part_heads;  // the head count the counters are laid out for
   // Paged layout (page > 0): each layer's K and V are pools of n_pages pages
   // of `page` positions, and position p of sequence s lives in page
   // ptab[s * maxp + p / page]. Pages are taken from a free list as a

@@ -65,7 +65,12 @@ syn_status_t allow_smem(const void* fn, size_t bytes) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> g(mu);
   if (done.count({fn, dev})) return SYN_OK;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  // the most dynamic shared memory the kernel can have next to its static part
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(227 * 1024 - fa.sharedSizeBytes));
   if (e != cudaSuccess) {
     set_last_cuda_error(e, "cudaFuncSetAttribute");
     return SYN_ERR_CUDA;
@@ -1455,9 +1460,12 @@ syn_status_t launch_swiglu(const float* gate, const float* up, size_t ld_in, siz
                      "k_swiglu");
 }
 
+// Scratch: AM_MAX_ROWS arrival counters at a fixed place (they must stay
+// zero between launches whatever the rows of a call), then the states.
+constexpr size_t AM_MAX_ROWS = 4096;
 size_t argmax_scratch_bytes(size_t rows, size_t n) {
   const size_t nct = (n + AM_SEG - 1) / AM_SEG;
-  return rows * nct * sizeof(AmState) + rows * sizeof(int) + 64;
+  return rows * nct * sizeof(AmState) + AM_MAX_ROWS * sizeof(int) + 64;
 }
 
 syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
@@ -1465,10 +1473,10 @@ syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, in
                            void* scratch, cudaStream_t st) {
   if (!rows || !n) return SYN_OK;
   const size_t nct = (n + AM_SEG - 1) / AM_SEG;
-  if (nct > 65535 || rows > 65535) return SYN_ERR_UNSUPPORTED;
+  if (nct > 65535 || rows > AM_MAX_ROWS) return SYN_ERR_UNSUPPORTED;
   int* cnt = static_cast<int*>(scratch);  // zero before the first launch; left zero
   AmState* part = reinterpret_cast<AmState*>(static_cast<uint8_t*>(scratch) +
-                                             ((rows * sizeof(int) + 63) & ~size_t(63)));
+                                             AM_MAX_ROWS * sizeof(int));
   return cuda_status(launch_pdl(k_argmax, dim3((unsigned)nct, (unsigned)rows), dim3(AM_THREADS), 0,
                                 st, x, (long long)ldx, (int)n, out, len_adv, adv, max_len, hist,
                                 hist_ld, part,
@@ -1544,10 +1552,14 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
   syn_cuda_kvcache_t* c = a.cache;
   const int nsplit = (int)((eff + FD_CH - 1) / FD_CH);
   if (nsplit > 32 * (p.hd + 4)) return SYN_ERR_UNSUPPORTED;  // combine factors fit in smem
-  const size_t pbytes = (batch * p.n_heads * (size_t)nsplit * (p.hd + 2) * sizeof(float) + 255) &
-                        ~size_t(255);
-  const size_t need = pbytes + batch * p.n_heads * sizeof(int);
-  if (need > c->part_bytes) {  // grows outside graph capture only; counters start at zero
+  // arrival counters first, sized for every sequence slot, so that their
+  // place does not move with the batch of a call (they must stay zero
+  // between launches); the partials after them
+  const size_t cbytes = (c->batch * p.n_heads * sizeof(int) + 255) & ~size_t(255);
+  const size_t pbytes = batch * p.n_heads * (size_t)nsplit * (p.hd + 2) * sizeof(float);
+  const size_t need = cbytes + pbytes;
+  if (need > c->part_bytes || c->part_heads != p.n_heads) {
+    // grows outside graph capture only; counters start at zero
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cs);
     if (cs != cudaStreamCaptureStatusNone) return SYN_ERR_UNSUPPORTED;
@@ -1558,8 +1570,10 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
     if (cudaMalloc(&c->part, need) != cudaSuccess) return SYN_ERR_OUT_OF_MEMORY;
     if (cudaMemset(c->part, 0, need) != cudaSuccess) return SYN_ERR_CUDA;
     c->part_bytes = need;
+    c->part_heads = p.n_heads;
   }
-  int* cnt = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(c->part) + pbytes);
+  int* cnt = reinterpret_cast<int*>(c->part);
+  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c->part) + cbytes);
   void (*split)(const AttnParams, float*, int*, int) = nullptr;
   switch (p.hd) {
     case 32: split = k_attn_decode_split<32>; break;
@@ -1571,7 +1585,7 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
   syn_status_t s = allow_smem((const void*)split, smem);
   if (s) return s;
   return cuda_status(launch_pdl(split, dim3((unsigned)batch, (unsigned)p.n_heads, (unsigned)nsplit),
-                                dim3(FD_THREADS), smem, st, p, c->part, cnt, nsplit),
+                                dim3(FD_THREADS), smem, st, p, part, cnt, nsplit),
                      "k_attn_decode_split");
 }
 

@@ -175,7 +175,7 @@ def test_attention_prefill_bit_exact(ctx, S, hq, hkv, hd, flash):
 def test_attention_prefill_tensor_core_long(ctx, S, hd):
     """The block-format prefill attention (tcgen05, split bf16 operands) on
     prompts of several 128-query tiles and 64-key tiles, against
-    syn_fused_attention's restatement: within f32 reassociation."""
+    syn_fused_attention's restatement: normwise error <= 1e-4."""
     rng = np.random.default_rng(S + hd)
     hq, hkv = 4, 2
     qd, kvd = hq * hd, hkv * hd
@@ -194,7 +194,11 @@ def test_attention_prefill_tensor_core_long(ctx, S, hd):
     v3 = qkv[:, qd + kvd:].reshape(S, hkv, hd)
     for h in range(hq):
         st, o = O.fused_attention(S, S, hd, q3[:, h], k3[:, h // 2], v3[:, h // 2])
-        assert close(out[:, h * hd:(h + 1) * hd], o.reshape(S, hd), True), h
+        o = o.reshape(S, hd)
+        err = np.max(np.abs(out[:, h * hd:(h + 1) * hd] - o)) / np.max(np.abs(o))
+        # products are f32-grade (split operands), the MMA's fp32 sums and the
+        # 3x-scaled inputs' peaky softmax give a few 1e-6 normwise
+        assert err <= 1e-4, (h, err)
     cache.close()
 
 

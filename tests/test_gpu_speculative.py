@@ -80,3 +80,19 @@ def test_speculative_full_draft_accepts_everything(ctx):
     assert got == m.generate_greedy([5, 6, 7], 25)
     assert accepted == drafted
     m.close()
+
+
+def test_span_many_argmax_segments(ctx):
+    """A vocabulary of several argmax segments (2048 logits each): the span
+    step's per-row greedy tokens after one-token steps of other widths."""
+    import copy
+    cfg = copy.deepcopy(synth.lm_config("tiny"))
+    cfg["architecture"]["vocab_size"] = 9000
+    w = synth.gen_lm_weights(cfg, "INT8_KN", seed=43)
+    m = sb.Model(ctx, cfg, w, 96)
+    prompt = [4, 8, 15, 16, 23, 42, 8000, 8999]
+    want = m.generate_greedy(prompt, 20)
+    m.reset()
+    got, _, _ = m.generate_speculative(prompt, 20, k=5, draft_layers=1)
+    assert got == want
+    m.close()
