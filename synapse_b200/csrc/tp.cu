@@ -122,9 +122,12 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   return v;
 }
 
+// gather != nullptr: all-gather instead -- step 3 copies the world rows
+// into gather[r * n4 * 4 ..] in rank order, and x is only read.
 __global__ void __launch_bounds__(PEER_THREADS) k_peer_allreduce(float* x, int n4, int world,
                                                                  int rank, float* const* bufs,
-                                                                 int* sync, int* err) {
+                                                                 int* sync, int* err,
+                                                                 float* gather) {
   griddep_wait();  // x comes from the kernel before; the epoch from the call before
   const int cta = blockIdx.x, nct = gridDim.x, tid = threadIdx.x;
   const int e = *reinterpret_cast<volatile int*>(sync);
@@ -162,8 +165,14 @@ __global__ void __launch_bounds__(PEER_THREADS) k_peer_allreduce(float* x, int n
     }
   }
   __syncthreads();
-  // 3. sum in rank order
-  if (ok) {
+  // 3. sum in rank order (or gather)
+  if (ok && gather) {
+    const float4* mine = reinterpret_cast<const float4*>(bufs[rank]) + (size_t)slot * world * row4;
+    float4* g = reinterpret_cast<float4*>(gather);
+    for (int r = 0; r < world; r++)
+      for (int i = c0 + tid; i < c1; i += PEER_THREADS)
+        g[(size_t)r * n4 + i] = __ldcv(mine + (size_t)r * row4 + i);
+  } else if (ok) {
     const float4* mine = reinterpret_cast<const float4*>(bufs[rank]) + (size_t)slot * world * row4;
     for (int i = c0 + tid; i < c1; i += PEER_THREADS) {
       float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -294,7 +303,8 @@ syn_status_t tp_allreduce_sum(syn_cuda_ctx_s* ctx, float* buf, size_t count, cud
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, k_peer_allreduce, buf, n4, ps->world, ps->rank,
-                                       (float* const*)ps->d_bufs, ps->d_sync, ctx->err);
+                                       (float* const*)ps->d_bufs, ps->d_sync, ctx->err,
+                                       (float*)nullptr);
     if (e != cudaSuccess) {
       set_last_cuda_error(e, "k_peer_allreduce");
       return SYN_ERR_CUDA;
@@ -309,6 +319,29 @@ syn_status_t tp_allreduce_sum(syn_cuda_ctx_s* ctx, float* buf, size_t count, cud
 syn_status_t tp_allgather(syn_cuda_ctx_s* ctx, const float* send, float* recv, size_t count,
                           cudaStream_t st) {
   if (!ctx->nccl) return SYN_ERR_INVALID_ARG;
+  auto* ps = static_cast<PeerState*>(ctx->tp_peer);
+  if (ps && count <= PEER_CAP && count % 4 == 0 && (reinterpret_cast<uintptr_t>(send) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(recv) & 15) == 0) {
+    const int n4 = (int)(count / 4);
+    const int ctas = std::max(1, std::min(PEER_CTAS, (n4 + PEER_THREADS - 1) / PEER_THREADS));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(PEER_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_peer_allreduce, const_cast<float*>(send), n4,
+                                       ps->world, ps->rank, (float* const*)ps->d_bufs,
+                                       ps->d_sync, ctx->err, recv);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e, "k_peer_allreduce(gather)");
+      return SYN_ERR_CUDA;
+    }
+    return SYN_OK;
+  }
   return nccl_status(nccl().all_gather(send, recv, count, ncclFloat32,
                                        static_cast<ncclComm_t>(ctx->nccl), st),
                      "ncclAllGather");
