@@ -225,6 +225,8 @@ struct AttnParams {
   // k_norm_rope_append: RoPE at the cache slot (len + t) instead of the
   // reference prefill's offset t (attention.rs:171-190)
   int rope_at_slot;
+  // k_attn_decode: K / V rows staged in shared memory (set by the launch)
+  int krows, vrows;
   float* out;          // [rows][n_heads*hd]
   long long ldo;
   float scale;
@@ -304,26 +306,78 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return m;
 }
 
-// ---------------------------------------------------------------------------
-// Decode: one CTA of DEC_THREADS per (sequence, query head):
-// cached_attention_decode (ops/attention.rs:24-147). Every CTA of a KV group
-// normalises and rotates the new K itself (same bits), the group's first
-// CTA appends K and V to the cache, and the new position is read from smem,
-// so no CTA waits for another.
-// ---------------------------------------------------------------------------
 constexpr int DEC_THREADS = 128;
-constexpr int DEC_CH = 64;  // V rows staged per chunk
+constexpr int DEC_KR = DEC_THREADS;  // K rows staged (one per thread)
+constexpr int DEC_VMAX = 256;        // V rows staged per pass
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Copies cached rows [ra, rb) (positions off + r) of one KV head into
+// staged rows r * VS, 16 bytes per copy, all threads.
+template <int HD>
+__device__ __forceinline__ void stage_rows_async(float* dst, const float* cb, const AttnParams& p,
+                                                 int sq, int off, int ra, int rb, int kvd) {
+  constexpr int Q4 = HD / 4, VS = HD + 4;
+  for (int t = threadIdx.x + ra * Q4; t < rb * Q4; t += DEC_THREADS) {
+    const int r = t / Q4, c4 = t - r * Q4;
+    cp_async16(dst + r * VS + 4 * c4, cb + kv_slot(p, sq, off + r) * kvd + 4 * c4);
+  }
+}
+
+// acc = q . k in element order, each product rounded then added, or fused
+// (the reference's @mulAdd), as chain() does
+template <int HD>
+__device__ __forceinline__ float dot_in_order(const float* q, const float* k, bool fused) {
+  const float4* q4 = reinterpret_cast<const float4*>(q);
+  const float4* k4 = reinterpret_cast<const float4*>(k);
+  float acc = 0.0f;
+  if (fused) {
+#pragma unroll 4
+    for (int c = 0; c < HD / 4; c++) {
+      const float4 a = q4[c], b = k4[c];
+      acc = __fmaf_rn(a.x, b.x, acc);
+      acc = __fmaf_rn(a.y, b.y, acc);
+      acc = __fmaf_rn(a.z, b.z, acc);
+      acc = __fmaf_rn(a.w, b.w, acc);
+    }
+  } else {
+#pragma unroll 4
+    for (int c = 0; c < HD / 4; c++) {
+      const float4 a = q4[c], b = k4[c];
+      acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+      acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+      acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+      acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+    }
+  }
+  return acc;
+}
+
+// Decode: one CTA of DEC_THREADS per (row, query head):
+// cached_attention_decode (ops/attention.rs:24-147), in its order. Every CTA
+// of a KV group normalises and rotates the new K itself (same bits), the
+// group's first CTA appends K and V to the cache, and the new position is
+// read from shared memory, so no CTA waits for another. The first DEC_KR K
+// rows and the first p.vrows V rows of the context are copied into shared
+// memory with cp.async before griddepcontrol.wait (they were written by
+// earlier steps), so their latency overlaps the preceding QKV matmul and no
+// row lives in registers.
 template <int HD>
 __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p) {
   extern __shared__ __align__(16) float sm[];
-  constexpr int Q4 = HD / 4;
-  constexpr int VS = HD + 4;             // staged row stride
-  constexpr int PER = (DEC_CH * Q4 + DEC_THREADS - 1) / DEC_THREADS;  // V float4 per thread
+  constexpr int VS = HD + 4;             // staged row stride (conflict-free float4 rows)
+  const int KR = p.krows, VR = p.vrows;  // staged K / V rows (<= the longest context)
   float* xs = sm;                        // q (HD) then k (HD), then v (HD)
   float* cs = xs + 3 * HD;               // RoPE cos (HD/2) then sin (HD/2) at pos
-  float* vb = cs + HD;                   // DEC_CH staged V rows
-  float* lanes = vb + DEC_CH * VS;       // 8
+  float* kst = cs + HD;                  // KR staged K rows
+  float* vst = kst + KR * VS;            // VR staged V rows
+  float* lanes = vst + VR * VS;          // 8
   float* scl = lanes + 8;                // 2 (+2 pad)
   float* red = scl + 4;                  // DEC_THREADS / 32
   float* sc = red + DEC_THREADS / 32;    // scores, eff
@@ -331,10 +385,9 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   const int G = p.n_heads / p.n_kv, kvh = h / G, kvd = p.n_kv * HD;
   // Before griddepcontrol.wait only data written two or more kernels back is
   // read: the committed length (argmax of the previous step), the cached
-  // rows below it (previous steps' attention) and the RoPE tables. Their
-  // loads overlap the tail of the Q/K/V matmul. Span mode: rows from len0 on
-  // were appended by the kernel before, so only rows below len0 are read
-  // early.
+  // rows below it (previous steps' attention) and the RoPE tables. Span
+  // mode: rows from len0 on were appended by the kernel before, so only rows
+  // below len0 are read early.
   const int sq = p.span ? p.seq0 : p.slots ? p.slots[b] : b;  // this row's sequence
   const int len0 = p.len[sq];
   const int pos = p.span ? len0 + b : len0;
@@ -349,44 +402,23 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
   const int L = pos + 1;
   const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
   const int eff = L - off;
+  const bool fresh = !p.span;  // the new row's K/V come from q/k/v, not the cache
   for (int i = tid; i < HD / 2; i += DEC_THREADS) {
     cs[i] = p.cos_t[(size_t)pos * (HD / 2) + i];
     cs[HD / 2 + i] = p.sin_t[(size_t)pos * (HD / 2) + i];
   }
-  float4 kv[Q4];  // K row of position `tid` (first pass of the score loop)
-  const bool kpre = tid < eff && off + tid < early;
-  if (kpre) {
-#pragma unroll
-    for (int c = 0; c < Q4; c++)
-      kv[c] = reinterpret_cast<const float4*>(kcb + kv_slot(p, sq, off + tid) * kvd)[c];
-  }
-  const int cn0 = min(DEC_CH, eff);
-  {  // first V chunk (the new position is filled in after its RoPE/append)
-    float4 tmp[PER];
-#pragma unroll
-    for (int u = 0; u < PER; u++) {
-      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < cn0 && off + r < early)
-        tmp[u] = reinterpret_cast<const float4*>(vcb + kv_slot(p, sq, off + r) * kvd)[c4];
-    }
-#pragma unroll
-    for (int u = 0; u < PER; u++) {
-      const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-      if (r < cn0 && off + r < early) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
-    }
-  }
+  const int kn = min(KR, eff), vn = min(VR, eff);
+  const int pre = max(0, min(early - off, eff));  // staged rows available before the wait
+  stage_rows_async<HD>(kst, kcb, p, sq, off, 0, min(kn, pre), kvd);
+  stage_rows_async<HD>(vst, vcb, p, sq, off, 0, min(vn, pre), kvd);
   griddep_wait();
   const float* qrow = p.q + (long long)b * p.ld + (long long)h * HD;
   const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
   const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
-  if (p.span) {  // q is ready; this step's K/V rows are in the cache
+  if (!fresh) {  // q is ready; this step's K/V rows are in the cache
     for (int i = tid; i < HD; i += DEC_THREADS) xs[i] = qrow[i];
-    for (int t = tid; t < cn0 * Q4; t += DEC_THREADS) {
-      const int r = t / Q4, c4 = t - r * Q4;
-      if (off + r >= early)
-        reinterpret_cast<float4*>(vb + r * VS)[c4] =
-            reinterpret_cast<const float4*>(vcb + kv_slot(p, sq, off + r) * kvd)[c4];
-    }
+    stage_rows_async<HD>(kst, kcb, p, sq, off, min(kn, pre), kn, kvd);
+    stage_rows_async<HD>(vst, vcb, p, sq, off, min(vn, pre), vn, kvd);
     __syncthreads();
   } else {
     for (int i = tid; i < HD; i += DEC_THREADS) {
@@ -401,32 +433,25 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
         kcb[kv_slot(p, sq, pos) * kvd + i] = xs[HD + i];
         vcb[kv_slot(p, sq, pos) * kvd + i] = xs[2 * HD + i];
       }
-    if (pos - off < cn0)  // the new V row in the first chunk
-      for (int i = tid; i < HD; i += DEC_THREADS) vb[(pos - off) * VS + i] = xs[2 * HD + i];
+    // the new row into the staged rows (it is the last of the context)
+    const int r = pos - off;
+    for (int i = tid; i < HD; i += DEC_THREADS) {
+      if (r < kn) kst[r * VS + i] = xs[HD + i];
+      if (r < vn) vst[r * VS + i] = xs[2 * HD + i];
+    }
   }
+  cp_async_wait_all();
+  __syncthreads();
 
   // scores: below 64 positions the reference's scalar loop (sum += a*b);
-  // from 64 on matmul_t (@mulAdd except the last eff%8 columns). Each thread
-  // holds one K row in registers (all loads in flight at once).
+  // from 64 on matmul_t (@mulAdd except the last eff%8 columns)
   const int s_full = eff < 64 ? 0 : eff - (eff & 7);
   for (int s = tid; s < eff; s += DEC_THREADS) {
     const int row = off + s;
-    if (!(s == tid && kpre)) {
-      const float* kr = row == pos && !p.span ? xs + HD : kcb + kv_slot(p, sq, row) * kvd;
-#pragma unroll
-      for (int c = 0; c < Q4; c++) kv[c] = reinterpret_cast<const float4*>(kr)[c];
-    }
-    const bool fused = s < s_full;
-    float acc = 0.0f;
-#pragma unroll
-    for (int c = 0; c < Q4; c++) {
-      const float4 q = reinterpret_cast<const float4*>(xs)[c];
-      acc = chain(fused, q.x, kv[c].x, acc);
-      acc = chain(fused, q.y, kv[c].y, acc);
-      acc = chain(fused, q.z, kv[c].z, acc);
-      acc = chain(fused, q.w, kv[c].w, acc);
-    }
-    sc[s] = __fmul_rn(acc, p.scale);
+    const float* kr = s < kn                   ? kst + s * VS
+                      : (row == pos && fresh) ? xs + HD
+                                              : kcb + kv_slot(p, sq, row) * kvd;
+    sc[s] = __fmul_rn(dot_in_order<HD>(xs, kr, s < s_full), p.scale);
   }
   __syncthreads();
   // softmax_slice (ops/activation.rs:117-130)
@@ -442,31 +467,21 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
     for (int s = tid; s < eff; s += DEC_THREADS) sc[s] = __fdiv_rn(sc[s], sum);
   griddep_launch();
   // score * V: below 64 positions sum += p*v; from 64 on matmul_nn
-  // (@mulAdd except the last hd%32 columns). V rows staged DEC_CH at a time
-  // (the first chunk was staged before the wait).
+  // (@mulAdd except the last hd%32 columns). Rows past the staged ones pass
+  // through the same buffer VR at a time.
   const bool vfused = eff >= 64 && tid < HD - (HD & 31);
   float acc = 0.0f;
-  for (int c0 = 0; c0 < eff; c0 += DEC_CH) {
-    const int cn = min(DEC_CH, eff - c0);
-    __syncthreads();  // previous chunk consumed (and sc final on the first pass)
+  for (int c0 = 0; c0 < eff; c0 += VR) {
+    const int cn = min(VR, eff - c0);
     if (c0 > 0) {
-      float4 tmp[PER];
-#pragma unroll
-      for (int u = 0; u < PER; u++) {
-        const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-        if (r < cn) {
-          const int row = off + c0 + r;
-          tmp[u] = row == pos && !p.span
-                       ? reinterpret_cast<const float4*>(xs + 2 * HD)[c4]
-                       : reinterpret_cast<const float4*>(vcb + kv_slot(p, sq, row) * kvd)[c4];
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < PER; u++) {
-        const int t = tid + u * DEC_THREADS, r = t / Q4, c4 = t - r * Q4;
-        if (r < cn) reinterpret_cast<float4*>(vb + r * VS)[c4] = tmp[u];
-      }
+      __syncthreads();  // the previous rows are consumed (and sc is final)
+      stage_rows_async<HD>(vst, vcb, p, sq, off + c0, 0, cn, kvd);
+      cp_async_wait_all();
       __syncthreads();
+      if (fresh && pos - off - c0 < cn) {  // the new row was not in the cache when staged
+        for (int i = tid; i < HD; i += DEC_THREADS) vst[(pos - off - c0) * VS + i] = xs[2 * HD + i];
+        __syncthreads();
+      }
     }
     if (tid < HD) {
       const float* pr = sc + c0;
@@ -476,19 +491,33 @@ __global__ void __launch_bounds__(DEC_THREADS) k_attn_decode(const AttnParams p)
 #pragma unroll
         for (int u = 0; u < 8; u++) {
           pv[u] = pr[s + u];
-          vv[u] = vb[(s + u) * VS + tid];
+          vv[u] = vst[(s + u) * VS + tid];
         }
 #pragma unroll
         for (int u = 0; u < 8; u++) acc = chain(vfused, pv[u], vv[u], acc);
       }
-      for (; s < cn; s++) acc = chain(vfused, pr[s], vb[s * VS + tid], acc);
+      for (; s < cn; s++) acc = chain(vfused, pr[s], vst[s * VS + tid], acc);
     }
   }
   if (tid < HD) p.out[(long long)b * p.ldo + (long long)h * HD + tid] = acc;
 }
 
+// Staged rows of k_attn_decode for contexts up to `eff` positions.
+void decode_stage_rows(int hd, int eff, int* kr, int* vr) {
+  *kr = std::min(eff, DEC_KR);
+  int v = std::min(eff, DEC_VMAX);
+  auto bytes = [&](int vv) {
+    return ((size_t)4 * hd + (size_t)(*kr + vv) * (hd + 4) + 8 + 4 + DEC_THREADS / 32 + eff) *
+           sizeof(float);
+  };
+  while (v > 8 && bytes(v) > kMaxSmem) v /= 2;
+  *vr = v;
+}
+
 size_t decode_smem_floats(int hd, int eff) {
-  return (size_t)4 * hd + (size_t)DEC_CH * (hd + 4) + 8 + 4 + DEC_THREADS / 32 + eff;
+  int kr, vr;
+  decode_stage_rows(hd, eff, &kr, &vr);
+  return (size_t)4 * hd + (size_t)(kr + vr) * (hd + 4) + 8 + 4 + DEC_THREADS / 32 + eff;
 }
 
 // ---------------------------------------------------------------------------
@@ -888,6 +917,275 @@ __global__ void __launch_bounds__(FD_THREADS) k_attn_decode_split(const AttnPara
     p.out[(long long)b * p.ldo + (long long)h * HD + tid] = o / lsum;
   }
   if (tid == 0) cnt[b * p.n_heads + h] = 0;  // ready for the next launch
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention for the block-format models, grouped by KV head: one CTA
+// per (row, KV head, split) serves the G query heads that share the KV head,
+// so each cached K/V row crosses HBM once per step (the per-query-head
+// kernel above reads it G times). The split length follows the row's actual
+// context, ceil(eff / nsplit) rounded up to the warp step, so a graph
+// captured for max_seq keeps every split busy at whatever length it replays.
+// A warp takes GQ_RB consecutive rows per step, with the next step's rows in
+// flight: lane l holds elements [E*l, E*l + E) of a row (512 coalesced bytes
+// for HD 128), the q.k partials are summed across the warp by butterfly
+// shuffles, and each head keeps a running max, sum and output slice in
+// registers (online softmax). The four warps merge in shared memory into one
+// partial (max, sum, o[HD]) per head and split; the last CTA of the (row, KV
+// head) merges the splits. q and the new row's k are normalised and rotated
+// by norm_rope, the same bits as the other kernels, and the CTA whose range
+// holds the new position appends its K and V.
+// ---------------------------------------------------------------------------
+constexpr int GQ_THREADS = 128, GQ_WARPS = 4, GQ_RB = 4;
+
+template <int HD> struct GqVec;
+template <> struct GqVec<64> {
+  using T = float2;
+  __device__ static float at(const float2& v, int e) { return e == 0 ? v.x : v.y; }
+};
+template <> struct GqVec<128> {
+  using T = float4;
+  __device__ static float at(const float4& v, int e) {
+    return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+  }
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(GQ_THREADS) k_attn_decode_gqa(const AttnParams p, float* part,
+                                                                int* cnt, int nsplit) {
+  constexpr int E = HD / 32;
+  using VT = GqVec<HD>;
+  using V = typename VT::T;
+  __shared__ __align__(16) float xs[(G + 2) * HD];  // q heads, then k and v of the new row
+  __shared__ float lanes[4 * (G + 1)], scl[G + 1], red[GQ_WARPS];
+  __shared__ float wst[GQ_WARPS][G][2];              // per-warp (max, sum)
+  __shared__ __align__(16) float wo[GQ_WARPS][G][HD];  // per-warp output slices
+  __shared__ int last;
+  const int b = blockIdx.x, kvh = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int kvd = p.n_kv * HD;
+  // Before griddepcontrol.wait only data written two or more kernels back is
+  // read: the committed length and the cached rows below it.
+  const int sq = p.span ? p.seq0 : p.slots ? p.slots[b] : b;
+  const int len0 = p.len[sq];
+  const int pos = p.span ? len0 + b : len0;
+  const int early = p.span ? len0 : pos;  // rows [0, early) may be read before the wait
+  if (pos >= p.max_seq) {  // cache full: nothing is written (the host reports it)
+    griddep_wait();
+    if (tid == 0 && p.err) atomicExch(p.err, SYN_ERR_INVALID_ARG);
+    return;
+  }
+  const int L = pos + 1;
+  const int off = (p.window > 0 && L > p.window) ? L - p.window : 0;
+  const int eff = L - off;
+  int sl = (eff + nsplit - 1) / nsplit;
+  sl = (sl + GQ_RB - 1) / GQ_RB * GQ_RB;
+  const int r0 = off + min(eff, sp * sl), r1 = off + min(eff, (sp + 1) * sl);
+  const float* kcb = p.kc + kvh * HD;
+  const float* vcb = p.vc + kvh * HD;
+  const bool fresh = !p.span;  // the new row's K/V come from q/k/v, not the cache
+  const V zero = {};
+
+  V kr[GQ_RB], vr[GQ_RB];
+  const int rb0 = r0 + warp * GQ_RB;
+#pragma unroll
+  for (int j = 0; j < GQ_RB; j++) {
+    kr[j] = zero;
+    vr[j] = zero;
+    const int row = rb0 + j;
+    if (row < r1 && row < early) {
+      const size_t s = kv_slot(p, sq, row) * kvd;
+      kr[j] = reinterpret_cast<const V*>(kcb + s)[lane];
+      vr[j] = reinterpret_cast<const V*>(vcb + s)[lane];
+    }
+  }
+  griddep_wait();
+  const bool has_new = fresh && pos >= r0 && pos < r1;
+  {
+    const float* qrow = p.q + (long long)b * p.ld + (long long)kvh * G * HD;
+    for (int i = tid; i < G * HD; i += GQ_THREADS) xs[i] = qrow[i];
+    if (has_new) {
+      const float* krow = p.k + (long long)b * p.ld + (long long)kvh * HD;
+      const float* vrow = p.v + (long long)b * p.ld + (long long)kvh * HD;
+      for (int i = tid; i < HD; i += GQ_THREADS) {
+        xs[G * HD + i] = krow[i];
+        xs[(G + 1) * HD + i] = vrow[i];
+      }
+    }
+    __syncthreads();
+    if (fresh)
+      norm_rope(xs, has_new ? G + 1 : G, HD, p.qn, p.kn, G, p.eps, p.cos_t, p.sin_t, pos, lanes,
+                scl, GQ_THREADS);
+    if (has_new) {
+      const size_t s = kv_slot(p, sq, pos) * kvd;
+      for (int i = tid; i < HD; i += GQ_THREADS) {
+        p.kc[s + kvh * HD + i] = xs[G * HD + i];
+        p.vc[s + kvh * HD + i] = xs[(G + 1) * HD + i];
+      }
+    }
+  }
+  float q[G][E];
+#pragma unroll
+  for (int g = 0; g < G; g++)
+#pragma unroll
+    for (int e = 0; e < E; e++) q[g][e] = xs[g * HD + lane * E + e];
+  if (!fresh) {  // span: rows from len0 on were appended by the preceding kernel
+#pragma unroll
+    for (int j = 0; j < GQ_RB; j++) {
+      const int row = rb0 + j;
+      if (row < r1 && row >= early) {
+        const size_t s = kv_slot(p, sq, row) * kvd;
+        kr[j] = reinterpret_cast<const V*>(kcb + s)[lane];
+        vr[j] = reinterpret_cast<const V*>(vcb + s)[lane];
+      }
+    }
+  }
+
+  float m[G], l[G], o[G][E];
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    m[g] = -INFINITY;
+    l[g] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; e++) o[g][e] = 0.0f;
+  }
+  constexpr int STEP = GQ_WARPS * GQ_RB;
+  for (int rb = rb0; rb < r1; rb += STEP) {
+    if (has_new) {
+#pragma unroll
+      for (int j = 0; j < GQ_RB; j++)
+        if (rb + j == pos) {
+          kr[j] = reinterpret_cast<const V*>(xs + G * HD)[lane];
+          vr[j] = reinterpret_cast<const V*>(xs + (G + 1) * HD)[lane];
+        }
+    }
+    V kn[GQ_RB], vn[GQ_RB];  // the next step's rows, in flight meanwhile
+#pragma unroll
+    for (int j = 0; j < GQ_RB; j++) {
+      kn[j] = zero;
+      vn[j] = zero;
+      const int row = rb + STEP + j;
+      if (row < r1 && !(fresh && row == pos)) {
+        const size_t s = kv_slot(p, sq, row) * kvd;
+        kn[j] = reinterpret_cast<const V*>(kcb + s)[lane];
+        vn[j] = reinterpret_cast<const V*>(vcb + s)[lane];
+      }
+    }
+    float s[G][GQ_RB];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+      for (int j = 0; j < GQ_RB; j++) {
+        float a = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++) a = fmaf(q[g][e], VT::at(kr[j], e), a);
+        s[g][j] = a;
+      }
+#pragma unroll
+    for (int x = 16; x; x >>= 1)
+#pragma unroll
+      for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int j = 0; j < GQ_RB; j++) s[g][j] += __shfl_xor_sync(0xffffffffu, s[g][j], x);
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      float mx = m[g];
+#pragma unroll
+      for (int j = 0; j < GQ_RB; j++) {
+        s[g][j] = rb + j < r1 ? s[g][j] * p.scale : -INFINITY;
+        mx = fmaxf(mx, s[g][j]);
+      }
+      const float corr = m[g] == -INFINITY ? 0.0f : expf(m[g] - mx);
+      l[g] *= corr;
+#pragma unroll
+      for (int e = 0; e < E; e++) o[g][e] *= corr;
+#pragma unroll
+      for (int j = 0; j < GQ_RB; j++) {
+        const float pj = s[g][j] == -INFINITY ? 0.0f : expf(s[g][j] - mx);
+        l[g] += pj;
+#pragma unroll
+        for (int e = 0; e < E; e++) o[g][e] = fmaf(pj, VT::at(vr[j], e), o[g][e]);
+      }
+      m[g] = mx;
+    }
+#pragma unroll
+    for (int j = 0; j < GQ_RB; j++) {
+      kr[j] = kn[j];
+      vr[j] = vn[j];
+    }
+  }
+
+  // merge the warps: one partial per head of this split
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    if (lane == 0) {
+      wst[warp][g][0] = m[g];
+      wst[warp][g][1] = l[g];
+    }
+#pragma unroll
+    for (int e = 0; e < E; e++) wo[warp][g][lane * E + e] = o[g][e];
+  }
+  __syncthreads();
+  const size_t hstride = (size_t)nsplit * (HD + 2);  // one head's partials
+  float* hbase = part + ((size_t)b * p.n_heads + (size_t)kvh * G) * hstride;
+  for (int i = tid; i < G * HD; i += GQ_THREADS) {
+    const int g = i / HD, d = i - g * HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < GQ_WARPS; w++) M = fmaxf(M, wst[w][g][0]);
+    float O = 0.0f, Ls = 0.0f;
+#pragma unroll
+    for (int w = 0; w < GQ_WARPS; w++) {
+      const float f = wst[w][g][0] == -INFINITY ? 0.0f : expf(wst[w][g][0] - M);
+      O = fmaf(f, wo[w][g][d], O);
+      Ls = fmaf(f, wst[w][g][1], Ls);
+    }
+    float* dst = hbase + g * hstride + (size_t)sp * (HD + 2);
+    dst[2 + d] = O;
+    if (d == 0) {
+      dst[0] = M;
+      dst[1] = Ls;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  int* cn = &cnt[b * p.n_heads + kvh * G];
+  if (tid == 0) last = atomicAdd(cn, 1) == nsplit - 1;
+  __syncthreads();
+  griddep_launch();
+  if (!last) return;
+  __threadfence();
+  // merge the splits of each head (as k_attn_decode_split's last CTA)
+  float* fac = &wo[0][0][0];  // nsplit <= GQ_WARPS * G * HD factors
+  for (int g = 0; g < G; g++) {
+    const float* base = hbase + g * hstride;
+    float M = -INFINITY;
+    for (int c = tid; c < nsplit; c += GQ_THREADS) M = fmaxf(M, __ldcg(base + c * (HD + 2)));
+    M = block_max(M, red);
+    float lsum = 0.0f;
+    for (int c = tid; c < nsplit; c += GQ_THREADS) {
+      const float mc = __ldcg(base + c * (HD + 2));
+      const float f = mc == -INFINITY ? 0.0f : expf(mc - M);
+      fac[c] = f;
+      lsum += f * __ldcg(base + c * (HD + 2) + 1);
+    }
+    lsum = block_sum(lsum, red);  // (its barriers also publish fac)
+    if (tid < HD) {
+      float ov = 0.0f;
+      int c = 0;
+      for (; c + 8 <= nsplit; c += 8) {
+        float t[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) t[u] = __ldcg(base + (c + u) * (HD + 2) + 2 + tid);
+#pragma unroll
+        for (int u = 0; u < 8; u++) ov = fmaf(t[u], fac[c + u], ov);
+      }
+      for (; c < nsplit; c++) ov = fmaf(__ldcg(base + c * (HD + 2) + 2 + tid), fac[c], ov);
+      p.out[(long long)b * p.ldo + (long long)(kvh * G + g) * HD + tid] = ov / lsum;
+    }
+    __syncthreads();  // fac is rewritten for the next head
+  }
+  if (tid == 0) *cn = 0;  // ready for the next launch
 }
 
 size_t flash_decode_smem(int hd) {
@@ -1547,10 +1845,44 @@ syn_status_t make_params(const AttnArgs& a, AttnParams& p, int seq0, int ntok) {
 
 }  // namespace
 
+template <int HD>
+void* gqa_kernel(int g) {
+  switch (g) {
+    case 1: return (void*)k_attn_decode_gqa<HD, 1>;
+    case 2: return (void*)k_attn_decode_gqa<HD, 2>;
+    case 4: return (void*)k_attn_decode_gqa<HD, 4>;
+    case 8: return (void*)k_attn_decode_gqa<HD, 8>;
+  }
+  return nullptr;
+}
+
 syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t batch, size_t eff,
                                  cudaStream_t st) {
   syn_cuda_kvcache_t* c = a.cache;
-  const int nsplit = (int)((eff + FD_CH - 1) / FD_CH);
+  // KV-head-grouped kernel for head dims 64/128 and 1, 2, 4 or 8 query heads
+  // per KV head (SYN_ATTN_GQA=0: the per-query-head kernel). Splits: about
+  // four CTAs per SM over all (row, KV head) pairs, at most one per 32
+  // positions of the longest context the launch may see.
+  const int G = p.n_heads / p.n_kv;
+  void* gqa = nullptr;
+  static const bool gqa_on = [] {
+    const char* e = getenv("SYN_ATTN_GQA");
+    return !(e && e[0] == '0');
+  }();
+  if (gqa_on) gqa = p.hd == 128 ? gqa_kernel<128>(G) : p.hd == 64 ? gqa_kernel<64>(G) : nullptr;
+  int nsplit;
+  if (gqa) {
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long pairs = (long long)batch * p.n_kv;
+    const long long want = (4LL * sms + pairs - 1) / pairs;
+    const long long cap = std::min<long long>(256, ((long long)eff + 31) / 32);
+    nsplit = (int)std::max<long long>(1, std::min(want, cap));
+  } else {
+    nsplit = (int)((eff + FD_CH - 1) / FD_CH);
+  }
   if (nsplit > 32 * (p.hd + 4)) return SYN_ERR_UNSUPPORTED;  // combine factors fit in smem
   // arrival counters first, sized for every sequence slot, so that their
   // place does not move with the batch of a call (they must stay zero
@@ -1574,6 +1906,13 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
   }
   int* cnt = reinterpret_cast<int*>(c->part);
   float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c->part) + cbytes);
+  if (gqa) {
+    using K = void (*)(const AttnParams, float*, int*, int);
+    return cuda_status(launch_pdl(reinterpret_cast<K>(gqa),
+                                  dim3((unsigned)batch, (unsigned)p.n_kv, (unsigned)nsplit),
+                                  dim3(GQ_THREADS), 0, st, p, part, cnt, nsplit),
+                       "k_attn_decode_gqa");
+  }
   void (*split)(const AttnParams, float*, int*, int) = nullptr;
   switch (p.hd) {
     case 32: split = k_attn_decode_split<32>; break;
@@ -1637,6 +1976,7 @@ syn_status_t launch_decode_p(const AttnArgs& a, AttnParams& p, size_t batch, cud
   if (a.flash) return launch_decode_flash(a, p, batch, eff, st);
   const size_t smem = decode_smem_floats(p.hd, (int)eff) * sizeof(float);
   if (smem > kMaxSmem) return SYN_ERR_UNSUPPORTED;
+  decode_stage_rows(p.hd, (int)eff, &p.krows, &p.vrows);
   void (*kern)(const AttnParams) = nullptr;
   switch (p.hd) {
     case 32: kern = k_attn_decode<32>; break;

@@ -98,12 +98,14 @@ def _oracle_head_norm_rope(x, w, heads, hd, eps, cos, sin, pos):
 
 
 @pytest.mark.parametrize("hq,hkv,hd", [(4, 2, 32), (8, 2, 64), (16, 8, 128), (32, 8, 128)])
-@pytest.mark.parametrize("lengths", [(1, 5), (63, 64), (65, 130)])
+@pytest.mark.parametrize("lengths", [(1, 5), (63, 64), (65, 130), (257, 600)])
 @pytest.mark.parametrize("window,norm", [(0, True), (24, False)])
 @pytest.mark.parametrize("flash", [False, True])
 def test_attention_decode_bit_exact(ctx, hq, hkv, hd, lengths, window, norm, flash):
+    # contexts past 128 / 256 rows take the exact kernel's unstaged K rows and
+    # its second V pass
     rng = np.random.default_rng(hq * 1000 + hd + lengths[0] + window)
-    max_seq, B = 160, 2
+    max_seq, B = max(160, max(lengths) + 8), 2
     qd, kvd = hq * hd, hkv * hd
     eps = 1e-6
     cache = sb.KVCache(ctx, max_seq, hkv, hd, 1, batch=B)
