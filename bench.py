@@ -543,6 +543,74 @@ def run_configs(local_rank, cpu_leg=False):
     return out
 
 
+def run_config2_batched(local_rank, reps=5):
+    """Config 2 at M = 16, 128 and 512: every (format, N, K) of the decode
+    sweep as a batched matmul through the public QuantizedWeight.matmul (the
+    tcgen05 GEMMs; M = 16 may take the GEMV). Per (format, M): the 15 shapes
+    back to back, `reps` timed passes with the L2 flushed between passes
+    (CUDA events around the matmuls only). M = 16 is reported against HBM
+    (weight bytes), M = 128 / 512 against the tensor pipe (INT8 kind::i8
+    against twice the measured bf16 peak, the nominal dense int8 rate)."""
+    import torch
+    import synapse_b200 as sb
+    from synapse_b200 import synth
+    ctx = sb.Context(local_rank)
+    rng = np.random.default_rng(4321)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    out = {}
+    hbm_peak, _ = peaks()
+    for fmt in synth.FORMATS:
+        ws = []
+        for n in synth.SWEEP_N:
+            for k in synth.SWEEP_K:
+                data, scales = synth.gen_weight(fmt, n, k, rng)
+                ws.append((sb.QuantizedWeight(ctx, fmt, data, n, k, scales), n, k))
+        wbytes = sum(synth.format_bytes(fmt, n, k) for _, n, k in ws)
+        for m in (16, 128, 512):
+            xs = {k: torch.from_numpy(synth.gen_activations(m, k, rng)).cuda()
+                  for k in synth.SWEEP_K}
+            ys = [torch.empty(m, n, device="cuda") for _, n, _ in ws]
+
+            def run():
+                for (w, n, k), y in zip(ws, ys):
+                    w.matmul(xs[k], out=y)
+            for _ in range(2):
+                run()
+            torch.cuda.synchronize()
+            ms = 0.0
+            for _ in range(reps):
+                flush.fill_(1)
+                e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+                e0.record()
+                run()
+                e1.record()
+                torch.cuda.synchronize()
+                ms += e0.elapsed_time(e1)
+            sec = ms / 1e3 / reps
+            flops = sum(2.0 * m * n * k for _, n, k in ws)
+            entry = {"us_per_pass": round(sec * 1e6, 1), "shapes": len(ws),
+                     "tflops": round(flops / sec / 1e12, 1)}
+            if m == 16:
+                entry["roofline"] = roof_hbm(wbytes / sec, wbytes)
+            else:
+                r = roof_tensor(flops / sec)
+                if fmt == sb.QFormat.INT8_KN:
+                    r["peak"] = round(2 * r["peak"], 1)
+                    r["frac"] = round(r["achieved"] / r["peak"], 4)
+                    r["unit"] = "TOP/s"
+                    r["peak_source"] = "2x the measured bf16 dense peak (nominal dense int8 rate)"
+                entry["roofline"] = r
+            out[f"{fmt.name}:M{m}"] = entry
+            del xs, ys
+        for w, _, _ in ws:
+            w.close()
+    del flush
+    ctx.close()
+    return {"workload": "config 2: 5 formats x N{1024,3072,4096,11008,14336} x K{1024,2048,4096} "
+                        "at M 16/128/512, one pass = the 15 shapes of a format",
+            "l2": "flushed (256 MB write) between timed passes", "per_format_m": out}
+
+
 def run_gemm_case(args):
     """--gemm FMT:M:N:K: times one prefill matmul (tcgen05 GEMM) on cuda:0 and
     prints its TFLOP/s (profiling aid; not the benchmark line)."""
@@ -579,6 +647,15 @@ def run_decode_only(args, local_rank):
     torch.cuda.set_device(local_rank)
     out = run_decode(args, local_rank, None, cpu_leg=False)
     print(json.dumps({"decode": out}), flush=True)
+
+
+def run_tp_decode_only(args, local_rank):
+    """The config-4 decode leg alone on one GPU (TP1): the command its
+    launch list is taken from."""
+    import torch
+    torch.cuda.set_device(local_rank)
+    out = run_tp_decode(args, 0, 1, local_rank, None)
+    print(json.dumps({"tp_decode": out}), flush=True)
 
 
 def run_synapse(args, rank, world, local_rank):
@@ -727,8 +804,10 @@ def run_synapse(args, rank, world, local_rank):
                             cpu_leg=rank == 0 and world == 1 and not args.no_cpu_baseline)
         tp_decode = run_tp_decode(args, rank, world, local_rank, dist)
     configs = None
+    config2 = None
     if not args.no_decode and world == 1 and not args.no_configs:
         configs = run_configs(local_rank, cpu_leg=not args.no_cpu_baseline)
+        config2 = run_config2_batched(local_rank)
 
     if rank == 0:
         line = {
@@ -761,6 +840,7 @@ def run_synapse(args, rank, world, local_rank):
             "decode": decode,
             "tp_decode": tp_decode,
             "configs_3_5": configs,
+            "config_2_batched": config2,
             # the multi-GPU work of this path: config-4 tensor-parallel decode
             # over all N ranks (TP1 at N=1); `value` stays the sharded sweep
             "tp_decode_tok_s": tp_decode["tok_s"] if tp_decode else None,
@@ -923,6 +1003,8 @@ def main():
                     help="skip the config-3/5 decode legs (LLaMA Q4_K batch 1/8, Qwen3 Q8_0 serving)")
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the config-1 decode leg (profiling one decode step)")
+    ap.add_argument("--tp-decode-only", action="store_true",
+                    help="the config-4 (Mistral-7B shape) decode leg alone on one GPU")
     args = ap.parse_args()
     global CASE_FILTER
     CASE_FILTER = args.case
@@ -938,6 +1020,8 @@ def main():
         run_gemm_case(args)
     elif args.decode_only:
         run_decode_only(args, local_rank)
+    elif args.tp_decode_only:
+        run_tp_decode_only(args, local_rank)
     elif args.impl == "reference":
         run_reference(args, rank, world)
     else:

@@ -150,7 +150,7 @@ __device__ __forceinline__ void griddep_launch() {
 }
 
 // ----------------------------------------------------------------------------
-// mbarrier and 1-D bulk (TMA) copies global -> shared (no multicast).
+// mbarrier and 1-D bulk (TMA) copies global -> this CTA's shared memory.
 // ----------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -199,7 +199,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // ----------------------------------------------------------------------------
 // Thread-block clusters: distributed shared memory and remote mbarrier
-// arrivals (no TMA multicast).
+// arrivals (plain TMA copies only).
 // ----------------------------------------------------------------------------
 // Split cluster barrier: every thread arrives once right after set-up, and
 // waits (for all non-exited threads of the cluster) only before its first

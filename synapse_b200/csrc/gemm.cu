@@ -158,7 +158,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// 4-D tiled TMA load (no multicast) into this CTA's shared memory.
+// 4-D tiled TMA load into this CTA's own shared memory only.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1,
                                             int c2, int c3, uint64_t* bar) {
   asm volatile(

@@ -92,7 +92,8 @@ struct Stage {
   static constexpr int OFF_SC = OFF_QH + SB * QHT;
   static constexpr int OFF_D6 = OFF_SC + SB * SCT;
   static constexpr int BYTES = (OFF_D6 + (SB / 8) * D6T + 127) / 128 * 128;
-  static constexpr int NS = eight_bit(FMT) ? 3 : 4;  // ring depth
+  static constexpr int NS = 6;                                   // deepest ring
+  static constexpr int NS_WIDE = eight_bit(FMT) ? 3 : 4;         // grids of >= 1 CTA per SM
 };
 
 struct GemvParams {
@@ -1131,6 +1132,7 @@ size_t tma_smem(const Plan& pl, int fmt, int rg, int ns) {
 int tma_occupancy(int fmt, int mt, int rg, size_t smem);
 size_t stage_bytes(int fmt);
 int stage_depth(int fmt);
+int stage_depth_wide(int fmt);
 
 // xs_bytes: the fused norm's row staged in shared memory (all of K).
 Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
@@ -1188,7 +1190,16 @@ Plan make_plan(int fmt, size_t m, size_t n, size_t kp, size_t xs_bytes = 0) {
     // All CTAs resident at once: row pairs only while two CTAs still fit on
     // an SM, and a shallower ring where one more CTA per SM would otherwise
     // spill the grid into a second wave.
-    const int nsmax = stage_depth(fmt);
+    // Grids of at least one CTA per SM: 3 stages (8-bit formats) or 4. A
+    // smaller grid (the decode step's narrow matmuls) gets a ring as deep as
+    // its CTAs' stage count, up to 6, so that every stage is requested before
+    // griddepcontrol.wait instead of after the first ones are consumed.
+    const long long grid0 =
+        (long long)((pl.groups + pl.rg - 1) / pl.rg) * pl.nks * mslices;
+    const int cta_stages = (pl.kr + SB - 1) / SB;
+    int nsmax = stage_depth_wide(fmt);
+    if (grid0 < sms && cta_stages > nsmax)
+      nsmax = std::min(stage_depth(fmt), cta_stages);
     auto occ = [&](int rg, int ns) {
       return tma_occupancy(fmt, pl.mt, rg, tma_smem(pl, fmt, rg, ns));
     };
@@ -1265,6 +1276,8 @@ size_t stage_bytes(int fmt) {
   }
   return 0;
 }
+
+int stage_depth_wide(int fmt) { return eight_bit(fmt) ? Stage<F_INT8>::NS_WIDE : Stage<F_Q4_0>::NS_WIDE; }
 
 int stage_depth(int fmt) {
   switch (fmt) {

@@ -957,7 +957,7 @@ __global__ void __launch_bounds__(GQ_THREADS) k_attn_decode_gqa(const AttnParams
   using VT = GqVec<HD>;
   using V = typename VT::T;
   __shared__ __align__(16) float xs[(G + 2) * HD];  // q heads, then k and v of the new row
-  __shared__ float lanes[4 * (G + 1)], scl[G + 1], red[GQ_WARPS];
+  __shared__ float lanes[4 * (G + 1)], scl[G + 1];
   __shared__ float wst[GQ_WARPS][G][2];              // per-warp (max, sum)
   __shared__ __align__(16) float wo[GQ_WARPS][G][HD];  // per-warp output slices
   __shared__ int last;
@@ -1155,35 +1155,37 @@ __global__ void __launch_bounds__(GQ_THREADS) k_attn_decode_gqa(const AttnParams
   griddep_launch();
   if (!last) return;
   __threadfence();
-  // merge the splits of each head (as k_attn_decode_split's last CTA)
-  float* fac = &wo[0][0][0];  // nsplit <= GQ_WARPS * G * HD factors
-  for (int g = 0; g < G; g++) {
+  // merge the splits: warp w takes heads w, w + 4, ...; lanes stride over
+  // the splits for the maximum and the rescaled sums, then each lane sums
+  // its E output columns over the splits (factors in shared memory)
+  for (int g = warp; g < G; g += GQ_WARPS) {
     const float* base = hbase + g * hstride;
+    float* fac = &wo[warp][0][0];  // nsplit <= G * HD factors of this warp
     float M = -INFINITY;
-    for (int c = tid; c < nsplit; c += GQ_THREADS) M = fmaxf(M, __ldcg(base + c * (HD + 2)));
-    M = block_max(M, red);
+    for (int c = lane; c < nsplit; c += 32) M = fmaxf(M, __ldcg(base + c * (HD + 2)));
+    M = warp_max(M);
     float lsum = 0.0f;
-    for (int c = tid; c < nsplit; c += GQ_THREADS) {
+    for (int c = lane; c < nsplit; c += 32) {
       const float mc = __ldcg(base + c * (HD + 2));
       const float f = mc == -INFINITY ? 0.0f : expf(mc - M);
       fac[c] = f;
       lsum += f * __ldcg(base + c * (HD + 2) + 1);
     }
-    lsum = block_sum(lsum, red);  // (its barriers also publish fac)
-    if (tid < HD) {
-      float ov = 0.0f;
-      int c = 0;
-      for (; c + 8 <= nsplit; c += 8) {
-        float t[8];
+    lsum = warp_sum(lsum);
+    __syncwarp();
+    float ov[E];
 #pragma unroll
-        for (int u = 0; u < 8; u++) t[u] = __ldcg(base + (c + u) * (HD + 2) + 2 + tid);
+    for (int e = 0; e < E; e++) ov[e] = 0.0f;
+    for (int c = 0; c < nsplit; c++) {  // (o sits 2 floats into a record: scalar loads)
+      const float f = fac[c];
+      const float* t = base + c * (HD + 2) + 2 + lane * E;
 #pragma unroll
-        for (int u = 0; u < 8; u++) ov = fmaf(t[u], fac[c + u], ov);
-      }
-      for (; c < nsplit; c++) ov = fmaf(__ldcg(base + c * (HD + 2) + 2 + tid), fac[c], ov);
-      p.out[(long long)b * p.ldo + (long long)(kvh * G + g) * HD + tid] = ov / lsum;
+      for (int e = 0; e < E; e++) ov[e] = fmaf(__ldcg(t + e), f, ov[e]);
     }
-    __syncthreads();  // fac is rewritten for the next head
+    float* orow = p.out + (long long)b * p.ldo + (long long)(kvh * G + g) * HD + lane * E;
+#pragma unroll
+    for (int e = 0; e < E; e++) orow[e] = ov[e] / lsum;
+    __syncwarp();  // fac is rewritten for the warp's next head
   }
   if (tid == 0) *cn = 0;  // ready for the next launch
 }
@@ -1861,7 +1863,7 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
   syn_cuda_kvcache_t* c = a.cache;
   // KV-head-grouped kernel for head dims 64/128 and 1, 2, 4 or 8 query heads
   // per KV head (SYN_ATTN_GQA=0: the per-query-head kernel). Splits: about
-  // four CTAs per SM over all (row, KV head) pairs, at most one per 32
+  // four CTAs per SM over all (row, KV head) pairs, at most one per 64
   // positions of the longest context the launch may see.
   const int G = p.n_heads / p.n_kv;
   void* gqa = nullptr;
@@ -1878,7 +1880,8 @@ syn_status_t launch_decode_flash(const AttnArgs& a, const AttnParams& p, size_t 
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long long pairs = (long long)batch * p.n_kv;
     const long long want = (4LL * sms + pairs - 1) / pairs;
-    const long long cap = std::min<long long>(256, ((long long)eff + 31) / 32);
+    // (the merge keeps a warp's split factors in its G * hd output slice)
+    const long long cap = std::min<long long>(std::min(256, G * p.hd), ((long long)eff + 63) / 64);
     nsplit = (int)std::max<long long>(1, std::min(want, cap));
   } else {
     nsplit = (int)((eff + FD_CH - 1) / FD_CH);

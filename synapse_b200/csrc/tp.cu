@@ -82,8 +82,8 @@ size_t blk_bytes(int fmt) {
 }
 
 // ---------------------------------------------------------------------------
-// One-shot all-reduce over peer memory (NVLink P2P stores and loads, no
-// multicast). Every rank holds one buffer, mapped into every other rank with
+// One-shot all-reduce over peer memory (plain NVLink P2P stores and loads).
+// Every rank holds one buffer, mapped into every other rank with
 // CUDA IPC: two data slots of [world][PEER_CAP] floats (double-buffered by
 // call parity) and [world][PEER_CTAS] arrival flags. A call with epoch e:
 //   1. each CTA stores its chunk of the local partial into slot e&1, row

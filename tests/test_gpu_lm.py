@@ -141,6 +141,32 @@ def test_attention_decode_bit_exact(ctx, hq, hkv, hd, lengths, window, norm, fla
     cache.close()
 
 
+@pytest.mark.parametrize("flash", [False, True])
+def test_attention_decode_long_context(ctx, flash):
+    """4000 positions: the grouped flash kernel runs more than 32 splits per
+    (row, KV head), the exact kernel many passes of staged V rows."""
+    rng = np.random.default_rng(4000)
+    hq, hkv, hd, L = 8, 2, 128, 4000
+    max_seq, eps = L + 8, 1e-6
+    qd, kvd = hq * hd, hkv * hd
+    cache = sb.KVCache(ctx, max_seq, hkv, hd, 1, batch=1)
+    cos, sin = sb.rope_tables(1e6, max_seq, hd)
+    oc, os_ = O.rope_tables(1e6, max_seq, hd)
+    kh = rng.standard_normal((L - 1, kvd)).astype(np.float32)
+    vh = rng.standard_normal((L - 1, kvd)).astype(np.float32)
+    cache.append(0, cuda(kh), cuda(vh), seq=0)
+    cache.advance(L - 1, seq=0)
+    qkv = rng.standard_normal((1, qd + 2 * kvd)).astype(np.float32)
+    out = sb.attention_decode(cache, 0, cuda(qkv), hq, None, None, eps, cuda(cos), cuda(sin),
+                              batch=1, flash=flash).cpu().numpy()
+    q = _oracle_head_norm_rope(qkv[0, :qd], None, hq, hd, eps, oc, os_, L - 1)
+    k = _oracle_head_norm_rope(qkv[0, qd:qd + kvd], None, hkv, hd, eps, oc, os_, L - 1)
+    want = O.attention_decode(q, np.concatenate([kh, k[None]]),
+                              np.concatenate([vh, qkv[0, qd + kvd:][None]]), L, hq, hkv, hd, 0)
+    assert close(out[0], want, flash), np.abs(out[0] - want).max()
+    cache.close()
+
+
 @pytest.mark.parametrize("S", [1, 5, 16, 17, 33, 40, 70, 130])
 @pytest.mark.parametrize("hq,hkv,hd,flash", [(4, 2, 32, False), (8, 2, 128, False),
                                              (4, 2, 64, True), (8, 2, 128, True)])
