@@ -246,6 +246,17 @@ size_t argmax_scratch_bytes(size_t rows, size_t n);
 syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, int32_t* out,
                            int* len_adv, int adv, int max_len, int32_t* hist, int hist_ld,
                            void* scratch, cudaStream_t st);
+// Tensor-parallel greedy token: launch_argmax_slice writes each row's argmax
+// state over this rank's vocabulary slice (indices offset by idx_off) as 16
+// bytes into pairs[row]; after an all-gather of the pairs into [world][rows]
+// (rank = vocabulary order), launch_argmax_pairs combines them in rank order
+// into the token of one argmax over the whole row (ties: the later index;
+// the last NaN wins), with launch_argmax's length advance and history.
+syn_status_t launch_argmax_slice(const float* x, size_t ldx, size_t rows, size_t n, int idx_off,
+                                 void* pairs, void* scratch, cudaStream_t st);
+syn_status_t launch_argmax_pairs(const void* pairs, int world, size_t rows, int32_t* out,
+                                 int* len_adv, int adv, int max_len, int32_t* hist, int hist_ld,
+                                 cudaStream_t st);
 // Device lengths of the sequences slots[0, n) (device array) advanced by one.
 syn_status_t launch_kv_advance_slots(syn_cuda_kvcache_t* c, const int* slots, size_t n,
                                      cudaStream_t st);

@@ -1176,7 +1176,21 @@ __global__ void __launch_bounds__(GQ_THREADS) k_attn_decode_gqa(const AttnParams
     float ov[E];
 #pragma unroll
     for (int e = 0; e < E; e++) ov[e] = 0.0f;
-    for (int c = 0; c < nsplit; c++) {  // (o sits 2 floats into a record: scalar loads)
+    // (o sits 2 floats into a record: scalar loads), 8 splits' loads in
+    // flight at a time: each is an L2 round trip
+    int c = 0;
+    for (; c + 8 <= nsplit; c += 8) {
+      float t[8][E];
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int e = 0; e < E; e++) t[u][e] = __ldcg(base + (c + u) * (HD + 2) + 2 + lane * E + e);
+#pragma unroll
+      for (int u = 0; u < 8; u++)
+#pragma unroll
+        for (int e = 0; e < E; e++) ov[e] = fmaf(t[u][e], fac[c + u], ov[e]);
+    }
+    for (; c < nsplit; c++) {
       const float f = fac[c];
       const float* t = base + c * (HD + 2) + 2 + lane * E;
 #pragma unroll
@@ -1662,7 +1676,8 @@ __global__ void __launch_bounds__(AM_THREADS) k_argmax(const float* __restrict__
                                                        int* len_adv, int adv, int max_len,
                                                        int32_t* hist, int hist_ld,
                                                        AmState* __restrict__ part,
-                                                       int* __restrict__ cnt) {
+                                                       int* __restrict__ cnt,
+                                                       int4* __restrict__ pair_out, int idx_off) {
   __shared__ AmState ws[AM_THREADS / 32];
   __shared__ int last;
   griddep_wait();
@@ -1706,6 +1721,12 @@ __global__ void __launch_bounds__(AM_THREADS) k_argmax(const float* __restrict__
     __threadfence();
     AmState t = part[row * nct];
     for (int k = 1; k < nct; k++) t = am_combine(t, part[row * nct + k]);
+    if (pair_out) {  // a vocabulary slice: its state, with global indices
+      cnt[row] = 0;
+      pair_out[row] = make_int4(t.nan >= 0 ? t.nan + idx_off : -1, t.i >= 0 ? t.i + idx_off : -1,
+                                __float_as_int(t.v), 0);
+      return;
+    }
     const int r = t.i >= 0 ? t.i : (t.nan >= 0 ? t.nan : 0);
     out[row] = r;
     cnt[row] = 0;  // ready for the next launch
@@ -1780,8 +1801,62 @@ syn_status_t launch_argmax(const float* x, size_t ldx, size_t rows, size_t n, in
   return cuda_status(launch_pdl(k_argmax, dim3((unsigned)nct, (unsigned)rows), dim3(AM_THREADS), 0,
                                 st, x, (long long)ldx, (int)n, out, len_adv, adv, max_len, hist,
                                 hist_ld, part,
-                                cnt),
+                                cnt, static_cast<int4*>(nullptr), 0),
                      "k_argmax");
+}
+
+// Tensor-parallel greedy token: each rank's argmax state over its vocabulary
+// slice (global indices) into pairs[row] ...
+syn_status_t launch_argmax_slice(const float* x, size_t ldx, size_t rows, size_t n, int idx_off,
+                                 void* pairs, void* scratch, cudaStream_t st) {
+  if (!rows || !n) return SYN_OK;
+  const size_t nct = (n + AM_SEG - 1) / AM_SEG;
+  if (nct > 65535 || rows > AM_MAX_ROWS) return SYN_ERR_UNSUPPORTED;
+  int* cnt = static_cast<int*>(scratch);
+  AmState* part = reinterpret_cast<AmState*>(static_cast<uint8_t*>(scratch) +
+                                             AM_MAX_ROWS * sizeof(int));
+  return cuda_status(launch_pdl(k_argmax, dim3((unsigned)nct, (unsigned)rows), dim3(AM_THREADS), 0,
+                                st, x, (long long)ldx, (int)n, static_cast<int32_t*>(nullptr),
+                                static_cast<int*>(nullptr), 0, 0, static_cast<int32_t*>(nullptr),
+                                0, part, cnt, static_cast<int4*>(pairs), idx_off),
+                     "k_argmax");
+}
+
+// ... and, after the all-gather of the pairs ([world][rows], rank = vocabulary
+// order), the combine in rank order: the same token as one argmax over the
+// whole row (the later slice wins ties; the last NaN wins), then the length
+// advance and token history of k_argmax.
+__global__ void k_argmax_pairs(const int4* __restrict__ pairs, int world, int rows,
+                               int32_t* __restrict__ out, int* len_adv, int adv, int max_len,
+                               int32_t* hist, int hist_ld) {
+  griddep_wait();
+  griddep_launch();
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  AmState t{-1, -1, 0.0f};
+  for (int r = 0; r < world; r++) {
+    const int4 q = pairs[(size_t)r * rows + row];
+    t = am_combine(t, AmState{q.x, q.y, __int_as_float(q.z)});
+  }
+  const int tok = t.i >= 0 ? t.i : (t.nan >= 0 ? t.nan : 0);
+  out[row] = tok;
+  if (len_adv) {
+    int nl = len_adv[row] + adv;
+    nl = nl <= max_len ? nl : max_len;
+    len_adv[row] = nl;
+    if (hist) hist[(size_t)row * hist_ld + nl] = tok;
+  }
+}
+
+syn_status_t launch_argmax_pairs(const void* pairs, int world, size_t rows, int32_t* out,
+                                 int* len_adv, int adv, int max_len, int32_t* hist, int hist_ld,
+                                 cudaStream_t st) {
+  if (!rows) return SYN_OK;
+  const unsigned blocks = (unsigned)((rows + 127) / 128);
+  return cuda_status(launch_pdl(k_argmax_pairs, dim3(blocks), dim3(128), 0, st,
+                                static_cast<const int4*>(pairs), world, (int)rows, out, len_adv,
+                                adv, max_len, hist, hist_ld),
+                     "k_argmax_pairs");
 }
 
 }  // namespace syn

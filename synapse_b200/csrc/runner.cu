@@ -253,6 +253,10 @@ struct syn_cuda_model_s {
   int32_t* hist = nullptr;  // [max_batch][max_seq + 1] generated token per position
   void* am_scratch = nullptr;
   float* logits_l = nullptr;  // this rank's vocabulary slice of the logits (tp > 1)
+  // tp > 1, greedy steps without host logits: each row's argmax state over
+  // this rank's slice (16 B) and all ranks' states ([tp][max_batch])
+  int32_t* am_pair_l = nullptr;
+  int32_t* am_pair_g = nullptr;
   float* resid2 = nullptr;     // second residual buffer (fused single-row steps)
   bool no_fuse = false;        // SYN_RUNNER_FUSE=0 keeps the norms as separate kernels
   float *resid = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *o = nullptr,
@@ -461,10 +465,36 @@ syn_status_t forward(syn_cuda_model_s* m, size_t rows, bool prefill, size_t seq,
                                    cudaMemcpyDeviceToHost, st));
     return SYN_OK;
   }
-  if (tp) {  // vocab-parallel LM head: gather each row's logits in rank (= vocab) order
+  // vocab-parallel LM head. A greedy step without host logits gathers each
+  // rank's argmax state over its slice (16 bytes per row), not the logits;
+  // SYN_TP_ARGMAX_PAIRS=0 gathers the logits always.
+  static const bool pairs_on = [] {
+    const char* e = getenv("SYN_TP_ARGMAX_PAIRS");
+    return !(e && e[0] == '0');
+  }();
+  const bool tp_pairs = tp && pairs_on && !want_logits && !slots;
+  if (tp && !tp_pairs) {  // gather each row's logits in rank (= vocab) order
     for (size_t b = 0; b < nr; b++)
       if ((s = tp_allgather(m->ctx, m->logits_l + b * m->v_l, m->logits + b * m->V, m->v_l, st)))
         return s;
+  }
+  if (tp_pairs) {
+    s = launch_argmax_slice(m->logits_l, m->v_l, nr, m->v_l, (int)(m->tp_rank * m->v_l),
+                            m->am_pair_l, m->am_scratch, st);
+    if (s) return s;
+    s = tp_allgather(m->ctx, reinterpret_cast<const float*>(m->am_pair_l),
+                     reinterpret_cast<float*>(m->am_pair_g), 4 * nr, st);
+    if (s) return s;
+    s = launch_argmax_pairs(m->am_pair_g, m->tp, nr, m->tok + (prefill ? seq : 0),
+                            m->cache->d_len + (prefill ? seq : 0), prefill ? (int)rows : 1,
+                            (int)m->max_seq, m->hist + (prefill ? seq : 0) * (m->max_seq + 1),
+                            (int)(m->max_seq + 1), st);
+    if (s) return s;
+    if (chained) return SYN_OK;
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->tok_h, m->tok + (prefill ? seq : 0), nr * sizeof(int32_t),
+                                 cudaMemcpyDeviceToHost, st));
+    SYN_CUDA_TRY(cudaMemcpyAsync(m->err_h, m->ctx->err, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    return SYN_OK;
   }
   if (slots) {  // row b's token into tok[b]; each mapped sequence advances by one
     s = launch_argmax(m->logits, m->V, nr, m->V, m->tok, nullptr, 0, (int)m->max_seq, nullptr, 0,
@@ -705,6 +735,10 @@ syn_status_t syn_cuda_model_finalize(syn_cuda_model_t* m) {
   if ((s = dev_alloc_t(m, &m->gu, R * 2 * m->ff_l))) return s;
   if ((s = dev_alloc_t(m, &m->hid, R * m->ff_l))) return s;
   if (m->tp > 1 && (s = dev_alloc_t(m, &m->logits_l, m->max_batch * m->v_l))) return s;
+  if (m->tp > 1 && (s = dev_alloc_t(m, &m->am_pair_l, m->max_batch * 4))) return s;
+  if (m->tp > 1 &&
+      (s = dev_alloc_t(m, &m->am_pair_g, (size_t)m->tp * m->max_batch * 4)))
+    return s;
   if ((s = dev_alloc_t(m, &m->dn, R * h))) return s;
   if ((s = dev_alloc_t(m, &m->logits, m->max_batch * m->V))) return s;
   if ((s = dev_alloc_t(m, &m->span_logits, 16 * m->V))) return s;
