@@ -640,6 +640,49 @@ def run_gemm_case(args):
                       "tflops": round(2 * m * n * k / us / 1e6, 1)}), flush=True)
 
 
+def run_attn_case(args):
+    """--attn MODE:B:L:HQ:HKV:HD: times one decode-attention launch on cuda:0
+    (MODE exact = the reference-order kernel, flash = the block-format
+    models' grouped kernel) for B rows whose caches hold L-1 positions, and
+    prints the KV bytes it must read per second (profiling aid; not the
+    benchmark line)."""
+    import torch
+    import synapse_b200 as sb
+    mode, b, L, hq, hkv, hd = args.attn.split(":")
+    b, L, hq, hkv, hd = int(b), int(L), int(hq), int(hkv), int(hd)
+    ctx = sb.Context(0)
+    rng = np.random.default_rng(7)
+    cache = sb.KVCache(ctx, L + 8, hkv, hd, 1, batch=b)
+    kvd, qd = hkv * hd, hq * hd
+    for i in range(b):
+        kh = torch.from_numpy(rng.standard_normal((L - 1, kvd)).astype(np.float32)).cuda()
+        vh = torch.from_numpy(rng.standard_normal((L - 1, kvd)).astype(np.float32)).cuda()
+        cache.append(0, kh, vh, seq=i)
+        cache.advance(L - 1, seq=i)
+    cos, sin = sb.rope_tables(1e6, L + 8, hd)
+    cos, sin = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    qkv = torch.from_numpy(rng.standard_normal((b, qd + 2 * kvd)).astype(np.float32)).cuda()
+
+    def run():
+        return sb.attention_decode(cache, 0, qkv, hq, None, None, 1e-6, cos, sin, batch=b,
+                                   flash=mode == "flash")
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    kv_bytes = b * L * 2 * kvd * 4
+    print(json.dumps({"attn": args.attn, "us": round(us, 2),
+                      "kv_GB/s": round(kv_bytes / us / 1e3, 1)}), flush=True)
+    cache.close()
+    ctx.close()
+
+
 def run_decode_only(args, local_rank):
     """The config-1 decode leg alone (one process, no sweep, no CPU leg): the
     command the decode-step launch list is taken from."""
@@ -999,6 +1042,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the model decode leg")
     ap.add_argument("--case", default=None, help="FMT:N:K -- time one GEMV only (profiling)")
     ap.add_argument("--gemm", default=None, help="FMT:M:N:K -- time one GEMM only (profiling)")
+    ap.add_argument("--attn", default=None,
+                    help="exact|flash:B:L:HQ:HKV:HD -- time one decode attention (profiling)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the config-3/5 decode legs (LLaMA Q4_K batch 1/8, Qwen3 Q8_0 serving)")
     ap.add_argument("--decode-only", action="store_true",
@@ -1018,6 +1063,8 @@ def main():
         args.warmup = 3
     if args.gemm:
         run_gemm_case(args)
+    elif args.attn:
+        run_attn_case(args)
     elif args.decode_only:
         run_decode_only(args, local_rank)
     elif args.tp_decode_only:

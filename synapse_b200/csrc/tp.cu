@@ -215,8 +215,10 @@ void peer_release(syn_cuda_ctx_s* ctx) {
 // leaves ctx->tp_peer null and the NCCL path in use.
 syn_status_t peer_init(syn_cuda_ctx_s* ctx) {
   if (ctx->tp_world < 2 || ctx->tp_world > PEER_MAX_WORLD) return SYN_OK;
+  // Opt-in (SYN_TP_PEER_ALLREDUCE=1): on two B200s the Mistral-7B-shape
+  // decode ran at 395 tok/s with it against 421 tok/s with NCCL's.
   const char* env = getenv("SYN_TP_PEER_ALLREDUCE");
-  if (env && env[0] == '0') return SYN_OK;
+  if (!(env && env[0] == '1')) return SYN_OK;
   auto* ps = new (std::nothrow) PeerState();
   if (!ps) return SYN_ERR_OUT_OF_MEMORY;
   ps->world = ctx->tp_world;

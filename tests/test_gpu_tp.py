@@ -35,11 +35,12 @@ def _weights(fmt, name):
     return cfg, w
 
 
-def _rank(rank, world, port, fmt, name, q):
+def _rank(rank, world, port, fmt, name, q, peer="0"):
     import sys
     sys.path.insert(0, ROOT)
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      SYN_TP_PEER_ALLREDUCE=peer)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         _run_rank(rank, world, fmt, name, q, dist)
@@ -59,7 +60,7 @@ def _run_rank(rank, world, fmt, name, q, dist):
         dist.broadcast_object_list(obj, src=0)
         ctx.tp_init(rank, world, obj[0])
         cfg, w = _weights(fmt, name)
-        m = sb.Model(ctx, cfg, w, 64)
+        m = sb.Model(ctx, cfg, w, len(PROMPT) + STEPS + 8)
         tok, lg = m.forward_prefill(PROMPT)
         logits, toks = [lg], [tok]
         for _ in range(STEPS):
@@ -77,15 +78,16 @@ def _run_rank(rank, world, fmt, name, q, dist):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("peer", ["0", "1"])  # NCCL collectives / the peer-memory kernel
 @pytest.mark.parametrize("fmt,name", [("Q4_0", "tiny"), ("Q4_K", "tiny-k-tp")])
-def test_tp2_model_matches_oracle(fmt, name):
+def test_tp2_model_matches_oracle(fmt, name, peer):
     import torch.multiprocessing as mp
     from oracle import oracle as O
     from oracle.lm import OracleLM
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, fmt, name, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, fmt, name, q, peer)) for r in range(2)]
     for p in procs:
         p.start()
     got = q.get(timeout=300)
@@ -95,7 +97,7 @@ def test_tp2_model_matches_oracle(fmt, name):
         p.join(timeout=120)
         assert p.exitcode == 0
     cfg, w = _weights(fmt, name)
-    ref = OracleLM(cfg, w, 64)
+    ref = OracleLM(cfg, w, len(PROMPT) + STEPS + 8)
     lref = ref.forward_prefill(PROMPT)
     assert gen == toks[1:]  # on-device generation == per-step API
     for i in range(STEPS + 1):
@@ -114,7 +116,8 @@ def _ar_rank(rank, world, port, q):
     import sys
     sys.path.insert(0, ROOT)
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      SYN_TP_PEER_ALLREDUCE="1")  # the peer-memory kernel (opt-in)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         import synapse_b200 as sb
