@@ -41,7 +41,8 @@ def test_gemm_int8_bit_exact(ctx, m, n, k):
                                    (9, 8192, 512), (24, 8320, 256), (48, 8192, 512),
                                    (48, 384, 1024), (64, 160, 2048), (65, 256, 512),
                                    (128, 3072, 2048), (300, 100, 1024), (512, 1024, 4096),
-                                   (129, 4096, 512), (200, 300, 2048), (144, 256, 1024)])
+                                   (129, 4096, 512), (200, 300, 2048), (144, 256, 1024),
+                                   (32, 4096, 2048), (13, 4160, 1280)])
 def test_gemm_block_formats_within_tol(ctx, fmt, m, n, k):
     import synapse_b200 as sb
     from synapse_b200 import synth
@@ -159,3 +160,4 @@ def test_gemm_tm_crossover_both_paths(fmt, m, tmp_path):
     for y in outs:
         assert max(max_rel_err(y[i], yo[i]) for i in range(m)) <= TOL
     assert max(max_rel_err(outs[0][i], outs[1][i]) for i in range(m)) <= 2 * TOL
+
